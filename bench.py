@@ -1,0 +1,317 @@
+"""Benchmark of the B200 MoE hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1]
+
+A step is one MoE layer forward (router -> top-k -> dispatch -> 4-bit SwiGLU
+experts -> combine) over one batch of seeded synthetic tokens.  The default
+workload is BASELINE config 1: one Qwen3-30B-A3B MoE layer (E=128, top-8,
+H=2048, I=768, 4-bit group-64 experts, 8-bit router), batched prefill of
+T=512 tokens.  Config 0 (decode of one token) is selectable with --config 0.
+
+* value     tokens/s of the whole job, inputs resident in HBM, device-timed
+            (CUDA events, barrier + synchronize both sides, max over ranks).
+            Steps rotate over 4 resident layers (1.36 GB of weights, far more
+            than the 126 MB L2), so no step reads the previous step's weights
+            from L2.
+* e2e       the same metric through obs_moe_forward_host: pinned host input,
+            host->device copy, the layer, device->host copy of the output.
+* roofline  the dominant kernel (the gate/up grouped GEMM at T=512, the decode
+            gate/up mat-vec at T=1), algorithmic bytes per launch / its mean
+            CUDA-event duration on the launching stream, against the measured
+            HBM copy bandwidth in MEASURED_PEAKS.json.
+* cpu_baseline  the C oracle (oracle/, all host threads) on the same layer.
+
+--impl reference runs the reference's own kernels (shaders/*.metal compiled
+for the CPU into oracle/_ref) on the host cores over a bounded token sample.
+Multi-GPU (torchrun): every rank runs its own T-token batch against its own
+copy of the layers (replicas; weak scaling), timed on the device, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "project-obsidian_b200"))
+
+H, I, E, K = 2048, 768, 128, 8
+EXPERT_BYTES = 2_654_208        # one expert: 3 projections of 4-bit codes + bf16 scales/biases
+GATEUP_BYTES = 2 * 884_736      # the gate and up projections of one expert
+ROUTER_BYTES = 278_528
+N_ROT = 4                       # resident layers the steps rotate over
+CONFIGS = {
+    0: dict(T=1, name="config0: Qwen3-30B-A3B MoE layer, decode of 1 token"),
+    1: dict(T=512, name="config1: Qwen3-30B-A3B MoE layer, batched prefill of T=512 tokens"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self, index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        for r in rows:
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
+                               r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def cpu_baseline(L_host, x_host, T):
+    """The C oracle on the host cores (all threads), the same layer and tokens."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    n = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    O.moe_layer(L_host, x_host, nthreads=n)
+    dt = time.perf_counter() - t0
+    return {"value": T / dt, "unit": "tokens/s", "cores": n, "kind": "port",
+            "sample": f"the full {T}-token layer once through oracle/obs_oracle.c ({dt:.2f} s)"}
+
+
+def run_reference(args, rank, world):
+    """The reference's own kernels on the host cores (oracle/_ref)."""
+    cfg = CONFIGS[args.config]
+    T = cfg["T"]
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    if O.ref_lib() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libobs_refshaders.so was not built"}))
+        return
+    n = os.cpu_count() or 1
+    Ts = min(T, 64)  # bounded sample: one step is Ts tokens of the workload
+    L = O.synth_layer(0, 0, E=E, H=H, I=I, K=K)
+    x = O.synth_x(0, 0, Ts, H)
+    for _ in range(args.warmup):
+        O.ref_moe_prefill(L, x, nthreads=n)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.ref_moe_prefill(L, x, nthreads=n)
+    dt = time.perf_counter() - t0
+    value = Ts * args.steps / dt
+    sample = (f"{Ts} of the {T} tokens per step through the reference's shaders/*.metal kernels compiled "
+              f"for the CPU (oracle/_ref), strung as src/forward.rs:164-232, {n} threads")
+    print(json.dumps({
+        "impl": "reference", "metric": "MoE layer tokens/s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded, BASELINE config distributions)",
+        "config": {"workload": cfg["name"], "T": T, "E": E, "K": K, "H": H, "I": I, "sample_tokens": Ts},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": n, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import numpy as np
+    import torch
+
+    import obsmoe
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    cfg = CONFIGS[args.config]
+    T = cfg["T"]
+    path = obsmoe.PATH_DECODE if T <= 4 else obsmoe.PATH_PREFILL
+    shape = obsmoe.MoeShape(H, I, E, K, n_layers=N_ROT, max_tokens=max(T, 16))
+    ctx = obsmoe.MoeContext(shape, local)
+    for l in range(N_ROT):
+        ctx.synth_layer(l, 0)  # layer l of seed 0 (config 2's per-layer seeding)
+    xs = [torch.empty((T, H), dtype=torch.int16, device="cuda") for _ in range(N_ROT)]
+    for l, x in enumerate(xs):
+        obsmoe.synth_activations(rank, l, 0, T, H, x)
+    out = torch.empty((T, H), dtype=torch.int16, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        l = i % N_ROT
+        ctx.moe_forward(l, xs[l], out, T, path=path, stream=stream)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    ctx.check_device()
+    # ------------------------------------------------------------ timed region
+    clocks = Clocks(local)
+    ctx.profile(True)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    clk = clocks.stop()
+    ctx.check_device()
+    ms_t = torch.tensor([ms], device="cuda")
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    value = world * T * args.steps / (ms / 1e3)
+
+    # ---------------------------------------------------------------- e2e
+    xh = [torch.empty((T, H), dtype=torch.int16).pin_memory() for _ in range(N_ROT)]
+    for l in range(N_ROT):
+        xh[l].copy_(xs[l].cpu())
+    oh = torch.empty((T, H), dtype=torch.int16).pin_memory()
+    for i in range(3):
+        ctx.moe_forward_host(i % N_ROT, xh[i % N_ROT], oh, T, path=path, stream=stream)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        ctx.moe_forward_host(i % N_ROT, xh[i % N_ROT], oh, T, path=path, stream=stream)
+    e1.record(stream)
+    barrier()
+    ems_t = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+    if dist is not None:
+        dist.all_reduce(ems_t, op=dist.ReduceOp.MAX)
+    e2e_value = world * T * args.steps / (float(ems_t.item()) / 1e3)
+
+    # ------------------------------------------------ roofline of the top kernel
+    hbm, bf16, peak_kind = peaks()
+    # distinct experts per step (U), from the same routing the timed steps used
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    U = []
+    for l in range(N_ROT):
+        ctx.gate_gpu(l, xs[l], logits, T, stream=stream)
+        ctx.route(logits, T, ids, wts, stream=stream)
+        U.append(len(np.unique(ids.cpu().numpy())))
+    U_mean = sum(U) / len(U)
+    if path == obsmoe.PATH_PREFILL:
+        top = "gemm_gateup"
+        # gate+up weights of the U routed experts, the T*K permuted rows read, h written
+        alg = U_mean * GATEUP_BYTES + T * K * H * 2 + T * K * I * 2
+        kname = "k_gemm<kEpiSwiglu> (tcgen05 grouped gate/up GEMM + SwiGLU)"
+    else:
+        top = "decode_gateup"
+        alg = U_mean * GATEUP_BYTES + T * H * 2 + T * K * I * 2
+        kname = "k_decode_gateup (4-bit gate/up mat-vec)"
+    kms, kn = prof[top]
+    k_avg_s = kms / max(kn, 1) / 1e3
+    achieved = alg / k_avg_s / 1e9
+    stage_us = {k: round(v[0] / max(v[1], 1) * 1e3, 2) for k, v in prof.items() if v[1]}
+    layer_bytes = U_mean * EXPERT_BYTES + ROUTER_BYTES + 2 * T * H * 2
+    line = {
+        "metric": "MoE layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; BASELINE config distributions; weights generated on the device)",
+        "config": {"workload": cfg["name"], "T": T, "E": E, "K": K, "H": H, "I": I, "weights": "4-bit g64 (router 8-bit)",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2: steps rotate over {N_ROT} resident layers ({N_ROT * 340} MB)",
+                   "path": "prefill (tcgen05 grouped GEMM)" if path == obsmoe.PATH_PREFILL else "decode (mat-vec)"},
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "algorithmic_bytes_per_launch": alg, "traffic": None,
+                     "kernel_us": k_avg_s * 1e6},
+        "layer_hbm_gbs": layer_bytes / (ms / args.steps / 1e3) / 1e9,
+        "layer_tflops": 2 * T * K * 4_718_592 / (ms / args.steps / 1e3) / 1e12,
+        "stage_us": stage_us, "distinct_experts": U_mean,
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2},
+        "gpu_launches": sum(v[1] for v in prof.values()),
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+
+        Lh = O.synth_layer(0, 0, E=E, H=H, I=I, K=K)
+        line["cpu_baseline"] = cpu_baseline(Lh, xs[0].cpu().numpy().view(np.uint16), T)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,161 @@
+/*
+ * obs_moe.h -- C ABI of the B200 (sm_100a) MoE hot path for project-obsidian.
+ *
+ * The library replaces the MoE section of the reference's per-layer forward
+ * (src/forward.rs:421-441 decode, :164-247 batched prefill) and the Metal
+ * helpers it encodes through ObsidianExecutor (src/executor.rs:60-70).  Every
+ * entry point is plain C: pointers, sizes, an opaque context, a CUDA stream
+ * passed as void*.  All return an int status (OBS_OK = 0); obs_last_error()
+ * gives the message, the way the reference's helpers return Result<_, String>.
+ *
+ * Data formats are the reference's (MLX affine quantisation, row-major):
+ *   router   W uint32 [E, H/4]   8-bit codes, byte i of a row = column i
+ *            s, b bf16 [E, H/64]                       (dequant_matvec_8bit.metal:8-31)
+ *   experts  W uint32 [E, out, in/8]  4-bit codes, nibble j of a word = (w>>4j)&15
+ *            s, b bf16 [E, out, in/64]                 (fused_dequant_matvec_4bit.metal:14-53,
+ *                                                       tools/split_experts.py:63-75)
+ *   gate/up: out = I, in = H;  down: out = H, in = I.
+ *   activations bf16 [T, H] (the reference uses f16; bf16 here, fp32 accumulate).
+ *
+ * Threading: one context per GPU, driven from one host thread at a time; the
+ * context owns its scratch, so calls on one context must not overlap on the
+ * GPU.  Device pointers unless a name ends in _host.
+ */
+#ifndef OBS_MOE_H
+#define OBS_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OBS_ABI_VERSION 1
+
+enum obs_status {
+    OBS_OK = 0,
+    OBS_ERR_INVALID = 1,   /* bad argument or shape */
+    OBS_ERR_CUDA = 2,      /* a CUDA runtime call failed */
+    OBS_ERR_NOMEM = 3,     /* device or host allocation failed */
+    OBS_ERR_STATE = 4,     /* e.g. layer not loaded, EP not initialised */
+    OBS_ERR_TIMEOUT = 5,   /* a bounded device-side wait gave up */
+    OBS_ERR_NCCL = 6,      /* an NCCL call failed or a peer went away */
+    OBS_ERR_UNSUPPORTED = 7
+};
+
+/* Execution path of obs_moe_forward. */
+enum obs_path {
+    OBS_PATH_AUTO = 0,     /* decode mat-vec for T <= decode_max_tokens, else prefill */
+    OBS_PATH_DECODE = 1,   /* per-token fused 4-bit mat-vec (fused_dequant_matvec_4bit) */
+    OBS_PATH_PREFILL = 2   /* dispatch + tcgen05 grouped GEMM (matmul_dequant_4bit) */
+};
+
+typedef struct obs_ctx obs_ctx;
+
+/* Model shape; mirrors the fields of Qwen3MoeConfig the MoE path reads
+ * (src/model.rs:7-23). */
+typedef struct obs_config {
+    int32_t hidden;            /* H: multiple of 2048 */
+    int32_t inter;             /* I: moe_intermediate_size, multiple of 128 */
+    int32_t n_experts;         /* E: <= 256 */
+    int32_t top_k;             /* K: <= 16 */
+    int32_t group_size;        /* must be 64 */
+    int32_t n_layers;          /* layers whose weights the context holds */
+    int32_t max_tokens;        /* largest T of one call (sizes the scratch) */
+    int32_t norm_topk;         /* renormalise the top-k weights (norm_topk_prob) */
+    int32_t decode_max_tokens; /* OBS_PATH_AUTO threshold; <= 0 picks 4 */
+    float rms_eps;             /* RMSNorm epsilon of the fused input norm */
+} obs_config;
+
+/* One layer's weights in the reference format (host or device memory). */
+typedef struct obs_layer_weights {
+    const uint32_t* router_w; const uint16_t* router_s; const uint16_t* router_b;
+    const uint32_t* gate_w;   const uint16_t* gate_s;   const uint16_t* gate_b;
+    const uint32_t* up_w;     const uint16_t* up_s;     const uint16_t* up_b;
+    const uint32_t* down_w;   const uint16_t* down_s;   const uint16_t* down_b;
+} obs_layer_weights;
+
+/* ---------------------------------------------------------------- context */
+int obs_abi_version(void);
+/* Replaces ObsidianExecutor::new (src/executor.rs:39-58) and the expert pools
+ * of Model::new (src/forward.rs:79-89): selects `device`, allocates the
+ * HBM-resident expert store for n_layers layers and all scratch up front. */
+int obs_create(const obs_config* cfg, int device, obs_ctx** out);
+int obs_destroy(obs_ctx* ctx);
+const char* obs_last_error(const obs_ctx* ctx);
+/* Bytes of device memory the context holds (weights + scratch). */
+int obs_memory_bytes(const obs_ctx* ctx, size_t* weights, size_t* scratch);
+
+/* Replaces ExpertIndex::open + read_experts_parallel (src/disk_io.rs:24-102)
+ * and the router part of Weights::load_non_expert (src/weight_loader.rs:19-71):
+ * copies one layer into the context's HBM store, re-tiled for the kernels.
+ * src_on_device != 0 if the pointers are device memory.  Synchronous. */
+int obs_load_layer(obs_ctx* ctx, int layer, const obs_layer_weights* w, int src_on_device);
+
+/* Seeded synthetic layer generated on the device (bench/test support): the
+ * same values oracle/obs_oracle.c produces on the host for (seed, layer). */
+int obs_synth_layer(obs_ctx* ctx, int layer, uint64_t seed);
+/* Seeded synthetic activations rows [row0, row0+T) of (seed, layer),
+ * RMSNormed with eps, written to x [T, H] bf16 on `stream`. */
+int obs_synth_activations(uint64_t seed, uint32_t layer, int row0, int T, int H, float eps,
+                          uint16_t* x, void* stream);
+
+/* ------------------------------------------------------ the MoE layer path */
+/* out = [residual +] sum_k w_k * expert_k(x): router -> top-k -> dispatch ->
+ * 4-bit SwiGLU experts -> rank-order combine, all on `stream`, no host sync.
+ * Replaces forward.rs:421-441 (decode) and :164-232 (batched prefill).
+ * residual and logit_bias (fp32 [E], added to the router logits) may be NULL.
+ * x and out are bf16 [T, H] device arrays; T <= max_tokens. */
+int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint16_t* out,
+                    const uint16_t* residual, int T, const float* logit_bias, int path,
+                    void* stream);
+/* Same, from and to host memory: copies x (and residual) in, out back, and
+ * waits for the stream.  Pinned host memory gives the full copy bandwidth. */
+int obs_moe_forward_host(obs_ctx* ctx, int layer, const uint16_t* x_host, uint16_t* out_host,
+                         const uint16_t* residual_host, int T, const float* logit_bias_host,
+                         int path, void* stream);
+
+/* ----------------------------------- stage entry points (tests, debugging) */
+/* gate_gpu / dequant_matvec_8bit (forward.rs:386-397): router logits fp32
+ * [T, E] in the canonical reduction order: 32 lanes, lane l chains
+ * acc = fma(w, x, acc) over its 64-column groups in column order, then the
+ * lane sums meet in the adjacent pairwise tree (offsets 1, 2, 4, 8, 16). */
+int obs_gate(obs_ctx* ctx, int layer, const uint16_t* x, float* logits, int T, void* stream);
+/* moe_routing_topk (moe_routing_topk.metal:15-57; router.rs:25-94): softmax,
+ * top-k with the lowest index winning ties, renormalised weights. */
+int obs_route(obs_ctx* ctx, const float* logits, const float* logit_bias, int T,
+              int32_t* ids, float* weights, void* stream);
+/* Token -> expert grouping (forward.rs:176-216) on the device: counts [E],
+ * padded segment starts seg [E+1] (each segment a multiple of 16 rows), and
+ * slot_of [T*K] (slots ordered by expert, then token). */
+int obs_dispatch(obs_ctx* ctx, const int32_t* ids, int T, int32_t* counts, int32_t* seg,
+                 int32_t* slot_of, void* stream);
+/* Expert outputs y [T*K, H] bf16 in (token, rank) order for given routes,
+ * through the decode mat-vec or the prefill grouped GEMM path. */
+int obs_expert_ffn(obs_ctx* ctx, int layer, const uint16_t* x, const int32_t* ids, int T,
+                   int path, uint16_t* y, void* stream);
+/* One expert projection on the tcgen05 grouped GEMM with a plain fp32
+ * epilogue: y [n, out] = x [n, in] . dequant(W)^T (matmul_dequant_4bit.metal:21-66).
+ * proj 0 gate, 1 up, 2 down.  n <= max_tokens * top_k. */
+int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert, const uint16_t* x, int n,
+                        float* y, void* stream);
+/* Per-stage device timing of obs_moe_forward for benchmarks: when enabled,
+ * every kernel launch of the layer is bracketed by CUDA events on the
+ * caller's stream.  obs_profile_read fills ms_total[OBS_N_STAGES] and
+ * launches[OBS_N_STAGES] with the sums since the last read, then resets. */
+#define OBS_N_STAGES 8
+enum obs_stage {
+    OBS_STAGE_ROUTER = 0, OBS_STAGE_TOPK = 1, OBS_STAGE_DISPATCH = 2, OBS_STAGE_GEMM_GATEUP = 3,
+    OBS_STAGE_GEMM_DOWN = 4, OBS_STAGE_COMBINE = 5, OBS_STAGE_DECODE_GATEUP = 6, OBS_STAGE_DECODE_DOWN = 7
+};
+int obs_profile_enable(obs_ctx* ctx, int enable);
+int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches);
+/* Waits for the stream and reports any device-side error flag (bounded waits
+ * that gave up) raised since the last check; clears the flags. */
+int obs_check_device(obs_ctx* ctx, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OBS_MOE_H */

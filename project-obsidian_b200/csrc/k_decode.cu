@@ -1,0 +1,196 @@
+// k_decode.cu -- decode expert FFN: fused 4-bit dequant mat-vec on CUDA cores.
+//
+// Replaces the reference's per-rank loop of fused_dequant_matvec_4bit x3 +
+// ew_swiglu + ew_scaled_add (src/forward.rs:431-441; shaders/
+// fused_dequant_matvec_4bit.metal:14-53, ops.metal:18-29).  Weights are read
+// once, fully coalesced, from the tiled 4608-byte blocks (128 rows x 64
+// columns + scales + biases); dequantisation is w = fma(q, s, b) in fp32 as in
+// the reference.  Split-K partial sums meet in a fixed order in the last CTA
+// to finish (a per-tile arrival counter that resets itself), so results do
+// not depend on CTA scheduling.
+#include "obs_internal.cuh"
+
+namespace obs {
+namespace {
+
+constexpr int kSplitGU = 4;  // k-splits of the gate/up mat-vec
+
+// exact float of a 4-bit code without I2F: (2^23 | q) - 2^23
+__device__ __forceinline__ float nib_f(uint32_t w, int j) {
+    return __fsub_rn(__uint_as_float(0x4B000000u | ((w >> (4 * j)) & 0xFu)), 8388608.0f);
+}
+
+// One warp, one 128x64 block: lane l covers rows (l>>1) + 16 i (i < 8) and the
+// 32 columns of half (l & 1).  xr: the lane's 32 activations (fp32).
+__device__ __forceinline__ void block_dot(const uint8_t* __restrict__ blk, const float (&xr)[32], int lane,
+                                          float (&acc)[8]) {
+    const uint4* wq = reinterpret_cast<const uint4*>(blk);
+    const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
+    uint4 q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = __ldg(wq + i * 32 + lane);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int row = (lane >> 1) + 16 * i;
+        const float sc = bf2f(__ldg(sb + row)), bi = bf2f(__ldg(sb + kRowTile + row));
+        const uint32_t ws[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
+        float a = acc[i];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a = __fmaf_rn(__fmaf_rn(nib_f(ws[c], j), sc, bi), xr[c * 8 + j], a);
+        acc[i] = a;
+    }
+}
+
+__device__ __forceinline__ void load_x32(const uint16_t* __restrict__ x, float (&xr)[32]) {
+    const uint4* p = reinterpret_cast<const uint4*>(x);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        uint4 q = __ldg(p + v);
+        uint32_t qs[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            xr[v * 8 + 2 * c] = __uint_as_float(qs[c] << 16);
+            xr[v * 8 + 2 * c + 1] = __uint_as_float(qs[c] & 0xFFFF0000u);
+        }
+    }
+}
+
+// An out-of-range expert id is reported and replaced by 0, so every CTA still
+// takes part in its tile's arrival count and no weight outside the layer is read.
+__device__ __forceinline__ int checked_expert(int e, int E, int* err) {
+    if (e >= 0 && e < E) return e;
+    if (threadIdx.x == 0) atomicExch(err, kDevBadRoute);
+    return 0;
+}
+
+// grid (I/128, kSplitGU, T*K), 256 threads.  warp w: projection w & 1,
+// k-tiles kt0 + (w >> 1) + 4 j.
+__global__ void __launch_bounds__(256) k_decode_gateup(const uint8_t* __restrict__ gateup,
+                                                       const uint16_t* __restrict__ x,
+                                                       const int32_t* __restrict__ ids, int H, int I, int K,
+                                                       int E, DecodeBufs d) {
+    __shared__ float s_part[8][kRowTile];
+    __shared__ float s_gu[2][kRowTile];
+    __shared__ int s_last;
+    const int rt = blockIdx.x, ks = blockIdx.y, p = blockIdx.z;
+    const int n_rt = gridDim.x, KT = H / kGroup, nkt = KT / kSplitGU;
+    const int t = p / K, e = checked_expert(ids[p], E, d.err);
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, proj = w & 1;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = (w >> 1); j < nkt; j += 4) {
+        const int kt = ks * nkt + j;
+        const uint8_t* blk = gateup + ((((size_t)e * n_rt + rt) * KT + kt) * 2 + proj) * kBlockBytes;
+        float xr[32];
+        load_x32(x + (size_t)t * H + kt * kGroup + (lane & 1) * 32, xr);
+        block_dot(blk, xr, lane, acc);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float v = acc[i] + __shfl_xor_sync(0xffffffffu, acc[i], 1);
+        if ((lane & 1) == 0) s_part[w][(lane >> 1) + 16 * i] = v;
+    }
+    __syncthreads();
+    // fixed-order sum of the 4 warps of each projection
+    const int pr = tid >> 7, row = tid & 127;
+    const float v = ((s_part[pr][row] + s_part[pr + 2][row]) + s_part[pr + 4][row]) + s_part[pr + 6][row];
+    float* part = d.part + (((size_t)p * n_rt + rt) * kSplitGU) * 2 * kRowTile;
+    part[(size_t)ks * 2 * kRowTile + pr * kRowTile + row] = v;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t* c = d.cnt_gu + (size_t)p * n_rt + rt;
+        unsigned old = atomicAdd(c, 1u);
+        s_last = (old == kSplitGU - 1);
+        if (s_last) *c = 0;  // ready for the next call
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kSplitGU; ++j) sum += __ldcg(part + (size_t)j * 2 * kRowTile + pr * kRowTile + row);
+    s_gu[pr][row] = sum;
+    __syncthreads();
+    if (tid < kRowTile) {
+        const float g = s_gu[0][tid], u = s_gu[1][tid];
+        d.h[(size_t)p * I + rt * kRowTile + tid] = f2bf((g / (1.0f + expf(-g))) * u);  // ops.metal:21
+    }
+}
+
+// grid (H/128, K, T), 256 threads.  warp w: k-tiles w, w+8, ...
+__global__ void __launch_bounds__(256) k_decode_down(const uint8_t* __restrict__ down,
+                                                     const int32_t* __restrict__ ids, const float* __restrict__ wts,
+                                                     const uint16_t* __restrict__ residual, int H, int I, int K,
+                                                     int E, DecodeBufs d, uint16_t* __restrict__ out,
+                                                     int do_combine) {
+    __shared__ float s_part[8][kRowTile];
+    __shared__ int s_last;
+    const int rt = blockIdx.x, k = blockIdx.y, t = blockIdx.z;
+    const int n_rt = gridDim.x, KT = I / kGroup;
+    const int p = t * K + k, e = checked_expert(ids[p], E, d.err);
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int kt = w; kt < KT; kt += 8) {
+        const uint8_t* blk = down + (((size_t)e * n_rt + rt) * KT + kt) * kBlockBytes;
+        float xr[32];
+        load_x32(d.h + (size_t)p * I + kt * kGroup + (lane & 1) * 32, xr);
+        block_dot(blk, xr, lane, acc);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float v = acc[i] + __shfl_xor_sync(0xffffffffu, acc[i], 1);
+        if ((lane & 1) == 0) s_part[w][(lane >> 1) + 16 * i] = v;
+    }
+    __syncthreads();
+    if (tid < kRowTile) {
+        float v = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v += s_part[j][tid];
+        d.y[(size_t)p * H + rt * kRowTile + tid] = f2bf(v);
+    }
+    if (!do_combine) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t* c = d.cnt_dn + (size_t)t * n_rt + rt;
+        unsigned old = atomicAdd(c, 1u);
+        s_last = (old == (unsigned)K - 1);
+        if (s_last) *c = 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid < kRowTile) {
+        // rank-order combine, same operation order as k_combine (forward.rs:225-232)
+        const int f = rt * kRowTile + tid;
+        float a = residual ? bf2f(residual[(size_t)t * H + f]) : 0.0f;
+        for (int j = 0; j < K; ++j) {
+            const uint16_t yv = __ldcg(d.y + ((size_t)t * K + j) * H + f);
+            a = __fmaf_rn(wts[(size_t)t * K + j], bf2f(yv), a);
+        }
+        out[(size_t)t * H + f] = f2bf(a);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_decode_gateup(const LayerDev& L, const Shape& sh, const uint16_t* x, const int32_t* ids, int T,
+                                 const DecodeBufs& d, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    dim3 grid(sh.I / kRowTile, kSplitGU, T * sh.K);
+    k_decode_gateup<<<grid, 256, 0, st>>>(L.gateup, x, ids, sh.H, sh.I, sh.K, sh.E, d);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t* ids, const float* w,
+                               const uint16_t* residual, int T, const DecodeBufs& d, uint16_t* out, int do_combine,
+                               cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    dim3 grid(sh.H / kRowTile, sh.K, T);
+    k_decode_down<<<grid, 256, 0, st>>>(L.down, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, do_combine);
+    return cudaGetLastError();
+}
+
+}  // namespace obs

@@ -1,0 +1,194 @@
+// k_dispatch.cu -- token -> expert dispatch and the weighted combine.
+//
+// Replaces the reference's CPU grouping and gather (src/forward.rs:176-216:
+// union of routed experts, per-expert token lists, memcpy of rows) and the
+// rank-order scatter of scaled adds (forward.rs:225-232, ops.metal:25-29).
+// Slots are ordered by expert, then token (the order of the reference's
+// per-expert lists); each expert's segment is padded to 16 rows so a GEMM tile
+// never straddles two experts and its row count is a legal tcgen05 N.
+#include "obs_internal.cuh"
+
+namespace obs {
+namespace {
+
+constexpr int kDispThreads = 512;
+
+__device__ __forceinline__ int pad_rows(int c) { return (c + kSegAlign - 1) / kSegAlign * kSegAlign; }
+
+// grid = E; CTA e computes its segment, the stable slot order of its tokens,
+// its GEMM token tiles, and copies its rows into the tiled activation layout.
+__global__ void __launch_bounds__(kDispThreads) k_dispatch(const int32_t* __restrict__ ids,
+                                                           const uint16_t* __restrict__ x, int T, int H, int E,
+                                                           int K, DispatchBufs d, int permute) {
+    __shared__ int s_red[2][kDispThreads / 32];
+    __shared__ int s_warp[kDispThreads / 32];
+    __shared__ int s_base;
+    const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int bn = d.bn;
+
+    // padded segment start and tile start of expert e
+    int my_seg = 0, my_tiles = 0;
+    for (int i = tid; i < e; i += kDispThreads) {
+        int p = pad_rows(d.counts[i]);
+        my_seg += p;
+        my_tiles += (p + bn - 1) / bn;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        my_seg += __shfl_xor_sync(0xffffffffu, my_seg, o);
+        my_tiles += __shfl_xor_sync(0xffffffffu, my_tiles, o);
+    }
+    if (lane == 0) s_red[0][wid] = my_seg, s_red[1][wid] = my_tiles;
+    if (tid == 0) s_base = 0;
+    __syncthreads();
+    int seg = 0, tile0 = 0;
+    for (int i = 0; i < kDispThreads / 32; ++i) seg += s_red[0][i], tile0 += s_red[1][i];
+    const int cnt = d.counts[e];
+    const int P = pad_rows(cnt);
+    const int ntile = (P + bn - 1) / bn;
+
+    // stable ordered compaction of the tokens routed to e
+    for (int c0 = 0; c0 < T; c0 += kDispThreads) {
+        int t = c0 + tid, kfound = -1;
+        if (t < T)
+            for (int k = 0; k < K; ++k)
+                if (ids[(size_t)t * K + k] == e) kfound = k;
+        unsigned bal = __ballot_sync(0xffffffffu, kfound >= 0);
+        if (lane == 0) s_warp[wid] = __popc(bal);
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int i = 0; i < kDispThreads / 32; ++i) {
+            int v = s_warp[i];
+            if (i < wid) before += v;
+            total += v;
+        }
+        if (kfound >= 0) {
+            int slot = seg + s_base + before + __popc(bal & ((1u << lane) - 1u));
+            d.slot_of[(size_t)t * K + kfound] = slot;
+            d.src[slot] = t;
+        }
+        __syncthreads();
+        if (tid == 0) s_base += total;
+        __syncthreads();
+    }
+    for (int r = cnt + tid; r < P; r += kDispThreads) d.src[seg + r] = -1;
+    for (int j = tid; j < ntile; j += kDispThreads)
+        d.tiles[tile0 + j] = make_int4(e, seg + j * bn, min(bn, P - j * bn), 0);
+    if (e == E - 1 && tid == 0) {
+        *d.n_tiles = tile0 + ntile;
+        d.seg[E] = seg + P;
+    }
+    if (tid == 0) d.seg[e] = seg;
+    if (!permute) return;
+    __syncthreads();  // d.src of this segment written above by this CTA
+
+    // copy rows into the tiled layout: one 16-byte chunk per thread
+    const int chunks = H / 8;
+    for (size_t i = tid; i < (size_t)P * chunks; i += kDispThreads) {
+        int r = (int)(i / chunks), c = (int)(i % chunks) * 8;
+        int slot = seg + r;
+        int t = d.src[slot];
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (t >= 0) v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + c));
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(d.xp) + tiled_off(slot, c, d.atoms)) = v;
+    }
+}
+
+// out[t] = bf16(residual[t] + sum_k w[t,k] * y[slot_of[t,k]]), rank order, fp32
+__global__ void __launch_bounds__(256) k_combine(const uint16_t* __restrict__ y, int y_ld,
+                                                 const int32_t* __restrict__ slot_of, const float* __restrict__ w,
+                                                 const uint16_t* __restrict__ residual, int H, int K,
+                                                 uint16_t* __restrict__ out) {
+    const int t = blockIdx.x;
+    for (int f = threadIdx.x * 8; f < H; f += blockDim.x * 8) {
+        float acc[8];
+        if (residual) {
+            uint4 r = __ldg(reinterpret_cast<const uint4*>(residual + (size_t)t * H + f));
+            uint32_t rs[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[2 * c] = __uint_as_float(rs[c] << 16), acc[2 * c + 1] = __uint_as_float(rs[c] & 0xFFFF0000u);
+        } else {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
+        }
+        for (int k = 0; k < K; ++k) {
+            int slot = slot_of[(size_t)t * K + k];
+            float wk = w[(size_t)t * K + k];
+            uint4 v = __ldg(reinterpret_cast<const uint4*>(y + (size_t)slot * y_ld + f));
+            uint32_t vs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                acc[2 * c] = __fmaf_rn(wk, __uint_as_float(vs[c] << 16), acc[2 * c]);
+                acc[2 * c + 1] = __fmaf_rn(wk, __uint_as_float(vs[c] & 0xFFFF0000u), acc[2 * c + 1]);
+            }
+        }
+        uint4 o = make_uint4(pack_bf2(acc[0], acc[1]), pack_bf2(acc[2], acc[3]), pack_bf2(acc[4], acc[5]),
+                             pack_bf2(acc[6], acc[7]));
+        *reinterpret_cast<uint4*>(out + (size_t)t * H + f) = o;
+    }
+}
+
+// counts[e] += 1 per route; ids outside [0, E) are skipped and flagged
+__global__ void k_histogram(const int32_t* __restrict__ ids, int n, int E, int32_t* __restrict__ counts,
+                            int* __restrict__ err) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        int e = ids[i];
+        if (e >= 0 && e < E) atomicAdd(counts + e, 1);
+        else atomicExch(err, kDevBadRoute);
+    }
+}
+
+__global__ void k_gather_rows(const uint16_t* __restrict__ y, const int32_t* __restrict__ slot_of, int H,
+                              uint16_t* __restrict__ out) {
+    const int i = blockIdx.x;
+    const int slot = slot_of[i];
+    for (int f = threadIdx.x * 8; f < H; f += blockDim.x * 8)
+        *reinterpret_cast<uint4*>(out + (size_t)i * H + f) =
+            __ldg(reinterpret_cast<const uint4*>(y + (size_t)slot * H + f));
+}
+
+__global__ void k_tile_rows(const uint16_t* __restrict__ x, int n, int cols, int atoms, uint16_t* __restrict__ dst) {
+    const int r = blockIdx.x;  // rows [n, pad16(n)) are zero-filled
+    for (int c = threadIdx.x * 8; c < cols; c += blockDim.x * 8) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < n) v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)r * cols + c));
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(dst) + tiled_off(r, c, atoms)) = v;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_dispatch(const int32_t* ids, const uint16_t* x, int T, const Shape& sh, const DispatchBufs& d,
+                            int permute, cudaStream_t st) {
+    k_dispatch<<<sh.E, kDispThreads, 0, st>>>(ids, x, T, sh.H, sh.E, sh.K, d, permute);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const uint16_t* y, int y_ld, const int32_t* slot_of, const float* w,
+                           const uint16_t* residual, int T, int H, int K, uint16_t* out, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    k_combine<<<T, 256, 0, st>>>(y, y_ld, slot_of, w, residual, H, K, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_histogram(const int32_t* ids, int n, int E, int32_t* counts, int* err, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_histogram<<<(n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024, 256, 0, st>>>(ids, n, E, counts, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const uint16_t* y, const int32_t* slot_of, int rows, int H, uint16_t* out,
+                               cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    k_gather_rows<<<rows, 256, 0, st>>>(y, slot_of, H, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tile_rows(const uint16_t* x, int n, int cols, int atoms, uint16_t* dst, cudaStream_t st) {
+    int rows = (n + kSegAlign - 1) / kSegAlign * kSegAlign;
+    if (rows <= 0) return cudaSuccess;
+    k_tile_rows<<<rows, 256, 0, st>>>(x, n, cols, atoms, dst);
+    return cudaGetLastError();
+}
+
+}  // namespace obs

@@ -1,0 +1,602 @@
+// obs_api.cu -- the C ABI (include/obs_moe.h): context, HBM-resident weight
+// store, scratch, and the MoE layer schedule on one CUDA stream.
+//
+// The reference keeps experts on SSD and pages the routed ones in per token
+// (src/disk_io.rs:79-102, src/forward.rs:424-434), with the CPU blocking on the
+// router every layer (src/router.rs:47-48).  Here every layer's experts are
+// resident in HBM (about 340 MB per Qwen3-30B-A3B layer, 16.3 GB for 48), all
+// scratch is allocated once in obs_create, and a forward call is a fixed
+// sequence of kernel launches with no host synchronisation.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/obs_moe.h"
+#include "obs_internal.cuh"
+
+using namespace obs;
+
+namespace {
+constexpr int kDecodeMaxT = 64;  // largest T the decode path's scratch covers
+constexpr int kBNTile = 128;     // GEMM token tile
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+}  // namespace
+
+struct obs_ctx {
+    obs_config cfg{};
+    Shape sh{};
+    int device = 0, num_sms = 148;
+    std::string err;
+    std::vector<LayerDev> layers;
+    uint8_t* wmem = nullptr;
+    uint8_t* smem_pool = nullptr;
+    size_t wbytes = 0, sbytes = 0;
+    size_t layer_bytes = 0;
+    // scratch
+    float* logits = nullptr;
+    int32_t* ids = nullptr;
+    float* wts = nullptr;
+    DispatchBufs disp{};
+    uint16_t* hbuf = nullptr;
+    uint16_t* ybuf = nullptr;
+    float* yf32 = nullptr;
+    DecodeBufs dec{};
+    int* err_flag = nullptr;
+    uint16_t* x_dev = nullptr;
+    uint16_t* out_dev = nullptr;
+    uint16_t* res_dev = nullptr;
+    float* bias_dev = nullptr;
+    int R_cap = 0, max_tiles = 0, decode_max = 4;
+    // optional per-stage event timing (obs_profile_enable)
+    bool prof = false;
+    std::vector<cudaEvent_t> ev_pool;
+    std::vector<std::pair<int, int>> ev_marks;  // (stage, index of start event; stop = +1)
+};
+
+static void prof_begin(obs_ctx* c, int stage, cudaStream_t st) {
+    if (!c->prof) return;
+    size_t i = c->ev_marks.size() * 2;
+    while (c->ev_pool.size() < i + 2) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        c->ev_pool.push_back(e);
+    }
+    cudaEventRecord(c->ev_pool[i], st);
+    c->ev_marks.push_back({stage, (int)i});
+}
+static void prof_end(obs_ctx* c, cudaStream_t st) {
+    if (!c->prof || c->ev_marks.empty()) return;
+    cudaEventRecord(c->ev_pool[c->ev_marks.back().second + 1], st);
+}
+
+#define OBS_CHECK_CTX(c)                  \
+    do {                                  \
+        if (!(c)) return OBS_ERR_INVALID; \
+    } while (0)
+
+static int fail(obs_ctx* c, int code, const std::string& msg) {
+    if (c) c->err = msg;
+    return code;
+}
+static int cuda_fail(obs_ctx* c, cudaError_t e, const char* what) {
+    return fail(c, OBS_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+#define CU(call, what)                                          \
+    do {                                                        \
+        cudaError_t e_ = (call);                                \
+        if (e_ != cudaSuccess) return cuda_fail(ctx, e_, what); \
+    } while (0)
+
+static inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ------------------------------------------------------------------ context
+extern "C" int obs_abi_version(void) { return OBS_ABI_VERSION; }
+
+// obs_create has no context to hold its message yet: it lands here (per thread)
+static thread_local std::string g_create_err;
+
+extern "C" const char* obs_last_error(const obs_ctx* ctx) { return ctx ? ctx->err.c_str() : g_create_err.c_str(); }
+
+static size_t layer_weight_bytes(const Shape& s) {
+    size_t router = align_up((size_t)s.E * s.H, 256) + 2 * align_up((size_t)s.E * (s.H / 64) * 2, 256);
+    size_t gu = (size_t)s.E * (s.I / kRowTile) * (s.H / kGroup) * 2 * kBlockBytes;
+    size_t dn = (size_t)s.E * (s.H / kRowTile) * (s.I / kGroup) * kBlockBytes;
+    return router + align_up(gu, 256) + align_up(dn, 256);
+}
+
+extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
+    if (!cfg || !out) return OBS_ERR_INVALID;
+    *out = nullptr;
+    obs_ctx* ctx = new obs_ctx();
+    ctx->cfg = *cfg;
+    ctx->sh = Shape{cfg->hidden, cfg->inter, cfg->n_experts, cfg->top_k};
+    const Shape& s = ctx->sh;
+    auto bad = [&](const char* m) {
+        g_create_err = m;
+        delete ctx;
+        return OBS_ERR_INVALID;
+    };
+    if (cfg->group_size != 64) return bad("group_size must be 64");
+    if (s.H <= 0 || s.H % 2048) return bad("hidden must be a multiple of 2048");
+    if (s.I <= 0 || s.I % kRowTile) return bad("inter must be a multiple of 128");
+    if (s.E <= 0 || s.E > 256) return bad("n_experts must be in 1..256");
+    if (s.K <= 0 || s.K > 16 || s.K > s.E) return bad("top_k must be in 1..min(16, n_experts)");
+    if (cfg->n_layers <= 0 || cfg->max_tokens <= 0) return bad("n_layers and max_tokens must be positive");
+    ctx->decode_max = cfg->decode_max_tokens > 0 ? cfg->decode_max_tokens : 4;
+    if (ctx->decode_max > kDecodeMaxT) ctx->decode_max = kDecodeMaxT;
+    ctx->device = device;
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) {
+        g_create_err = std::string("device: ") + cudaGetErrorString(e);
+        delete ctx;
+        return OBS_ERR_CUDA;
+    }
+
+    // weights for all layers
+    ctx->layer_bytes = layer_weight_bytes(s);
+    ctx->wbytes = ctx->layer_bytes * cfg->n_layers;
+    e = cudaMalloc(&ctx->wmem, ctx->wbytes);
+    if (e != cudaSuccess) {
+        ctx->wmem = nullptr;
+        g_create_err = std::string("weights: ") + cudaGetErrorString(e);
+        obs_destroy(ctx);
+        return OBS_ERR_NOMEM;
+    }
+    ctx->layers.resize(cfg->n_layers);
+    for (int l = 0; l < cfg->n_layers; ++l) {
+        uint8_t* p = ctx->wmem + ctx->layer_bytes * l;
+        LayerDev& L = ctx->layers[l];
+        L.router_w = reinterpret_cast<uint32_t*>(p);
+        p += align_up((size_t)s.E * s.H, 256);
+        L.router_s = reinterpret_cast<uint16_t*>(p);
+        p += align_up((size_t)s.E * (s.H / 64) * 2, 256);
+        L.router_b = reinterpret_cast<uint16_t*>(p);
+        p += align_up((size_t)s.E * (s.H / 64) * 2, 256);
+        L.gateup = p;
+        p += align_up((size_t)s.E * (s.I / kRowTile) * (s.H / kGroup) * 2 * kBlockBytes, 256);
+        L.down = p;
+        L.loaded = false;
+    }
+
+    // scratch, one pool
+    const int T = cfg->max_tokens, K = s.K, E = s.E;
+    ctx->R_cap = (int)align_up((size_t)T * K + (size_t)E * (kSegAlign - 1), 128);
+    ctx->max_tiles = ctx->R_cap / kBNTile + E + 1;
+    const int DT = ctx->decode_max > 0 ? kDecodeMaxT : 0;
+    struct Item { void** p; size_t bytes; };
+    std::vector<Item> items = {
+        {(void**)&ctx->logits, (size_t)T * E * 4},
+        {(void**)&ctx->ids, (size_t)T * K * 4},
+        {(void**)&ctx->wts, (size_t)T * K * 4},
+        {(void**)&ctx->disp.counts, (size_t)E * 4},
+        {(void**)&ctx->disp.seg, (size_t)(E + 1) * 4},
+        {(void**)&ctx->disp.slot_of, (size_t)T * K * 4},
+        {(void**)&ctx->disp.src, (size_t)ctx->R_cap * 4},
+        {(void**)&ctx->disp.tiles, (size_t)ctx->max_tiles * 16},
+        {(void**)&ctx->disp.n_tiles, 16},
+        {(void**)&ctx->disp.xp, (size_t)ctx->R_cap * s.H * 2},
+        {(void**)&ctx->hbuf, (size_t)ctx->R_cap * s.I * 2},
+        {(void**)&ctx->ybuf, (size_t)ctx->R_cap * s.H * 2},
+        {(void**)&ctx->dec.part, (size_t)DT * K * (s.I / kRowTile) * 4 * 2 * kRowTile * 4},
+        {(void**)&ctx->dec.cnt_gu, (size_t)DT * K * (s.I / kRowTile) * 4},
+        {(void**)&ctx->dec.h, (size_t)DT * K * s.I * 2},
+        {(void**)&ctx->dec.y, (size_t)DT * K * s.H * 2},
+        {(void**)&ctx->dec.cnt_dn, (size_t)DT * (s.H / kRowTile) * 4},
+        {(void**)&ctx->err_flag, 16},
+        {(void**)&ctx->x_dev, (size_t)T * s.H * 2},
+        {(void**)&ctx->out_dev, (size_t)T * s.H * 2},
+        {(void**)&ctx->res_dev, (size_t)T * s.H * 2},
+        {(void**)&ctx->bias_dev, (size_t)E * 4},
+    };
+    size_t total = 0;
+    for (auto& it : items) total += align_up(it.bytes ? it.bytes : 16, 1024);
+    e = cudaMalloc(&ctx->smem_pool, total);
+    if (e != cudaSuccess) {
+        ctx->smem_pool = nullptr;
+        g_create_err = std::string("scratch: ") + cudaGetErrorString(e);
+        obs_destroy(ctx);
+        return OBS_ERR_NOMEM;
+    }
+    ctx->sbytes = total;
+    size_t off = 0;
+    for (auto& it : items) {
+        *it.p = ctx->smem_pool + off;
+        off += align_up(it.bytes ? it.bytes : 16, 1024);
+    }
+    ctx->dec.err = ctx->err_flag;
+    ctx->disp.atoms = ctx->R_cap / 8;
+    ctx->disp.bn = kBNTile;
+    // counters must start at zero; the tiled buffers are zeroed so padding rows are finite
+    e = cudaMemset(ctx->smem_pool, 0, total);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        g_create_err = std::string("scratch init: ") + cudaGetErrorString(e);
+        obs_destroy(ctx);
+        return OBS_ERR_CUDA;
+    }
+    *out = ctx;
+    return OBS_OK;
+}
+
+extern "C" int obs_destroy(obs_ctx* ctx) {
+    if (!ctx) return OBS_OK;
+    cudaSetDevice(ctx->device);
+    for (auto e : ctx->ev_pool) cudaEventDestroy(e);
+    if (ctx->wmem) cudaFree(ctx->wmem);
+    if (ctx->smem_pool) cudaFree(ctx->smem_pool);
+    delete ctx;
+    return OBS_OK;
+}
+
+extern "C" int obs_memory_bytes(const obs_ctx* ctx, size_t* weights, size_t* scratch) {
+    if (!ctx) return OBS_ERR_INVALID;
+    if (weights) *weights = ctx->wbytes;
+    if (scratch) *scratch = ctx->sbytes;
+    return OBS_OK;
+}
+
+// ------------------------------------------------------------------ loading
+static int check_layer(obs_ctx* ctx, int layer, bool need_loaded) {
+    if (layer < 0 || layer >= (int)ctx->layers.size()) return fail(ctx, OBS_ERR_INVALID, "layer out of range");
+    if (need_loaded && !ctx->layers[layer].loaded) return fail(ctx, OBS_ERR_STATE, "layer not loaded");
+    return OBS_OK;
+}
+
+// Copies (host or device) reference-format weights of one layer, re-tiles the
+// experts into 4608-byte blocks.  src == nullptr: generate them (synth).
+static int load_impl(obs_ctx* ctx, int layer, const obs_layer_weights* w, int on_dev, uint64_t seed, bool synth) {
+    int rc = check_layer(ctx, layer, false);
+    if (rc) return rc;
+    CU(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const Shape& s = ctx->sh;
+    LayerDev& L = ctx->layers[layer];
+    const size_t maxw = (size_t)s.E * s.I * s.H / 8 * 4;  // one projection's words (all same size)
+    const size_t maxg = (size_t)s.E * s.I * s.H / 64 * 2;
+    uint8_t* stage = nullptr;
+    CU(cudaMalloc(&stage, maxw + 2 * maxg), "staging alloc");
+    uint32_t* sw = reinterpret_cast<uint32_t*>(stage);
+    uint16_t* ss = reinterpret_cast<uint16_t*>(stage + maxw);
+    uint16_t* sb = reinterpret_cast<uint16_t*>(stage + maxw + maxg);
+    cudaMemcpyKind kind = on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    cudaError_t e = cudaSuccess;
+    auto step = [&](cudaError_t r) { if (e == cudaSuccess) e = r; };
+    if (synth) {
+        step(launch_synth_router(seed, (uint32_t)layer, s.E, s.H, L.router_w, L.router_s, L.router_b, 0));
+    } else {
+        step(cudaMemcpy(L.router_w, w->router_w, (size_t)s.E * s.H, kind));
+        step(cudaMemcpy(L.router_s, w->router_s, (size_t)s.E * (s.H / 64) * 2, kind));
+        step(cudaMemcpy(L.router_b, w->router_b, (size_t)s.E * (s.H / 64) * 2, kind));
+    }
+    for (int proj = 0; proj < 3 && e == cudaSuccess; ++proj) {
+        const int out_f = proj == 2 ? s.H : s.I, in_f = proj == 2 ? s.I : s.H;
+        const size_t nw = (size_t)s.E * out_f * in_f / 8 * 4, ng = (size_t)s.E * out_f * (in_f / 64) * 2;
+        if (synth) {
+            step(launch_synth_proj(seed, (uint32_t)layer, proj, s.E, out_f, in_f, sw, ss, sb, 0));
+        } else {
+            const uint32_t* pw = proj == 0 ? w->gate_w : proj == 1 ? w->up_w : w->down_w;
+            const uint16_t* ps = proj == 0 ? w->gate_s : proj == 1 ? w->up_s : w->down_s;
+            const uint16_t* pb = proj == 0 ? w->gate_b : proj == 1 ? w->up_b : w->down_b;
+            if (!pw || !ps || !pb) {
+                cudaFree(stage);
+                return fail(ctx, OBS_ERR_INVALID, "null weight pointer");
+            }
+            step(cudaMemcpy(sw, pw, nw, kind));
+            step(cudaMemcpy(ss, ps, ng, kind));
+            step(cudaMemcpy(sb, pb, ng, kind));
+        }
+        if (proj < 2) step(launch_retile(sw, ss, sb, s.E, out_f, in_f, L.gateup, 2, proj, 0));
+        else step(launch_retile(sw, ss, sb, s.E, out_f, in_f, L.down, 1, 0, 0));
+        step(cudaDeviceSynchronize());
+    }
+    cudaFree(stage);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "load layer");
+    L.loaded = true;
+    return OBS_OK;
+}
+
+extern "C" int obs_load_layer(obs_ctx* ctx, int layer, const obs_layer_weights* w, int src_on_device) {
+    OBS_CHECK_CTX(ctx);
+    if (!w || !w->router_w || !w->router_s || !w->router_b) return fail(ctx, OBS_ERR_INVALID, "null weights");
+    return load_impl(ctx, layer, w, src_on_device, 0, false);
+}
+
+extern "C" int obs_synth_layer(obs_ctx* ctx, int layer, uint64_t seed) {
+    OBS_CHECK_CTX(ctx);
+    return load_impl(ctx, layer, nullptr, 1, seed, true);
+}
+
+extern "C" int obs_synth_activations(uint64_t seed, uint32_t layer, int row0, int T, int H, float eps,
+                                     uint16_t* x, void* stream) {
+    if (!x || T < 0 || H <= 0 || row0 < 0) return OBS_ERR_INVALID;
+    return launch_synth_x(seed, layer, row0, T, H, eps, x, as_stream(stream)) == cudaSuccess ? OBS_OK
+                                                                                              : OBS_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------- stages
+static int check_T(obs_ctx* ctx, int T) {
+    if (T < 0 || T > ctx->cfg.max_tokens) return fail(ctx, OBS_ERR_INVALID, "T out of range (0..max_tokens)");
+    return OBS_OK;
+}
+
+extern "C" int obs_gate(obs_ctx* ctx, int layer, const uint16_t* x, float* logits, int T, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    int rc = check_layer(ctx, layer, true);
+    if (rc || (rc = check_T(ctx, T))) return rc;
+    if (T == 0) return OBS_OK;
+    if (!x || !logits) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    CU(launch_router_logits(ctx->layers[layer], ctx->sh, x, T, logits, as_stream(stream)), "router");
+    return OBS_OK;
+}
+
+extern "C" int obs_route(obs_ctx* ctx, const float* logits, const float* bias, int T, int32_t* ids, float* w,
+                         void* stream) {
+    OBS_CHECK_CTX(ctx);
+    int rc = check_T(ctx, T);
+    if (rc) return rc;
+    if (T == 0) return OBS_OK;
+    if (!logits || !ids || !w) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    CU(launch_topk(logits, bias, T, ctx->sh.E, ctx->sh.K, ctx->cfg.norm_topk, ids, w, nullptr, ctx->err_flag,
+                   as_stream(stream)),
+       "topk");
+    return OBS_OK;
+}
+
+// histogram of given routes into ctx->disp.counts, then the dispatch kernel
+static int dispatch_from_ids(obs_ctx* ctx, const int32_t* ids, const uint16_t* x, int T, int permute,
+                             cudaStream_t st);
+
+extern "C" int obs_dispatch(obs_ctx* ctx, const int32_t* ids, int T, int32_t* counts, int32_t* seg,
+                            int32_t* slot_of, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    int rc = check_T(ctx, T);
+    if (rc) return rc;
+    if (!ids) return fail(ctx, OBS_ERR_INVALID, "null ids");
+    cudaStream_t st = as_stream(stream);
+    rc = dispatch_from_ids(ctx, ids, nullptr, T, 0, st);
+    if (rc) return rc;
+    const Shape& s = ctx->sh;
+    if (counts) CU(cudaMemcpyAsync(counts, ctx->disp.counts, s.E * 4, cudaMemcpyDeviceToDevice, st), "copy");
+    if (seg) CU(cudaMemcpyAsync(seg, ctx->disp.seg, (s.E + 1) * 4, cudaMemcpyDeviceToDevice, st), "copy");
+    if (slot_of && T)
+        CU(cudaMemcpyAsync(slot_of, ctx->disp.slot_of, (size_t)T * s.K * 4, cudaMemcpyDeviceToDevice, st), "copy");
+    return OBS_OK;
+}
+
+static int dispatch_from_ids(obs_ctx* ctx, const int32_t* ids, const uint16_t* x, int T, int permute,
+                             cudaStream_t st) {
+    const Shape& s = ctx->sh;
+    CU(cudaMemsetAsync(ctx->disp.counts, 0, s.E * 4, st), "memset");
+    if (T) CU(cudaMemsetAsync(ctx->disp.slot_of, 0, (size_t)T * s.K * 4, st), "memset");
+    CU(launch_histogram(ids, T * s.K, s.E, ctx->disp.counts, ctx->err_flag, st), "histogram");
+    CU(launch_dispatch(ids, x, T, s, ctx->disp, permute, st), "dispatch");
+    return OBS_OK;
+}
+
+static GemmArgs gemm_gateup(obs_ctx* ctx, const LayerDev& L) {
+    const Shape& s = ctx->sh;
+    GemmArgs g{};
+    g.wblocks = L.gateup;
+    g.wstride = 2;
+    g.woff = 0;
+    g.act = ctx->disp.xp;
+    g.atoms = ctx->disp.atoms;
+    g.tiles = ctx->disp.tiles;
+    g.n_tiles = ctx->disp.n_tiles;
+    g.n_rt = s.I / kRowTile;
+    g.n_kt = s.H / kGroup;
+    g.bn = kBNTile;
+    g.out = ctx->hbuf;
+    g.out_atoms = ctx->disp.atoms;
+    g.row_limit = ctx->R_cap;
+    g.err = ctx->err_flag;
+    return g;
+}
+
+static GemmArgs gemm_down(obs_ctx* ctx, const LayerDev& L) {
+    const Shape& s = ctx->sh;
+    GemmArgs g{};
+    g.wblocks = L.down;
+    g.wstride = 1;
+    g.woff = 0;
+    g.act = ctx->hbuf;
+    g.atoms = ctx->disp.atoms;
+    g.tiles = ctx->disp.tiles;
+    g.n_tiles = ctx->disp.n_tiles;
+    g.n_rt = s.H / kRowTile;
+    g.n_kt = s.I / kGroup;
+    g.bn = kBNTile;
+    g.out = ctx->ybuf;
+    g.out_ld = s.H;
+    g.row_limit = ctx->R_cap;
+    g.err = ctx->err_flag;
+    return g;
+}
+
+// prefill expert FFN over the current dispatch: xp -> hbuf -> ybuf (slot rows)
+static int prefill_ffn(obs_ctx* ctx, const LayerDev& L, cudaStream_t st) {
+    CU(launch_gemm(gemm_gateup(ctx, L), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");
+    CU(launch_gemm(gemm_down(ctx, L), kEpiBf16, ctx->num_sms, st), "gemm down");
+    return OBS_OK;
+}
+
+extern "C" int obs_expert_ffn(obs_ctx* ctx, int layer, const uint16_t* x, const int32_t* ids, int T, int path,
+                              uint16_t* y, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    int rc = check_layer(ctx, layer, true);
+    if (rc || (rc = check_T(ctx, T))) return rc;
+    if (T == 0) return OBS_OK;
+    if (!x || !ids || !y) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    const Shape& s = ctx->sh;
+    const LayerDev& L = ctx->layers[layer];
+    cudaStream_t st = as_stream(stream);
+    if (path == OBS_PATH_DECODE) {
+        if (T > kDecodeMaxT) return fail(ctx, OBS_ERR_INVALID, "decode path: T above its scratch (64)");
+        CU(launch_decode_gateup(L, s, x, ids, T, ctx->dec, st), "decode gate/up");
+        CU(launch_decode_down(L, s, ids, nullptr, nullptr, T, ctx->dec, nullptr, 0, st), "decode down");
+        CU(cudaMemcpyAsync(y, ctx->dec.y, (size_t)T * s.K * s.H * 2, cudaMemcpyDeviceToDevice, st), "copy");
+        return OBS_OK;
+    }
+    if (path != OBS_PATH_PREFILL) return fail(ctx, OBS_ERR_INVALID, "path must be DECODE or PREFILL");
+    rc = dispatch_from_ids(ctx, ids, x, T, 1, st);
+    if (rc) return rc;
+    rc = prefill_ffn(ctx, L, st);
+    if (rc) return rc;
+    CU(launch_gather_rows(ctx->ybuf, ctx->disp.slot_of, T * s.K, s.H, y, st), "gather");
+    return OBS_OK;
+}
+
+extern "C" int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert, const uint16_t* x, int n,
+                                   float* y, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    int rc = check_layer(ctx, layer, true);
+    if (rc) return rc;
+    const Shape& s = ctx->sh;
+    if (proj < 0 || proj > 2 || expert < 0 || expert >= s.E) return fail(ctx, OBS_ERR_INVALID, "bad proj/expert");
+    if (n < 0 || n > ctx->R_cap - kSegAlign) return fail(ctx, OBS_ERR_INVALID, "n out of range");
+    if (n == 0) return OBS_OK;
+    if (!x || !y) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    const LayerDev& L = ctx->layers[layer];
+    const int in_f = proj == 2 ? s.I : s.H, out_f = proj == 2 ? s.H : s.I;
+    const int rows = (n + kSegAlign - 1) / kSegAlign * kSegAlign;
+    std::vector<int4> tiles;
+    for (int r = 0; r < rows; r += kBNTile) tiles.push_back(make_int4(expert, r, std::min(kBNTile, rows - r), 0));
+    int nt = (int)tiles.size();
+    CU(cudaMemcpyAsync(ctx->disp.tiles, tiles.data(), tiles.size() * sizeof(int4), cudaMemcpyHostToDevice, st),
+       "tiles");
+    CU(cudaMemcpyAsync(ctx->disp.n_tiles, &nt, 4, cudaMemcpyHostToDevice, st), "tiles");
+    CU(launch_tile_rows(x, n, in_f, ctx->disp.atoms, ctx->disp.xp, st), "tile rows");
+    GemmArgs g{};
+    g.wblocks = proj == 2 ? L.down : L.gateup;
+    g.wstride = proj == 2 ? 1 : 2;
+    g.woff = proj == 2 ? 0 : proj;
+    g.act = ctx->disp.xp;
+    g.atoms = ctx->disp.atoms;
+    g.tiles = ctx->disp.tiles;
+    g.n_tiles = ctx->disp.n_tiles;
+    g.n_rt = out_f / kRowTile;
+    g.n_kt = in_f / kGroup;
+    g.bn = kBNTile;
+    g.out = y;
+    g.out_ld = out_f;
+    g.row_limit = n;
+    g.err = ctx->err_flag;
+    CU(launch_gemm(g, kEpiF32, ctx->num_sms, st), "gemm f32");
+    CU(cudaStreamSynchronize(st), "sync");  // the host tile list must outlive its copy
+    return OBS_OK;
+}
+
+// ------------------------------------------------------------- the layer
+extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint16_t* out, const uint16_t* residual,
+                               int T, const float* logit_bias, int path, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    int rc = check_layer(ctx, layer, true);
+    if (rc || (rc = check_T(ctx, T))) return rc;
+    if (T == 0) return OBS_OK;
+    if (!x || !out) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    if (path == OBS_PATH_AUTO) path = T <= ctx->decode_max ? OBS_PATH_DECODE : OBS_PATH_PREFILL;
+    if (path == OBS_PATH_DECODE && T > kDecodeMaxT) return fail(ctx, OBS_ERR_INVALID, "decode path: T > 64");
+    if (path != OBS_PATH_DECODE && path != OBS_PATH_PREFILL) return fail(ctx, OBS_ERR_INVALID, "bad path");
+    const Shape& s = ctx->sh;
+    const LayerDev& L = ctx->layers[layer];
+    cudaStream_t st = as_stream(stream);
+    prof_begin(ctx, OBS_STAGE_ROUTER, st);
+    CU(launch_router_logits(L, s, x, T, ctx->logits, st), "router");
+    prof_end(ctx, st);
+    if (path == OBS_PATH_DECODE) {
+        prof_begin(ctx, OBS_STAGE_TOPK, st);
+        CU(launch_topk(ctx->logits, logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids, ctx->wts, nullptr,
+                       ctx->err_flag, st),
+           "topk");
+        prof_end(ctx, st);
+        prof_begin(ctx, OBS_STAGE_DECODE_GATEUP, st);
+        CU(launch_decode_gateup(L, s, x, ctx->ids, T, ctx->dec, st), "decode gate/up");
+        prof_end(ctx, st);
+        prof_begin(ctx, OBS_STAGE_DECODE_DOWN, st);
+        CU(launch_decode_down(L, s, ctx->ids, ctx->wts, residual, T, ctx->dec, out, 1, st), "decode down");
+        prof_end(ctx, st);
+        return OBS_OK;
+    }
+    CU(cudaMemsetAsync(ctx->disp.counts, 0, s.E * 4, st), "memset");
+    prof_begin(ctx, OBS_STAGE_TOPK, st);
+    CU(launch_topk(ctx->logits, logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids, ctx->wts, ctx->disp.counts,
+                   ctx->err_flag, st),
+       "topk");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_DISPATCH, st);
+    CU(launch_dispatch(ctx->ids, x, T, s, ctx->disp, 1, st), "dispatch");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_GEMM_GATEUP, st);
+    CU(launch_gemm(gemm_gateup(ctx, L), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_GEMM_DOWN, st);
+    CU(launch_gemm(gemm_down(ctx, L), kEpiBf16, ctx->num_sms, st), "gemm down");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_COMBINE, st);
+    CU(launch_combine(ctx->ybuf, s.H, ctx->disp.slot_of, ctx->wts, residual, T, s.H, s.K, out, st), "combine");
+    prof_end(ctx, st);
+    return OBS_OK;
+}
+
+extern "C" int obs_moe_forward_host(obs_ctx* ctx, int layer, const uint16_t* x_host, uint16_t* out_host,
+                                    const uint16_t* residual_host, int T, const float* bias_host, int path,
+                                    void* stream) {
+    OBS_CHECK_CTX(ctx);
+    int rc = check_T(ctx, T);
+    if (rc) return rc;
+    if (T == 0) return OBS_OK;
+    if (!x_host || !out_host) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    const Shape& s = ctx->sh;
+    cudaStream_t st = as_stream(stream);
+    const size_t bytes = (size_t)T * s.H * 2;
+    CU(cudaMemcpyAsync(ctx->x_dev, x_host, bytes, cudaMemcpyHostToDevice, st), "h2d x");
+    if (residual_host) CU(cudaMemcpyAsync(ctx->res_dev, residual_host, bytes, cudaMemcpyHostToDevice, st), "h2d");
+    if (bias_host) CU(cudaMemcpyAsync(ctx->bias_dev, bias_host, s.E * 4, cudaMemcpyHostToDevice, st), "h2d");
+    rc = obs_moe_forward(ctx, layer, ctx->x_dev, ctx->out_dev, residual_host ? ctx->res_dev : nullptr, T,
+                         bias_host ? ctx->bias_dev : nullptr, path, stream);
+    if (rc) return rc;
+    CU(cudaMemcpyAsync(out_host, ctx->out_dev, bytes, cudaMemcpyDeviceToHost, st), "d2h out");
+    CU(cudaStreamSynchronize(st), "sync");
+    return OBS_OK;
+}
+
+extern "C" int obs_check_device(obs_ctx* ctx, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    CU(cudaStreamSynchronize(as_stream(stream)), "stream sync");
+    CU(cudaGetLastError(), "pending error");
+    int flag = 0;
+    CU(cudaMemcpy(&flag, ctx->err_flag, 4, cudaMemcpyDeviceToHost), "read flag");
+    if (flag) {
+        CU(cudaMemset(ctx->err_flag, 0, 4), "clear flag");
+        if (flag == kDevTimeout) return fail(ctx, OBS_ERR_TIMEOUT, "a device-side wait gave up (timeout)");
+        return fail(ctx, OBS_ERR_INVALID, "device reported an invalid route (expert id out of range)");
+    }
+    return OBS_OK;
+}
+
+extern "C" int obs_profile_enable(obs_ctx* ctx, int enable) {
+    OBS_CHECK_CTX(ctx);
+    ctx->prof = enable != 0;
+    ctx->ev_marks.clear();
+    return OBS_OK;
+}
+
+extern "C" int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches) {
+    OBS_CHECK_CTX(ctx);
+    if (!ms_total || !launches) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    for (int i = 0; i < OBS_N_STAGES; ++i) ms_total[i] = 0.0f, launches[i] = 0;
+    for (auto& m : ctx->ev_marks) {
+        CU(cudaEventSynchronize(ctx->ev_pool[m.second + 1]), "event sync");
+        float ms = 0.0f;
+        CU(cudaEventElapsedTime(&ms, ctx->ev_pool[m.second], ctx->ev_pool[m.second + 1]), "event time");
+        ms_total[m.first] += ms;
+        launches[m.first] += 1;
+    }
+    ctx->ev_marks.clear();
+    return OBS_OK;
+}

@@ -1,0 +1,219 @@
+"""Python front end of libobsmoe.so (include/obs_moe.h) for the B200 MoE path.
+
+Mirrors the reference's MoE helpers in src/forward.rs and src/router.rs by name
+and argument meaning: ``gate_gpu`` (forward.rs:386-397), ``route``
+(router.rs:25-56), ``dispatch`` (the grouping of forward.rs:203-216),
+``expert_ffn`` (dequant/matmul_raw + swiglu, forward.rs:303-321,370-375),
+``moe_forward`` (the MoE section of forward_layer / prefill_batched).  Errors
+raise ``ObsError`` carrying the library's message, the way the reference's
+helpers return ``Err(String)``.
+
+Device buffers are passed as raw pointers: any object with ``data_ptr()``
+(a torch CUDA tensor, used here only as device-memory plumbing) or an int.
+There is no CPU fallback: if the CUDA library is missing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libobsmoe.so")
+
+OBS_OK = 0
+PATH_AUTO, PATH_DECODE, PATH_PREFILL = 0, 1, 2
+_STATUS = {1: "INVALID", 2: "CUDA", 3: "NOMEM", 4: "STATE", 5: "TIMEOUT", 6: "NCCL", 7: "UNSUPPORTED"}
+
+# every entry point include/obs_moe.h declares
+EXPORTS = (
+    "obs_abi_version", "obs_create", "obs_destroy", "obs_last_error", "obs_memory_bytes",
+    "obs_load_layer", "obs_synth_layer", "obs_synth_activations", "obs_moe_forward",
+    "obs_moe_forward_host", "obs_gate", "obs_route", "obs_dispatch", "obs_expert_ffn",
+    "obs_expert_gemm_f32", "obs_check_device", "obs_profile_enable", "obs_profile_read",
+)
+STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down")
+
+
+class ObsError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"obs {_STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+class Config(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("inter", C.c_int32), ("n_experts", C.c_int32),
+                ("top_k", C.c_int32), ("group_size", C.c_int32), ("n_layers", C.c_int32),
+                ("max_tokens", C.c_int32), ("norm_topk", C.c_int32),
+                ("decode_max_tokens", C.c_int32), ("rms_eps", C.c_float)]
+
+
+class LayerWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "router_w", "router_s", "router_b", "gate_w", "gate_s", "gate_b",
+        "up_w", "up_s", "up_b", "down_w", "down_s", "down_b")]
+
+
+_LIB = None
+
+
+def lib() -> C.CDLL:
+    """Load libobsmoe.so (built by project-obsidian_b200/build.py)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with python project-obsidian_b200/build.py")
+        L = C.CDLL(LIB_PATH)
+        vp, i32, i64 = C.c_void_p, C.c_int, C.c_uint64
+        L.obs_abi_version.restype = i32
+        L.obs_create.argtypes = [C.POINTER(Config), i32, C.POINTER(vp)]
+        L.obs_destroy.argtypes = [vp]
+        L.obs_last_error.restype = C.c_char_p
+        L.obs_last_error.argtypes = [vp]
+        L.obs_memory_bytes.argtypes = [vp, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]
+        L.obs_load_layer.argtypes = [vp, i32, C.POINTER(LayerWeights), i32]
+        L.obs_synth_layer.argtypes = [vp, i32, i64]
+        L.obs_synth_activations.argtypes = [i64, C.c_uint32, i32, i32, i32, C.c_float, vp, vp]
+        L.obs_moe_forward.argtypes = [vp, i32, vp, vp, vp, i32, vp, i32, vp]
+        L.obs_moe_forward_host.argtypes = [vp, i32, vp, vp, vp, i32, vp, i32, vp]
+        L.obs_gate.argtypes = [vp, i32, vp, vp, i32, vp]
+        L.obs_route.argtypes = [vp, vp, vp, i32, vp, vp, vp]
+        L.obs_dispatch.argtypes = [vp, vp, i32, vp, vp, vp, vp]
+        L.obs_expert_ffn.argtypes = [vp, i32, vp, vp, i32, i32, vp, vp]
+        L.obs_expert_gemm_f32.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp]
+        L.obs_check_device.argtypes = [vp, vp]
+        L.obs_profile_enable.argtypes = [vp, i32]
+        L.obs_profile_read.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(C.c_int32)]
+        for name in EXPORTS:
+            if name not in ("obs_last_error", "obs_abi_version"):
+                getattr(L, name).restype = i32
+        _LIB = L
+    return _LIB
+
+
+def _ptr(x) -> int | None:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):  # numpy array (host memory)
+        return x.ctypes.data
+    raise TypeError(f"cannot take a pointer of {type(x)}")
+
+
+def _stream(s) -> int | None:
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s
+    return s.cuda_stream  # torch.cuda.Stream
+
+
+@dataclass
+class MoeShape:
+    hidden: int = 2048
+    inter: int = 768
+    n_experts: int = 128
+    top_k: int = 8
+    n_layers: int = 1
+    max_tokens: int = 512
+    norm_topk: bool = True
+    decode_max_tokens: int = 4
+    rms_eps: float = 1e-6
+
+
+class MoeContext:
+    """One GPU's HBM-resident MoE layers (obs_create ... obs_destroy)."""
+
+    def __init__(self, shape: MoeShape, device: int = 0):
+        self.shape = shape
+        cfg = Config(shape.hidden, shape.inter, shape.n_experts, shape.top_k, 64, shape.n_layers,
+                     shape.max_tokens, int(shape.norm_topk), shape.decode_max_tokens, shape.rms_eps)
+        h = C.c_void_p()
+        rc = lib().obs_create(C.byref(cfg), device, C.byref(h))
+        if rc != OBS_OK:
+            raise ObsError(rc, lib().obs_last_error(None).decode())
+        self._h = h
+        self.device = device
+
+    # -- plumbing
+    def _chk(self, rc: int):
+        if rc != OBS_OK:
+            raise ObsError(rc, lib().obs_last_error(self._h).decode())
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().obs_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def memory_bytes(self):
+        w, s = C.c_size_t(), C.c_size_t()
+        self._chk(lib().obs_memory_bytes(self._h, C.byref(w), C.byref(s)))
+        return w.value, s.value
+
+    # -- weights
+    def load_layer(self, layer: int, w, on_device: bool = False):
+        """Copy one layer in the reference format (attributes router_w ... down_b)."""
+        lw = LayerWeights(*[_ptr(getattr(w, n)) for n, _ in LayerWeights._fields_])
+        self._chk(lib().obs_load_layer(self._h, layer, C.byref(lw), int(on_device)))
+
+    def synth_layer(self, layer: int, seed: int = 0):
+        self._chk(lib().obs_synth_layer(self._h, layer, seed))
+
+    # -- the reference helpers
+    def gate_gpu(self, layer, x, logits, T, stream=None):
+        self._chk(lib().obs_gate(self._h, layer, _ptr(x), _ptr(logits), T, _stream(stream)))
+
+    def route(self, logits, T, ids, weights, bias=None, stream=None):
+        self._chk(lib().obs_route(self._h, _ptr(logits), _ptr(bias), T, _ptr(ids), _ptr(weights),
+                                  _stream(stream)))
+
+    def dispatch(self, ids, T, counts=None, seg=None, slot_of=None, stream=None):
+        self._chk(lib().obs_dispatch(self._h, _ptr(ids), T, _ptr(counts), _ptr(seg), _ptr(slot_of),
+                                     _stream(stream)))
+
+    def expert_ffn(self, layer, x, ids, T, y, path=PATH_PREFILL, stream=None):
+        self._chk(lib().obs_expert_ffn(self._h, layer, _ptr(x), _ptr(ids), T, path, _ptr(y),
+                                       _stream(stream)))
+
+    def matmul_raw_f32(self, layer, proj, expert, x, n, y, stream=None):
+        """One expert projection on the tcgen05 GEMM, fp32 out (matmul_dequant_4bit)."""
+        self._chk(lib().obs_expert_gemm_f32(self._h, layer, proj, expert, _ptr(x), n, _ptr(y),
+                                            _stream(stream)))
+
+    def moe_forward(self, layer, x, out, T, residual=None, bias=None, path=PATH_AUTO, stream=None):
+        self._chk(lib().obs_moe_forward(self._h, layer, _ptr(x), _ptr(out), _ptr(residual), T,
+                                        _ptr(bias), path, _stream(stream)))
+
+    def moe_forward_host(self, layer, x_host, out_host, T, residual_host=None, bias_host=None,
+                         path=PATH_AUTO, stream=None):
+        self._chk(lib().obs_moe_forward_host(self._h, layer, _ptr(x_host), _ptr(out_host),
+                                             _ptr(residual_host), T, _ptr(bias_host), path,
+                                             _stream(stream)))
+
+    def profile(self, enable: bool):
+        self._chk(lib().obs_profile_enable(self._h, int(enable)))
+
+    def profile_read(self) -> dict:
+        """{stage: (total ms, launches)} since the last read (event times on the caller's stream)."""
+        ms = (C.c_float * len(STAGES))()
+        n = (C.c_int32 * len(STAGES))()
+        self._chk(lib().obs_profile_read(self._h, ms, n))
+        return {name: (ms[i], n[i]) for i, name in enumerate(STAGES)}
+
+    def check_device(self, stream=None):
+        self._chk(lib().obs_check_device(self._h, _stream(stream)))
+
+
+def synth_activations(seed, layer, row0, T, H, x, eps=1e-6, stream=None):
+    rc = lib().obs_synth_activations(seed, layer, row0, T, H, eps, _ptr(x), _stream(stream))
+    if rc != OBS_OK:
+        raise ObsError(rc, "synth_activations")
