@@ -151,6 +151,13 @@ enum obs_stage {
 };
 int obs_profile_enable(obs_ctx* ctx, int enable);
 int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches);
+/* Pipeline trace of the gate/up grouped GEMM (diagnostics): while set, the
+ * GEMM's CTA 0 writes %globaltimer (ns) into trace[role * n_steps + i] for
+ * k-step (or item) i of each role: 0 weight copy issued, 1 token tile ready,
+ * 2 dequant start, 3 dequant done, 4 MMA start, 5 MMA committed, 6 epilogue
+ * start, 7 epilogue done, 8 dequant stores done, 9 MMA fences passed.
+ * trace = NULL switches it off.  Device memory of 10 * n_steps uint64. */
+int obs_trace_enable(obs_ctx* ctx, uint64_t* trace, int n_steps);
 /* Waits for the stream and reports any device-side error flag (bounded waits
  * that gave up) raised since the last check; clears the flags. */
 int obs_check_device(obs_ctx* ctx, void* stream);

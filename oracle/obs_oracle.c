@@ -28,7 +28,31 @@ uint16_t orc_f32_to_bf16(float f) {
     return (uint16_t)(u >> 16);
 }
 
-static inline float bf16_round(float f) { return orc_bf16_to_f32(orc_f32_to_bf16(f)); }
+/* bf16 nearest-even rounding of a double, in one step (no intermediate fp32
+ * rounding); normal bf16 range only, other values go through fp32. */
+static uint16_t d2bf(double d) {
+    uint64_t u;
+    memcpy(&u, &d, 8);
+    int e = (int)((u >> 52) & 0x7FF) - 1023 + 127;
+    if (e < 1 || e > 254) return orc_f32_to_bf16((float)d);
+    uint64_t sign = u >> 63, man = u & 0xFFFFFFFFFFFFFull;
+    uint64_t keep = man >> 45, rest = man & ((1ull << 45) - 1), half = 1ull << 44;
+    if (rest > half || (rest == half && (keep & 1))) keep++;
+    uint32_t v = ((uint32_t)e << 7) + (uint32_t)keep; /* a carry out of the mantissa bumps the exponent */
+    return (uint16_t)((sign << 15) | v);
+}
+
+void orc_dequant4_bf16(const uint32_t* w, const uint16_t* s, const uint16_t* b, int out_f, int in_f,
+                       uint16_t* out) {
+    int groups = in_f / 64, words = in_f / 8;
+    for (int r = 0; r < out_f; ++r)
+        for (int c = 0; c < in_f; ++c) {
+            uint32_t q = (w[(size_t)r * words + c / 8] >> (4 * (c % 8))) & 0xFu;
+            double sc = orc_bf16_to_f32(s[(size_t)r * groups + c / 64]);
+            double bi = orc_bf16_to_f32(b[(size_t)r * groups + c / 64]);
+            out[(size_t)r * in_f + c] = d2bf((double)q * sc + bi); /* q*s + b is exact in double */
+        }
+}
 
 /* ---------------------------------------------------------- synthetic data */
 #define GOLDEN_GAMMA 0x9E3779B97F4A7C15ull
@@ -267,10 +291,14 @@ static void dequant_proj(const orc_experts* ex, int proj, int e, int wmode, floa
     const uint16_t* s = proj == 0 ? ex->gate_s : proj == 1 ? ex->up_s : ex->down_s;
     const uint16_t* b = proj == 0 ? ex->gate_b : proj == 1 ? ex->up_b : ex->down_b;
     size_t wo = (size_t)e * out_f * (in_f / 8), so = (size_t)e * out_f * (in_f / 64);
-    orc_dequant4(w + wo, s + so, b + so, out_f, in_f, out);
     if (wmode == 1) {
         size_t n = (size_t)out_f * in_f;
-        for (size_t i = 0; i < n; ++i) out[i] = bf16_round(out[i]);
+        uint16_t* tmp = (uint16_t*)malloc(sizeof(uint16_t) * n);
+        orc_dequant4_bf16(w + wo, s + so, b + so, out_f, in_f, tmp);
+        for (size_t i = 0; i < n; ++i) out[i] = orc_bf16_to_f32(tmp[i]);
+        free(tmp);
+    } else {
+        orc_dequant4(w + wo, s + so, b + so, out_f, in_f, out);
     }
 }
 

@@ -60,6 +60,10 @@ void orc_rmsnorm_row(const uint16_t* x, int H, float eps, uint16_t* out);
  * fp32, so this equals the reference's mul-then-add. */
 void orc_dequant4(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                   int out_f, int in_f, float* out);
+/* The tensor-core path's weights: bf16 nearest-even rounding of the exact
+ * q*scale + bias (one rounding, as fma.rn.bf16x2).  bf16 [out, in]. */
+void orc_dequant4_bf16(const uint32_t* w, const uint16_t* s, const uint16_t* b,
+                       int out_f, int in_f, uint16_t* out);
 void orc_dequant8(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                   int out_f, int in_f, float* out);
 
@@ -85,7 +89,7 @@ void orc_dispatch(const int32_t* ids, int T, int E, int K,
 
 /* ---- a4/a5/a6: expert FFN + combine for a whole layer ----
  * wmode 0: weights dequantised in fp32 (reference matvec);
- * wmode 1: weights rounded to bf16 after dequant (tensor-core GEMM path).
+ * wmode 1: weights rounded once to bf16 (orc_dequant4_bf16, tensor-core GEMM path).
  * g,u fp32; h = bf16(silu(g)*u) (ops.metal:21); y = bf16(W_d h);
  * out[t] = bf16(residual[t] + sum_k w_k y_k) in rank order (forward.rs:225-232),
  * residual may be NULL.  Optional y_out [T*K, H] bf16 (slot = t*K+k) for tests. */

@@ -46,6 +46,7 @@ def lib():
         L.orc_rmsnorm_row.argtypes = [_u16p, C.c_int, C.c_float, _u16p]
         L.orc_dequant4.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int, _f32p]
         L.orc_dequant8.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int, _f32p]
+        L.orc_dequant4_bf16.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int, _u16p]
         L.orc_router_logits.restype = C.c_int
         L.orc_router_logits.argtypes = [_u32p, _u16p, _u16p, _u16p, C.c_int, C.c_int, C.c_int, _f32p]
         L.orc_topk.argtypes = [_f32p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _f32p]
@@ -139,6 +140,15 @@ def dequant4(w, s, b):
     out = np.empty((out_f, words * 8), np.float32)
     lib().orc_dequant4(np.ascontiguousarray(w), np.ascontiguousarray(s), np.ascontiguousarray(b),
                        out_f, words * 8, out)
+    return out
+
+
+def dequant4_bf16(w, s, b):
+    """Tensor-core path weights: bf16 of the exact q*s + b, one rounding."""
+    out_f, words = w.shape[-2], w.shape[-1]
+    out = np.empty((out_f, words * 8), np.uint16)
+    lib().orc_dequant4_bf16(np.ascontiguousarray(w), np.ascontiguousarray(s), np.ascontiguousarray(b),
+                            out_f, words * 8, out)
     return out
 
 

@@ -24,11 +24,11 @@ __device__ __forceinline__ float nib_f(uint32_t w, int j) {
 // 32 columns of half (l & 1).  xr: the lane's 32 activations (fp32).
 __device__ __forceinline__ void block_dot(const uint8_t* __restrict__ blk, const float (&xr)[32], int lane,
                                           float (&acc)[8]) {
-    const uint4* wq = reinterpret_cast<const uint4*>(blk);
+    const uint4* wq = reinterpret_cast<const uint4*>(blk + (lane & 1) * 2048);
     const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
     uint4 q[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = __ldg(wq + i * 32 + lane);
+    for (int i = 0; i < 8; ++i) q[i] = __ldg(wq + (lane >> 1) + 16 * i);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int row = (lane >> 1) + 16 * i;
@@ -38,7 +38,8 @@ __device__ __forceinline__ void block_dot(const uint8_t* __restrict__ blk, const
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) a = __fmaf_rn(__fmaf_rn(nib_f(ws[c], j), sc, bi), xr[c * 8 + j], a);
+            for (int j = 0; j < 8; ++j)  // nibble j holds column nib_col(j) of the word
+                a = __fmaf_rn(__fmaf_rn(nib_f(ws[c], j), sc, bi), xr[c * 8 + nib_col(j)], a);
         acc[i] = a;
     }
 }

@@ -82,15 +82,27 @@ __global__ void __launch_bounds__(kDispThreads) k_dispatch(const int32_t* __rest
     if (!permute) return;
     __syncthreads();  // d.src of this segment written above by this CTA
 
-    // copy rows into the tiled layout: one 16-byte chunk per thread
+    // copy rows into the tiled layout: 16-byte chunks, 8 loads in flight per thread
     const int chunks = H / 8;
-    for (size_t i = tid; i < (size_t)P * chunks; i += kDispThreads) {
-        int r = (int)(i / chunks), c = (int)(i % chunks) * 8;
-        int slot = seg + r;
-        int t = d.src[slot];
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (t >= 0) v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + c));
-        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(d.xp) + tiled_off(slot, c, d.atoms)) = v;
+    const size_t total = (size_t)P * chunks;
+    for (size_t i0 = tid; i0 < total; i0 += (size_t)kDispThreads * 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            size_t i = i0 + (size_t)u * kDispThreads;
+            v[u] = make_uint4(0, 0, 0, 0);
+            if (i < total) {
+                int t = d.src[seg + (int)(i / chunks)];
+                if (t >= 0) v[u] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + (i % chunks) * 8));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            size_t i = i0 + (size_t)u * kDispThreads;
+            if (i < total)
+                *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(d.xp) +
+                                          tiled_off(seg + (int)(i / chunks), (int)(i % chunks) * 8, d.atoms)) = v[u];
+        }
     }
 }
 

@@ -4,17 +4,33 @@
 // (shaders/matmul_dequant_4bit.metal:21-66; host src/forward.rs:313-321,
 // per-expert calls :219-222) and the ew_swiglu between them (ops.metal:18-22).
 //
-// One persistent CTA per SM walks work items (token tile, weight row tile):
-//   warp 0      producer: 1-D bulk async copies of the packed weight block(s)
-//               (4608 B each, contiguous by construction of the HBM layout)
-//               and of the token tile (pre-swizzled rows, contiguous per
-//               k-tile) into a ring of shared-memory stages;
-//   warp 1      MMA issuer (one thread): tcgen05.mma kind::f16, M = 128 weight
-//               rows, N = token rows, K = 16, fp32 accumulators in TMEM;
-//   warps 2-5   dequantise the packed block into the bf16 A tile in the
-//               128-byte-swizzled K-major layout (w = fma(q, s, b), rounded to
-//               bf16), then run the epilogue from TMEM (SwiGLU -> tiled H, or
-//               a plain bf16 / fp32 store).
+// One persistent CTA per SM walks work items (token tile of <= 64 rows, weight
+// row tile of 128 rows), sixteen warps in five roles:
+//   warp 0      weight producer: 1-D bulk async copies of the packed weight
+//               block(s) (4608 B each, contiguous by construction of the HBM
+//               layout) into a deep shared-memory ring (W);
+//   warps 1-2   token-tile producer into the B ring: for gate/up, rows of the
+//               layer input gathered by source token with 16-byte cp.async
+//               into the 128-byte-swizzled K-major slots (zero fill for padding
+//               rows), each thread's completion arriving on the stage's full
+//               barrier; for down, bulk copies of the tiled H rows;
+//   warps 4-11  dequantise a W stage (released as soon as it is read) straight
+//               into tensor memory: two codes per bf16x2 register,
+//               q = (0x4300 | n) - 128, w = fma.rn.bf16x2(q, s, b) (the correctly
+//               rounded bf16 of q*s + b), written with tcgen05.st into an A stage
+//               of TMEM (one weight row per TMEM lane); each warp owns the TMEM
+//               lane quarter it may access;
+//   warp 3      MMA issuer (one thread): tcgen05.mma kind::f16 with A in TMEM and
+//               B in shared memory, M = 128 weight rows, N = token rows, K = 16,
+//               fp32 accumulators in TMEM, two accumulator buffers so the
+//               epilogue overlaps the next item;
+//   warps 12-15 epilogue: tcgen05.ld, SwiGLU (or plain), results staged in
+//               shared memory in the global layout and written back with bulk
+//               copies (fp32 debug output: direct stores).
+// Keeping A out of shared memory leaves shared-memory bandwidth to the weight
+// and token streams.  The packed words hold their codes in the nibble order
+// (c0,c2,c4,c6,c1,c3,c5,c7) (set by the loader), so (w >> 4j) & 0x000F000F is
+// the bf16x2 pair of columns (2j, 2j+1).
 // Every mbarrier wait is bounded; a CTA that gives up records kDevTimeout,
 // drains its outstanding copies (bounded), frees its TMEM and returns.
 #include "obs_internal.cuh"
@@ -22,28 +38,84 @@
 namespace obs {
 namespace {
 
-constexpr int kBN = 128;  // token rows per tile (tcgen05 N <= 128 here)
-constexpr int kThreads = 192;
+constexpr int kBN = 64;  // token rows per tile (tcgen05 N <= 64 here)
+constexpr int kDqWarps = 16, kEpWarps = 4;
+constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 3, kWarpDq = 4, kWarpEp = kWarpDq + kDqWarps;
+constexpr int kThreads = 32 * (kWarpEp + kEpWarps);  // 768
+constexpr int kEpThreads = 32 * kEpWarps;
 
 template <int EPI>
 struct Cfg {
-    static constexpr int NP = EPI == kEpiSwiglu ? 2 : 1;   // projections per tile (gate, up)
-    static constexpr int A_BYTES = NP * kRowTile * 128;     // bf16 A tiles, 16 KB each
-    static constexpr int B_BYTES = kBN * 128;
-    static constexpr int PACK_BYTES = NP * kBlockBytes;
-    static constexpr int STAGE = ((A_BYTES + B_BYTES + PACK_BYTES) + 1023) / 1024 * 1024;
-    static constexpr int STAGES = EPI == kEpiSwiglu ? 3 : 5;
-    static constexpr int TMEM_COLS = NP * kBN;               // 256 or 128
-    static constexpr int BAR_OFF = STAGES * STAGE;
-    static constexpr int SMEM = BAR_OFF + (3 * STAGES + 2) * 8 + 16 + 1024;  // + alignment slack
+    static constexpr bool GATHER = EPI == kEpiSwiglu;    // token tile gathered from x rows
+    static constexpr int NP = EPI == kEpiSwiglu ? 2 : 1;  // projections per tile (gate, up)
+    static constexpr int W_STAGE = NP * kBlockBytes;      // packed weights (16-byte multiple)
+    static constexpr int SW = EPI == kEpiSwiglu ? 12 : 24;
+    static constexpr int B_STAGE = kBN * 128;
+    static constexpr int SA = 4;                          // A stages in TMEM
+    static constexpr int SB = SA;                         // B stages advance with A: one "stage free" commit
+    // accumulators per buffer: gate + up, or (single projection) even + odd k-slices,
+    // so consecutive MMAs always target independent accumulators
+    static constexpr int ACC_COLS = 2 * kBN;              // one accumulator buffer (fp32 columns)
+    static constexpr int A_COLS = NP * 32;                // one A stage: 64 bf16 per row = 32 columns
+    static constexpr int A_TMEM = 2 * ACC_COLS;           // first A stage column
+    static constexpr int TMEM_COLS = 512;
+    static_assert(A_TMEM + SA * A_COLS <= TMEM_COLS, "tmem");
+    static constexpr int STG = kBN * 256;                 // epilogue staging: 64 rows x 128 features bf16
+    static constexpr int B_OFF = 0;                       // 1024-aligned tiles first
+    static constexpr int STG_OFF = B_OFF + SB * B_STAGE;
+    static constexpr int W_OFF = STG_OFF + 2 * STG;
+    static constexpr int BAR_OFF = (W_OFF + SW * W_STAGE + 7) / 8 * 8;
+    static constexpr int N_BARS = 2 * SW + 2 * SB + 2 * SA + 4;  // (aempty unused: empty_b frees both)
+    static constexpr int SMEM = BAR_OFF + N_BARS * 8 + 32 + 1024;  // + alignment slack
 };
+static_assert(Cfg<kEpiSwiglu>::SMEM <= 232448, "smem");
+static_assert(Cfg<kEpiBf16>::SMEM <= 232448, "smem");
 
-__device__ __forceinline__ uint4 dequant_word(uint32_t w, float sc, float bi) {
-    float f[8];
+__device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// 8 codes of one word (nibble order c0,c2,c4,c6,c1,c3,c5,c7) -> 4 bf16x2 in column order
+__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t s2, uint32_t b2, uint32_t* out) {
+    const uint32_t magic = 0x43004300u;  // bf16x2 (128, 128)
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-        f[j] = __fmaf_rn(__fsub_rn(__uint_as_float(0x4B000000u | ((w >> (4 * j)) & 0xFu)), 8388608.0f), sc, bi);
-    return make_uint4(pack_bf2(f[0], f[1]), pack_bf2(f[2], f[3]), pack_bf2(f[4], f[5]), pack_bf2(f[6], f[7]));
+    for (int j = 0; j < 4; ++j) out[j] = bf2_fma(bf2_sub(((w >> (4 * j)) & 0x000F000Fu) | magic, magic), s2, b2);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// the mbarrier receives one arrival when all prior cp.async of this thread complete
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
+__device__ __forceinline__ bool wait_all(uint32_t bar, uint32_t parity, volatile int* abort) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort));
+}
+
+// After giving up, a producer waits (bounded) until the newest copy it issued
+// into each stage of its ring has landed, so no copy targets freed memory.
+__device__ __forceinline__ void drain_ring(uint32_t bar0, int stages, int issued) {
+    for (int st = 0; st < stages && st < issued; ++st) {
+        const int last = st + (issued - 1 - st) / stages * stages;
+        const uint32_t par = (last / stages) & 1;
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(bar0 + 8 * st, par) && global_ns() - t0 < kWaitLimitNs) {
+        }
+    }
+}
+
+__device__ __forceinline__ void trace_at(const GemmArgs& a, int role, int i) {
+    if (a.trace && blockIdx.x == 0 && i < a.trace_n) a.trace[(size_t)role * a.trace_n + i] = global_ns();
 }
 
 template <int EPI>
@@ -53,32 +125,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * C::STAGES + 2);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::N_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    volatile int* consumed = reinterpret_cast<volatile int*>(tmem_slot + 2);
-    auto full_bar = [&](int s) { return smem_u32(bars + s); };
-    auto ready_bar = [&](int s) { return smem_u32(bars + C::STAGES + s); };
-    auto empty_bar = [&](int s) { return smem_u32(bars + 2 * C::STAGES + s); };
-    const uint32_t accfull_bar = smem_u32(bars + 3 * C::STAGES);
-    const uint32_t accempty_bar = smem_u32(bars + 3 * C::STAGES + 1);
-    auto a_smem = [&](int s) { return sbase + s * C::STAGE; };
-    auto b_smem = [&](int s) { return sbase + s * C::STAGE + C::A_BYTES; };
-    auto p_smem = [&](int s) { return smem + s * C::STAGE + C::A_BYTES + C::B_BYTES; };
+    const uint32_t bar_base = smem_u32(bars);
+    auto full_w = [&](int s) { return bar_base + 8 * s; };
+    auto empty_w = [&](int s) { return bar_base + 8 * (C::SW + s); };
+    auto full_b = [&](int s) { return bar_base + 8 * (2 * C::SW + s); };
+    auto empty_b = [&](int s) { return bar_base + 8 * (2 * C::SW + C::SB + s); };
+    auto aready = [&](int s) { return bar_base + 8 * (2 * C::SW + 2 * C::SB + s); };
+    auto aempty = [&](int s) { return bar_base + 8 * (2 * C::SW + 2 * C::SB + C::SA + s); };
+    auto accfull = [&](int b) { return bar_base + 8 * (2 * C::SW + 2 * C::SB + 2 * C::SA + b); };
+    auto accempty = [&](int b) { return bar_base + 8 * (2 * C::SW + 2 * C::SB + 2 * C::SA + 2 + b); };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(full_bar(s), 1);
-            mbar_init(ready_bar(s), 128);
-            mbar_init(empty_bar(s), 1);
-        }
-        mbar_init(accfull_bar, 1);
-        mbar_init(accempty_bar, 128);
+        for (int s = 0; s < C::SW; ++s) mbar_init(full_w(s), 1), mbar_init(empty_w(s), kDqWarps);
+        for (int s = 0; s < C::SB; ++s) mbar_init(full_b(s), C::GATHER ? 64 : 1), mbar_init(empty_b(s), 1);
+        for (int s = 0; s < C::SA; ++s) mbar_init(aready(s), kDqWarps), mbar_init(aempty(s), 1);
+        for (int b = 0; b < 2; ++b) mbar_init(accfull(b), 1), mbar_init(accempty(b), kEpThreads);
         *abort_flag = 0;
-        *consumed = 0;
         fence_mbar_init();
     }
-    if (warp == 1) {
+    if (warp == kWarpMma) {
         tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
         tmem_relinquish();
     }
@@ -86,147 +154,288 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
     const int n_items = *a.n_tiles * a.n_rt;
     const int KT = a.n_kt;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ producer
+    if (warp == kWarpW) {
+        // ---------------------------------------------- weight producer (bulk)
         if (lane == 0) {
-            const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
+            const uint64_t pol = policy_evict_first();
             int s = 0, ph = 0, issued = 0;
             for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
                 const int4 tl = a.tiles[item / a.n_rt];
                 const int rt = item % a.n_rt;
                 const uint8_t* wsrc =
                     a.wblocks + (((size_t)tl.x * a.n_rt + rt) * KT * a.wstride + a.woff) * kBlockBytes;
-                const uint32_t bbytes = (uint32_t)tl.z * 128u;
                 for (int kt = 0; kt < KT; ++kt) {
-                    if (!mbar_wait(empty_bar(s), ph ^ 1, abort_flag)) break;
-                    mbar_arrive_expect_tx(full_bar(s), C::PACK_BYTES + bbytes);
-                    bulk_g2s_hint(smem_u32(p_smem(s)), wsrc + (size_t)kt * a.wstride * kBlockBytes, C::PACK_BYTES,
-                                  full_bar(s), pol_w);
-                    bulk_g2s_hint(b_smem(s), reinterpret_cast<const uint8_t*>(a.act) +
-                                                 ((size_t)kt * a.atoms + (tl.y >> 3)) * 1024,
-                                  bbytes, full_bar(s), pol_x);
+                    if (!mbar_wait(empty_w(s), ph ^ 1, abort_flag)) break;
+                    mbar_arrive_expect_tx(full_w(s), C::W_STAGE);
+                    bulk_g2s_hint(sbase + C::W_OFF + s * C::W_STAGE, wsrc + (size_t)kt * a.wstride * kBlockBytes,
+                                  C::W_STAGE, full_w(s), pol);
+                    trace_at(a, kTrWIssue, issued);
                     ++issued;
-                    if (++s == C::STAGES) s = 0, ph ^= 1;
+                    if (++s == C::SW) s = 0, ph ^= 1;
                 }
             }
-            // drain: copies still in flight must land before the CTA exits
-            if (*abort_flag) {
-                for (int i = *consumed; i < issued; ++i) {
-                    const int st = i % C::STAGES, par = (i / C::STAGES) & 1;
-                    uint64_t t0 = global_ns();
-                    while (!mbar_try_wait(full_bar(st), par) && global_ns() - t0 < kWaitLimitNs) {
-                    }
-                }
-            }
+            if (*abort_flag) drain_ring(full_w(0), C::SW, issued);
         }
         __syncwarp();
-    } else if (warp == 1) {
+    } else if (warp == kWarpB || warp == kWarpB + 1) {
+        // ----------------------------------------------- token-tile producer
+        if constexpr (C::GATHER) {
+            const int wb = warp - kWarpB, c = lane & 7, rsub = 4 * wb + (lane >> 3);
+            int s = 0, ph = 0, step = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+                const int4 tl = a.tiles[item / a.n_rt];
+                const int passes = tl.z >> 3;  // 8 rows per pass of the two warps
+                int tok[kBN / 8];
+#pragma unroll
+                for (int p = 0; p < kBN / 8; ++p) tok[p] = p < passes ? a.src[tl.y + 8 * p + rsub] : -1;
+                for (int kt = 0; kt < KT; ++kt, ++step) {
+                    if (!wait_all(empty_b(s), ph ^ 1, abort_flag)) { ok = false; break; }
+                    const uint32_t bst = sbase + C::B_OFF + s * C::B_STAGE;
+#pragma unroll
+                    for (int p = 0; p < kBN / 8; ++p) {
+                        if (p < passes) {
+                            const int j = 8 * p + rsub, t = tok[p];
+                            const uint16_t* src = a.x_rows + (size_t)(t >= 0 ? t : 0) * a.x_ld + kt * kGroup + c * 8;
+                            cp_async16(bst + (j >> 3) * 1024 + (j & 7) * 128 + ((c ^ (j & 7)) << 4), src,
+                                       t >= 0 ? 16u : 0u);
+                        }
+                    }
+                    cp_async_arrive_noinc(full_b(s));
+                    if (wb == 0 && lane == 0) trace_at(a, kTrBSignal, step);
+                    if (++s == C::SB) s = 0, ph ^= 1;
+                }
+            }
+            cp_async_wait_all();  // nothing may land after the CTA exits
+        } else if (warp == kWarpB && lane == 0) {
+            const uint64_t pol = policy_evict_last();
+            int s = 0, ph = 0, issued = 0;
+            for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
+                const int4 tl = a.tiles[item / a.n_rt];
+                const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(a.act) + (size_t)(tl.y >> 3) * 1024;
+                const uint32_t bbytes = (uint32_t)tl.z * 128u;
+                for (int kt = 0; kt < KT; ++kt) {
+                    if (!mbar_wait(empty_b(s), ph ^ 1, abort_flag)) break;
+                    mbar_arrive_expect_tx(full_b(s), bbytes);
+                    bulk_g2s_hint(sbase + C::B_OFF + s * C::B_STAGE, xsrc + (size_t)kt * a.atoms * 1024, bbytes,
+                                  full_b(s), pol);
+                    trace_at(a, kTrBSignal, issued);
+                    ++issued;
+                    if (++s == C::SB) s = 0, ph ^= 1;
+                }
+            }
+            if (*abort_flag) drain_ring(full_b(0), C::SB, issued);
+        }
+        __syncwarp();
+    } else if (warp == kWarpMma) {
         // ---------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            int s = 0, ph = 0, it = 0;
+            int sa = 0, pha = 0, sb = 0, phb = 0, it = 0, step = 0;
+            const uint32_t a_tmem0 = tmem + C::A_TMEM;
+            const uint64_t b_desc0 = sw128_desc(sbase + C::B_OFF);
             for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, ++it) {
                 const int4 tl = a.tiles[item / a.n_rt];
                 const uint32_t idesc = idesc_bf16(128, tl.z);
-                if (!mbar_wait(accempty_bar, (it & 1) ^ 1, abort_flag)) break;
+                const int buf = it & 1;
+                if (!mbar_wait(accempty(buf), ((it >> 1) & 1) ^ 1, abort_flag)) break;
                 tc_fence_after();
+                const uint32_t dbase = tmem + buf * C::ACC_COLS;
                 bool ok = true;
                 for (int kt = 0; kt < KT; ++kt) {
-                    if (!mbar_wait(ready_bar(s), ph, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(aready(sa), pha, abort_flag) || !mbar_wait(full_b(sb), phb, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    trace_at(a, kTrMmaStart, step);
                     tc_fence_after();
-#pragma unroll
-                    for (int p = 0; p < C::NP; ++p)
+                    trace_at(a, kTrMmaFenced, step);
+                    // descriptors: plain adds on precomputed bases (the start address field
+                    // advances 16 bytes per unit; stages stay below 256 KB)
+                    const uint32_t abase = a_tmem0 + sa * C::A_COLS;
+                    const uint64_t bdesc = b_desc0 + (uint64_t)(sb * (C::B_STAGE >> 4));
+                    const uint32_t acc0 = kt != 0;
+                    if constexpr (C::NP == 2) {  // gate and up chains interleaved
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            tc_mma_f16(tmem + p * kBN, sw128_desc(a_smem(s) + p * kRowTile * 128 + kk * 32),
-                                       sw128_desc(b_smem(s) + kk * 32), idesc, (kt | kk) != 0);
-                    tc_commit(empty_bar(s));
-                    if (++s == C::STAGES) s = 0, ph ^= 1;
+#pragma unroll
+                            for (int p = 0; p < 2; ++p)
+                                tc_mma_f16_ts(dbase + p * kBN, abase + p * 32 + kk * 8, bdesc + 2 * kk, idesc,
+                                              kk == 0 ? acc0 : 1u);
+                    } else {  // even and odd k-slices into two accumulators, summed by the epilogue
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            tc_mma_f16_ts(dbase + (kk & 1) * kBN, abase + kk * 8, bdesc + 2 * kk, idesc,
+                                          kk < 2 ? acc0 : 1u);
+                    }
+                    tc_commit(empty_b(sb));  // frees B stage sb and A stage sa (same index)
+                    trace_at(a, kTrMmaIssued, step++);
+                    if (++sa == C::SA) sa = 0, pha ^= 1;
+                    if (++sb == C::SB) sb = 0, phb ^= 1;
                 }
                 if (!ok) break;
-                tc_commit(accfull_bar);
+                tc_commit(accfull(buf));
             }
         }
         __syncwarp();
-    } else {
-        // ------------------------------------------------- dequant + epilogue
-        const int t = tid - 64;             // weight row of the tile
-        const int q = warp & 3;             // TMEM lane quarter of this warp
-        const int frow = q * 32 + lane;     // accumulator row read in the epilogue
-        int s = 0, ph = 0, it = 0, done = 0;
+    } else if (warp < kWarpEp) {
+        // ------------------------------------------------------------ dequant
+        const int dw = warp - kWarpDq;           // 0..15
+        const int q = warp & 3;                  // TMEM lane quarter this warp may write
+        const int r = q * 32 + lane;             // weight row of the tile = TMEM lane
+        const int part = dw >> 2;                // 0..3: which quarter of the (projections x words) of the row
+        // gate/up: part = projection * 2 + half (4 words each); plain: part = 2-word quarter of the row
+        const int p = C::NP == 2 ? (part >> 1) : 0;
+        const int wofs = C::NP == 2 ? (part & 1) * 4 : part * 2;  // first word of this part
+        const int nw = C::NP == 2 ? 4 : 2;                       // words per part
+        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + C::A_TMEM + p * 32 + wofs * 4;
+        int sw = 0, phw = 0, sa = 0, pha = 0, step = 0, prev_sa = -1;
         bool ok = true;
-        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+        // step i's TMEM store is waited for (and its stage signalled ready) after
+        // step i+1 has been dequantised, so the store overlaps the next step's work
+        auto signal_prev = [&]() {
+            if (prev_sa >= 0) {
+                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(aready(prev_sa));
+                if (dw == 0 && lane == 0) trace_at(a, kTrDqDone, step - 1);
+                prev_sa = -1;
+            }
+        };
+        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+            for (int kt = 0; kt < KT; ++kt, ++step) {
+                if (!wait_all(full_w(sw), phw, abort_flag) || !wait_all(empty_b(sa), pha ^ 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                if (dw == 0 && lane == 0) trace_at(a, kTrDqStart, step);
+                tc_fence_after();
+                const uint8_t* blk = smem + C::W_OFF + sw * C::W_STAGE + p * kBlockBytes;
+                const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
+                const uint32_t sv = sb[r], bv = sb[kRowTile + r];
+                // words [wofs, wofs + nw) of row r: plane wofs/4 of the block
+                const uint8_t* wp = blk + (wofs >> 2) * 2048 + r * 16 + (wofs & 3) * 4;
+                uint32_t ws[4];
+                if (nw == 4) {
+                    const uint4 w0 = *reinterpret_cast<const uint4*>(wp);
+                    ws[0] = w0.x, ws[1] = w0.y, ws[2] = w0.z, ws[3] = w0.w;
+                } else {
+                    const uint2 w0 = *reinterpret_cast<const uint2*>(wp);
+                    ws[0] = w0.x, ws[1] = w0.y, ws[2] = 0, ws[3] = 0;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty_w(sw));  // packed block consumed: recycle early
+                const uint32_t s2v = sv | (sv << 16), b2v = bv | (bv << 16);
+                const uint32_t at = trow + sa * C::A_COLS;
+                if constexpr (C::NP == 2) {
+                    uint32_t v[16];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) dequant_word(ws[c], s2v, b2v, &v[4 * c]);
+                    signal_prev();
+                    tmem_st16(at, v);
+                } else {
+                    uint32_t v[8];
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) dequant_word(ws[c], s2v, b2v, &v[4 * c]);
+                    signal_prev();
+                    tmem_st8(at, v);
+                }
+                if (dw == 0 && lane == 0) trace_at(a, kTrDqStored, step);
+                prev_sa = sa;
+                if (++sw == C::SW) sw = 0, phw ^= 1;
+                if (++sa == C::SA) sa = 0, pha ^= 1;
+            }
+        }
+        if (ok) signal_prev();
+    } else {
+        // ----------------------------------------------------------- epilogue
+        const int q = warp & 3;          // TMEM lane quarter of this warp
+        const int f = q * 32 + lane;     // accumulator row = weight row (feature) of the tile
+        const int et = tid - 32 * kWarpEp;
+        int it = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
             const int4 tl = a.tiles[item / a.n_rt];
             const int rt = item % a.n_rt;
-            for (int kt = 0; kt < KT; ++kt) {
-                if (!__all_sync(0xffffffffu, mbar_wait(full_bar(s), ph, abort_flag))) { ok = false; break; }
-                const uint8_t* pk = p_smem(s);
-#pragma unroll
-                for (int p = 0; p < C::NP; ++p) {
-                    const uint8_t* blk = pk + p * kBlockBytes;
-                    const uint4 w0 = *reinterpret_cast<const uint4*>(blk + t * 32);
-                    const uint4 w1 = *reinterpret_cast<const uint4*>(blk + t * 32 + 16);
-                    const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
-                    const float sc = bf2f(sb[t]), bi = bf2f(sb[kRowTile + t]);
-                    const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                    uint8_t* arow = smem + s * C::STAGE + p * kRowTile * 128 + (t >> 3) * 1024 + (t & 7) * 128;
-#pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        *reinterpret_cast<uint4*>(arow + ((c ^ (t & 7)) << 4)) = dequant_word(ws[c], sc, bi);
-                }
-                fence_proxy_async_smem();
-                mbar_arrive(ready_bar(s));
-                ++done;
-                if (t == 0) *consumed = done;
-                if (++s == C::STAGES) s = 0, ph ^= 1;
-            }
-            if (!ok) break;
-            // epilogue
-            if (!__all_sync(0xffffffffu, mbar_wait(accfull_bar, it & 1, abort_flag))) { ok = false; break; }
+            const int buf = it & 1;
+            if (!wait_all(accfull(buf), (it >> 1) & 1, abort_flag)) break;
+            if (et == 0) trace_at(a, kTrEpStart, it);
             tc_fence_after();
-            const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
-            const int feat = rt * kRowTile + frow;
-            const int nstore = min(tl.z, a.row_limit - tl.y);
-            for (int j0 = 0; j0 < tl.z; j0 += 16) {
-                float g[16];
-                tmem_ld16(tq + j0, g);
-                if constexpr (EPI == kEpiSwiglu) {
-                    float u[16];
-                    tmem_ld16(tq + kBN + j0, u);
+            const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + buf * C::ACC_COLS;
+            if constexpr (EPI == kEpiF32) {
+                const int nstore = min(tl.z, a.row_limit - tl.y);
+                float* y = reinterpret_cast<float*>(a.out);
+                for (int j0 = 0; j0 < tl.z; j0 += 16) {
+                    float g[16], g1[16];
+                    tmem_ld16(tq + j0, g);
+                    tmem_ld16(tq + kBN + j0, g1);
                     tc_wait_ld();
-                    uint8_t* hb = reinterpret_cast<uint8_t*>(a.out);
 #pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) {
-                        if (j0 + jj >= nstore) break;
-                        const float gv = g[jj];
-                        const float hv = (gv / (1.0f + expf(-gv))) * u[jj];  // ops.metal:21
-                        *reinterpret_cast<uint16_t*>(hb + tiled_off(tl.y + j0 + jj, feat, a.out_atoms)) = f2bf(hv);
+                    for (int jj = 0; jj < 16; ++jj)
+                        if (j0 + jj < nstore) y[(size_t)(tl.y + j0 + jj) * a.out_ld + rt * kRowTile + f] = g[jj] + g1[jj];
+                }
+                tc_fence_before();
+                mbar_arrive(accempty(buf));
+            } else {
+                // the staging buffer of two items ago must have been read by its bulk store
+                if (et == 0) bulk_wait_read1();
+                named_bar_sync(1, kEpThreads);
+                uint8_t* stg = smem + C::STG_OFF + buf * C::STG;
+                for (int j0 = 0; j0 < tl.z; j0 += 16) {
+                    float g[16], u[16];
+                    tmem_ld16(tq + j0, g);
+                    tmem_ld16(tq + kBN + j0, u);  // up projection, or the odd k-slices
+                    if constexpr (EPI == kEpiSwiglu) {
+                        tc_wait_ld();
+                        // staging = two k-tile planes of H (features f>>6), swizzled like the global layout
+                        const int fc = f & 63;
+                        uint8_t* pl = stg + (f >> 6) * (kBN * 128) + ((fc & 7) << 1);
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) {
+                            const int j = j0 + jj;
+                            const float gv = g[jj];
+                            const float hv = (gv / (1.0f + expf(-gv))) * u[jj];  // ops.metal:21
+                            *reinterpret_cast<uint16_t*>(pl + (j >> 3) * 1024 + (j & 7) * 128 + (((fc >> 3) ^ (j & 7)) << 4)) =
+                                f2bf(hv);
+                        }
+                    } else {
+                        tc_wait_ld();
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj)
+                            *reinterpret_cast<uint16_t*>(stg + (j0 + jj) * 256 + f * 2) = f2bf(g[jj] + u[jj]);
                     }
-                } else if constexpr (EPI == kEpiBf16) {
-                    tc_wait_ld();
-                    uint16_t* y = reinterpret_cast<uint16_t*>(a.out);
+                }
+                tc_fence_before();
+                mbar_arrive(accempty(buf));  // accumulator drained: the next item may start
+                fence_proxy_async_smem();    // staging written by threads -> read by the bulk copy
+                named_bar_sync(1, kEpThreads);
+                if (et == 0) {
+                    if constexpr (EPI == kEpiSwiglu) {
+                        uint8_t* hb = reinterpret_cast<uint8_t*>(a.out);
 #pragma unroll
-                    for (int jj = 0; jj < 16; ++jj)
-                        if (j0 + jj < nstore) y[(size_t)(tl.y + j0 + jj) * a.out_ld + feat] = f2bf(g[jj]);
-                } else {
-                    tc_wait_ld();
-                    float* y = reinterpret_cast<float*>(a.out);
-#pragma unroll
-                    for (int jj = 0; jj < 16; ++jj)
-                        if (j0 + jj < nstore) y[(size_t)(tl.y + j0 + jj) * a.out_ld + feat] = g[jj];
+                        for (int pln = 0; pln < 2; ++pln)
+                            bulk_s2g(hb + ((size_t)(rt * 2 + pln) * a.out_atoms + (tl.y >> 3)) * 1024,
+                                     sbase + C::STG_OFF + buf * C::STG + pln * (kBN * 128), (uint32_t)tl.z * 128u);
+                    } else {
+                        uint8_t* yb = reinterpret_cast<uint8_t*>(a.out);
+                        const int nstore = min(tl.z, a.row_limit - tl.y);
+                        for (int j = 0; j < nstore; ++j)
+                            bulk_s2g(yb + ((size_t)(tl.y + j) * a.out_ld + rt * kRowTile) * 2,
+                                     sbase + C::STG_OFF + buf * C::STG + j * 256, 256u);
+                    }
+                    bulk_commit();
+                    trace_at(a, kTrEpDone, it);
                 }
             }
-            tc_fence_before();
-            mbar_arrive(accempty_bar);
         }
+        if (et == 0) bulk_wait0();  // results are in global memory before the CTA exits
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+    if (warp == kWarpMma) tmem_dealloc(tmem, C::TMEM_COLS);
     if (tid == 0 && *abort_flag) atomicExch(a.err, kDevTimeout);
 }
 
@@ -235,6 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
 size_t gemm_smem_bytes(int epi) {
     return epi == kEpiSwiglu ? Cfg<kEpiSwiglu>::SMEM : epi == kEpiBf16 ? Cfg<kEpiBf16>::SMEM : Cfg<kEpiF32>::SMEM;
 }
+int gemm_tile_rows() { return kBN; }
 
 template <int EPI>
 static cudaError_t launch_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
@@ -246,7 +456,7 @@ static cudaError_t launch_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
 }
 
 cudaError_t launch_gemm(const GemmArgs& a, int epi, int num_sms, cudaStream_t st) {
-    if (a.bn > kBN || a.bn % kSegAlign || a.wstride < Cfg<kEpiSwiglu>::NP * (epi == kEpiSwiglu))
+    if (a.bn > kBN || a.bn % kSegAlign || (epi == kEpiSwiglu && (a.wstride < 2 || !a.x_rows || !a.src)))
         return cudaErrorInvalidValue;
     switch (epi) {
         case kEpiSwiglu: return launch_t<kEpiSwiglu>(a, num_sms, st);

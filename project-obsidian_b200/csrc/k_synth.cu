@@ -87,8 +87,21 @@ __global__ void k_synth_x(uint64_t kx, int row0, int T, int H, float eps, uint16
     for (int i = 0; i < H; ++i) row[i] = f2bf(__fdiv_rn(bf2f(row[i]), rms));
 }
 
+// MLX word (column c at nibble c) -> block word (column nib_col(p) at nibble p)
+__device__ __forceinline__ uint32_t nib_order(uint32_t w) {
+    uint32_t o = 0;
+#pragma unroll
+    for (int p = 0; p < 8; ++p) o |= ((w >> (4 * nib_col(p))) & 0xFu) << (4 * p);
+    return o;
+}
+__device__ __forceinline__ uint4 nib_order(uint4 v) {
+    return make_uint4(nib_order(v.x), nib_order(v.y), nib_order(v.z), nib_order(v.w));
+}
+
 // Thread per (block, row): 8 packed words + scale + bias.  Group size 64 equals
-// the block width, so block kt uses scale/bias column kt.
+// the block width, so block kt uses scale/bias column kt.  Rows' first and
+// second 16-byte halves go to separate 2 KB planes of the block, so 16-byte
+// reads by consecutive rows are contiguous.
 __global__ void k_retile(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
                          const uint16_t* __restrict__ b, int E, int out_f, int in_f, uint8_t* __restrict__ dst,
                          int interleave, int p) {
@@ -104,9 +117,8 @@ __global__ void k_retile(const uint32_t* __restrict__ w, const uint16_t* __restr
         size_t row = (size_t)e * out_f + (size_t)rt * kRowTile + r;
         const uint4* src = reinterpret_cast<const uint4*>(w + row * (in_f / 8) + (size_t)kt * 8);
         uint8_t* d = dst + (blk * interleave + p) * (size_t)kBlockBytes;
-        uint4* dw = reinterpret_cast<uint4*>(d + r * 32);
-        dw[0] = src[0];
-        dw[1] = src[1];
+        *reinterpret_cast<uint4*>(d + r * 16) = nib_order(src[0]);         // words 0-3
+        *reinterpret_cast<uint4*>(d + 2048 + r * 16) = nib_order(src[1]);  // words 4-7
         uint16_t* ds = reinterpret_cast<uint16_t*>(d + kBlockWords * 4);
         ds[r] = s[row * (in_f / kGroup) + kt];
         ds[kRowTile + r] = b[row * (in_f / kGroup) + kt];

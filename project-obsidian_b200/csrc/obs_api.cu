@@ -21,7 +21,7 @@ using namespace obs;
 
 namespace {
 constexpr int kDecodeMaxT = 64;  // largest T the decode path's scratch covers
-constexpr int kBNTile = 128;     // GEMM token tile
+constexpr int kBNTile = 64;      // GEMM token tile (gemm_tile_rows())
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 }  // namespace
@@ -51,6 +51,8 @@ struct obs_ctx {
     uint16_t* res_dev = nullptr;
     float* bias_dev = nullptr;
     int R_cap = 0, max_tiles = 0, decode_max = 4;
+    uint64_t* trace = nullptr;  // obs_trace_enable
+    int trace_n = 0;
     // optional per-stage event timing (obs_profile_enable)
     bool prof = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -170,7 +172,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     const int DT = ctx->decode_max > 0 ? kDecodeMaxT : 0;
     struct Item { void** p; size_t bytes; };
     std::vector<Item> items = {
-        {(void**)&ctx->logits, (size_t)T * E * 4},
+        {(void**)&ctx->logits, (size_t)8 * T * E * 4},  // router partial planes
         {(void**)&ctx->ids, (size_t)T * K * 4},
         {(void**)&ctx->wts, (size_t)T * K * 4},
         {(void**)&ctx->disp.counts, (size_t)E * 4},
@@ -329,7 +331,13 @@ extern "C" int obs_gate(obs_ctx* ctx, int layer, const uint16_t* x, float* logit
     if (rc || (rc = check_T(ctx, T))) return rc;
     if (T == 0) return OBS_OK;
     if (!x || !logits) return fail(ctx, OBS_ERR_INVALID, "null pointer");
-    CU(launch_router_logits(ctx->layers[layer], ctx->sh, x, T, logits, as_stream(stream)), "router");
+    cudaStream_t st = as_stream(stream);
+    if (router_parts(T) == 1) {
+        CU(launch_router_logits(ctx->layers[layer], ctx->sh, x, T, logits, st), "router");
+    } else {
+        CU(launch_router_logits(ctx->layers[layer], ctx->sh, x, T, ctx->logits, st), "router");
+        CU(launch_router_finish(ctx->logits, T, ctx->sh.E, logits, st), "router finish");
+    }
     return OBS_OK;
 }
 
@@ -340,7 +348,7 @@ extern "C" int obs_route(obs_ctx* ctx, const float* logits, const float* bias, i
     if (rc) return rc;
     if (T == 0) return OBS_OK;
     if (!logits || !ids || !w) return fail(ctx, OBS_ERR_INVALID, "null pointer");
-    CU(launch_topk(logits, bias, T, ctx->sh.E, ctx->sh.K, ctx->cfg.norm_topk, ids, w, nullptr, ctx->err_flag,
+    CU(launch_topk(logits, 1, bias, T, ctx->sh.E, ctx->sh.K, ctx->cfg.norm_topk, ids, w, nullptr, nullptr,
                    as_stream(stream)),
        "topk");
     return OBS_OK;
@@ -377,14 +385,15 @@ static int dispatch_from_ids(obs_ctx* ctx, const int32_t* ids, const uint16_t* x
     return OBS_OK;
 }
 
-static GemmArgs gemm_gateup(obs_ctx* ctx, const LayerDev& L) {
+static GemmArgs gemm_gateup(obs_ctx* ctx, const LayerDev& L, const uint16_t* x) {
     const Shape& s = ctx->sh;
     GemmArgs g{};
     g.wblocks = L.gateup;
     g.wstride = 2;
     g.woff = 0;
-    g.act = ctx->disp.xp;
-    g.atoms = ctx->disp.atoms;
+    g.x_rows = x;
+    g.src = ctx->disp.src;
+    g.x_ld = s.H;
     g.tiles = ctx->disp.tiles;
     g.n_tiles = ctx->disp.n_tiles;
     g.n_rt = s.I / kRowTile;
@@ -394,6 +403,8 @@ static GemmArgs gemm_gateup(obs_ctx* ctx, const LayerDev& L) {
     g.out_atoms = ctx->disp.atoms;
     g.row_limit = ctx->R_cap;
     g.err = ctx->err_flag;
+    g.trace = ctx->trace;
+    g.trace_n = ctx->trace_n;
     return g;
 }
 
@@ -418,8 +429,8 @@ static GemmArgs gemm_down(obs_ctx* ctx, const LayerDev& L) {
 }
 
 // prefill expert FFN over the current dispatch: xp -> hbuf -> ybuf (slot rows)
-static int prefill_ffn(obs_ctx* ctx, const LayerDev& L, cudaStream_t st) {
-    CU(launch_gemm(gemm_gateup(ctx, L), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");
+static int prefill_ffn(obs_ctx* ctx, const LayerDev& L, const uint16_t* x, cudaStream_t st) {
+    CU(launch_gemm(gemm_gateup(ctx, L, x), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");
     CU(launch_gemm(gemm_down(ctx, L), kEpiBf16, ctx->num_sms, st), "gemm down");
     return OBS_OK;
 }
@@ -442,9 +453,9 @@ extern "C" int obs_expert_ffn(obs_ctx* ctx, int layer, const uint16_t* x, const 
         return OBS_OK;
     }
     if (path != OBS_PATH_PREFILL) return fail(ctx, OBS_ERR_INVALID, "path must be DECODE or PREFILL");
-    rc = dispatch_from_ids(ctx, ids, x, T, 1, st);
+    rc = dispatch_from_ids(ctx, ids, x, T, 0, st);
     if (rc) return rc;
-    rc = prefill_ffn(ctx, L, st);
+    rc = prefill_ffn(ctx, L, x, st);
     if (rc) return rc;
     CU(launch_gather_rows(ctx->ybuf, ctx->disp.slot_of, T * s.K, s.H, y, st), "gather");
     return OBS_OK;
@@ -510,8 +521,8 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
     prof_end(ctx, st);
     if (path == OBS_PATH_DECODE) {
         prof_begin(ctx, OBS_STAGE_TOPK, st);
-        CU(launch_topk(ctx->logits, logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids, ctx->wts, nullptr,
-                       ctx->err_flag, st),
+        CU(launch_topk(ctx->logits, router_parts(T), logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids,
+                       ctx->wts, nullptr, nullptr, st),
            "topk");
         prof_end(ctx, st);
         prof_begin(ctx, OBS_STAGE_DECODE_GATEUP, st);
@@ -524,15 +535,15 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
     }
     CU(cudaMemsetAsync(ctx->disp.counts, 0, s.E * 4, st), "memset");
     prof_begin(ctx, OBS_STAGE_TOPK, st);
-    CU(launch_topk(ctx->logits, logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids, ctx->wts, ctx->disp.counts,
-                   ctx->err_flag, st),
+    CU(launch_topk(ctx->logits, router_parts(T), logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids,
+                   ctx->wts, ctx->disp.counts, nullptr, st),
        "topk");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_DISPATCH, st);
-    CU(launch_dispatch(ctx->ids, x, T, s, ctx->disp, 1, st), "dispatch");
+    CU(launch_dispatch(ctx->ids, x, T, s, ctx->disp, 0, st), "dispatch");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_GEMM_GATEUP, st);
-    CU(launch_gemm(gemm_gateup(ctx, L), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");
+    CU(launch_gemm(gemm_gateup(ctx, L, x), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_GEMM_DOWN, st);
     CU(launch_gemm(gemm_down(ctx, L), kEpiBf16, ctx->num_sms, st), "gemm down");
@@ -598,5 +609,13 @@ extern "C" int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches
         launches[m.first] += 1;
     }
     ctx->ev_marks.clear();
+    return OBS_OK;
+}
+
+extern "C" int obs_trace_enable(obs_ctx* ctx, uint64_t* trace, int n_steps) {
+    OBS_CHECK_CTX(ctx);
+    if (trace && n_steps <= 0) return fail(ctx, OBS_ERR_INVALID, "n_steps must be positive");
+    ctx->trace = trace;
+    ctx->trace_n = trace ? n_steps : 0;
     return OBS_OK;
 }

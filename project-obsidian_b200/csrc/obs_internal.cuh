@@ -8,8 +8,9 @@
 
 namespace obs {
 
-// One 128-row x 64-column block of a tiled 4-bit projection: 128 rows of
-// 8 uint32 words, then 128 bf16 scales, then 128 bf16 biases (4608 bytes).
+// One 128-row x 64-column block of a tiled 4-bit projection (4608 bytes):
+// words 0-3 of the 128 rows, words 4-7 of the 128 rows, 128 bf16 scales,
+// 128 bf16 biases.
 // gate and up are interleaved per block (gate, up) so one copy brings both.
 struct LayerDev {
     uint32_t* router_w;   // [E, H/4]   reference layout
@@ -36,10 +37,16 @@ cudaError_t launch_retile(const uint32_t* w, const uint16_t* s, const uint16_t* 
                           uint8_t* dst, int interleave, int p, cudaStream_t st);
 
 // --------------------------------------------------------------- k_router.cu
-cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint16_t* x, int T, float* logits,
+// Router logits for T tokens: router_parts(T) partial planes [parts][T][E]
+// (1: final logits; 8: subtree sums that launch_topk / launch_router_finish
+// combine in the fixed tree).  `parts` must hold 8*T*E floats.
+int router_parts(int T);
+cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint16_t* x, int T, float* parts,
                                  cudaStream_t st);
-cudaError_t launch_topk(const float* logits, const float* bias, int T, int E, int K, int norm, int32_t* ids,
-                        float* w, int32_t* counts, int* err, cudaStream_t st);
+cudaError_t launch_router_finish(const float* parts, int T, int E, float* logits, cudaStream_t st);
+// logits_out (optional) receives the combined logits.
+cudaError_t launch_topk(const float* logits, int nparts, const float* bias, int T, int E, int K, int norm,
+                        int32_t* ids, float* w, int32_t* counts, float* logits_out, cudaStream_t st);
 
 // ------------------------------------------------------------- k_dispatch.cu
 struct DispatchBufs {
@@ -83,8 +90,11 @@ struct GemmArgs {
     const uint8_t* wblocks;   // tiled weight blocks of the projection(s)
     int wstride;              // blocks per k-tile step (2 for the gate/up array, 1 for down)
     int woff;                 // block offset inside a step (0 gate, 1 up)
-    const uint16_t* act;      // tiled activations (B operand)
+    const uint16_t* act;      // tiled activations (B operand) for the bulk-copy form
     int atoms;                // row atoms of the activation layout
+    const uint16_t* x_rows;   // kEpiSwiglu: the layer input [T, x_ld] bf16, gathered by row
+    const int32_t* src;       // kEpiSwiglu: source token of each slot (-1: padding row)
+    int x_ld;
     const int4* tiles;        // token tiles {expert, row0, nrows, 0}
     const int32_t* n_tiles;   // device count of token tiles
     int n_rt;                 // weight row tiles per expert
@@ -95,8 +105,25 @@ struct GemmArgs {
     int out_atoms;            // row atoms of the tiled output
     int row_limit;            // rows >= row_limit are not stored
     int* err;                 // device error flag
+    uint64_t* trace;          // optional: CTA 0 records %globaltimer per role and k-step
+    int trace_n;              // k-steps recorded per role
+};
+// trace roles (rows of the trace buffer, trace_n entries each)
+enum TraceRole : int {
+    kTrWIssue = 0,     // weight producer issued the copy of k-step i
+    kTrBSignal = 1,    // token-tile producer signalled k-step i full
+    kTrDqStart = 2,    // dequant warp 0 passed its waits for k-step i
+    kTrDqDone = 3,     // dequant warp 0 arrived "A ready" for k-step i
+    kTrMmaStart = 4,   // MMA thread passed its waits for k-step i
+    kTrMmaIssued = 5,  // MMA thread committed k-step i
+    kTrEpStart = 6,    // epilogue passed accfull of item i
+    kTrEpDone = 7,     // epilogue released the accumulator of item i
+    kTrDqStored = 8,   // dequant warp 0 finished its shared-memory stores of k-step i
+    kTrMmaFenced = 9,  // MMA thread passed its fences for k-step i
+    kTrRoles = 10
 };
 cudaError_t launch_gemm(const GemmArgs& a, int epi, int num_sms, cudaStream_t st);
 size_t gemm_smem_bytes(int epi);
+int gemm_tile_rows();  // token rows per GEMM tile (the dispatch's tile size)
 
 }  // namespace obs

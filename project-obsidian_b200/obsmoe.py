@@ -31,6 +31,7 @@ EXPORTS = (
     "obs_load_layer", "obs_synth_layer", "obs_synth_activations", "obs_moe_forward",
     "obs_moe_forward_host", "obs_gate", "obs_route", "obs_dispatch", "obs_expert_ffn",
     "obs_expert_gemm_f32", "obs_check_device", "obs_profile_enable", "obs_profile_read",
+    "obs_trace_enable",
 )
 STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down")
 
@@ -84,6 +85,7 @@ def lib() -> C.CDLL:
         L.obs_check_device.argtypes = [vp, vp]
         L.obs_profile_enable.argtypes = [vp, i32]
         L.obs_profile_read.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(C.c_int32)]
+        L.obs_trace_enable.argtypes = [vp, vp, i32]
         for name in EXPORTS:
             if name not in ("obs_last_error", "obs_abi_version"):
                 getattr(L, name).restype = i32
@@ -208,6 +210,10 @@ class MoeContext:
         n = (C.c_int32 * len(STAGES))()
         self._chk(lib().obs_profile_read(self._h, ms, n))
         return {name: (ms[i], n[i]) for i, name in enumerate(STAGES)}
+
+    def trace(self, buf, n_steps: int):
+        """Record the gate/up GEMM pipeline timeline of CTA 0 into buf (uint64 [8, n_steps])."""
+        self._chk(lib().obs_trace_enable(self._h, _ptr(buf), n_steps if buf is not None else 0))
 
     def check_device(self, stream=None):
         self._chk(lib().obs_check_device(self._h, _stream(stream)))

@@ -196,3 +196,17 @@ def test_oracle_matches_reference_shaders_live():
     assert all(set(a) == set(b) for a, b in zip(ids, rids))
     ref = rout.astype(np.float32)
     assert np.abs(O.bf16_to_f32(out) - ref).max() <= 1e-2 * np.abs(ref).max()
+
+
+def test_dequant4_bf16_single_rounding():
+    # for these distributions q*s + b is exact in fp32, so one rounding equals fp32-then-bf16
+    w, s, b = O.synth_proj(2, 0, 1, 1, 128, 2048)
+    a = O.dequant4_bf16(w[0], s[0], b[0])
+    c = O.f32_to_bf16(O.dequant4(w[0], s[0], b[0]))
+    assert np.array_equal(a, c)
+    # a tie case: 1 + 2^-8 lies halfway between two bf16 values -> even mantissa (1.0)
+    w1 = np.zeros((1, 8), np.uint32)
+    w1[0, 0] = 1                                  # code 1 in column 0
+    s1 = np.array([[O.f32_to_bf16(np.float32(2.0 ** -8))]], np.uint16)
+    b1 = np.array([[O.f32_to_bf16(np.float32(1.0))]], np.uint16)
+    assert O.dequant4_bf16(w1, s1, b1)[0, 0] == O.f32_to_bf16(np.float32(1.0))
