@@ -162,6 +162,32 @@ int obs_trace_enable(obs_ctx* ctx, uint64_t* trace, int n_steps);
  * that gave up) raised since the last check; clears the flags. */
 int obs_check_device(obs_ctx* ctx, void* stream);
 
+/* ------------------------------------------- allocation-free decode FFN */
+/* No counterpart in the reference.  For callers that cannot allocate device
+ * memory -- code running while a CUDA graph is being captured, hosts whose
+ * framework owns every device byte through its own arena, latency-critical
+ * loops that cannot pay for an allocation's implicit synchronisation -- this
+ * computes, without a context and without allocating:
+ *   out[t] = bf16([residual[t] +] sum_k weights[t,k] * down_e(silu(gate_e x_t) * up_e x_t)),
+ * e = ids[t,k], the decode path's arithmetic, from expert weights in the
+ * reference (MLX) layout given as device pointers in w (router fields unused).
+ * Its scratch is one fixed device array inside the library (about 3.7 MB,
+ * held on every GPU that loads the library until the process exits).
+ * Limits: T * top_k <= OBS_STATIC_MAX_PAIRS, hidden a multiple of 256 up to
+ * OBS_STATIC_MAX_HIDDEN, inter a multiple of 128 up to OBS_STATIC_MAX_INTER;
+ * larger calls return OBS_ERR_INVALID.  ids must lie in [0, n_experts): an
+ * out-of-range id reads expert 0.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  All calls on a device share the array, so calls that
+ * overlap on the GPU (different streams, no ordering) race; the arrival
+ * counters are cleared at the start of each call. */
+#define OBS_STATIC_MAX_PAIRS 64
+#define OBS_STATIC_MAX_HIDDEN 4096
+#define OBS_STATIC_MAX_INTER 1536
+int obs_decode_ffn_static(const obs_layer_weights* w, int n_experts, int hidden, int inter, int top_k,
+                          const uint16_t* x, const int32_t* ids, const float* weights,
+                          const uint16_t* residual, int T, uint16_t* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

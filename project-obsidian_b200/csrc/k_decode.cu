@@ -3,11 +3,13 @@
 // Replaces the reference's per-rank loop of fused_dequant_matvec_4bit x3 +
 // ew_swiglu + ew_scaled_add (src/forward.rs:431-441; shaders/
 // fused_dequant_matvec_4bit.metal:14-53, ops.metal:18-29).  Weights are read
-// once, fully coalesced, from the tiled 4608-byte blocks (128 rows x 64
-// columns + scales + biases); dequantisation is w = fma(q, s, b) in fp32 as in
-// the reference.  Split-K partial sums meet in a fixed order in the last CTA
-// to finish (a per-tile arrival counter that resets itself), so results do
-// not depend on CTA scheduling.
+// once, coalesced, 128 rows x 64 columns at a time; dequantisation is
+// w = fma(q, s, b) in fp32 as in the reference.  Split-K partial sums meet in
+// a fixed order in the last CTA to finish (a per-tile arrival counter that
+// resets itself), so results do not depend on CTA scheduling.
+//
+// The kernels read either the context's tiled 4608-byte blocks or the
+// reference's MLX row-major layout directly.
 #include "obs_internal.cuh"
 
 namespace obs {
@@ -20,26 +22,60 @@ __device__ __forceinline__ float nib_f(uint32_t w, int j) {
     return __fsub_rn(__uint_as_float(0x4B000000u | ((w >> (4 * j)) & 0xFu)), 8388608.0f);
 }
 
-// One warp, one 128x64 block: lane l covers rows (l>>1) + 16 i (i < 8) and the
-// 32 columns of half (l & 1).  xr: the lane's 32 activations (fp32).
-__device__ __forceinline__ void block_dot(const uint8_t* __restrict__ blk, const float (&xr)[32], int lane,
-                                          float (&acc)[8]) {
-    const uint4* wq = reinterpret_cast<const uint4*>(blk + (lane & 1) * 2048);
-    const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
-    uint4 q[8];
+// Weight sources: 128 rows x 64 columns of one projection of one expert.
+// Lane l covers rows (l>>1) + 16 i (i < 8) and the 32 columns of half (l & 1).
+struct TiledSrc {  // the context's blocks; nibble order c0,c2,c4,c6,c1,c3,c5,c7
+    const uint8_t* base;
+    int n_rt, KT, stride, off;  // block (e, rt, kt) = base + (((e*n_rt + rt)*KT + kt)*stride + off) * 4608
+    static constexpr bool kNatural = false;
+    __device__ __forceinline__ void load(int e, int rt, int kt, int lane, uint4 (&q)[8], float (&sc)[8],
+                                         float (&bi)[8]) const {
+        const uint8_t* blk = base + ((((size_t)e * n_rt + rt) * KT + kt) * stride + off) * kBlockBytes;
+        const uint4* wq = reinterpret_cast<const uint4*>(blk + (lane & 1) * 2048);
+        const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = __ldg(wq + (lane >> 1) + 16 * i);
+        for (int i = 0; i < 8; ++i) {
+            const int row = (lane >> 1) + 16 * i;
+            q[i] = __ldg(wq + row);
+            sc[i] = bf2f(__ldg(sb + row));
+            bi[i] = bf2f(__ldg(sb + kRowTile + row));
+        }
+    }
+};
+struct MlxSrc {  // reference layout: w [E, out, in/8] (column c at nibble c), s/b [E, out, in/64]
+    const uint32_t* w;
+    const uint16_t* s;
+    const uint16_t* b;
+    int out_f, in_f;
+    static constexpr bool kNatural = true;
+    __device__ __forceinline__ void load(int e, int rt, int kt, int lane, uint4 (&q)[8], float (&sc)[8],
+                                         float (&bi)[8]) const {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const size_t row = (size_t)e * out_f + rt * kRowTile + (lane >> 1) + 16 * i;
+            q[i] = __ldg(reinterpret_cast<const uint4*>(w + row * (in_f / 8) + kt * 8 + (lane & 1) * 4));
+            sc[i] = bf2f(__ldg(s + row * (in_f / kGroup) + kt));
+            bi[i] = bf2f(__ldg(b + row * (in_f / kGroup) + kt));
+        }
+    }
+};
+
+template <class Src>
+__device__ __forceinline__ void block_dot(const Src& src, int e, int rt, int kt, const float (&xr)[32], int lane,
+                                          float (&acc)[8]) {
+    uint4 q[8];
+    float sc[8], bi[8];
+    src.load(e, rt, kt, lane, q, sc, bi);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const int row = (lane >> 1) + 16 * i;
-        const float sc = bf2f(__ldg(sb + row)), bi = bf2f(__ldg(sb + kRowTile + row));
         const uint32_t ws[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
         float a = acc[i];
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int j = 0; j < 8; ++j)  // nibble j holds column nib_col(j) of the word
-                a = __fmaf_rn(__fmaf_rn(nib_f(ws[c], j), sc, bi), xr[c * 8 + nib_col(j)], a);
+            for (int j = 0; j < 8; ++j)  // nibble j holds column j (MLX) or nib_col(j) (tiled)
+                a = __fmaf_rn(__fmaf_rn(nib_f(ws[c], j), sc[i], bi[i]), xr[c * 8 + (Src::kNatural ? j : nib_col(j))],
+                              a);
         acc[i] = a;
     }
 }
@@ -68,10 +104,10 @@ __device__ __forceinline__ int checked_expert(int e, int E, int* err) {
 
 // grid (I/128, kSplitGU, T*K), 256 threads.  warp w: projection w & 1,
 // k-tiles kt0 + (w >> 1) + 4 j.
-__global__ void __launch_bounds__(256) k_decode_gateup(const uint8_t* __restrict__ gateup,
-                                                       const uint16_t* __restrict__ x,
-                                                       const int32_t* __restrict__ ids, int H, int I, int K,
-                                                       int E, DecodeBufs d) {
+template <class Src>
+__global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const uint16_t* __restrict__ x,
+                                                       const int32_t* __restrict__ ids, int H, int I, int K, int E,
+                                                       DecodeBufs d) {
     __shared__ float s_part[8][kRowTile];
     __shared__ float s_gu[2][kRowTile];
     __shared__ int s_last;
@@ -82,10 +118,9 @@ __global__ void __launch_bounds__(256) k_decode_gateup(const uint8_t* __restrict
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int j = (w >> 1); j < nkt; j += 4) {
         const int kt = ks * nkt + j;
-        const uint8_t* blk = gateup + ((((size_t)e * n_rt + rt) * KT + kt) * 2 + proj) * kBlockBytes;
         float xr[32];
         load_x32(x + (size_t)t * H + kt * kGroup + (lane & 1) * 32, xr);
-        block_dot(blk, xr, lane, acc);
+        block_dot(proj ? usrc : gsrc, e, rt, kt, xr, lane, acc);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -121,8 +156,9 @@ __global__ void __launch_bounds__(256) k_decode_gateup(const uint8_t* __restrict
 }
 
 // grid (H/128, K, T), 256 threads.  warp w: k-tiles w, w+8, ...
-__global__ void __launch_bounds__(256) k_decode_down(const uint8_t* __restrict__ down,
-                                                     const int32_t* __restrict__ ids, const float* __restrict__ wts,
+template <class Src>
+__global__ void __launch_bounds__(256) k_decode_down(Src dsrc, const int32_t* __restrict__ ids,
+                                                     const float* __restrict__ wts,
                                                      const uint16_t* __restrict__ residual, int H, int I, int K,
                                                      int E, DecodeBufs d, uint16_t* __restrict__ out,
                                                      int do_combine) {
@@ -134,10 +170,9 @@ __global__ void __launch_bounds__(256) k_decode_down(const uint8_t* __restrict__
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int kt = w; kt < KT; kt += 8) {
-        const uint8_t* blk = down + (((size_t)e * n_rt + rt) * KT + kt) * kBlockBytes;
         float xr[32];
         load_x32(d.h + (size_t)p * I + kt * kGroup + (lane & 1) * 32, xr);
-        block_dot(blk, xr, lane, acc);
+        block_dot(dsrc, e, rt, kt, xr, lane, acc);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -180,8 +215,9 @@ __global__ void __launch_bounds__(256) k_decode_down(const uint8_t* __restrict__
 cudaError_t launch_decode_gateup(const LayerDev& L, const Shape& sh, const uint16_t* x, const int32_t* ids, int T,
                                  const DecodeBufs& d, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
+    const TiledSrc g{L.gateup, sh.I / kRowTile, sh.H / kGroup, 2, 0}, u{L.gateup, sh.I / kRowTile, sh.H / kGroup, 2, 1};
     dim3 grid(sh.I / kRowTile, kSplitGU, T * sh.K);
-    k_decode_gateup<<<grid, 256, 0, st>>>(L.gateup, x, ids, sh.H, sh.I, sh.K, sh.E, d);
+    k_decode_gateup<TiledSrc><<<grid, 256, 0, st>>>(g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
     return cudaGetLastError();
 }
 
@@ -189,8 +225,25 @@ cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t
                                const uint16_t* residual, int T, const DecodeBufs& d, uint16_t* out, int do_combine,
                                cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
+    const TiledSrc dn{L.down, sh.H / kRowTile, sh.I / kGroup, 1, 0};
     dim3 grid(sh.H / kRowTile, sh.K, T);
-    k_decode_down<<<grid, 256, 0, st>>>(L.down, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, do_combine);
+    k_decode_down<TiledSrc><<<grid, 256, 0, st>>>(dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, do_combine);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_decode_ffn_mlx(const uint32_t* gw, const uint16_t* gs, const uint16_t* gb, const uint32_t* uw,
+                                  const uint16_t* us, const uint16_t* ub, const uint32_t* dw, const uint16_t* ds,
+                                  const uint16_t* db, const Shape& sh, const uint16_t* x, const int32_t* ids,
+                                  const float* w, const uint16_t* residual, int T, const DecodeBufs& d, uint16_t* out,
+                                  cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    const MlxSrc g{gw, gs, gb, sh.I, sh.H}, u{uw, us, ub, sh.I, sh.H}, dn{dw, ds, db, sh.H, sh.I};
+    dim3 g1(sh.I / kRowTile, kSplitGU, T * sh.K);
+    k_decode_gateup<MlxSrc><<<g1, 256, 0, st>>>(g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    dim3 g2(sh.H / kRowTile, sh.K, T);
+    k_decode_down<MlxSrc><<<g2, 256, 0, st>>>(dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, 1);
     return cudaGetLastError();
 }
 

@@ -103,6 +103,11 @@ static thread_local std::string g_create_err;
 
 extern "C" const char* obs_last_error(const obs_ctx* ctx) { return ctx ? ctx->err.c_str() : g_create_err.c_str(); }
 
+namespace obs {
+// message of a context-free entry point, read back with obs_last_error(NULL)
+void set_thread_error(const char* msg) { g_create_err = msg ? msg : ""; }
+}  // namespace obs
+
 static size_t layer_weight_bytes(const Shape& s) {
     size_t router = align_up((size_t)s.E * s.H, 256) + 2 * align_up((size_t)s.E * (s.H / 64) * 2, 256);
     size_t gu = (size_t)s.E * (s.I / kRowTile) * (s.H / kGroup) * 2 * kBlockBytes;
