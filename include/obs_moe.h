@@ -171,9 +171,9 @@ int obs_check_device(obs_ctx* ctx, void* stream);
  *   out[t] = bf16([residual[t] +] sum_k weights[t,k] * down_e(silu(gate_e x_t) * up_e x_t)),
  * e = ids[t,k], the decode path's arithmetic, from expert weights in the
  * reference (MLX) layout given as device pointers in w (router fields unused).
- * Its scratch is one fixed device array inside the library (about 3.7 MB,
+ * Its scratch is one fixed device array inside the library (about 7 MB,
  * held on every GPU that loads the library until the process exits).
- * Limits: T * top_k <= OBS_STATIC_MAX_PAIRS, hidden a multiple of 256 up to
+ * Limits: T * top_k <= OBS_STATIC_MAX_PAIRS, hidden a multiple of 512 up to
  * OBS_STATIC_MAX_HIDDEN, inter a multiple of 128 up to OBS_STATIC_MAX_INTER;
  * larger calls return OBS_ERR_INVALID.  ids must lie in [0, n_experts): an
  * out-of-range id reads expert 0.  The first call on a device looks up the

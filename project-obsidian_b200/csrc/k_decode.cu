@@ -3,10 +3,14 @@
 // Replaces the reference's per-rank loop of fused_dequant_matvec_4bit x3 +
 // ew_swiglu + ew_scaled_add (src/forward.rs:431-441; shaders/
 // fused_dequant_matvec_4bit.metal:14-53, ops.metal:18-29).  Weights are read
-// once, coalesced, 128 rows x 64 columns at a time; dequantisation is
-// w = fma(q, s, b) in fp32 as in the reference.  Split-K partial sums meet in
-// a fixed order in the last CTA to finish (a per-tile arrival counter that
-// resets itself), so results do not depend on CTA scheduling.
+// once, coalesced, 128 rows x 64 columns at a time, all of a warp's loads in
+// flight together.  The group's affine dequantisation is factored out of the
+// inner loop: over one 64-column group, sum_j (q_j s + b) x_j =
+// 16 s (sum_j f_j x_j - sum_j x_j) + b sum_j x_j with f_j = 1 + q_j/16, a float
+// built from the code with one shift and one logic op; per weight that is a
+// shift, a logic op and one fp32 FMA.  Split-K partial sums meet in a fixed
+// order in the last CTA to finish (a per-tile arrival counter that resets
+// itself), so results do not depend on CTA scheduling.
 //
 // The kernels read either the context's tiled 4608-byte blocks or the
 // reference's MLX row-major layout directly.
@@ -15,11 +19,12 @@
 namespace obs {
 namespace {
 
-constexpr int kSplitGU = 4;  // k-splits of the gate/up mat-vec
+constexpr int kSplitGU = kDecodeSplit;  // k-splits of the gate/up mat-vec (one 64-column block per warp)
 
-// exact float of a 4-bit code without I2F: (2^23 | q) - 2^23
-__device__ __forceinline__ float nib_f(uint32_t w, int j) {
-    return __fsub_rn(__uint_as_float(0x4B000000u | ((w >> (4 * j)) & 0xFu)), 8388608.0f);
+// 1 + q/16 as a float, q the 4-bit code at nibble j: the code becomes mantissa bits 19-22
+__device__ __forceinline__ float nib_f16th(uint32_t w, int j) {
+    const uint32_t m = (4 * j <= 19) ? (w << (19 - 4 * j)) : (w >> (4 * j - 19));
+    return __uint_as_float((m & 0x00780000u) | 0x3F800000u);
 }
 
 // Weight sources: 128 rows x 64 columns of one projection of one expert.
@@ -61,27 +66,28 @@ struct MlxSrc {  // reference layout: w [E, out, in/8] (column c at nibble c), s
 };
 
 template <class Src>
-__device__ __forceinline__ void block_dot(const Src& src, int e, int rt, int kt, const float (&xr)[32], int lane,
-                                          float (&acc)[8]) {
+__device__ __forceinline__ void block_dot(const Src& src, int e, int rt, int kt, const float (&xr)[32], float xsum,
+                                          int lane, float (&acc)[8]) {
     uint4 q[8];
     float sc[8], bi[8];
     src.load(e, rt, kt, lane, q, sc, bi);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const uint32_t ws[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
-        float a = acc[i];
+        float f = 0.0f;  // sum_j (1 + q_j/16) x_j over the lane's 32 columns
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
             for (int j = 0; j < 8; ++j)  // nibble j holds column j (MLX) or nib_col(j) (tiled)
-                a = __fmaf_rn(__fmaf_rn(nib_f(ws[c], j), sc[i], bi[i]), xr[c * 8 + (Src::kNatural ? j : nib_col(j))],
-                              a);
-        acc[i] = a;
+                f = __fmaf_rn(nib_f16th(ws[c], j), xr[c * 8 + (Src::kNatural ? j : nib_col(j))], f);
+        // s * sum q x + b * sum x, with sum q x = 16 (f - sum x)
+        acc[i] = __fmaf_rn(16.0f * sc[i], f - xsum, __fmaf_rn(bi[i], xsum, acc[i]));
     }
 }
 
-__device__ __forceinline__ void load_x32(const uint16_t* __restrict__ x, float (&xr)[32]) {
+__device__ __forceinline__ float load_x32(const uint16_t* __restrict__ x, float (&xr)[32]) {
     const uint4* p = reinterpret_cast<const uint4*>(x);
+    float sum = 0.0f;
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
         uint4 q = __ldg(p + v);
@@ -90,8 +96,10 @@ __device__ __forceinline__ void load_x32(const uint16_t* __restrict__ x, float (
         for (int c = 0; c < 4; ++c) {
             xr[v * 8 + 2 * c] = __uint_as_float(qs[c] << 16);
             xr[v * 8 + 2 * c + 1] = __uint_as_float(qs[c] & 0xFFFF0000u);
+            sum += xr[v * 8 + 2 * c] + xr[v * 8 + 2 * c + 1];
         }
     }
+    return sum;
 }
 
 // An out-of-range expert id is reported and replaced by 0, so every CTA still
@@ -103,7 +111,7 @@ __device__ __forceinline__ int checked_expert(int e, int E, int* err) {
 }
 
 // grid (I/128, kSplitGU, T*K), 256 threads.  warp w: projection w & 1,
-// k-tiles kt0 + (w >> 1) + 4 j.
+// k-tiles kt0 + (w >> 1) + 4 j (one block per warp for H = 2048).
 template <class Src>
 __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const uint16_t* __restrict__ x,
                                                        const int32_t* __restrict__ ids, int H, int I, int K, int E,
@@ -119,8 +127,8 @@ __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const
     for (int j = (w >> 1); j < nkt; j += 4) {
         const int kt = ks * nkt + j;
         float xr[32];
-        load_x32(x + (size_t)t * H + kt * kGroup + (lane & 1) * 32, xr);
-        block_dot(proj ? usrc : gsrc, e, rt, kt, xr, lane, acc);
+        const float xs = load_x32(x + (size_t)t * H + kt * kGroup + (lane & 1) * 32, xr);
+        block_dot(proj ? usrc : gsrc, e, rt, kt, xr, xs, lane, acc);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -155,24 +163,24 @@ __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const
     }
 }
 
-// grid (H/128, K, T), 256 threads.  warp w: k-tiles w, w+8, ...
+// grid (H/128, K, T), 32 * min(I/64, 16) threads.  warp w: k-tiles w, w + nwarps, ...
 template <class Src>
-__global__ void __launch_bounds__(256) k_decode_down(Src dsrc, const int32_t* __restrict__ ids,
+__global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __restrict__ ids,
                                                      const float* __restrict__ wts,
                                                      const uint16_t* __restrict__ residual, int H, int I, int K,
                                                      int E, DecodeBufs d, uint16_t* __restrict__ out,
                                                      int do_combine) {
-    __shared__ float s_part[8][kRowTile];
+    __shared__ float s_part[16][kRowTile];
     __shared__ int s_last;
     const int rt = blockIdx.x, k = blockIdx.y, t = blockIdx.z;
-    const int n_rt = gridDim.x, KT = I / kGroup;
+    const int n_rt = gridDim.x, KT = I / kGroup, nwarps = blockDim.x >> 5;
     const int p = t * K + k, e = checked_expert(ids[p], E, d.err);
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int kt = w; kt < KT; kt += 8) {
+    for (int kt = w; kt < KT; kt += nwarps) {
         float xr[32];
-        load_x32(d.h + (size_t)p * I + kt * kGroup + (lane & 1) * 32, xr);
-        block_dot(dsrc, e, rt, kt, xr, lane, acc);
+        const float xs = load_x32(d.h + (size_t)p * I + kt * kGroup + (lane & 1) * 32, xr);
+        block_dot(dsrc, e, rt, kt, xr, xs, lane, acc);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -182,8 +190,7 @@ __global__ void __launch_bounds__(256) k_decode_down(Src dsrc, const int32_t* __
     __syncthreads();
     if (tid < kRowTile) {
         float v = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v += s_part[j][tid];
+        for (int j = 0; j < nwarps; ++j) v += s_part[j][tid];
         d.y[(size_t)p * H + rt * kRowTile + tid] = f2bf(v);
     }
     if (!do_combine) return;
@@ -210,6 +217,8 @@ __global__ void __launch_bounds__(256) k_decode_down(Src dsrc, const int32_t* __
     }
 }
 
+int down_threads(int I) { return 32 * (I / kGroup < 16 ? I / kGroup : 16); }
+
 }  // namespace
 
 cudaError_t launch_decode_gateup(const LayerDev& L, const Shape& sh, const uint16_t* x, const int32_t* ids, int T,
@@ -227,7 +236,8 @@ cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t
     if (T <= 0) return cudaSuccess;
     const TiledSrc dn{L.down, sh.H / kRowTile, sh.I / kGroup, 1, 0};
     dim3 grid(sh.H / kRowTile, sh.K, T);
-    k_decode_down<TiledSrc><<<grid, 256, 0, st>>>(dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, do_combine);
+    k_decode_down<TiledSrc><<<grid, down_threads(sh.I), 0, st>>>(dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out,
+                                                                 do_combine);
     return cudaGetLastError();
 }
 
@@ -243,7 +253,7 @@ cudaError_t launch_decode_ffn_mlx(const uint32_t* gw, const uint16_t* gs, const 
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     dim3 g2(sh.H / kRowTile, sh.K, T);
-    k_decode_down<MlxSrc><<<g2, 256, 0, st>>>(dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, 1);
+    k_decode_down<MlxSrc><<<g2, down_threads(sh.I), 0, st>>>(dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, 1);
     return cudaGetLastError();
 }
 

@@ -189,7 +189,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->disp.xp, (size_t)ctx->R_cap * s.H * 2},
         {(void**)&ctx->hbuf, (size_t)ctx->R_cap * s.I * 2},
         {(void**)&ctx->ybuf, (size_t)ctx->R_cap * s.H * 2},
-        {(void**)&ctx->dec.part, (size_t)DT * K * (s.I / kRowTile) * 4 * 2 * kRowTile * 4},
+        {(void**)&ctx->dec.part, (size_t)DT * K * (s.I / kRowTile) * kDecodeSplit * 2 * kRowTile * 4},
         {(void**)&ctx->dec.cnt_gu, (size_t)DT * K * (s.I / kRowTile) * 4},
         {(void**)&ctx->dec.h, (size_t)DT * K * s.I * 2},
         {(void**)&ctx->dec.y, (size_t)DT * K * s.H * 2},

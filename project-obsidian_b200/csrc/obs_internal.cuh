@@ -70,8 +70,9 @@ cudaError_t launch_histogram(const int32_t* ids, int n, int E, int32_t* counts, 
 cudaError_t launch_tile_rows(const uint16_t* x, int n, int cols, int atoms, uint16_t* dst, cudaStream_t st);
 
 // --------------------------------------------------------------- k_decode.cu
+constexpr int kDecodeSplit = 8;  // k-splits of the decode gate/up mat-vec
 struct DecodeBufs {
-    float* part;        // [T*K][n_rt_gu][KSPLIT][2][128] gate/up partials
+    float* part;        // [T*K][n_rt_gu][kDecodeSplit][2][128] gate/up partials
     uint32_t* cnt_gu;   // [T*K][n_rt_gu]
     uint16_t* h;        // [T*K][I] bf16
     uint16_t* y;        // [T*K][H] bf16

@@ -28,7 +28,7 @@ void set_thread_error(const char* msg);
 
 namespace {
 // scratch layout for the largest allowed call (OBS_STATIC_MAX_*)
-constexpr size_t kPartBytes = (size_t)OBS_STATIC_MAX_PAIRS * (OBS_STATIC_MAX_INTER / 128) * 4 * 2 * 128 * 4;
+constexpr size_t kPartBytes = (size_t)OBS_STATIC_MAX_PAIRS * (OBS_STATIC_MAX_INTER / 128) * obs::kDecodeSplit * 2 * 128 * 4;
 constexpr size_t kCntGuBytes = (size_t)OBS_STATIC_MAX_PAIRS * (OBS_STATIC_MAX_INTER / 128) * 4;
 constexpr size_t kCntDnBytes = (size_t)OBS_STATIC_MAX_PAIRS * (OBS_STATIC_MAX_HIDDEN / 128) * 4;
 constexpr size_t kErrBytes = 256;
@@ -42,7 +42,7 @@ constexpr size_t kZeroBytes = kOffErr + kErrBytes;
 constexpr size_t kOffPart = (kZeroBytes + 255) / 256 * 256;
 constexpr size_t kOffH = kOffPart + kPartBytes;
 constexpr size_t kOffY = kOffH + kHBytes;
-constexpr size_t kScratchBytes = kOffY + kYBytes;  // about 3.7 MB
+constexpr size_t kScratchBytes = kOffY + kYBytes;  // about 7 MB
 constexpr int kMaxDevices = 64;
 
 std::mutex g_mu;
@@ -84,8 +84,8 @@ extern "C" int obs_decode_ffn_static(const obs_layer_weights* w, int n_experts, 
         return fail(OBS_ERR_INVALID, "obs_decode_ffn_static: bad T, top_k or n_experts");
     if ((long)T * top_k > OBS_STATIC_MAX_PAIRS)
         return fail(OBS_ERR_INVALID, "obs_decode_ffn_static: T * top_k above OBS_STATIC_MAX_PAIRS (64)");
-    if (hidden <= 0 || hidden > OBS_STATIC_MAX_HIDDEN || hidden % 256)
-        return fail(OBS_ERR_INVALID, "obs_decode_ffn_static: hidden must be a multiple of 256, at most 4096");
+    if (hidden <= 0 || hidden > OBS_STATIC_MAX_HIDDEN || hidden % 512)
+        return fail(OBS_ERR_INVALID, "obs_decode_ffn_static: hidden must be a multiple of 512, at most 4096");
     if (inter <= 0 || inter > OBS_STATIC_MAX_INTER || inter % 128)
         return fail(OBS_ERR_INVALID, "obs_decode_ffn_static: inter must be a multiple of 128, at most 1536");
     if (T == 0) return OBS_OK;
