@@ -5,26 +5,30 @@
 // per-expert calls :219-222) and the ew_swiglu between them (ops.metal:18-22).
 //
 // One persistent CTA per SM walks work items (token tile of <= 64 rows, weight
-// row tile of 128 rows), sixteen warps in five roles:
+// row tile of 128 rows), seventeen warps in five roles:
 //   warp 0      weight producer: 1-D bulk async copies of the packed weight
 //               block(s) (4608 B each, contiguous by construction of the HBM
 //               layout) into a deep shared-memory ring (W);
-//   warps 1-2   token-tile producer into the B ring: for gate/up, rows of the
-//               layer input gathered by source token with 16-byte cp.async
-//               into the 128-byte-swizzled K-major slots (zero fill for padding
-//               rows), each thread's completion arriving on the stage's full
-//               barrier; for down, bulk copies of the tiled H rows;
-//   warps 4-11  dequantise a W stage (released as soon as it is read) straight
+//   warps 1-2   token-tile producer into the B ring (eight k-steps deep): for
+//               gate/up, rows of the layer input gathered by source token with
+//               16-byte cp.async (L2 evict-last) into the 128-byte-swizzled
+//               K-major slots (zero fill for padding rows), each thread's
+//               completion arriving on the stage's full barrier; for down,
+//               bulk copies of the tiled H rows;
+//   warps 3-4   MMA issuers (one thread each): tcgen05.mma kind::f16 with A in
+//               TMEM and B in shared memory, M = 128 weight rows, N = token
+//               rows, K = 16, fp32 accumulators in TMEM.  Issuer 0 owns the
+//               gate chain (or the even k-slices), issuer 1 the up chain (odd
+//               k-slices); two accumulator buffers let the epilogue overlap the
+//               next item.  A stage and its B stage are free once both issuers'
+//               commits of that k-step have arrived;
+//   warps 5-12  dequantise a W stage (released as soon as it is read) straight
 //               into tensor memory: two codes per bf16x2 register,
 //               q = (0x4300 | n) - 128, w = fma.rn.bf16x2(q, s, b) (the correctly
 //               rounded bf16 of q*s + b), written with tcgen05.st into an A stage
-//               of TMEM (one weight row per TMEM lane); each warp owns the TMEM
-//               lane quarter it may access;
-//   warp 3      MMA issuer (one thread): tcgen05.mma kind::f16 with A in TMEM and
-//               B in shared memory, M = 128 weight rows, N = token rows, K = 16,
-//               fp32 accumulators in TMEM, two accumulator buffers so the
-//               epilogue overlaps the next item;
-//   warps 12-15 epilogue: tcgen05.ld, SwiGLU (or plain), results staged in
+//               of TMEM (one weight row per TMEM lane, four A stages); each warp
+//               owns the TMEM lane quarter it may access;
+//   warps 13-16 epilogue: tcgen05.ld, SwiGLU (or plain), results staged in
 //               shared memory in the global layout and written back with bulk
 //               copies (fp32 debug output: direct stores).
 // Keeping A out of shared memory leaves shared-memory bandwidth to the weight
@@ -39,20 +43,33 @@ namespace obs {
 namespace {
 
 constexpr int kBN = 64;  // token rows per tile (tcgen05 N <= 64 here)
-constexpr int kDqWarps = 16, kEpWarps = 4;
-constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 3, kWarpDq = 4, kWarpEp = kWarpDq + kDqWarps;
-constexpr int kThreads = 32 * (kWarpEp + kEpWarps);  // 768
+constexpr int kDqWarps = 8, kEpWarps = 4;
+// two MMA issuers in two warps: one thread issues a tcgen05.mma about every 50
+// cycles, and every other instruction it runs between MMAs (a barrier wait, a
+// branch) leaves the tensor pipe idle; two issuers feeding independent
+// accumulators keep it busy (M=128, N=64, K=16 every ~32 cycles)
+constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 3, kMmaWarps = 2, kWarpDq = kWarpMma + kMmaWarps,
+              kWarpEp = kWarpDq + kDqWarps;
+constexpr int kThreads = 32 * (kWarpEp + kEpWarps);  // 544
 constexpr int kEpThreads = 32 * kEpWarps;
 
 template <int EPI>
 struct Cfg {
     static constexpr bool GATHER = EPI == kEpiSwiglu;    // token tile gathered from x rows
     static constexpr int NP = EPI == kEpiSwiglu ? 2 : 1;  // projections per tile (gate, up)
-    static constexpr int W_STAGE = NP * kBlockBytes;      // packed weights (16-byte multiple)
-    static constexpr int SW = EPI == kEpiSwiglu ? 12 : 24;
+    static constexpr int W_STAGE = NP * kBlockBytes;      // packed weights of one k-step (16-byte multiple)
+    // W ring: chunks of a.wchunk consecutive k-steps, one bulk copy each (a lone
+    // producer thread issues roughly one copy per 0.3 us, so small copies cap
+    // the weight stream well below HBM bandwidth); W_BYTES / (chunk bytes) stages
+    static constexpr int W_BYTES = 6 * 4 * kBlockBytes;   // 110592
+    static constexpr int SW = W_BYTES / kBlockBytes;      // barrier slots for the smallest chunk
     static constexpr int B_STAGE = kBN * 128;
     static constexpr int SA = 4;                          // A stages in TMEM
-    static constexpr int SB = SA;                         // B stages advance with A: one "stage free" commit
+    // B stages: twice as deep as A, so the token-tile latency (a gather from L2)
+    // is hidden behind eight k-steps.  One commit per k-step, to the B stage's
+    // "free" barrier, also frees the A stage of that k-step; a dequant warp
+    // reusing A stage (i mod SA) waits for the commit of k-step i - SA.
+    static constexpr int SB = 2 * SA;
     // accumulators per buffer: gate + up, or (single projection) even + odd k-slices,
     // so consecutive MMAs always target independent accumulators
     static constexpr int ACC_COLS = 2 * kBN;              // one accumulator buffer (fp32 columns)
@@ -64,8 +81,8 @@ struct Cfg {
     static constexpr int B_OFF = 0;                       // 1024-aligned tiles first
     static constexpr int STG_OFF = B_OFF + SB * B_STAGE;
     static constexpr int W_OFF = STG_OFF + 2 * STG;
-    static constexpr int BAR_OFF = (W_OFF + SW * W_STAGE + 7) / 8 * 8;
-    static constexpr int N_BARS = 2 * SW + 2 * SB + 2 * SA + 4;  // (aempty unused: empty_b frees both)
+    static constexpr int BAR_OFF = (W_OFF + W_BYTES + 7) / 8 * 8;
+    static constexpr int N_BARS = 2 * SW + 2 * SB + 2 * SA + 4;  // (aempty unused: empty_b frees A too)
     static constexpr int SMEM = BAR_OFF + N_BARS * 8 + 32 + 1024;  // + alignment slack
 };
 static_assert(Cfg<kEpiSwiglu>::SMEM <= 232448, "smem");
@@ -88,8 +105,10 @@ __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t s2, uint32_t b
     for (int j = 0; j < 4; ++j) out[j] = bf2_fma(bf2_sub(((w >> (4 * j)) & 0x000F000Fu) | magic, magic), s2, b2);
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(dst), "l"(src),
+                 "r"(src_bytes), "l"(policy)
+                 : "memory");
 }
 // the mbarrier receives one arrival when all prior cp.async of this thread complete
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
@@ -114,11 +133,15 @@ __device__ __forceinline__ void drain_ring(uint32_t bar0, int stages, int issued
     }
 }
 
+// Pipeline trace (CTA 0 only), compiled into the TRACE instances alone: the
+// branch costs the MMA issuer tensor-pipe time.
+template <bool TRACE>
 __device__ __forceinline__ void trace_at(const GemmArgs& a, int role, int i) {
-    if (a.trace && blockIdx.x == 0 && i < a.trace_n) a.trace[(size_t)role * a.trace_n + i] = global_ns();
+    if constexpr (TRACE)
+        if (blockIdx.x == 0 && i < a.trace_n) a.trace[(size_t)role * a.trace_n + i] = global_ns();
 }
 
-template <int EPI>
+template <int EPI, bool TRACE>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     using C = Cfg<EPI>;
     extern __shared__ uint8_t smem_raw[];
@@ -140,9 +163,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < C::SW; ++s) mbar_init(full_w(s), 1), mbar_init(empty_w(s), kDqWarps);
-        for (int s = 0; s < C::SB; ++s) mbar_init(full_b(s), C::GATHER ? 64 : 1), mbar_init(empty_b(s), 1);
+        // "stage free" and "accumulator full" complete on one commit from each issuer
+        for (int s = 0; s < C::SB; ++s) mbar_init(full_b(s), C::GATHER ? 64 : 1), mbar_init(empty_b(s), kMmaWarps);
         for (int s = 0; s < C::SA; ++s) mbar_init(aready(s), kDqWarps), mbar_init(aempty(s), 1);
-        for (int b = 0; b < 2; ++b) mbar_init(accfull(b), 1), mbar_init(accempty(b), kEpThreads);
+        for (int b = 0; b < 2; ++b) mbar_init(accfull(b), kMmaWarps), mbar_init(accempty(b), kEpThreads);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -157,33 +181,40 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     const int n_items = *a.n_tiles * a.n_rt;
     const int KT = a.n_kt;
 
+    const int wch = a.wchunk;                         // k-steps per weight copy
+    const uint32_t wcbytes = (uint32_t)wch * C::W_STAGE;
+    const int nsw = C::W_BYTES / (int)wcbytes;        // W ring stages
+
     if (warp == kWarpW) {
         // ---------------------------------------------- weight producer (bulk)
-        if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
-            int s = 0, ph = 0, issued = 0;
-            for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
-                const int4 tl = a.tiles[item / a.n_rt];
-                const int rt = item % a.n_rt;
-                const uint8_t* wsrc =
-                    a.wblocks + (((size_t)tl.x * a.n_rt + rt) * KT * a.wstride + a.woff) * kBlockBytes;
-                for (int kt = 0; kt < KT; ++kt) {
-                    if (!mbar_wait(empty_w(s), ph ^ 1, abort_flag)) break;
-                    mbar_arrive_expect_tx(full_w(s), C::W_STAGE);
-                    bulk_g2s_hint(sbase + C::W_OFF + s * C::W_STAGE, wsrc + (size_t)kt * a.wstride * kBlockBytes,
-                                  C::W_STAGE, full_w(s), pol);
-                    trace_at(a, kTrWIssue, issued);
-                    ++issued;
-                    if (++s == C::SW) s = 0, ph ^= 1;
+        // the whole warp runs the loop, one elected lane issues
+        const uint64_t pol = policy_evict_first();
+        int s = 0, ph = 0, issued = 0;
+        for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
+            const int4 tl = a.tiles[item / a.n_rt];
+            const int rt = item % a.n_rt;
+            const uint8_t* wsrc =
+                a.wblocks + (((size_t)tl.x * a.n_rt + rt) * KT * a.wstride + a.woff) * kBlockBytes;
+            for (int kt = 0; kt < KT; kt += wch) {
+                if (!wait_all(empty_w(s), ph ^ 1, abort_flag)) break;
+                if (elect_one()) {
+                    mbar_arrive_expect_tx(full_w(s), wcbytes);
+                    bulk_g2s_hint(sbase + C::W_OFF + s * wcbytes, wsrc + (size_t)kt * a.wstride * kBlockBytes, wcbytes,
+                                  full_w(s), pol);
                 }
+                __syncwarp();
+                if (lane == 0) trace_at<TRACE>(a, kTrWIssue, issued);
+                ++issued;
+                if (++s == nsw) s = 0, ph ^= 1;
             }
-            if (*abort_flag) drain_ring(full_w(0), C::SW, issued);
         }
+        if (*abort_flag && lane == 0) drain_ring(full_w(0), nsw, issued);
         __syncwarp();
     } else if (warp == kWarpB || warp == kWarpB + 1) {
         // ----------------------------------------------- token-tile producer
         if constexpr (C::GATHER) {
             const int wb = warp - kWarpB, c = lane & 7, rsub = 4 * wb + (lane >> 3);
+            const uint64_t pol = policy_evict_last();  // the rows are re-read by every row tile
             int s = 0, ph = 0, step = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
@@ -201,11 +232,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                             const int j = 8 * p + rsub, t = tok[p];
                             const uint16_t* src = a.x_rows + (size_t)(t >= 0 ? t : 0) * a.x_ld + kt * kGroup + c * 8;
                             cp_async16(bst + (j >> 3) * 1024 + (j & 7) * 128 + ((c ^ (j & 7)) << 4), src,
-                                       t >= 0 ? 16u : 0u);
+                                       t >= 0 ? 16u : 0u, pol);
                         }
                     }
                     cp_async_arrive_noinc(full_b(s));
-                    if (wb == 0 && lane == 0) trace_at(a, kTrBSignal, step);
+                    if (wb == 0 && lane == 0) trace_at<TRACE>(a, kTrBSignal, step);
                     if (++s == C::SB) s = 0, ph ^= 1;
                 }
             }
@@ -222,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                     mbar_arrive_expect_tx(full_b(s), bbytes);
                     bulk_g2s_hint(sbase + C::B_OFF + s * C::B_STAGE, xsrc + (size_t)kt * a.atoms * 1024, bbytes,
                                   full_b(s), pol);
-                    trace_at(a, kTrBSignal, issued);
+                    trace_at<TRACE>(a, kTrBSignal, issued);
                     ++issued;
                     if (++s == C::SB) s = 0, ph ^= 1;
                 }
@@ -230,126 +261,131 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             if (*abort_flag) drain_ring(full_b(0), C::SB, issued);
         }
         __syncwarp();
-    } else if (warp == kWarpMma) {
-        // ---------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            int sa = 0, pha = 0, sb = 0, phb = 0, it = 0, step = 0;
-            const uint32_t a_tmem0 = tmem + C::A_TMEM;
-            const uint64_t b_desc0 = sw128_desc(sbase + C::B_OFF);
-            for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, ++it) {
-                const int4 tl = a.tiles[item / a.n_rt];
-                const uint32_t idesc = idesc_bf16(128, tl.z);
-                const int buf = it & 1;
-                if (!mbar_wait(accempty(buf), ((it >> 1) & 1) ^ 1, abort_flag)) break;
-                tc_fence_after();
-                const uint32_t dbase = tmem + buf * C::ACC_COLS;
-                bool ok = true;
-                for (int kt = 0; kt < KT; ++kt) {
-                    if (!mbar_wait(aready(sa), pha, abort_flag) || !mbar_wait(full_b(sb), phb, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    trace_at(a, kTrMmaStart, step);
-                    tc_fence_after();
-                    trace_at(a, kTrMmaFenced, step);
-                    // descriptors: plain adds on precomputed bases (the start address field
-                    // advances 16 bytes per unit; stages stay below 256 KB)
-                    const uint32_t abase = a_tmem0 + sa * C::A_COLS;
-                    const uint64_t bdesc = b_desc0 + (uint64_t)(sb * (C::B_STAGE >> 4));
-                    const uint32_t acc0 = kt != 0;
-                    if constexpr (C::NP == 2) {  // gate and up chains interleaved
-#pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-                            for (int p = 0; p < 2; ++p)
-                                tc_mma_f16_ts(dbase + p * kBN, abase + p * 32 + kk * 8, bdesc + 2 * kk, idesc,
-                                              kk == 0 ? acc0 : 1u);
-                    } else {  // even and odd k-slices into two accumulators, summed by the epilogue
-#pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            tc_mma_f16_ts(dbase + (kk & 1) * kBN, abase + kk * 8, bdesc + 2 * kk, idesc,
-                                          kk < 2 ? acc0 : 1u);
-                    }
-                    tc_commit(empty_b(sb));  // frees B stage sb and A stage sa (same index)
-                    trace_at(a, kTrMmaIssued, step++);
-                    if (++sa == C::SA) sa = 0, pha ^= 1;
-                    if (++sb == C::SB) sb = 0, phb ^= 1;
-                }
-                if (!ok) break;
-                tc_commit(accfull(buf));
-            }
-        }
-        __syncwarp();
-    } else if (warp < kWarpEp) {
-        // ------------------------------------------------------------ dequant
-        const int dw = warp - kWarpDq;           // 0..15
-        const int q = warp & 3;                  // TMEM lane quarter this warp may write
-        const int r = q * 32 + lane;             // weight row of the tile = TMEM lane
-        const int part = dw >> 2;                // 0..3: which quarter of the (projections x words) of the row
-        // gate/up: part = projection * 2 + half (4 words each); plain: part = 2-word quarter of the row
-        const int p = C::NP == 2 ? (part >> 1) : 0;
-        const int wofs = C::NP == 2 ? (part & 1) * 4 : part * 2;  // first word of this part
-        const int nw = C::NP == 2 ? 4 : 2;                       // words per part
-        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + C::A_TMEM + p * 32 + wofs * 4;
-        int sw = 0, phw = 0, sa = 0, pha = 0, step = 0, prev_sa = -1;
-        bool ok = true;
-        // step i's TMEM store is waited for (and its stage signalled ready) after
-        // step i+1 has been dequantised, so the store overlaps the next step's work
-        auto signal_prev = [&]() {
-            if (prev_sa >= 0) {
-                tc_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(aready(prev_sa));
-                if (dw == 0 && lane == 0) trace_at(a, kTrDqDone, step - 1);
-                prev_sa = -1;
-            }
-        };
-        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-            for (int kt = 0; kt < KT; ++kt, ++step) {
-                if (!wait_all(full_w(sw), phw, abort_flag) || !wait_all(empty_b(sa), pha ^ 1, abort_flag)) {
+    } else if (warp < kWarpMma + kMmaWarps) {
+        // --------------------------------------------------------- MMA issuers
+        // issuer mi: gate/up -> projection mi (its own accumulator chain);
+        // single projection -> k-slices kk = mi, mi + 2 into accumulator mi.
+        // The whole warp runs the loop (waits, descriptor arithmetic) and one
+        // elected lane issues: a loop run by lane 0 alone issues far slower.
+        const int mi = warp - kWarpMma;
+        int sa = 0, pha = 0, sb = 0, phb = 0, it = 0, step = 0;
+        const uint32_t a_tmem0 = tmem + C::A_TMEM;
+        const uint64_t b_desc0 = sw128_desc(sbase + C::B_OFF);
+        const bool tr = TRACE && mi == 0 && lane == 0;
+        for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, ++it) {
+            const int4 tl = a.tiles[item / a.n_rt];
+            const uint32_t idesc = idesc_bf16(128, tl.z);
+            const int buf = it & 1;
+            if (!wait_all(accempty(buf), ((it >> 1) & 1) ^ 1, abort_flag)) break;
+            tc_fence_after();
+            const uint32_t dbase = tmem + buf * C::ACC_COLS + mi * kBN;
+            bool ok = true;
+            for (int kt = 0; kt < KT; ++kt) {
+                if (!__all_sync(0xffffffffu, mbar_wait(aready(sa), pha, abort_flag) &&
+                                                  mbar_wait(full_b(sb), phb, abort_flag))) {
                     ok = false;
                     break;
                 }
-                if (dw == 0 && lane == 0) trace_at(a, kTrDqStart, step);
+                if (tr) trace_at<TRACE>(a, kTrMmaStart, step);
                 tc_fence_after();
-                const uint8_t* blk = smem + C::W_OFF + sw * C::W_STAGE + p * kBlockBytes;
-                const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
-                const uint32_t sv = sb[r], bv = sb[kRowTile + r];
-                // words [wofs, wofs + nw) of row r: plane wofs/4 of the block
-                const uint8_t* wp = blk + (wofs >> 2) * 2048 + r * 16 + (wofs & 3) * 4;
-                uint32_t ws[4];
-                if (nw == 4) {
-                    const uint4 w0 = *reinterpret_cast<const uint4*>(wp);
-                    ws[0] = w0.x, ws[1] = w0.y, ws[2] = w0.z, ws[3] = w0.w;
-                } else {
-                    const uint2 w0 = *reinterpret_cast<const uint2*>(wp);
-                    ws[0] = w0.x, ws[1] = w0.y, ws[2] = 0, ws[3] = 0;
+                if (tr) trace_at<TRACE>(a, kTrMmaFenced, step);
+                // descriptors: plain adds on precomputed bases (the start address field
+                // advances 16 bytes per unit; stages stay below 256 KB)
+                const uint32_t abase = a_tmem0 + sa * C::A_COLS;
+                const uint64_t bdesc = b_desc0 + (uint64_t)(sb * (C::B_STAGE >> 4));
+                const uint32_t acc0 = kt != 0;
+                if (elect_one()) {
+                    if constexpr (C::NP == 2) {  // this issuer's projection: 4 k-slices
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            tc_mma_f16_ts(dbase, abase + mi * 32 + kk * 8, bdesc + 2 * kk, idesc, kk == 0 ? acc0 : 1u);
+                    } else {  // even or odd k-slices into accumulator mi, summed by the epilogue
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk += 2)
+                            tc_mma_f16_ts(dbase, abase + (kk + mi) * 8, bdesc + 2 * (kk + mi), idesc,
+                                          kk == 0 ? acc0 : 1u);
+                    }
+                    tc_commit(empty_b(sb));  // with the other issuer's: frees B stage sb and A stage sa
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(empty_w(sw));  // packed block consumed: recycle early
-                const uint32_t s2v = sv | (sv << 16), b2v = bv | (bv << 16);
-                const uint32_t at = trow + sa * C::A_COLS;
-                if constexpr (C::NP == 2) {
-                    uint32_t v[16];
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) dequant_word(ws[c], s2v, b2v, &v[4 * c]);
-                    signal_prev();
-                    tmem_st16(at, v);
-                } else {
-                    uint32_t v[8];
-#pragma unroll
-                    for (int c = 0; c < 2; ++c) dequant_word(ws[c], s2v, b2v, &v[4 * c]);
-                    signal_prev();
-                    tmem_st8(at, v);
-                }
-                if (dw == 0 && lane == 0) trace_at(a, kTrDqStored, step);
-                prev_sa = sa;
-                if (++sw == C::SW) sw = 0, phw ^= 1;
+                if (tr) trace_at<TRACE>(a, kTrMmaIssued, step);
+                ++step;
                 if (++sa == C::SA) sa = 0, pha ^= 1;
+                if (++sb == C::SB) sb = 0, phb ^= 1;
             }
+            if (!ok) break;
+            if (elect_one()) tc_commit(accfull(buf));
+            __syncwarp();
         }
-        if (ok) signal_prev();
+    } else if (warp < kWarpEp) {
+        // ------------------------------------------------------------ dequant
+        const int dw = warp - kWarpDq;           // 0..7
+        const int q = warp & 3;                  // TMEM lane quarter this warp may write
+        const int r = q * 32 + lane;             // weight row of the tile = TMEM lane
+        const int part = dw >> 2;                // 0..1: which half of the (projections x words) of the row
+        // gate/up: part = projection (its 8 words); plain: part = half of the row's 8 words
+        const int p = C::NP == 2 ? part : 0;
+        const int wofs = C::NP == 2 ? 0 : part * 4;  // first word of this part
+        constexpr int NW = C::NP == 2 ? 8 : 4;       // words per part
+        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + C::A_TMEM + p * 32 + wofs * 4;
+        // This CTA's k-steps in order (items x k-tiles), software-pipelined per
+        // warp: the packed words of k-step i+1 are read from the W ring while
+        // the TMEM store of k-step i drains; k-step i's A stage is signalled
+        // ready as soon as its own store has completed.
+        const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+        const int total = my_items * KT;
+        uint32_t ws[NW], sv = 0, bv = 0;
+        int ls = 0, lph = 0, lj = 0;  // W ring stage, phase and k-step in chunk of the next load
+        // read the packed words (and the row's scale and bias) of k-step i; the
+        // chunk's stage is released after its last k-step has been read
+        auto load_w = [&](int i) -> bool {
+            if (lj == 0 && !wait_all(full_w(ls), lph, abort_flag)) return false;
+            if (dw == 0 && lane == 0) trace_at<TRACE>(a, kTrDqStart, i);
+            const uint8_t* blk = smem + C::W_OFF + ls * wcbytes + lj * C::W_STAGE + p * kBlockBytes;
+            const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
+            sv = sb[r];
+            bv = sb[kRowTile + r];
+            // words [wofs, wofs + NW) of row r: word w lives in plane w/4 of the block
+#pragma unroll
+            for (int pl = 0; pl < NW / 4; ++pl) {
+                const uint4 w0 = *reinterpret_cast<const uint4*>(blk + ((wofs >> 2) + pl) * 2048 + r * 16);
+                ws[4 * pl] = w0.x, ws[4 * pl + 1] = w0.y, ws[4 * pl + 2] = w0.z, ws[4 * pl + 3] = w0.w;
+            }
+            if (++lj == wch) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty_w(ls));  // chunk consumed: recycle early
+                lj = 0;
+                if (++ls == nsw) ls = 0, lph ^= 1;
+            }
+            return true;
+        };
+        bool ok = total == 0 || load_w(0);
+        for (int step = 0; step < total && ok; ++step) {
+            const int sa = step % C::SA;
+            const uint32_t s2v = sv | (sv << 16), b2v = bv | (bv << 16);
+            uint32_t v[4 * NW];
+#pragma unroll
+            for (int c = 0; c < NW; ++c) dequant_word(ws[c], s2v, b2v, &v[4 * c]);
+            // A stage sa was last read by the MMAs of k-step (step - SA)
+            const int prev = step - C::SA;
+            if (prev >= 0 && !wait_all(empty_b(prev % C::SB), (prev / C::SB) & 1, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t at = trow + sa * C::A_COLS;
+            if constexpr (NW == 8)
+                tmem_st32(at, v);
+            else
+                tmem_st16(at, v);
+            if (dw == 0 && lane == 0) trace_at<TRACE>(a, kTrDqStored, step);
+            if (step + 1 < total && !load_w(step + 1)) ok = false;  // overlaps the store
+            tc_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(aready(sa));
+            if (dw == 0 && lane == 0) trace_at<TRACE>(a, kTrDqDone, step);
+        }
     } else {
         // ----------------------------------------------------------- epilogue
         const int q = warp & 3;          // TMEM lane quarter of this warp
@@ -361,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const int rt = item % a.n_rt;
             const int buf = it & 1;
             if (!wait_all(accfull(buf), (it >> 1) & 1, abort_flag)) break;
-            if (et == 0) trace_at(a, kTrEpStart, it);
+            if (et == 0) trace_at<TRACE>(a, kTrEpStart, it);
             tc_fence_after();
             const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + buf * C::ACC_COLS;
             if constexpr (EPI == kEpiF32) {
@@ -426,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                                      sbase + C::STG_OFF + buf * C::STG + j * 256, 256u);
                     }
                     bulk_commit();
-                    trace_at(a, kTrEpDone, it);
+                    trace_at<TRACE>(a, kTrEpDone, it);
                 }
             }
         }
@@ -447,11 +483,22 @@ size_t gemm_smem_bytes(int epi) {
 int gemm_tile_rows() { return kBN; }
 
 template <int EPI>
-static cudaError_t launch_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
-    const int smem = Cfg<EPI>::SMEM;
-    cudaError_t err = cudaFuncSetAttribute(k_gemm<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+static cudaError_t launch_t(GemmArgs a, int num_sms, cudaStream_t st) {
+    using C = Cfg<EPI>;
+    // k-steps per weight copy: consecutive k-steps are contiguous when the
+    // array holds exactly this kernel's projections; up to 18 KB per copy
+    a.wchunk = 1;
+    if (a.wstride == C::NP)
+        for (int ch = 4; ch > 1; ch >>= 1)
+            if (a.n_kt % ch == 0 && ch * C::W_STAGE <= C::W_BYTES / 6) {
+                a.wchunk = ch;
+                break;
+            }
+    const int smem = C::SMEM;
+    auto kern = a.trace ? k_gemm<EPI, true> : k_gemm<EPI, false>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return err;
-    k_gemm<EPI><<<num_sms, kThreads, smem, st>>>(a);
+    kern<<<num_sms, kThreads, smem, st>>>(a);
     return cudaGetLastError();
 }
 

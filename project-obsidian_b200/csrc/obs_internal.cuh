@@ -90,6 +90,7 @@ enum GemmEpi : int { kEpiSwiglu = 0, kEpiBf16 = 1, kEpiF32 = 2 };
 struct GemmArgs {
     const uint8_t* wblocks;   // tiled weight blocks of the projection(s)
     int wstride;              // blocks per k-tile step (2 for the gate/up array, 1 for down)
+    int wchunk;               // k-steps per weight copy (set by launch_gemm)
     int woff;                 // block offset inside a step (0 gate, 1 up)
     const uint16_t* act;      // tiled activations (B operand) for the bulk-copy form
     int atoms;                // row atoms of the activation layout
