@@ -16,10 +16,9 @@ constexpr int kDispThreads = 512;
 __device__ __forceinline__ int pad_rows(int c) { return (c + kSegAlign - 1) / kSegAlign * kSegAlign; }
 
 // grid = E; CTA e computes its segment, the stable slot order of its tokens,
-// its GEMM token tiles, and copies its rows into the tiled activation layout.
-__global__ void __launch_bounds__(kDispThreads) k_dispatch(const int32_t* __restrict__ ids,
-                                                           const uint16_t* __restrict__ x, int T, int H, int E,
-                                                           int K, DispatchBufs d, int permute) {
+// and its GEMM token tiles.
+__global__ void __launch_bounds__(kDispThreads) k_dispatch(const int32_t* __restrict__ ids, int T, int E, int K,
+                                                           DispatchBufs d) {
     __shared__ int s_red[2][kDispThreads / 32];
     __shared__ int s_warp[kDispThreads / 32];
     __shared__ int s_base;
@@ -79,29 +78,31 @@ __global__ void __launch_bounds__(kDispThreads) k_dispatch(const int32_t* __rest
         d.seg[E] = seg + P;
     }
     if (tid == 0) d.seg[e] = seg;
-    if (!permute) return;
-    __syncthreads();  // d.src of this segment written above by this CTA
+}
 
-    // copy rows into the tiled layout: 16-byte chunks, 8 loads in flight per thread
+// The routed rows (slot order) into the tiled activation layout the grouped
+// GEMM reads with bulk copies: one warp per slot row, 16-byte chunks (coalesced
+// 512-byte reads of the source row, 128-byte runs per k-group in the
+// destination); padding rows (src = -1) are written as zeros.
+__global__ void __launch_bounds__(256) k_permute(const uint16_t* __restrict__ x, int H, const int32_t* __restrict__ src,
+                                                 const int32_t* __restrict__ seg_end, int atoms,
+                                                 uint16_t* __restrict__ xp) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= *seg_end) return;
+    const int t = src[row];
     const int chunks = H / 8;
-    const size_t total = (size_t)P * chunks;
-    for (size_t i0 = tid; i0 < total; i0 += (size_t)kDispThreads * 8) {
-        uint4 v[8];
+    for (int c0 = lane; c0 < chunks; c0 += 32 * 4) {
+        uint4 v[4];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            size_t i = i0 + (size_t)u * kDispThreads;
+        for (int u = 0; u < 4; ++u) {
+            const int c = c0 + 32 * u;
             v[u] = make_uint4(0, 0, 0, 0);
-            if (i < total) {
-                int t = d.src[seg + (int)(i / chunks)];
-                if (t >= 0) v[u] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + (i % chunks) * 8));
-            }
+            if (t >= 0 && c < chunks) v[u] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H) + c);
         }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            size_t i = i0 + (size_t)u * kDispThreads;
-            if (i < total)
-                *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(d.xp) +
-                                          tiled_off(seg + (int)(i / chunks), (int)(i % chunks) * 8, d.atoms)) = v[u];
+        for (int u = 0; u < 4; ++u) {
+            const int c = c0 + 32 * u;
+            if (c < chunks) *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(xp) + tiled_off(row, c * 8, atoms)) = v[u];
         }
     }
 }
@@ -172,7 +173,11 @@ __global__ void k_tile_rows(const uint16_t* __restrict__ x, int n, int cols, int
 
 cudaError_t launch_dispatch(const int32_t* ids, const uint16_t* x, int T, const Shape& sh, const DispatchBufs& d,
                             int permute, cudaStream_t st) {
-    k_dispatch<<<sh.E, kDispThreads, 0, st>>>(ids, x, T, sh.H, sh.E, sh.K, d, permute);
+    k_dispatch<<<sh.E, kDispThreads, 0, st>>>(ids, T, sh.E, sh.K, d);
+    if (!permute) return cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    k_permute<<<d.atoms, 256, 0, st>>>(x, sh.H, d.src, d.seg + sh.E, d.atoms, d.xp);  // 8 rows per CTA
     return cudaGetLastError();
 }
 

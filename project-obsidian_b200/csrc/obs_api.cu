@@ -396,9 +396,8 @@ static GemmArgs gemm_gateup(obs_ctx* ctx, const LayerDev& L, const uint16_t* x) 
     g.wblocks = L.gateup;
     g.wstride = 2;
     g.woff = 0;
-    g.x_rows = x;
-    g.src = ctx->disp.src;
-    g.x_ld = s.H;
+    g.act = ctx->disp.xp;  // the routed rows, permuted and tiled by the dispatch
+    g.atoms = ctx->disp.atoms;
     g.tiles = ctx->disp.tiles;
     g.n_tiles = ctx->disp.n_tiles;
     g.n_rt = s.I / kRowTile;
@@ -458,7 +457,7 @@ extern "C" int obs_expert_ffn(obs_ctx* ctx, int layer, const uint16_t* x, const 
         return OBS_OK;
     }
     if (path != OBS_PATH_PREFILL) return fail(ctx, OBS_ERR_INVALID, "path must be DECODE or PREFILL");
-    rc = dispatch_from_ids(ctx, ids, x, T, 0, st);
+    rc = dispatch_from_ids(ctx, ids, x, T, 1, st);
     if (rc) return rc;
     rc = prefill_ffn(ctx, L, x, st);
     if (rc) return rc;
@@ -545,7 +544,7 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
        "topk");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_DISPATCH, st);
-    CU(launch_dispatch(ctx->ids, x, T, s, ctx->disp, 0, st), "dispatch");
+    CU(launch_dispatch(ctx->ids, x, T, s, ctx->disp, 1, st), "dispatch");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_GEMM_GATEUP, st);
     CU(launch_gemm(gemm_gateup(ctx, L, x), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");

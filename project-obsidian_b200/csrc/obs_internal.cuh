@@ -90,13 +90,9 @@ enum GemmEpi : int { kEpiSwiglu = 0, kEpiBf16 = 1, kEpiF32 = 2 };
 struct GemmArgs {
     const uint8_t* wblocks;   // tiled weight blocks of the projection(s)
     int wstride;              // blocks per k-tile step (2 for the gate/up array, 1 for down)
-    int wchunk;               // k-steps per weight copy (set by launch_gemm)
     int woff;                 // block offset inside a step (0 gate, 1 up)
-    const uint16_t* act;      // tiled activations (B operand) for the bulk-copy form
+    const uint16_t* act;      // tiled activations (B operand): 8-row atoms of 1024 B per k-group
     int atoms;                // row atoms of the activation layout
-    const uint16_t* x_rows;   // kEpiSwiglu: the layer input [T, x_ld] bf16, gathered by row
-    const int32_t* src;       // kEpiSwiglu: source token of each slot (-1: padding row)
-    int x_ld;
     const int4* tiles;        // token tiles {expert, row0, nrows, 0}
     const int32_t* n_tiles;   // device count of token tiles
     int n_rt;                 // weight row tiles per expert
