@@ -9,7 +9,7 @@
 // steps of two k-groups (K = 128): every role synchronises once per step, so
 // the fixed cost of its barrier waits, fences and TMEM-store waits (each a few
 // hundred cycles on a busy SM) is spread over twice the work of one group.
-// Sixteen warps in five roles:
+// Twenty-four warps in five roles:
 //   warp 0      weight producer: 1-D bulk async copies of the packed weight
 //               blocks of one step (18 KB gate/up, 9 KB down; contiguous by
 //               construction of the HBM layout) into a shared-memory ring (W);
@@ -27,14 +27,14 @@
 //               accumulator buffers let the epilogue overlap the next item; a
 //               step's A and B stages are free once both issuers' commits of
 //               that step have arrived;
-//   warps 4-11  dequantise a W stage (released as soon as it is read) straight
+//   warps 4-19  dequantise a W stage (released as soon as it is read) straight
 //               into tensor memory: two codes per bf16x2 register,
 //               q = (0x4300 | n) - 128, w = fma.rn.bf16x2(q, s, b) (the correctly
 //               rounded bf16 of q*s + b), written with tcgen05.st into an A stage
 //               of TMEM (one weight row per TMEM lane); each warp owns the TMEM
 //               lane quarter it may access and is software-pipelined (the next
 //               step's packed words are read while its TMEM store drains);
-//   warps 12-15 epilogue: tcgen05.ld, SwiGLU (or plain), results staged in
+//   warps 20-23 epilogue: tcgen05.ld, SwiGLU (or plain), results staged in
 //               shared memory in the global layout and written back with bulk
 //               copies (fp32 debug output: direct stores).
 // Keeping A out of shared memory leaves shared-memory bandwidth to the weight
@@ -50,12 +50,13 @@ namespace {
 
 constexpr int kBN = 64;  // token rows per tile (tcgen05 N <= 64 here)
 constexpr int kKS = 2;   // k-groups (K = 64 each) per pipeline step
-constexpr int kDqWarps = 8, kEpWarps = 4;
-// sixteen warps, four per SM sub-partition (registers are allocated per
-// sub-partition: 4 x 32 x 128 fit its 16384)
+constexpr int kDqWarps = 16, kEpWarps = 4;
+// twenty-four warps, six per SM sub-partition (registers are allocated per
+// sub-partition: 6 x 32 x 80 fit its 16384); four dequant warps per
+// sub-partition hide each other's barrier and TMEM-store latency
 constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2, kMmaWarps = 2, kWarpDq = kWarpMma + kMmaWarps,
               kWarpEp = kWarpDq + kDqWarps;
-constexpr int kThreads = 32 * (kWarpEp + kEpWarps);  // 512
+constexpr int kThreads = 32 * (kWarpEp + kEpWarps);  // 768
 constexpr int kEpThreads = 32 * kEpWarps;
 
 template <int EPI>
@@ -150,11 +151,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < C::SW; ++s) mbar_init(full_w(s), 1), mbar_init(empty_w(s), kDqWarps);
+        // a W stage and an A stage are read / written by one group of eight dequant warps
+        for (int s = 0; s < C::SW; ++s) mbar_init(full_w(s), 1), mbar_init(empty_w(s), kDqWarps / 2);
         // "step done" (frees its B stage and its A stage) and "accumulator full"
         // complete on one commit from each issuer
         for (int s = 0; s < C::SB; ++s) mbar_init(full_b(s), 1), mbar_init(empty_b(s), kMmaWarps);
-        for (int s = 0; s < C::SA; ++s) mbar_init(aready(s), kDqWarps);
+        for (int s = 0; s < C::SA; ++s) mbar_init(aready(s), kDqWarps / 2);
         for (int b = 0; b < 2; ++b) mbar_init(accfull(b), kMmaWarps), mbar_init(accempty(b), kEpThreads);
         *abort_flag = 0;
         fence_mbar_init();
@@ -292,33 +294,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         }
     } else if (warp < kWarpEp) {
         // ------------------------------------------------------------ dequant
-        // warp dw: TMEM lane quarter q (rows 32q..32q+31) and part dw>>2: for
-        // gate/up the projection (its 8 words in each of the step's 2 k-groups),
-        // for a single projection the k-group (its 8 words)
-        constexpr int NG = C::NP == 2 ? kKS : 1;  // k-groups per warp and step
-        const int dw = warp - kWarpDq;           // 0..7
-        const int q = warp & 3;                  // TMEM lane quarter this warp may write
-        const int r = q * 32 + lane;             // weight row of the tile = TMEM lane
-        const int part = dw >> 2;
-        const int g0 = C::NP == 2 ? 0 : part;    // first k-group of the step
-        const int pj = C::NP == 2 ? part : 0;    // projection
+        // Two groups of eight warps take alternate steps (group gi the steps
+        // i = gi mod 2), so each warp's chain of waits, TMEM stores and loads
+        // spans two step periods.  Warp w of a group: TMEM lane quarter q (rows
+        // 32q..32q+31) and part p = w >> 2 of the step: gate/up -> projection p
+        // (its 8 words in each of the step's two k-groups), single projection ->
+        // k-group p (its 8 words).
+        constexpr int NGW = C::NP == 2 ? kKS : 1;  // k-groups per warp and step
+        const int dw = warp - kWarpDq;             // 0..15
+        const int gi = dw >> 3;                    // step parity of this group
+        const int q = warp & 3;                    // TMEM lane quarter this warp may write
+        const int r = q * 32 + lane;               // weight row of the tile = TMEM lane
+        const int part = (dw >> 2) & 1;
+        // packed block of (first k-group, projection) in a W stage
+        const int boff = C::NP == 2 ? part * kBlockBytes : part * C::KB;
         // A stage columns: [projection][k-group][32] (gate/up) or [k-group][32]
-        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + C::A_TMEM + part * NG * 32;
-        // This CTA's steps in order (items x steps), software-pipelined per
-        // warp: the packed words of step i+1 are read from the W ring while the
-        // TMEM store of step i drains; step i's A stage is signalled ready as
-        // soon as its own store has completed.
+        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + C::A_TMEM + part * NGW * 32;
+        const bool tr = TRACE && dw == 0 && lane == 0;
         const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
         const int total = my_items * KS;
-        uint32_t ws[8 * NG], s2v[NG], b2v[NG];
-        int ls = 0, lph = 0;  // W ring stage and phase of the next load
+        uint32_t ws[8 * NGW], s2v[NGW], b2v[NGW];
         // read the packed words (and the row's scales and biases) of step i, release the W stage
         auto load_w = [&](int i) -> bool {
-            if (!wait_all(full_w(ls), lph, abort_flag)) return false;
-            if (dw == 0 && lane == 0) trace_at<TRACE>(a, kTrDqStart, i);
+            const int ls = i % C::SW;
+            if (!wait_all(full_w(ls), (i / C::SW) & 1, abort_flag)) return false;
+            if (tr) trace_at<TRACE>(a, kTrDqStart, i);
 #pragma unroll
-            for (int g = 0; g < NG; ++g) {
-                const uint8_t* blk = smem + C::W_OFF + ls * C::W_STEP + (g0 + g) * C::KB + pj * kBlockBytes;
+            for (int g = 0; g < NGW; ++g) {
+                const uint8_t* blk = smem + C::W_OFF + ls * C::W_STEP + boff + g * C::KB;
                 const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
                 const uint32_t sv = sb[r], bv = sb[kRowTile + r];
                 s2v[g] = sv | (sv << 16);
@@ -333,36 +336,37 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(empty_w(ls));  // packed blocks consumed: recycle early
-            if (++ls == C::SW) ls = 0, lph ^= 1;
             return true;
         };
-        bool ok = total == 0 || load_w(0);
-        for (int step = 0; step < total && ok; ++step) {
+        bool ok = gi >= total || load_w(gi);
+        for (int step = gi; step < total && ok; step += 2) {
             const int sa = step % C::SA;
-            uint32_t v[32 * NG];
-#pragma unroll
-            for (int g = 0; g < NG; ++g)
-#pragma unroll
-                for (int c = 0; c < 8; ++c) dequant_word(ws[8 * g + c], s2v[g], b2v[g], &v[32 * g + 4 * c]);
-            // A stage sa was last read by the MMAs of step (step - SA)
-            const int prev = step - C::SA;
-            if (prev >= 0 && !wait_all(empty_b(prev % C::SB), (prev / C::SB) & 1, abort_flag)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
             const uint32_t at = trow + sa * C::A_COLS;
-            if constexpr (NG == 2)
-                tmem_st64(at, v);
-            else
-                tmem_st32(at, v);
-            if (dw == 0 && lane == 0) trace_at<TRACE>(a, kTrDqStored, step);
-            if (step + 1 < total && !load_w(step + 1)) ok = false;  // overlaps the store
+#pragma unroll
+            for (int g = 0; g < NGW; ++g) {
+                uint32_t v[32];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) dequant_word(ws[8 * g + c], s2v[g], b2v[g], &v[4 * c]);
+                if (g == 0) {
+                    // A stage sa was last read by the MMAs of step (step - SA)
+                    const int prev = step - C::SA;
+                    if (prev >= 0 && !wait_all(empty_b(prev % C::SB), (prev / C::SB) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                }
+                tmem_st32(at + g * 32, v);
+            }
+            if (!ok) break;
+            if (tr) trace_at<TRACE>(a, kTrDqStored, step);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(aready(sa));
-            if (dw == 0 && lane == 0) trace_at<TRACE>(a, kTrDqDone, step);
+            if (tr) trace_at<TRACE>(a, kTrDqDone, step);
+            // the group's next step is two steps away: its load is off the critical loop
+            if (step + 2 < total && !load_w(step + 2)) ok = false;
         }
     } else {
         // ----------------------------------------------------------- epilogue
