@@ -158,6 +158,10 @@ int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches);
  * start, 7 epilogue done, 8 dequant stores done, 9 MMA fences passed.
  * trace = NULL switches it off.  Device memory of 10 * n_steps uint64. */
 int obs_trace_enable(obs_ctx* ctx, uint64_t* trace, int n_steps);
+/* No counterpart in the reference.  *count = the number of kernel launches the
+ * library has issued in this process so far (all contexts and devices); the
+ * difference around a region is how many of the library's kernels it ran. */
+int obs_kernel_launches(uint64_t* count);
 /* Waits for the stream and reports any device-side error flag (bounded waits
  * that gave up) raised since the last check; clears the flags. */
 int obs_check_device(obs_ctx* ctx, void* stream);

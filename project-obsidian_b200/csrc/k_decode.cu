@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const
     __syncthreads();
     if (tid < kRowTile) {
         const float g = s_gu[0][tid], u = s_gu[1][tid];
-        d.h[(size_t)p * I + rt * kRowTile + tid] = f2bf((g / (1.0f + expf(-g))) * u);  // ops.metal:21
+        d.h[(size_t)p * I + rt * kRowTile + tid] = f2bf(silu_mul(g, u));
     }
 }
 
@@ -226,6 +226,7 @@ cudaError_t launch_decode_gateup(const LayerDev& L, const Shape& sh, const uint1
     if (T <= 0) return cudaSuccess;
     const TiledSrc g{L.gateup, sh.I / kRowTile, sh.H / kGroup, 2, 0}, u{L.gateup, sh.I / kRowTile, sh.H / kGroup, 2, 1};
     dim3 grid(sh.I / kRowTile, kSplitGU, T * sh.K);
+    note_launch();
     k_decode_gateup<TiledSrc><<<grid, 256, 0, st>>>(g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
     return cudaGetLastError();
 }
@@ -236,6 +237,7 @@ cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t
     if (T <= 0) return cudaSuccess;
     const TiledSrc dn{L.down, sh.H / kRowTile, sh.I / kGroup, 1, 0};
     dim3 grid(sh.H / kRowTile, sh.K, T);
+    note_launch();
     k_decode_down<TiledSrc><<<grid, down_threads(sh.I), 0, st>>>(dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out,
                                                                  do_combine);
     return cudaGetLastError();
@@ -249,10 +251,12 @@ cudaError_t launch_decode_ffn_mlx(const uint32_t* gw, const uint16_t* gs, const 
     if (T <= 0) return cudaSuccess;
     const MlxSrc g{gw, gs, gb, sh.I, sh.H}, u{uw, us, ub, sh.I, sh.H}, dn{dw, ds, db, sh.H, sh.I};
     dim3 g1(sh.I / kRowTile, kSplitGU, T * sh.K);
+    note_launch();
     k_decode_gateup<MlxSrc><<<g1, 256, 0, st>>>(g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     dim3 g2(sh.H / kRowTile, sh.K, T);
+    note_launch();
     k_decode_down<MlxSrc><<<g2, down_threads(sh.I), 0, st>>>(dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, 1);
     return cudaGetLastError();
 }

@@ -173,10 +173,12 @@ __global__ void k_tile_rows(const uint16_t* __restrict__ x, int n, int cols, int
 
 cudaError_t launch_dispatch(const int32_t* ids, const uint16_t* x, int T, const Shape& sh, const DispatchBufs& d,
                             int permute, cudaStream_t st) {
+    note_launch();
     k_dispatch<<<sh.E, kDispThreads, 0, st>>>(ids, T, sh.E, sh.K, d);
     if (!permute) return cudaGetLastError();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    note_launch();
     k_permute<<<d.atoms, 256, 0, st>>>(x, sh.H, d.src, d.seg + sh.E, d.atoms, d.xp);  // 8 rows per CTA
     return cudaGetLastError();
 }
@@ -184,12 +186,14 @@ cudaError_t launch_dispatch(const int32_t* ids, const uint16_t* x, int T, const 
 cudaError_t launch_combine(const uint16_t* y, int y_ld, const int32_t* slot_of, const float* w,
                            const uint16_t* residual, int T, int H, int K, uint16_t* out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
+    note_launch();
     k_combine<<<T, 256, 0, st>>>(y, y_ld, slot_of, w, residual, H, K, out);
     return cudaGetLastError();
 }
 
 cudaError_t launch_histogram(const int32_t* ids, int n, int E, int32_t* counts, int* err, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
+    note_launch();
     k_histogram<<<(n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024, 256, 0, st>>>(ids, n, E, counts, err);
     return cudaGetLastError();
 }
@@ -197,6 +201,7 @@ cudaError_t launch_histogram(const int32_t* ids, int n, int E, int32_t* counts, 
 cudaError_t launch_gather_rows(const uint16_t* y, const int32_t* slot_of, int rows, int H, uint16_t* out,
                                cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
+    note_launch();
     k_gather_rows<<<rows, 256, 0, st>>>(y, slot_of, H, out);
     return cudaGetLastError();
 }
@@ -204,6 +209,7 @@ cudaError_t launch_gather_rows(const uint16_t* y, const int32_t* slot_of, int ro
 cudaError_t launch_tile_rows(const uint16_t* x, int n, int cols, int atoms, uint16_t* dst, cudaStream_t st) {
     int rows = (n + kSegAlign - 1) / kSegAlign * kSegAlign;
     if (rows <= 0) return cudaSuccess;
+    note_launch();
     k_tile_rows<<<rows, 256, 0, st>>>(x, n, cols, atoms, dst);
     return cudaGetLastError();
 }

@@ -414,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                         for (int jj = 0; jj < 16; ++jj) {
                             const int j = j0 + jj;
                             const float gv = g[jj];
-                            const float hv = (gv / (1.0f + expf(-gv))) * u[jj];  // ops.metal:21
+                            const float hv = silu_mul(gv, u[jj]);
                             *reinterpret_cast<uint16_t*>(pl + (j >> 3) * 1024 + (j & 7) * 128 + (((fc >> 3) ^ (j & 7)) << 4)) =
                                 f2bf(hv);
                         }
@@ -427,24 +427,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                 }
                 tc_fence_before();
                 mbar_arrive(accempty(buf));  // accumulator drained: the next item may start
-                fence_proxy_async_smem();    // staging written by threads -> read by the bulk copy
-                named_bar_sync(1, kEpThreads);
-                if (et == 0) {
-                    if constexpr (EPI == kEpiSwiglu) {
+                if constexpr (EPI == kEpiSwiglu) {
+                    fence_proxy_async_smem();  // staging written by threads -> read by the bulk copy
+                    named_bar_sync(1, kEpThreads);
+                    if (et == 0) {
+                        // two 64-feature planes of the tiled H, each one contiguous run of the tile's atoms
                         uint8_t* hb = reinterpret_cast<uint8_t*>(a.out);
 #pragma unroll
                         for (int pln = 0; pln < 2; ++pln)
                             bulk_s2g(hb + ((size_t)(rt * 2 + pln) * a.out_atoms + (tl.y >> 3)) * 1024,
                                      sbase + C::STG_OFF + buf * C::STG + pln * (kBN * 128), (uint32_t)tl.z * 128u);
-                    } else {
-                        uint8_t* yb = reinterpret_cast<uint8_t*>(a.out);
-                        const int nstore = min(tl.z, a.row_limit - tl.y);
-                        for (int j = 0; j < nstore; ++j)
-                            bulk_s2g(yb + ((size_t)(tl.y + j) * a.out_ld + rt * kRowTile) * 2,
-                                     sbase + C::STG_OFF + buf * C::STG + j * 256, 256u);
+                        bulk_commit();
+                        trace_at<TRACE>(a, kTrEpDone, it);
                     }
-                    bulk_commit();
-                    trace_at<TRACE>(a, kTrEpDone, it);
+                } else {
+                    // row-major Y: 256 bytes per token row at a 2*out_ld stride; all
+                    // epilogue threads copy the staged rows out in 16-byte pieces
+                    named_bar_sync(1, kEpThreads);
+                    uint8_t* yb = reinterpret_cast<uint8_t*>(a.out) + ((size_t)tl.y * a.out_ld + rt * kRowTile) * 2;
+                    const int nstore = min(tl.z, a.row_limit - tl.y);
+                    for (int i = et; i < nstore * 16; i += kEpThreads) {
+                        const int j = i >> 4, c = i & 15;
+                        *reinterpret_cast<uint4*>(yb + (size_t)j * a.out_ld * 2 + c * 16) =
+                            *reinterpret_cast<const uint4*>(stg + j * 256 + c * 16);
+                    }
+                    if (et == 0) trace_at<TRACE>(a, kTrEpDone, it);
                 }
             }
         }
@@ -470,6 +477,7 @@ static cudaError_t launch_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
     auto kern = a.trace ? k_gemm<EPI, true> : k_gemm<EPI, false>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return err;
+    note_launch();
     kern<<<num_sms, kThreads, smem, st>>>(a);
     return cudaGetLastError();
 }

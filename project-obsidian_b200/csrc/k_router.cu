@@ -288,9 +288,11 @@ cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint1
     if (T <= 0) return cudaSuccess;
     if (router_parts(T) == 1) {
         dim3 grid((sh.E + 7) / 8, (T + kWarpTok - 1) / kWarpTok);
+        note_launch();
         k_router_warp<<<grid, 256, 0, st>>>(L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E, parts);
     } else {
         dim3 grid((T + kTT - 1) / kTT, (sh.E + kTE - 1) / kTE, kSplit);
+        note_launch();
         k_router_tiled<<<grid, 256, 0, st>>>(L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E, parts);
     }
     return cudaGetLastError();
@@ -299,6 +301,7 @@ cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint1
 cudaError_t launch_router_finish(const float* parts, int T, int E, float* logits, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     size_t n = (size_t)T * E;
+    note_launch();
     k_router_finish<<<(int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096), 256, 0, st>>>(parts, n, logits);
     return cudaGetLastError();
 }
@@ -307,6 +310,7 @@ cudaError_t launch_topk(const float* logits, int nparts, const float* bias, int 
                         int32_t* ids, float* w, int32_t* counts, float* logits_out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (E > kMaxE || K > kMaxK || K > 32) return cudaErrorInvalidValue;
+    note_launch();
     k_topk<<<(T + 7) / 8, 256, 0, st>>>(logits, nparts, bias, T, E, K, norm, ids, w, counts, logits_out);
     return cudaGetLastError();
 }

@@ -135,6 +135,7 @@ inline int grid_for(size_t n, int threads) {
 cudaError_t launch_synth_router(uint64_t seed, uint32_t layer, int E, int H, uint32_t* w, uint16_t* s,
                                 uint16_t* b, cudaStream_t st) {
     size_t nw = (size_t)E * (H / 4), ng = (size_t)E * (H / kGroup);
+    note_launch();
     k_synth_router<<<grid_for(nw, 256), 256, 0, st>>>(stream_key(seed, layer, T_ROUTER_W),
                                                       stream_key(seed, layer, T_ROUTER_S), nw, ng, w, s, b);
     return cudaGetLastError();
@@ -144,6 +145,7 @@ cudaError_t launch_synth_proj(uint64_t seed, uint32_t layer, int proj, int E, in
                               uint16_t* s, uint16_t* b, cudaStream_t st) {
     uint32_t tw = T_GATE_W + 3u * (uint32_t)proj;
     size_t nw = (size_t)E * out_f * (in_f / 8), ng = (size_t)E * out_f * (in_f / kGroup);
+    note_launch();
     k_synth_proj<<<grid_for(nw, 256), 256, 0, st>>>(stream_key(seed, layer, tw), stream_key(seed, layer, tw + 1),
                                                     stream_key(seed, layer, tw + 2), nw, ng, w, s, b);
     return cudaGetLastError();
@@ -152,6 +154,7 @@ cudaError_t launch_synth_proj(uint64_t seed, uint32_t layer, int proj, int E, in
 cudaError_t launch_synth_x(uint64_t seed, uint32_t layer, int row0, int T, int H, float eps, uint16_t* x,
                            cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
+    note_launch();
     k_synth_x<<<(T + 127) / 128, 128, 0, st>>>(stream_key(seed, layer, T_X), row0, T, H, eps, x);
     return cudaGetLastError();
 }
@@ -159,6 +162,7 @@ cudaError_t launch_synth_x(uint64_t seed, uint32_t layer, int row0, int T, int H
 cudaError_t launch_retile(const uint32_t* w, const uint16_t* s, const uint16_t* b, int E, int out_f, int in_f,
                           uint8_t* dst, int interleave, int p, cudaStream_t st) {
     size_t total = (size_t)E * (out_f / kRowTile) * (in_f / kGroup) * kRowTile;
+    note_launch();
     k_retile<<<grid_for(total, 256), 256, 0, st>>>(w, s, b, E, out_f, in_f, dst, interleave, p);
     return cudaGetLastError();
 }

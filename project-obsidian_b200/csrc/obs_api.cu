@@ -9,12 +9,14 @@
 // sequence of kernel launches with no host synchronisation.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <string>
 #include <vector>
 
 #include "../../include/obs_moe.h"
+
 #include "obs_internal.cuh"
 
 using namespace obs;
@@ -613,6 +615,17 @@ extern "C" int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches
         launches[m.first] += 1;
     }
     ctx->ev_marks.clear();
+    return OBS_OK;
+}
+
+namespace obs {
+static std::atomic<uint64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace obs
+
+extern "C" int obs_kernel_launches(uint64_t* count) {
+    if (!count) return OBS_ERR_INVALID;
+    *count = obs::g_launches.load(std::memory_order_relaxed);
     return OBS_OK;
 }
 

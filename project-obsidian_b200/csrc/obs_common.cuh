@@ -43,6 +43,12 @@ __device__ __forceinline__ size_t tiled_off(int row, int col, int atoms) {
     return ((size_t)kt * atoms + (row >> 3)) * 1024 + r * 128 + ((q ^ r) << 4) + ((col & 7) << 1);
 }
 
+// SwiGLU element h = silu(g) * u = g / (1 + e^-g) * u (ops.metal:18-22).  The
+// reference shader compiles with Metal's fast math; here too the exponential
+// and the division are the hardware approximations (a few fp32 ulp, far below
+// the bf16 rounding of h).
+__device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
+
 // ------------------------------------------------------------ time / waits
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;

@@ -8,6 +8,9 @@
 
 namespace obs {
 
+// Counts every kernel launch the library issues (obs_kernel_launches).
+void note_launch();
+
 // One 128-row x 64-column block of a tiled 4-bit projection (4608 bytes):
 // words 0-3 of the 128 rows, words 4-7 of the 128 rows, 128 bf16 scales,
 // 128 bf16 biases.

@@ -31,7 +31,7 @@ EXPORTS = (
     "obs_load_layer", "obs_synth_layer", "obs_synth_activations", "obs_moe_forward",
     "obs_moe_forward_host", "obs_gate", "obs_route", "obs_dispatch", "obs_expert_ffn",
     "obs_expert_gemm_f32", "obs_check_device", "obs_profile_enable", "obs_profile_read",
-    "obs_trace_enable", "obs_decode_ffn_static",
+    "obs_trace_enable", "obs_decode_ffn_static", "obs_kernel_launches",
 )
 STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down")
 
@@ -86,6 +86,7 @@ def lib() -> C.CDLL:
         L.obs_profile_enable.argtypes = [vp, i32]
         L.obs_profile_read.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(C.c_int32)]
         L.obs_trace_enable.argtypes = [vp, vp, i32]
+        L.obs_kernel_launches.argtypes = [C.POINTER(C.c_uint64)]
         L.obs_decode_ffn_static.argtypes = [C.POINTER(LayerWeights), i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp]
         for name in EXPORTS:
             if name not in ("obs_last_error", "obs_abi_version"):
@@ -229,6 +230,15 @@ def decode_ffn_static(w, n_experts, hidden, inter, top_k, x, ids, weights, T, ou
                                      _ptr(weights), _ptr(residual), T, _ptr(out), _stream(stream))
     if rc != OBS_OK:
         raise ObsError(rc, lib().obs_last_error(None).decode())
+
+
+def kernel_launches() -> int:
+    """Kernel launches the library has issued in this process (all contexts)."""
+    n = C.c_uint64(0)
+    rc = lib().obs_kernel_launches(C.byref(n))
+    if rc != OBS_OK:
+        raise ObsError(rc, "kernel_launches")
+    return int(n.value)
 
 
 def synth_activations(seed, layer, row0, T, H, x, eps=1e-6, stream=None):

@@ -324,3 +324,32 @@ def test_errors(small):
     with pytest.raises(obsmoe.ObsError, match="not loaded"):
         ctx.moe_forward(0, x, x, 1)
     ctx.close()
+
+
+@pytest.mark.parametrize("path,T", [(obsmoe.PATH_PREFILL, 100), (obsmoe.PATH_DECODE, 3)])
+def test_forward_replays_from_a_cuda_graph(small, path, T):
+    """The layer forward issues only stream-ordered work, so it can be captured
+    in a CUDA graph; replays give the eager result bit for bit and launch the
+    same kernels."""
+    torch = small.torch
+    x = dev(torch, small.x(T, row0=21))
+    eager = torch.empty((T, 2048), dtype=torch.int16, device="cuda")
+    n0 = obsmoe.kernel_launches()
+    small.ctx.moe_forward(0, x, eager, T, path=path)
+    per_forward = obsmoe.kernel_launches() - n0
+    assert per_forward >= 3
+    out = torch.full((T, 2048), -1, dtype=torch.int16, device="cuda")
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(g, stream=cap):
+            small.ctx.moe_forward(0, x, out, T, path=path, stream=cap)
+    torch.cuda.current_stream().wait_stream(cap)
+    for _ in range(2):
+        out.fill_(-1)
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+    del g
+    small.ctx.check_device()
