@@ -66,6 +66,8 @@ typedef struct obs_config {
     int32_t norm_topk;         /* renormalise the top-k weights (norm_topk_prob) */
     int32_t decode_max_tokens; /* OBS_PATH_AUTO threshold; <= 0 picks 4 */
     float rms_eps;             /* RMSNorm epsilon of the fused input norm */
+    int32_t ep_world;          /* expert parallelism: ranks sharing the experts (<= 1: off, max 8) */
+    int32_t ep_rank;           /* this context's rank: it holds experts [rank*E/world, (rank+1)*E/world) */
 } obs_config;
 
 /* One layer's weights in the reference format (host or device memory). */
@@ -165,6 +167,29 @@ int obs_kernel_launches(uint64_t* count);
 /* Waits for the stream and reports any device-side error flag (bounded waits
  * that gave up) raised since the last check; clears the flags. */
 int obs_check_device(obs_ctx* ctx, void* stream);
+
+/* ----------------------------------------------- expert parallelism (EP) */
+/* A context created with ep_world > 1 holds E/ep_world experts of each layer
+ * (obs_load_layer takes all E experts' host or device arrays and keeps its own
+ * slice; the router is replicated) and runs obs_moe_forward as expert
+ * parallelism: every rank routes its own T tokens, writes each routed row
+ * directly into the memory of the rank holding its expert (NVLink peer stores
+ * through CUDA IPC), runs the grouped GEMMs on the rows it received, writes the
+ * outputs back into the source rank's memory, and combines in rank order -- the
+ * result equals the single-GPU forward bit for bit.  Replaces the per-layer
+ * expert loop of forward.rs:164-247 when the experts span several GPUs (the
+ * reference has no multi-device path).  Setup, once per context:
+ *   obs_ep_handle(ctx, h)          this rank's buffer handle (OBS_EP_HANDLE_BYTES)
+ *   ... exchange the handles between the ranks (host side, any transport) ...
+ *   obs_ep_connect(ctx, all)       all = ep_world handles in rank order
+ * Every rank must then call obs_moe_forward for the same layers in the same
+ * order (T may differ, T = 0 included); the forward always takes the prefill
+ * (grouped GEMM) path.  Device-side waits for peers are bounded (2 s) and end
+ * in OBS_ERR_TIMEOUT from obs_check_device.  The stage entry points
+ * (obs_dispatch, obs_expert_ffn, obs_expert_gemm_f32) are single-GPU only. */
+#define OBS_EP_HANDLE_BYTES 64
+int obs_ep_handle(obs_ctx* ctx, void* handle);
+int obs_ep_connect(obs_ctx* ctx, const void* handles);
 
 /* ------------------------------------------- allocation-free decode FFN */
 /* No counterpart in the reference.  For callers that cannot allocate device

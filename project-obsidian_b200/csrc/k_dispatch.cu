@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(256) k_combine(const uint16_t* __restrict__ y,
             for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
         }
         for (int k = 0; k < K; ++k) {
-            int slot = slot_of[(size_t)t * K + k];
+            const int slot = slot_of ? slot_of[(size_t)t * K + k] : t * K + k;  // nullptr: rows in item order
             float wk = w[(size_t)t * K + k];
             uint4 v = __ldg(reinterpret_cast<const uint4*>(y + (size_t)slot * y_ld + f));
             uint32_t vs[4] = {v.x, v.y, v.z, v.w};

@@ -56,14 +56,16 @@ __global__ void k_synth_router(uint64_t kw, uint64_t ks, size_t nw, size_t ng, u
     }
 }
 
-__global__ void k_synth_proj(uint64_t kw, uint64_t ks, uint64_t kb, size_t nw, size_t ng, uint32_t* w,
-                             uint16_t* s, uint16_t* b) {
+// elements [w0, w0 + nw) / [g0, g0 + ng) of the projection's streams (a slice
+// of experts starts at its first expert's element index)
+__global__ void k_synth_proj(uint64_t kw, uint64_t ks, uint64_t kb, size_t w0, size_t nw, size_t g0, size_t ng,
+                             uint32_t* w, uint16_t* s, uint16_t* b) {
     const float lo = 0.002f, span = 0.02f - 0.002f;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < nw; i += (size_t)gridDim.x * blockDim.x)
-        w[i] = (uint32_t)stream_u64(kw, i);
+        w[i] = (uint32_t)stream_u64(kw, w0 + i);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < ng; i += (size_t)gridDim.x * blockDim.x) {
-        uint16_t sc = f2bf(__fmaf_rn(u24(stream_u64(ks, i)), span, lo));
-        float n = normal_ih(kb, i);
+        uint16_t sc = f2bf(__fmaf_rn(u24(stream_u64(ks, g0 + i)), span, lo));
+        float n = normal_ih(kb, g0 + i);
         s[i] = sc;
         b[i] = f2bf(__fmaf_rn(n, 1e-3f, __fmul_rn(-8.0f, bf2f(sc))));
     }
@@ -141,13 +143,14 @@ cudaError_t launch_synth_router(uint64_t seed, uint32_t layer, int E, int H, uin
     return cudaGetLastError();
 }
 
-cudaError_t launch_synth_proj(uint64_t seed, uint32_t layer, int proj, int E, int out_f, int in_f, uint32_t* w,
-                              uint16_t* s, uint16_t* b, cudaStream_t st) {
+cudaError_t launch_synth_proj(uint64_t seed, uint32_t layer, int proj, int e0, int E, int out_f, int in_f,
+                              uint32_t* w, uint16_t* s, uint16_t* b, cudaStream_t st) {
     uint32_t tw = T_GATE_W + 3u * (uint32_t)proj;
-    size_t nw = (size_t)E * out_f * (in_f / 8), ng = (size_t)E * out_f * (in_f / kGroup);
+    const size_t wpe = (size_t)out_f * (in_f / 8), gpe = (size_t)out_f * (in_f / kGroup);  // per expert
     note_launch();
-    k_synth_proj<<<grid_for(nw, 256), 256, 0, st>>>(stream_key(seed, layer, tw), stream_key(seed, layer, tw + 1),
-                                                    stream_key(seed, layer, tw + 2), nw, ng, w, s, b);
+    k_synth_proj<<<grid_for(E * wpe, 256), 256, 0, st>>>(stream_key(seed, layer, tw), stream_key(seed, layer, tw + 1),
+                                                         stream_key(seed, layer, tw + 2), e0 * wpe, E * wpe, e0 * gpe,
+                                                         E * gpe, w, s, b);
     return cudaGetLastError();
 }
 

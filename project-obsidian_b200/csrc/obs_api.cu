@@ -55,6 +55,12 @@ struct obs_ctx {
     int R_cap = 0, max_tiles = 0, decode_max = 4;
     uint64_t* trace = nullptr;  // obs_trace_enable
     int trace_n = 0;
+    // expert parallelism (ep_world > 1): this rank holds experts [e0, e0 + E_local)
+    int ep_world = 1, ep_rank = 0, E_local = 0, e0 = 0;
+    uint8_t* ep_buf = nullptr;  // this rank's buffer, opened by its peers through CUDA IPC
+    size_t ep_bytes = 0;
+    bool ep_connected = false;
+    EpArgs ep{};
     // optional per-stage event timing (obs_profile_enable)
     bool prof = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -110,10 +116,10 @@ namespace obs {
 void set_thread_error(const char* msg) { g_create_err = msg ? msg : ""; }
 }  // namespace obs
 
-static size_t layer_weight_bytes(const Shape& s) {
+static size_t layer_weight_bytes(const Shape& s, int E_local) {
     size_t router = align_up((size_t)s.E * s.H, 256) + 2 * align_up((size_t)s.E * (s.H / 64) * 2, 256);
-    size_t gu = (size_t)s.E * (s.I / kRowTile) * (s.H / kGroup) * 2 * kBlockBytes;
-    size_t dn = (size_t)s.E * (s.H / kRowTile) * (s.I / kGroup) * kBlockBytes;
+    size_t gu = (size_t)E_local * (s.I / kRowTile) * (s.H / kGroup) * 2 * kBlockBytes;
+    size_t dn = (size_t)E_local * (s.H / kRowTile) * (s.I / kGroup) * kBlockBytes;
     return router + align_up(gu, 256) + align_up(dn, 256);
 }
 
@@ -135,6 +141,13 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     if (s.E <= 0 || s.E > 256) return bad("n_experts must be in 1..256");
     if (s.K <= 0 || s.K > 16 || s.K > s.E) return bad("top_k must be in 1..min(16, n_experts)");
     if (cfg->n_layers <= 0 || cfg->max_tokens <= 0) return bad("n_layers and max_tokens must be positive");
+    ctx->ep_world = cfg->ep_world > 1 ? cfg->ep_world : 1;
+    ctx->ep_rank = ctx->ep_world > 1 ? cfg->ep_rank : 0;
+    if (ctx->ep_world > kMaxWorld) return bad("ep_world must be at most 8");
+    if (s.E % ctx->ep_world) return bad("n_experts must be a multiple of ep_world");
+    if (ctx->ep_rank < 0 || ctx->ep_rank >= ctx->ep_world) return bad("ep_rank must be in [0, ep_world)");
+    ctx->E_local = s.E / ctx->ep_world;
+    ctx->e0 = ctx->ep_rank * ctx->E_local;
     ctx->decode_max = cfg->decode_max_tokens > 0 ? cfg->decode_max_tokens : 4;
     if (ctx->decode_max > kDecodeMaxT) ctx->decode_max = kDecodeMaxT;
     ctx->device = device;
@@ -147,7 +160,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     }
 
     // weights for all layers
-    ctx->layer_bytes = layer_weight_bytes(s);
+    ctx->layer_bytes = layer_weight_bytes(s, ctx->E_local);
     ctx->wbytes = ctx->layer_bytes * cfg->n_layers;
     e = cudaMalloc(&ctx->wmem, ctx->wbytes);
     if (e != cudaSuccess) {
@@ -167,15 +180,16 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         L.router_b = reinterpret_cast<uint16_t*>(p);
         p += align_up((size_t)s.E * (s.H / 64) * 2, 256);
         L.gateup = p;
-        p += align_up((size_t)s.E * (s.I / kRowTile) * (s.H / kGroup) * 2 * kBlockBytes, 256);
+        p += align_up((size_t)ctx->E_local * (s.I / kRowTile) * (s.H / kGroup) * 2 * kBlockBytes, 256);
         L.down = p;
         L.loaded = false;
     }
 
     // scratch, one pool
-    const int T = cfg->max_tokens, K = s.K, E = s.E;
-    ctx->R_cap = (int)align_up((size_t)T * K + (size_t)E * (kSegAlign - 1), 128);
-    ctx->max_tiles = ctx->R_cap / kBNTile + E + 1;
+    const int T = cfg->max_tokens, K = s.K, E = s.E, W = ctx->ep_world, EL = ctx->E_local;
+    // rows the grouped GEMMs may see: every rank's routed rows for this rank's experts, padded
+    ctx->R_cap = (int)align_up((size_t)W * T * K + (size_t)EL * (kSegAlign - 1), 128);
+    ctx->max_tiles = ctx->R_cap / kBNTile + EL + 1;
     const int DT = ctx->decode_max > 0 ? kDecodeMaxT : 0;
     struct Item { void** p; size_t bytes; };
     std::vector<Item> items = {
@@ -184,7 +198,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->wts, (size_t)T * K * 4},
         {(void**)&ctx->disp.counts, (size_t)E * 4},
         {(void**)&ctx->disp.seg, (size_t)(E + 1) * 4},
-        {(void**)&ctx->disp.slot_of, (size_t)T * K * 4},
+        {(void**)&ctx->disp.slot_of, (size_t)W * T * K * 4},
         {(void**)&ctx->disp.src, (size_t)ctx->R_cap * 4},
         {(void**)&ctx->disp.tiles, (size_t)ctx->max_tiles * 16},
         {(void**)&ctx->disp.n_tiles, 16},
@@ -201,6 +215,11 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->out_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->res_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->bias_dev, (size_t)E * 4},
+        {(void**)&ctx->ep.send_cnt, (size_t)kMaxWorld * 4},
+        {(void**)&ctx->ep.done, 16},
+        {(void**)&ctx->ep.epoch, 16},
+        {(void**)&ctx->ep.ids_local, W > 1 ? (size_t)W * T * K * 4 : 0},
+        {(void**)&ctx->ep.src_item, W > 1 ? (size_t)W * T * K * 4 : 0},
     };
     size_t total = 0;
     for (auto& it : items) total += align_up(it.bytes ? it.bytes : 16, 1024);
@@ -218,6 +237,29 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         off += align_up(it.bytes ? it.bytes : 16, 1024);
     }
     ctx->dec.err = ctx->err_flag;
+    if (W > 1) {
+        // this rank's shared buffer (layout in k_ep.cu), zeroed: stamps and counts start at 0
+        EpArgs& a = ctx->ep;
+        a.world = W, a.rank = ctx->ep_rank, a.cap = T * K, a.H = s.H, a.K = K, a.E_local = EL;
+        a.counts = ctx->disp.counts;
+        a.err = ctx->err_flag;
+        size_t o = 0;
+        a.off_rx = o, o += align_up((size_t)W * a.cap * s.H * 2, 256);
+        a.off_meta = o, o += align_up((size_t)W * a.cap * 8, 256);
+        a.off_cnt = o, o += 256;
+        a.off_rflag = o, o += 256;
+        a.off_ret = o, o += align_up((size_t)a.cap * s.H * 2, 256);
+        a.off_retflag = o, o += 256;
+        ctx->ep_bytes = o;
+        e = cudaMalloc(&ctx->ep_buf, o);
+        if (e == cudaSuccess) e = cudaMemset(ctx->ep_buf, 0, o);
+        if (e != cudaSuccess) {
+            ctx->ep_buf = nullptr;
+            g_create_err = std::string("expert-parallel buffer: ") + cudaGetErrorString(e);
+            obs_destroy(ctx);
+            return OBS_ERR_NOMEM;
+        }
+    }
     ctx->disp.atoms = ctx->R_cap / 8;
     ctx->disp.bn = kBNTile;
     // counters must start at zero; the tiled buffers are zeroed so padding rows are finite
@@ -236,6 +278,10 @@ extern "C" int obs_destroy(obs_ctx* ctx) {
     if (!ctx) return OBS_OK;
     cudaSetDevice(ctx->device);
     for (auto e : ctx->ev_pool) cudaEventDestroy(e);
+    if (ctx->ep_connected)
+        for (int r = 0; r < ctx->ep_world; ++r)
+            if (r != ctx->ep_rank && ctx->ep.peer[r]) cudaIpcCloseMemHandle(ctx->ep.peer[r]);
+    if (ctx->ep_buf) cudaFree(ctx->ep_buf);
     if (ctx->wmem) cudaFree(ctx->wmem);
     if (ctx->smem_pool) cudaFree(ctx->smem_pool);
     delete ctx;
@@ -264,8 +310,9 @@ static int load_impl(obs_ctx* ctx, int layer, const obs_layer_weights* w, int on
     CU(cudaSetDevice(ctx->device), "cudaSetDevice");
     const Shape& s = ctx->sh;
     LayerDev& L = ctx->layers[layer];
-    const size_t maxw = (size_t)s.E * s.I * s.H / 8 * 4;  // one projection's words (all same size)
-    const size_t maxg = (size_t)s.E * s.I * s.H / 64 * 2;
+    const int EL = ctx->E_local, e0 = ctx->e0;  // this context's experts (all of them without EP)
+    const size_t maxw = (size_t)EL * s.I * s.H / 8 * 4;  // one projection's words (all same size)
+    const size_t maxg = (size_t)EL * s.I * s.H / 64 * 2;
     uint8_t* stage = nullptr;
     CU(cudaMalloc(&stage, maxw + 2 * maxg), "staging alloc");
     uint32_t* sw = reinterpret_cast<uint32_t*>(stage);
@@ -283,9 +330,9 @@ static int load_impl(obs_ctx* ctx, int layer, const obs_layer_weights* w, int on
     }
     for (int proj = 0; proj < 3 && e == cudaSuccess; ++proj) {
         const int out_f = proj == 2 ? s.H : s.I, in_f = proj == 2 ? s.I : s.H;
-        const size_t nw = (size_t)s.E * out_f * in_f / 8 * 4, ng = (size_t)s.E * out_f * (in_f / 64) * 2;
+        const size_t nw = (size_t)EL * out_f * in_f / 8 * 4, ng = (size_t)EL * out_f * (in_f / 64) * 2;
         if (synth) {
-            step(launch_synth_proj(seed, (uint32_t)layer, proj, s.E, out_f, in_f, sw, ss, sb, 0));
+            step(launch_synth_proj(seed, (uint32_t)layer, proj, e0, EL, out_f, in_f, sw, ss, sb, 0));
         } else {
             const uint32_t* pw = proj == 0 ? w->gate_w : proj == 1 ? w->up_w : w->down_w;
             const uint16_t* ps = proj == 0 ? w->gate_s : proj == 1 ? w->up_s : w->down_s;
@@ -294,12 +341,12 @@ static int load_impl(obs_ctx* ctx, int layer, const obs_layer_weights* w, int on
                 cudaFree(stage);
                 return fail(ctx, OBS_ERR_INVALID, "null weight pointer");
             }
-            step(cudaMemcpy(sw, pw, nw, kind));
-            step(cudaMemcpy(ss, ps, ng, kind));
-            step(cudaMemcpy(sb, pb, ng, kind));
+            step(cudaMemcpy(sw, pw + (size_t)e0 * out_f * (in_f / 8), nw, kind));
+            step(cudaMemcpy(ss, ps + (size_t)e0 * out_f * (in_f / 64), ng, kind));
+            step(cudaMemcpy(sb, pb + (size_t)e0 * out_f * (in_f / 64), ng, kind));
         }
-        if (proj < 2) step(launch_retile(sw, ss, sb, s.E, out_f, in_f, L.gateup, 2, proj, 0));
-        else step(launch_retile(sw, ss, sb, s.E, out_f, in_f, L.down, 1, 0, 0));
+        if (proj < 2) step(launch_retile(sw, ss, sb, EL, out_f, in_f, L.gateup, 2, proj, 0));
+        else step(launch_retile(sw, ss, sb, EL, out_f, in_f, L.down, 1, 0, 0));
         step(cudaDeviceSynchronize());
     }
     cudaFree(stage);
@@ -368,6 +415,7 @@ static int dispatch_from_ids(obs_ctx* ctx, const int32_t* ids, const uint16_t* x
 extern "C" int obs_dispatch(obs_ctx* ctx, const int32_t* ids, int T, int32_t* counts, int32_t* seg,
                             int32_t* slot_of, void* stream) {
     OBS_CHECK_CTX(ctx);
+    if (ctx->ep_world > 1) return fail(ctx, OBS_ERR_UNSUPPORTED, "stage entry points are single-GPU only (ep_world > 1)");
     int rc = check_T(ctx, T);
     if (rc) return rc;
     if (!ids) return fail(ctx, OBS_ERR_INVALID, "null ids");
@@ -444,6 +492,7 @@ static int prefill_ffn(obs_ctx* ctx, const LayerDev& L, const uint16_t* x, cudaS
 extern "C" int obs_expert_ffn(obs_ctx* ctx, int layer, const uint16_t* x, const int32_t* ids, int T, int path,
                               uint16_t* y, void* stream) {
     OBS_CHECK_CTX(ctx);
+    if (ctx->ep_world > 1) return fail(ctx, OBS_ERR_UNSUPPORTED, "stage entry points are single-GPU only (ep_world > 1)");
     int rc = check_layer(ctx, layer, true);
     if (rc || (rc = check_T(ctx, T))) return rc;
     if (T == 0) return OBS_OK;
@@ -470,6 +519,7 @@ extern "C" int obs_expert_ffn(obs_ctx* ctx, int layer, const uint16_t* x, const 
 extern "C" int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert, const uint16_t* x, int n,
                                    float* y, void* stream) {
     OBS_CHECK_CTX(ctx);
+    if (ctx->ep_world > 1) return fail(ctx, OBS_ERR_UNSUPPORTED, "stage entry points are single-GPU only (ep_world > 1)");
     int rc = check_layer(ctx, layer, true);
     if (rc) return rc;
     const Shape& s = ctx->sh;
@@ -508,12 +558,98 @@ extern "C" int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert
     return OBS_OK;
 }
 
+// ------------------------------------------------------ expert parallelism
+extern "C" int obs_ep_handle(obs_ctx* ctx, void* handle) {
+    OBS_CHECK_CTX(ctx);
+    if (!handle) return fail(ctx, OBS_ERR_INVALID, "null handle");
+    if (ctx->ep_world <= 1) return fail(ctx, OBS_ERR_STATE, "context has no expert parallelism (ep_world <= 1)");
+    static_assert(sizeof(cudaIpcMemHandle_t) == OBS_EP_HANDLE_BYTES, "handle size");
+    CU(cudaSetDevice(ctx->device), "cudaSetDevice");
+    cudaIpcMemHandle_t h;
+    CU(cudaIpcGetMemHandle(&h, ctx->ep_buf), "cudaIpcGetMemHandle");
+    memcpy(handle, &h, sizeof(h));
+    return OBS_OK;
+}
+
+extern "C" int obs_ep_connect(obs_ctx* ctx, const void* handles) {
+    OBS_CHECK_CTX(ctx);
+    if (!handles) return fail(ctx, OBS_ERR_INVALID, "null handles");
+    if (ctx->ep_world <= 1) return fail(ctx, OBS_ERR_STATE, "context has no expert parallelism (ep_world <= 1)");
+    if (ctx->ep_connected) return fail(ctx, OBS_ERR_STATE, "already connected");
+    CU(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+    for (int r = 0; r < ctx->ep_world; ++r) {
+        if (r == ctx->ep_rank) {
+            ctx->ep.peer[r] = ctx->ep_buf;
+            continue;
+        }
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h[r], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; ++q)
+                if (q != ctx->ep_rank && ctx->ep.peer[q]) cudaIpcCloseMemHandle(ctx->ep.peer[q]), ctx->ep.peer[q] = nullptr;
+            return cuda_fail(ctx, e, "cudaIpcOpenMemHandle (peer buffer)");
+        }
+        ctx->ep.peer[r] = static_cast<uint8_t*>(p);
+    }
+    ctx->ep_connected = true;
+    return OBS_OK;
+}
+
+// One layer with the experts spread over the ranks (layout and protocol in k_ep.cu).
+static int forward_ep(obs_ctx* ctx, const LayerDev& L, const uint16_t* x, uint16_t* out, const uint16_t* residual,
+                      int T, const float* logit_bias, cudaStream_t st) {
+    if (!ctx->ep_connected) return fail(ctx, OBS_ERR_STATE, "expert parallelism not connected (obs_ep_connect)");
+    const Shape& s = ctx->sh;
+    const EpArgs& a = ctx->ep;
+    prof_begin(ctx, OBS_STAGE_ROUTER, st);
+    if (T > 0) CU(launch_router_logits(L, s, x, T, ctx->logits, st), "router");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_TOPK, st);
+    if (T > 0)
+        CU(launch_topk(ctx->logits, router_parts(T), logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids, ctx->wts,
+                       nullptr, nullptr, st),
+           "topk");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_DISPATCH, st);
+    CU(launch_ep_send(ctx->ids, x, T, s.E, a, st), "ep send");
+    CU(cudaMemsetAsync(ctx->disp.counts, 0, ctx->E_local * 4, st), "memset");
+    CU(launch_ep_recv(a, st), "ep receive");
+    const Shape sl{s.H, s.I, ctx->E_local, 1};  // received rows: one local expert each
+    CU(launch_dispatch(a.ids_local, reinterpret_cast<const uint16_t*>(ctx->ep_buf + a.off_rx), a.world * a.cap, sl,
+                       ctx->disp, 1, st),
+       "dispatch");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_GEMM_GATEUP, st);
+    CU(launch_gemm(gemm_gateup(ctx, L, x), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_GEMM_DOWN, st);
+    CU(launch_gemm(gemm_down(ctx, L), kEpiBf16, ctx->num_sms, st), "gemm down");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_COMBINE, st);
+    CU(launch_ep_return(ctx->disp.slot_of, ctx->ybuf, a, st), "ep return");
+    CU(launch_ep_finish(a, st), "ep finish");
+    if (T > 0)
+        CU(launch_combine(reinterpret_cast<const uint16_t*>(ctx->ep_buf + a.off_ret), s.H, nullptr, ctx->wts, residual,
+                          T, s.H, s.K, out, st),
+           "combine");
+    prof_end(ctx, st);
+    return OBS_OK;
+}
+
 // ------------------------------------------------------------- the layer
 extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint16_t* out, const uint16_t* residual,
                                int T, const float* logit_bias, int path, void* stream) {
     OBS_CHECK_CTX(ctx);
     int rc = check_layer(ctx, layer, true);
     if (rc || (rc = check_T(ctx, T))) return rc;
+    if (ctx->ep_world > 1) {
+        // every rank takes part in every forward's exchange, T = 0 included
+        if (T > 0 && (!x || !out)) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+        if (path != OBS_PATH_AUTO && path != OBS_PATH_DECODE && path != OBS_PATH_PREFILL)
+            return fail(ctx, OBS_ERR_INVALID, "bad path");
+        return forward_ep(ctx, ctx->layers[layer], x, out, residual, T, logit_bias, as_stream(stream));
+    }
     if (T == 0) return OBS_OK;
     if (!x || !out) return fail(ctx, OBS_ERR_INVALID, "null pointer");
     if (path == OBS_PATH_AUTO) path = T <= ctx->decode_max ? OBS_PATH_DECODE : OBS_PATH_PREFILL;

@@ -31,7 +31,7 @@ struct Shape {
 // ---------------------------------------------------------------- k_synth.cu
 cudaError_t launch_synth_router(uint64_t seed, uint32_t layer, int E, int H, uint32_t* w, uint16_t* s,
                                 uint16_t* b, cudaStream_t st);
-cudaError_t launch_synth_proj(uint64_t seed, uint32_t layer, int proj, int E, int out_f, int in_f,
+cudaError_t launch_synth_proj(uint64_t seed, uint32_t layer, int proj, int e0, int E, int out_f, int in_f,
                               uint32_t* w, uint16_t* s, uint16_t* b, cudaStream_t st);
 cudaError_t launch_synth_x(uint64_t seed, uint32_t layer, int row0, int T, int H, float eps, uint16_t* x,
                            cudaStream_t st);
@@ -71,6 +71,25 @@ cudaError_t launch_gather_rows(const uint16_t* y, const int32_t* slot_of, int ro
                                cudaStream_t st);
 cudaError_t launch_histogram(const int32_t* ids, int n, int E, int32_t* counts, int* err, cudaStream_t st);
 cudaError_t launch_tile_rows(const uint16_t* x, int n, int cols, int atoms, uint16_t* dst, cudaStream_t st);
+
+// ------------------------------------------------------------------- k_ep.cu
+constexpr int kMaxWorld = 8;
+struct EpArgs {
+    uint8_t* peer[kMaxWorld];  // every rank's EP buffer (this rank's included), same layout
+    int world, rank, cap, H, K, E_local;
+    size_t off_rx, off_meta, off_cnt, off_rflag, off_ret, off_retflag;
+    int32_t* send_cnt;   // [world] rows sent to each rank (reset by the sender's last CTA)
+    uint32_t* done;      // [2] CTA completion counters of k_ep_send / k_ep_return
+    uint32_t* epoch;     // [1] completed forwards
+    int32_t* ids_local;  // [world * cap] local expert of each received row, -1 = empty
+    int32_t* src_item;   // [world * cap] source item t*K+k of each received row
+    int32_t* counts;     // [E_local] received rows per local expert (zeroed before k_ep_recv)
+    int* err;
+};
+cudaError_t launch_ep_send(const int32_t* ids, const uint16_t* x, int T, int E, const EpArgs& a, cudaStream_t st);
+cudaError_t launch_ep_recv(const EpArgs& a, cudaStream_t st);
+cudaError_t launch_ep_return(const int32_t* slot_of, const uint16_t* y, const EpArgs& a, cudaStream_t st);
+cudaError_t launch_ep_finish(const EpArgs& a, cudaStream_t st);
 
 // --------------------------------------------------------------- k_decode.cu
 constexpr int kDecodeSplit = 8;  // k-splits of the decode gate/up mat-vec

@@ -31,8 +31,9 @@ EXPORTS = (
     "obs_load_layer", "obs_synth_layer", "obs_synth_activations", "obs_moe_forward",
     "obs_moe_forward_host", "obs_gate", "obs_route", "obs_dispatch", "obs_expert_ffn",
     "obs_expert_gemm_f32", "obs_check_device", "obs_profile_enable", "obs_profile_read",
-    "obs_trace_enable", "obs_decode_ffn_static", "obs_kernel_launches",
+    "obs_trace_enable", "obs_decode_ffn_static", "obs_kernel_launches", "obs_ep_handle", "obs_ep_connect",
 )
+EP_HANDLE_BYTES = 64
 STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down")
 
 
@@ -46,7 +47,8 @@ class Config(C.Structure):
     _fields_ = [("hidden", C.c_int32), ("inter", C.c_int32), ("n_experts", C.c_int32),
                 ("top_k", C.c_int32), ("group_size", C.c_int32), ("n_layers", C.c_int32),
                 ("max_tokens", C.c_int32), ("norm_topk", C.c_int32),
-                ("decode_max_tokens", C.c_int32), ("rms_eps", C.c_float)]
+                ("decode_max_tokens", C.c_int32), ("rms_eps", C.c_float),
+                ("ep_world", C.c_int32), ("ep_rank", C.c_int32)]
 
 
 class LayerWeights(C.Structure):
@@ -87,6 +89,8 @@ def lib() -> C.CDLL:
         L.obs_profile_read.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(C.c_int32)]
         L.obs_trace_enable.argtypes = [vp, vp, i32]
         L.obs_kernel_launches.argtypes = [C.POINTER(C.c_uint64)]
+        L.obs_ep_handle.argtypes = [vp, vp]
+        L.obs_ep_connect.argtypes = [vp, vp]
         L.obs_decode_ffn_static.argtypes = [C.POINTER(LayerWeights), i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp]
         for name in EXPORTS:
             if name not in ("obs_last_error", "obs_abi_version"):
@@ -126,6 +130,8 @@ class MoeShape:
     norm_topk: bool = True
     decode_max_tokens: int = 4
     rms_eps: float = 1e-6
+    ep_world: int = 1    # expert parallelism: ranks sharing the experts
+    ep_rank: int = 0
 
 
 class MoeContext:
@@ -134,7 +140,8 @@ class MoeContext:
     def __init__(self, shape: MoeShape, device: int = 0):
         self.shape = shape
         cfg = Config(shape.hidden, shape.inter, shape.n_experts, shape.top_k, 64, shape.n_layers,
-                     shape.max_tokens, int(shape.norm_topk), shape.decode_max_tokens, shape.rms_eps)
+                     shape.max_tokens, int(shape.norm_topk), shape.decode_max_tokens, shape.rms_eps,
+                     shape.ep_world, shape.ep_rank)
         h = C.c_void_p()
         rc = lib().obs_create(C.byref(cfg), device, C.byref(h))
         if rc != OBS_OK:
@@ -192,6 +199,20 @@ class MoeContext:
         """One expert projection on the tcgen05 GEMM, fp32 out (matmul_dequant_4bit)."""
         self._chk(lib().obs_expert_gemm_f32(self._h, layer, proj, expert, _ptr(x), n, _ptr(y),
                                             _stream(stream)))
+
+    # -- expert parallelism
+    def ep_handle(self) -> bytes:
+        """This rank's buffer handle (obs_ep_handle), to be sent to the other ranks."""
+        buf = (C.c_uint8 * EP_HANDLE_BYTES)()
+        self._chk(lib().obs_ep_handle(self._h, buf))
+        return bytes(buf)
+
+    def ep_connect(self, handles):
+        """Open every rank's buffer (obs_ep_connect); handles in rank order."""
+        blob = b"".join(handles)
+        assert len(blob) == EP_HANDLE_BYTES * self.shape.ep_world
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        self._chk(lib().obs_ep_connect(self._h, buf))
 
     def moe_forward(self, layer, x, out, T, residual=None, bias=None, path=PATH_AUTO, stream=None):
         self._chk(lib().obs_moe_forward(self._h, layer, _ptr(x), _ptr(out), _ptr(residual), T,
