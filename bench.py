@@ -190,9 +190,15 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     cfg = CONFIGS[args.config]
     T = cfg["T"]
-    path = obsmoe.PATH_DECODE if T <= 4 else obsmoe.PATH_PREFILL
-    shape = obsmoe.MoeShape(H, I, E, K, n_layers=N_ROT, max_tokens=max(T, 16))
+    ep = world > 1  # N GPUs: expert parallelism, E/N experts per GPU, each GPU routes its own T tokens
+    path = obsmoe.PATH_DECODE if T <= 4 and not ep else obsmoe.PATH_PREFILL
+    shape = obsmoe.MoeShape(H, I, E, K, n_layers=N_ROT, max_tokens=max(T, 16),
+                            ep_world=world if ep else 1, ep_rank=rank if ep else 0)
     ctx = obsmoe.MoeContext(shape, local)
+    if ep:
+        handles = [None] * world
+        dist.all_gather_object(handles, ctx.ep_handle())
+        ctx.ep_connect(handles)
     for l in range(N_ROT):
         ctx.synth_layer(l, 0)  # layer l of seed 0 (config 2's per-layer seeding)
     xs = [torch.empty((T, H), dtype=torch.int16, device="cuda") for _ in range(N_ROT)]
@@ -283,16 +289,24 @@ def main():
     ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
     wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
     logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
-    U = []
+    U, R = [], []
+    e_lo, e_hi = (rank * E // world, (rank + 1) * E // world) if ep else (0, E)
     for l in range(N_ROT):
         ctx.gate_gpu(l, xs[l], logits, T, stream=stream)
         ctx.route(logits, T, ids, wts, stream=stream)
-        U.append(len(np.unique(ids.cpu().numpy())))
-    U_mean = sum(U) / len(U)
+        mine = ids.cpu().numpy().ravel()
+        if ep:  # this GPU's experts see every rank's rows routed to them
+            every = [None] * world
+            dist.all_gather_object(every, mine)
+            mine = np.concatenate(every)
+        local_ids = mine[(mine >= e_lo) & (mine < e_hi)]
+        U.append(len(np.unique(local_ids)))
+        R.append(len(local_ids))
+    U_mean, R_mean = sum(U) / len(U), sum(R) / len(R)
     if path == obsmoe.PATH_PREFILL:
         top = "gemm_gateup"
-        # gate+up weights of the U routed experts, the T*K permuted rows read, h written
-        alg = U_mean * GATEUP_BYTES + T * K * H * 2 + T * K * I * 2
+        # gate+up weights of the U routed experts (this GPU's), the routed rows read, h written
+        alg = U_mean * GATEUP_BYTES + R_mean * H * 2 + R_mean * I * 2
         kname = "k_gemm<kEpiSwiglu> (tcgen05 grouped gate/up GEMM + SwiGLU)"
     else:
         top = "decode_gateup"
@@ -309,7 +323,7 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; BASELINE config distributions; weights generated on the device)",
         "config": {"workload": cfg["name"], "T": T, "E": E, "K": K, "H": H, "I": I, "weights": "4-bit g64 (router 8-bit)",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "parallelism": f"expert parallel x{world} (NVLink peer all-to-all)" if ep else "single GPU",
                    "l2": f"inputs larger than L2: steps rotate over {N_ROT} resident layers ({N_ROT * 340} MB)",
                    "path": "prefill (tcgen05 grouped GEMM)" if path == obsmoe.PATH_PREFILL else "decode (mat-vec)"},
         "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": hbm, "unit": "GB/s",
