@@ -46,7 +46,11 @@ N_ROT = 4                       # resident layers the steps rotate over
 CONFIGS = {
     0: dict(T=1, name="config0: Qwen3-30B-A3B MoE layer, decode of 1 token"),
     1: dict(T=512, name="config1: Qwen3-30B-A3B MoE layer, batched prefill of T=512 tokens"),
+    2: dict(T=None, name="config2: 48-layer MoE stack, decode of B independent tokens per step", stack=True),
+    3: dict(T=4096, name="config3: 48-layer MoE stack, prefill of T=4096 tokens, Zipf(1.1) expert bias",
+            stack=True),
 }
+LAYER_FLOPS = 2 * K * 4_718_592  # per token and layer (router excluded)
 
 
 def parse():
@@ -57,6 +61,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=32, help="config 2: tokens per decode step (1, 8, 32, 128)")
+    ap.add_argument("--layers", type=int, default=48, help="configs 2 and 3: layers in the stack")
     return ap.parse_args()
 
 
@@ -131,10 +137,214 @@ def cpu_baseline(L_host, x_host, T):
             "sample": f"the full {T}-token layer once through oracle/obs_oracle.c ({dt:.2f} s)"}
 
 
+def zipf_bias(beta, seed=11):
+    """Config 3's per-expert logit bias: beta * log(r_e^-1.1) over a seeded rank
+    permutation r (1 = hottest)."""
+    import numpy as np
+
+    r = np.random.default_rng(seed).permutation(E) + 1
+    return (beta * -1.1 * np.log(r)).astype(np.float32)
+
+
+def run_stack(args, rank, world, local):
+    """Configs 2 and 3: a stack of MoE layers on a residual stream,
+    r <- r + MoE_l(RMSNorm(r)) for every layer (obs_moe_stack_forward); a step is
+    one pass of the batch through all layers, captured in one CUDA graph."""
+    import numpy as np
+    import torch
+
+    import obsmoe
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    cfg = CONFIGS[args.config]
+    nl = args.layers
+    T = args.batch if args.config == 2 else cfg["T"]
+    decode = args.config == 2
+    path = obsmoe.PATH_AUTO if decode else obsmoe.PATH_PREFILL
+    ep = world > 1
+    shape = obsmoe.MoeShape(H, I, E, K, n_layers=nl, max_tokens=max(T, 16),
+                            ep_world=world if ep else 1, ep_rank=rank if ep else 0)
+    ctx = obsmoe.MoeContext(shape, local)
+    if ep:
+        handles = [None] * world
+        dist.all_gather_object(handles, ctx.ep_handle())
+        ctx.ep_connect(handles)
+    for l in range(nl):
+        ctx.synth_layer(l, 0)
+    r0 = torch.empty((T, H), dtype=torch.int16, device="cuda")
+    obsmoe.synth_activations(rank, 0, 0, T, H, r0)
+    stream = torch.cuda.current_stream()
+    bias, beta, imbalance = None, None, None
+    if args.config == 3:
+        # calibrate beta so the hottest expert gets ~10x the mean load (layer 0's routing)
+        logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
+        ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+        wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
+        xn = torch.empty_like(r0)
+        ctx.rmsnorm(r0, xn, T)
+        ctx.gate_gpu(0, xn, logits, T)
+        best = None
+        for b in np.linspace(0.0, 8.0, 81):
+            bt = torch.from_numpy(zipf_bias(b)).cuda()
+            ctx.route(logits, T, ids, wts, bias=bt)
+            load = np.bincount(ids.cpu().numpy().ravel(), minlength=E)
+            ratio = load.max() / load.mean()
+            if best is None or abs(ratio - 10.0) < abs(best[1] - 10.0):
+                best = (float(b), float(ratio))
+        beta, imbalance = best
+        bias = torch.from_numpy(zipf_bias(beta)).cuda()
+    r = torch.empty_like(r0)
+
+    def step():
+        r.copy_(r0)
+        ctx.moe_stack_forward(0, nl, r, T, bias=bias, path=path, stream=stream)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    step()
+    barrier()
+    ctx.check_device()
+    n0 = obsmoe.kernel_launches()
+    step()
+    launches_per_step = obsmoe.kernel_launches() - n0
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(g, stream=cap):
+            r.copy_(r0)
+            ctx.moe_stack_forward(0, nl, r, T, bias=bias, path=path, stream=cap)
+    stream.wait_stream(cap)
+    barrier()
+    for _ in range(max(args.warmup, 3)):
+        g.replay()
+    barrier()
+    ctx.check_device()
+    clocks = Clocks(local)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        g.replay()
+    ev1.record(stream)
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    ctx.check_device()
+    ms_t = torch.tensor([ms], device="cuda")
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    step_s = ms / args.steps / 1e3
+    value = world * T / step_s
+
+    # e2e: the residual batch from pinned host memory, the stack, the result back
+    rh = r0.cpu().pin_memory()
+    oh = torch.empty_like(rh).pin_memory()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        r.copy_(rh, non_blocking=True)
+        ctx.moe_stack_forward(0, nl, r, T, bias=bias, path=path, stream=stream)
+        oh.copy_(r, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    ems_t = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+    if dist is not None:
+        dist.all_reduce(ems_t, op=dist.ReduceOp.MAX)
+    e2e_value = world * T * args.steps / (float(ems_t.item()) / 1e3)
+
+    # per-layer routing of this step (distinct experts), replayed eagerly layer by layer
+    hbm, bf16, peak_kind = peaks()
+    logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    xn = torch.empty_like(r0)
+    rr = r0.clone()
+    U, loads = [], []
+    for l in range(nl):
+        ctx.rmsnorm(rr, xn, T)
+        ctx.gate_gpu(l, xn, logits, T)
+        ctx.route(logits, T, ids, wts, bias=bias)
+        every = ids.cpu().numpy().ravel()
+        if ep:
+            parts = [None] * world
+            dist.all_gather_object(parts, every)
+            every = np.concatenate(parts)
+        U.append(len(np.unique(every)))
+        loads.append(np.bincount(every, minlength=E))
+        ctx.moe_stack_forward(l, 1, rr, T, bias=bias, path=path, stream=stream)
+    torch.cuda.synchronize()
+    load = np.sum(loads, axis=0)
+    if decode:
+        # HBM roofline: every routed expert's weights, the router and the activations, per layer
+        per_gpu_bytes = (sum(U) * EXPERT_BYTES / world + nl * ROUTER_BYTES + nl * 2 * T * H * 2 * 2)
+        achieved = per_gpu_bytes / step_s / 1e9
+        roof = {"bound": "hbm", "kernel": f"whole {nl}-layer decode step (router, top-k, 4-bit mat-vecs, combine, "
+                f"RMSNorm per layer)", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "algorithmic_bytes_per_launch": per_gpu_bytes, "traffic": None}
+    else:
+        flops = nl * T * LAYER_FLOPS  # per GPU (weak scaling: each GPU's T tokens)
+        achieved = flops / step_s / 1e12
+        roof = {"bound": "tensor", "kernel": f"whole {nl}-layer prefill step (grouped tcgen05 GEMMs dominate)",
+                "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops)",
+                "algorithmic_flops_per_launch": flops, "traffic": None}
+    line = {
+        "metric": "MoE stack tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; BASELINE config distributions; weights generated on the device)",
+        "config": {"workload": cfg["name"], "layers": nl, "T": T, "E": E, "K": K, "H": H, "I": I,
+                   "parallelism": f"expert parallel x{world} (NVLink peer all-to-all)" if ep else "single GPU",
+                   "l2": f"inputs larger than L2: {nl} resident layers ({nl * 340} MB) per step",
+                   "path": "decode (mat-vec)" if decode and T <= 4 and not ep else "prefill (tcgen05 grouped GEMM)",
+                   "zipf_beta": beta, "load_max_over_mean_layer0": imbalance,
+                   "load_max_over_mean_all_layers": float(load.max() / load.mean())},
+        "roofline": roof, "distinct_experts_per_layer": float(np.mean(U)),
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2},
+        "gpu_launches": launches_per_step * args.steps, "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+
+        # bounded sample: 2 layers and at most 32 tokens through the C oracle, scaled to the stack
+        nlo, Ts = 2, min(T, 32)
+        Ls = [O.synth_layer(0, l, E=E, H=H, I=I, K=K) for l in range(nlo)]
+        rs = r0[:Ts].cpu().numpy().view(np.uint16)
+        n = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        O.moe_stack(Ls, rs, bias=None if bias is None else bias.cpu().numpy(), nthreads=n)
+        dt = (time.perf_counter() - t0) * nl / nlo
+        line["cpu_baseline"] = {"value": Ts / dt, "unit": "tokens/s", "cores": n, "kind": "port",
+                                "sample": f"{Ts} tokens through {nlo} layers of oracle/obs_oracle.c, "
+                                          f"time scaled to {nl} layers"}
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
 def run_reference(args, rank, world):
     """The reference's own kernels on the host cores (oracle/_ref)."""
     cfg = CONFIGS[args.config]
-    T = cfg["T"]
+    T = cfg["T"] if cfg["T"] is not None else args.batch
     if rank != 0:
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -156,8 +366,13 @@ def run_reference(args, rank, world):
     value = Ts * args.steps / dt
     sample = (f"{Ts} of the {T} tokens per step through the reference's shaders/*.metal kernels compiled "
               f"for the CPU (oracle/_ref), strung as src/forward.rs:164-232, {n} threads")
+    metric = "MoE layer tokens/s"
+    if cfg.get("stack"):  # one layer timed, scaled to the stack's layer count
+        value /= args.layers
+        metric = "MoE stack tokens/s"
+        sample += f"; one layer per step, time scaled to {args.layers} layers"
     print(json.dumps({
-        "impl": "reference", "metric": "MoE layer tokens/s", "value": value, "unit": "tokens/s",
+        "impl": "reference", "metric": metric, "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded, BASELINE config distributions)",
@@ -174,6 +389,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if CONFIGS[args.config].get("stack"):
+        return run_stack(args, rank, world, local)
 
     import numpy as np
     import torch

@@ -168,6 +168,23 @@ int obs_kernel_launches(uint64_t* count);
  * that gave up) raised since the last check; clears the flags. */
 int obs_check_device(obs_ctx* ctx, void* stream);
 
+/* ----------------------------------------------------- the layer stack */
+/* The MoE input norm, rmsnorm.metal:9-37 (Model::rmsnorm, forward.rs:421):
+ * out[t] = x[t] / sqrt(mean(x[t]^2) + rms_eps) * weight (weight NULL: 1), in
+ * the reference kernel's own reduction order (bit-exact with the oracle).
+ * x, out [T, hidden] bf16 device memory (out may not alias x). */
+int obs_rmsnorm(obs_ctx* ctx, const uint16_t* x, const uint16_t* weight, int T, uint16_t* out, void* stream);
+/* n_layers consecutive MoE layers on a residual stream r ([T, hidden] bf16,
+ * device, updated in place), forward.rs:419-441 without the attention block
+ * (BASELINE configs 2 and 3):
+ *   for l = layer0 .. layer0 + n_layers - 1:  x = RMSNorm(r);  r = r + MoE_l(x)
+ * (combine and residual summed in fp32, rounded once).  logit_bias as in
+ * obs_moe_forward, applied to every layer.  Only stream-ordered work (CUDA
+ * graph capture is fine); with expert parallelism every rank runs the same
+ * layers. */
+int obs_moe_stack_forward(obs_ctx* ctx, int layer0, int n_layers, uint16_t* resid, int T, const float* logit_bias,
+                          int path, void* stream);
+
 /* ----------------------------------------------- expert parallelism (EP) */
 /* A context created with ep_world > 1 holds E/ep_world experts of each layer
  * (obs_load_layer takes all E experts' host or device arrays and keeps its own

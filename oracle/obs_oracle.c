@@ -134,6 +134,35 @@ void orc_rmsnorm_row(const uint16_t* x, int H, float eps, uint16_t* out) {
     for (int i = 0; i < H; ++i) out[i] = orc_f32_to_bf16(orc_bf16_to_f32(x[i]) / rms);
 }
 
+/* The layer-input RMSNorm of the MoE stack, in rmsnorm.metal:9-37's own order:
+ * 256 "threads", thread l sums v*v over elements l, l+256, ... (a rounded
+ * product, then a rounded add: ps += v * v uncontracted); the 256 partials meet
+ * in the halving tree
+ * sq[l] += sq[l + s], s = 128, 64, ..., 1; rms = sqrt(sq[0] / dim + eps);
+ * out = (x / rms) * w (w = NULL: 1).  x, w and out bf16. */
+float orc_rms_tg(const uint16_t* x, int H, float eps) {
+    float sq[256];
+    for (int l = 0; l < 256; ++l) {
+        float ps = 0.0f;
+        for (int i = l; i < H; i += 256) {
+            float v = orc_bf16_to_f32(x[i]);
+            ps = ps + v * v;
+        }
+        sq[l] = ps;
+    }
+    for (int st = 128; st > 0; st >>= 1)
+        for (int l = 0; l < st; ++l) sq[l] = sq[l] + sq[l + st];
+    return sqrtf(sq[0] / (float)H + eps);
+}
+
+void orc_rmsnorm_tg_row(const uint16_t* x, const uint16_t* w, int H, float eps, uint16_t* out) {
+    const float rms = orc_rms_tg(x, H, eps);
+    for (int i = 0; i < H; ++i) {
+        float v = orc_bf16_to_f32(x[i]) / rms;
+        out[i] = orc_f32_to_bf16(w ? v * orc_bf16_to_f32(w[i]) : v);
+    }
+}
+
 void orc_synth_x(uint64_t seed, uint32_t layer, int row0, int T, int H, float eps, uint16_t* x) {
     uint64_t kx = orc_stream_key(seed, layer, ORC_T_X);
     uint16_t* raw = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)H);

@@ -54,6 +54,8 @@ void orc_synth_x(uint64_t seed, uint32_t layer, int row0, int T, int H, float ep
 
 /* ---- a8: RMSNorm (rmsnorm.metal:20-36), sequential sum of squares ---- */
 void orc_rmsnorm_row(const uint16_t* x, int H, float eps, uint16_t* out);
+void orc_rmsnorm_tg_row(const uint16_t* x, const uint16_t* w, int H, float eps, uint16_t* out);
+float orc_rms_tg(const uint16_t* x, int H, float eps);
 
 /* ---- a1/a4 dequant (dequant_matvec_8bit.metal:22-27, fused_dequant_matvec_4bit.metal:33-45) ----
  * value = fmaf(q, scale, bias) in fp32.  For these formats q*scale is exact in

@@ -44,6 +44,9 @@ def lib():
                                      _u32p, _u16p, _u16p]
         L.orc_synth_x.argtypes = [C.c_uint64, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_float, _u16p]
         L.orc_rmsnorm_row.argtypes = [_u16p, C.c_int, C.c_float, _u16p]
+        L.orc_rmsnorm_tg_row.argtypes = [_u16p, C.c_void_p, C.c_int, C.c_float, _u16p]
+        L.orc_rms_tg.argtypes = [_u16p, C.c_int, C.c_float]
+        L.orc_rms_tg.restype = C.c_float
         L.orc_dequant4.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int, _f32p]
         L.orc_dequant8.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int, _f32p]
         L.orc_dequant4_bf16.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int, _u16p]
@@ -124,6 +127,21 @@ def synth_x(seed, layer, T, H, row0=0, eps=1e-6):
     x = np.empty((T, H), np.uint16)
     lib().orc_synth_x(seed, layer, row0, T, H, eps, x)
     return x
+
+
+def rmsnorm_layer(x, eps=1e-6):
+    """The MoE stack's layer-input RMSNorm in rmsnorm.metal's threadgroup order (weight 1)."""
+    x = np.ascontiguousarray(x, np.uint16)
+    out = np.empty_like(x)
+    for t in range(x.shape[0]):
+        lib().orc_rmsnorm_tg_row(x[t], None, x.shape[1], eps, out[t])
+    return out
+
+
+def rms_layer(x, eps=1e-6):
+    """The fp32 rms of each row in rmsnorm.metal's reduction order."""
+    x = np.ascontiguousarray(x, np.uint16)
+    return np.array([lib().orc_rms_tg(x[t], x.shape[1], eps) for t in range(x.shape[0])], np.float32)
 
 
 def rmsnorm(x, eps=1e-6):
@@ -251,6 +269,17 @@ def moe_layer(L: Layer, x, bias=None, residual=None, norm_topk=True, wmode=0, nt
     return out, ids, w
 
 
+def moe_stack(layers, r0, bias=None, eps=1e-6, wmode=0, nthreads=None):
+    """A chain of MoE layers with a residual stream (BASELINE configs 2 and 3,
+    forward.rs:419-441 without attention): x_l = RMSNorm(r_l) in rmsnorm.metal's
+    order, r_{l+1} = r_l + MoE_l(x_l) (combine with the residual, rounded once)."""
+    r = np.ascontiguousarray(r0, np.uint16)
+    for L in layers:
+        x = rmsnorm_layer(r, eps)
+        r, _, _ = moe_layer(L, x, bias=bias, residual=r, wmode=wmode, nthreads=nthreads)
+    return r
+
+
 # ------------------------------------------- reference shaders (CPU build)
 def ref_lib():
     """The reference's own kernels compiled for the CPU, or None if not built."""
@@ -268,6 +297,7 @@ def ref_lib():
         R.ref_moe_routing_topk.argtypes = [_f16p, C.c_int, C.c_int, C.c_int, _i32p, _f16p]
         R.ref_ew_swiglu.argtypes = [_f16p, _f16p, _f16p, C.c_int]
         R.ref_ew_scaled_add.argtypes = [_f16p, _f16p, C.c_float, C.c_int]
+        R.ref_rmsnorm.argtypes = [_f16p, _f16p, _f16p, C.c_int, C.c_int, C.c_float]
         R.ref_moe_prefill.restype = C.c_int
         R.ref_moe_prefill.argtypes = [C.c_void_p, _u16p, C.c_void_p, C.c_int, C.c_int, _f16p,
                                       _i32p, _f32p]

@@ -21,6 +21,7 @@ struct MmParams { unsigned in_features, out_features, group_size, n_tokens; }; /
 struct RtParams { unsigned n_experts, top_k, norm_topk; };                     // router.rs:8-14
 struct NParams { unsigned n; };
 struct ScaledNParams { unsigned n; float scale; };
+struct RmsParams { unsigned dim; float eps; };                               // rmsnorm.metal:7
 
 extern "C" {
 void dequant_matvec_8bit(const unsigned char*, const half*, const half*, const half*, half*,
@@ -32,6 +33,7 @@ void matmul_dequant_4bit(const unsigned char*, const half*, const half*, const h
 void moe_routing_topk(const half*, int*, half*, const RtParams&, unsigned);
 void ew_swiglu(const half*, const half*, half*, const NParams&, unsigned);
 void ew_scaled_add(half*, const half*, const ScaledNParams&, unsigned);
+void rmsnorm(const half*, const half*, half*, const RmsParams&, unsigned, unsigned);
 }
 
 template <class F>
@@ -87,6 +89,19 @@ void ref_matmul_dequant_4bit(const uint32_t* w, const half* s, const half* b, co
     parallel_for((long)n_tokens * out_f, nthreads, [&](long t) {
         matmul_dequant_4bit((const unsigned char*)w, s, b, x, out, p, (unsigned)t);
     });
+}
+
+// rmsnorm.metal: one threadgroup of 256 per row.  Its phases (partial sums, a
+// halving tree, the output loop) are separated by barriers, which the stand-in
+// header makes no-ops.  Running the 256 "threads" from 255 down to 0 lets every
+// tree step read a partner that has finished all of its own steps; a second
+// such pass then gives every thread the final sq[0] (thread 0 rewrites it last,
+// with the same value).
+void ref_rmsnorm(const half* x, const half* w, half* out, int rows, int dim, float eps) {
+    RmsParams p{(unsigned)dim, eps};
+    for (int r = 0; r < rows; ++r)
+        for (int pass = 0; pass < 2; ++pass)
+            for (int t = 255; t >= 0; --t) rmsnorm(x, w, out, p, (unsigned)r, (unsigned)t);
 }
 
 // router.rs:25-56: one threadgroup of 256; the serial section runs on thread 0

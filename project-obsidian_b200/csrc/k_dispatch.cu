@@ -107,6 +107,34 @@ __global__ void __launch_bounds__(256) k_permute(const uint16_t* __restrict__ x,
     }
 }
 
+// The MoE stack's layer-input RMSNorm (rmsnorm.metal:9-37), in the reference
+// kernel's own order: 256 threads per row, thread l sums v*v (rounded product,
+// rounded add) over elements l, l+256, ...; the partials meet in the halving
+// tree sq[l] += sq[l + s], s = 128 .. 1; rms = sqrt(sq[0] / H + eps);
+// out = (x / rms) * w.  IEEE divide and square root, as the oracle.
+__global__ void __launch_bounds__(256) k_rmsnorm(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                 int H, float eps, uint16_t* __restrict__ out) {
+    __shared__ float sq[256];
+    const int t = blockIdx.x, l = threadIdx.x;
+    const uint16_t* row = x + (size_t)t * H;
+    float ps = 0.0f;
+    for (int i = l; i < H; i += 256) {
+        const float v = bf2f(row[i]);
+        ps = __fadd_rn(ps, __fmul_rn(v, v));
+    }
+    sq[l] = ps;
+    __syncthreads();
+    for (int s = 128; s > 0; s >>= 1) {
+        if (l < s) sq[l] = __fadd_rn(sq[l], sq[l + s]);
+        __syncthreads();
+    }
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sq[0], (float)H), eps));
+    for (int i = l; i < H; i += 256) {
+        const float v = __fdiv_rn(bf2f(row[i]), rms);
+        out[(size_t)t * H + i] = f2bf(w ? __fmul_rn(v, bf2f(w[i])) : v);
+    }
+}
+
 // out[t] = bf16(residual[t] + sum_k w[t,k] * y[slot_of[t,k]]), rank order, fp32
 __global__ void __launch_bounds__(256) k_combine(const uint16_t* __restrict__ y, int y_ld,
                                                  const int32_t* __restrict__ slot_of, const float* __restrict__ w,
@@ -188,6 +216,14 @@ cudaError_t launch_combine(const uint16_t* y, int y_ld, const int32_t* slot_of, 
     if (T <= 0) return cudaSuccess;
     note_launch();
     k_combine<<<T, 256, 0, st>>>(y, y_ld, slot_of, w, residual, H, K, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps, uint16_t* out,
+                           cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    note_launch();
+    k_rmsnorm<<<T, 256, 0, st>>>(x, w, H, eps, out);
     return cudaGetLastError();
 }
 

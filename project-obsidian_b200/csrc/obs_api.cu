@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/obs_moe.h"
@@ -52,6 +53,8 @@ struct obs_ctx {
     uint16_t* out_dev = nullptr;
     uint16_t* res_dev = nullptr;
     float* bias_dev = nullptr;
+    uint16_t* xnorm_dev = nullptr;  // the layer stack's normalised input
+    uint16_t* rtmp_dev = nullptr;   // the layer stack's other residual buffer
     int R_cap = 0, max_tiles = 0, decode_max = 4;
     uint64_t* trace = nullptr;  // obs_trace_enable
     int trace_n = 0;
@@ -215,6 +218,8 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->out_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->res_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->bias_dev, (size_t)E * 4},
+        {(void**)&ctx->xnorm_dev, (size_t)T * s.H * 2},
+        {(void**)&ctx->rtmp_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->ep.send_cnt, (size_t)kMaxWorld * 4},
         {(void**)&ctx->ep.done, 16},
         {(void**)&ctx->ep.epoch, 16},
@@ -693,6 +698,41 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
     prof_begin(ctx, OBS_STAGE_COMBINE, st);
     CU(launch_combine(ctx->ybuf, s.H, ctx->disp.slot_of, ctx->wts, residual, T, s.H, s.K, out, st), "combine");
     prof_end(ctx, st);
+    return OBS_OK;
+}
+
+extern "C" int obs_rmsnorm(obs_ctx* ctx, const uint16_t* x, const uint16_t* weight, int T, uint16_t* out,
+                           void* stream) {
+    OBS_CHECK_CTX(ctx);
+    int rc = check_T(ctx, T);
+    if (rc) return rc;
+    if (T == 0) return OBS_OK;
+    if (!x || !out) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    if (x == out) return fail(ctx, OBS_ERR_INVALID, "out may not alias x");
+    CU(launch_rmsnorm(x, weight, T, ctx->sh.H, ctx->cfg.rms_eps, out, as_stream(stream)), "rmsnorm");
+    return OBS_OK;
+}
+
+extern "C" int obs_moe_stack_forward(obs_ctx* ctx, int layer0, int n_layers, uint16_t* resid, int T,
+                                     const float* logit_bias, int path, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    if (n_layers < 0 || layer0 < 0 || layer0 + n_layers > (int)ctx->layers.size())
+        return fail(ctx, OBS_ERR_INVALID, "layer range out of the context's layers");
+    int rc = check_T(ctx, T);
+    if (rc) return rc;
+    if (T > 0 && !resid) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    if (T == 0 && ctx->ep_world <= 1) return OBS_OK;
+    cudaStream_t st = as_stream(stream);
+    uint16_t* r = resid;
+    uint16_t* other = ctx->rtmp_dev;
+    for (int l = layer0; l < layer0 + n_layers; ++l) {
+        if (T > 0) CU(launch_rmsnorm(r, nullptr, T, ctx->sh.H, ctx->cfg.rms_eps, ctx->xnorm_dev, st), "rmsnorm");
+        rc = obs_moe_forward(ctx, l, ctx->xnorm_dev, other, r, T, logit_bias, path, stream);
+        if (rc) return rc;
+        std::swap(r, other);
+    }
+    if (r != resid && T > 0)
+        CU(cudaMemcpyAsync(resid, r, (size_t)T * ctx->sh.H * 2, cudaMemcpyDeviceToDevice, st), "copy");
     return OBS_OK;
 }
 

@@ -69,6 +69,8 @@ cudaError_t launch_combine(const uint16_t* y, int y_ld, const int32_t* slot_of, 
                            const uint16_t* residual, int T, int H, int K, uint16_t* out, cudaStream_t st);
 cudaError_t launch_gather_rows(const uint16_t* y, const int32_t* slot_of, int rows, int H, uint16_t* out,
                                cudaStream_t st);
+cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps, uint16_t* out,
+                           cudaStream_t st);
 cudaError_t launch_histogram(const int32_t* ids, int n, int E, int32_t* counts, int* err, cudaStream_t st);
 cudaError_t launch_tile_rows(const uint16_t* x, int n, int cols, int atoms, uint16_t* dst, cudaStream_t st);
 

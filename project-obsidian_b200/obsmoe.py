@@ -32,6 +32,7 @@ EXPORTS = (
     "obs_moe_forward_host", "obs_gate", "obs_route", "obs_dispatch", "obs_expert_ffn",
     "obs_expert_gemm_f32", "obs_check_device", "obs_profile_enable", "obs_profile_read",
     "obs_trace_enable", "obs_decode_ffn_static", "obs_kernel_launches", "obs_ep_handle", "obs_ep_connect",
+    "obs_rmsnorm", "obs_moe_stack_forward",
 )
 EP_HANDLE_BYTES = 64
 STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down")
@@ -91,6 +92,8 @@ def lib() -> C.CDLL:
         L.obs_kernel_launches.argtypes = [C.POINTER(C.c_uint64)]
         L.obs_ep_handle.argtypes = [vp, vp]
         L.obs_ep_connect.argtypes = [vp, vp]
+        L.obs_rmsnorm.argtypes = [vp, vp, vp, i32, vp, vp]
+        L.obs_moe_stack_forward.argtypes = [vp, i32, i32, vp, i32, vp, i32, vp]
         L.obs_decode_ffn_static.argtypes = [C.POINTER(LayerWeights), i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp]
         for name in EXPORTS:
             if name not in ("obs_last_error", "obs_abi_version"):
@@ -217,6 +220,14 @@ class MoeContext:
     def moe_forward(self, layer, x, out, T, residual=None, bias=None, path=PATH_AUTO, stream=None):
         self._chk(lib().obs_moe_forward(self._h, layer, _ptr(x), _ptr(out), _ptr(residual), T,
                                         _ptr(bias), path, _stream(stream)))
+
+    def rmsnorm(self, x, out, T, weight=None, stream=None):
+        self._chk(lib().obs_rmsnorm(self._h, _ptr(x), _ptr(weight), T, _ptr(out), _stream(stream)))
+
+    def moe_stack_forward(self, layer0, n_layers, resid, T, bias=None, path=PATH_AUTO, stream=None):
+        """resid <- n_layers of (r + MoE_l(RMSNorm(r))), in place."""
+        self._chk(lib().obs_moe_stack_forward(self._h, layer0, n_layers, _ptr(resid), T, _ptr(bias), path,
+                                              _stream(stream)))
 
     def moe_forward_host(self, layer, x_host, out_host, T, residual_host=None, bias_host=None,
                          path=PATH_AUTO, stream=None):

@@ -353,3 +353,42 @@ def test_forward_replays_from_a_cuda_graph(small, path, T):
         assert torch.equal(out, eager)
     del g
     small.ctx.check_device()
+
+
+def test_rmsnorm_bit_exact(small):
+    """The stack's layer-input norm: bit-exact with the oracle (rmsnorm.metal's order)."""
+    torch = small.torch
+    x = O.f32_to_bf16(O.bf16_to_f32(small.x(33, row0=7)) * np.float32(2.5) + np.float32(0.1))
+    out = torch.empty((33, 2048), dtype=torch.int16, device="cuda")
+    small.ctx.rmsnorm(dev(torch, x), out, 33)
+    assert np.array_equal(host(out, np.uint16), O.rmsnorm_layer(x))
+
+
+@pytest.mark.parametrize("T,path", [(40, obsmoe.PATH_PREFILL), (3, obsmoe.PATH_DECODE)])
+def test_layer_stack(cuda, T, path):
+    """Three layers on a residual stream: the stack entry equals the per-layer calls
+    bit for bit, and the oracle chain within tolerance."""
+    torch = cuda
+    n = 3
+    shape = obsmoe.MoeShape(2048, 256, 16, 4, n_layers=n, max_tokens=64)
+    ctx = obsmoe.MoeContext(shape, 0)
+    Ls = [O.synth_layer(9, l, E=16, H=2048, I=256, K=4) for l in range(n)]
+    for l, L in enumerate(Ls):
+        ctx.load_layer(l, L)
+    r0 = small_resid = O.synth_x(9, 5, T, 2048)
+    r = dev(torch, r0)
+    ctx.moe_stack_forward(0, n, r, T, path=path)
+    got = host(r, np.uint16)
+    # the same chain through the single-layer entry points
+    m = dev(torch, small_resid)
+    xn = torch.empty_like(m)
+    nxt = torch.empty_like(m)
+    for l in range(n):
+        ctx.rmsnorm(m, xn, T)
+        ctx.moe_forward(l, xn, nxt, T, residual=m, path=path)
+        m, nxt = nxt, m
+    assert np.array_equal(got, host(m, np.uint16))
+    ref = O.moe_stack(Ls, r0, wmode=1 if path == obsmoe.PATH_PREFILL else 0)
+    assert rel_err(O.bf16_to_f32(got), O.bf16_to_f32(ref)) < REL
+    ctx.check_device()
+    ctx.close()

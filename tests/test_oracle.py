@@ -210,3 +210,16 @@ def test_dequant4_bf16_single_rounding():
     s1 = np.array([[O.f32_to_bf16(np.float32(2.0 ** -8))]], np.uint16)
     b1 = np.array([[O.f32_to_bf16(np.float32(1.0))]], np.uint16)
     assert O.dequant4_bf16(w1, s1, b1)[0, 0] == O.f32_to_bf16(np.float32(1.0))
+
+
+def test_golden_rmsnorm_order(golden):
+    """The MoE stack's layer-input RMSNorm follows rmsnorm.metal's reduction order
+    exactly: with the oracle's fp32 rms, x / rms rounded to f16 reproduces the
+    reference kernel's f16 output bit for bit."""
+    g = golden("rmsnorm")
+    x = g["x"]
+    rms = O.rms_layer(x)
+    v = O.bf16_to_f32(x) / rms[:, None]
+    assert v.dtype == np.float32
+    assert np.array_equal(v.astype(np.float16).view(np.uint16), g["out"].view(np.uint16))
+    assert np.array_equal(O.rmsnorm_layer(x), O.f32_to_bf16(v))
