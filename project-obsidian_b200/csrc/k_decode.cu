@@ -116,6 +116,7 @@ template <class Src>
 __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const uint16_t* __restrict__ x,
                                                        const int32_t* __restrict__ ids, int H, int I, int K, int E,
                                                        DecodeBufs d) {
+    pdl_begin();
     __shared__ float s_part[8][kRowTile];
     __shared__ float s_gu[2][kRowTile];
     __shared__ int s_last;
@@ -170,6 +171,7 @@ __global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __
                                                      const uint16_t* __restrict__ residual, int H, int I, int K,
                                                      int E, DecodeBufs d, uint16_t* __restrict__ out,
                                                      int do_combine) {
+    pdl_begin();
     __shared__ float s_part[16][kRowTile];
     __shared__ int s_last;
     const int rt = blockIdx.x, k = blockIdx.y, t = blockIdx.z;
@@ -226,8 +228,10 @@ cudaError_t launch_decode_gateup(const LayerDev& L, const Shape& sh, const uint1
     if (T <= 0) return cudaSuccess;
     const TiledSrc g{L.gateup, sh.I / kRowTile, sh.H / kGroup, 2, 0}, u{L.gateup, sh.I / kRowTile, sh.H / kGroup, 2, 1};
     dim3 grid(sh.I / kRowTile, kSplitGU, T * sh.K);
-    note_launch();
-    k_decode_gateup<TiledSrc><<<grid, 256, 0, st>>>(g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
+    {
+        const cudaError_t le_ = launch_pdl(k_decode_gateup<TiledSrc>, dim3(grid), dim3(256), 0, st, g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
@@ -237,9 +241,11 @@ cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t
     if (T <= 0) return cudaSuccess;
     const TiledSrc dn{L.down, sh.H / kRowTile, sh.I / kGroup, 1, 0};
     dim3 grid(sh.H / kRowTile, sh.K, T);
-    note_launch();
-    k_decode_down<TiledSrc><<<grid, down_threads(sh.I), 0, st>>>(dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out,
+    {
+        const cudaError_t le_ = launch_pdl(k_decode_down<TiledSrc>, dim3(grid), dim3(down_threads(sh.I)), 0, st, dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out,
                                                                  do_combine);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
@@ -251,13 +257,17 @@ cudaError_t launch_decode_ffn_mlx(const uint32_t* gw, const uint16_t* gs, const 
     if (T <= 0) return cudaSuccess;
     const MlxSrc g{gw, gs, gb, sh.I, sh.H}, u{uw, us, ub, sh.I, sh.H}, dn{dw, ds, db, sh.H, sh.I};
     dim3 g1(sh.I / kRowTile, kSplitGU, T * sh.K);
-    note_launch();
-    k_decode_gateup<MlxSrc><<<g1, 256, 0, st>>>(g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
+    {
+        const cudaError_t le_ = launch_pdl(k_decode_gateup<MlxSrc>, dim3(g1), dim3(256), 0, st, g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
+        if (le_ != cudaSuccess) return le_;
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     dim3 g2(sh.H / kRowTile, sh.K, T);
-    note_launch();
-    k_decode_down<MlxSrc><<<g2, down_threads(sh.I), 0, st>>>(dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, 1);
+    {
+        const cudaError_t le_ = launch_pdl(k_decode_down<MlxSrc>, dim3(g2), dim3(down_threads(sh.I)), 0, st, dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, 1);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 

@@ -19,6 +19,7 @@ __device__ __forceinline__ int pad_rows(int c) { return (c + kSegAlign - 1) / kS
 // and its GEMM token tiles.
 __global__ void __launch_bounds__(kDispThreads) k_dispatch(const int32_t* __restrict__ ids, int T, int E, int K,
                                                            DispatchBufs d) {
+    pdl_begin();
     __shared__ int s_red[2][kDispThreads / 32];
     __shared__ int s_warp[kDispThreads / 32];
     __shared__ int s_base;
@@ -87,6 +88,7 @@ __global__ void __launch_bounds__(kDispThreads) k_dispatch(const int32_t* __rest
 __global__ void __launch_bounds__(256) k_permute(const uint16_t* __restrict__ x, int H, const int32_t* __restrict__ src,
                                                  const int32_t* __restrict__ seg_end, int atoms,
                                                  uint16_t* __restrict__ xp) {
+    pdl_begin();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= *seg_end) return;
     const int t = src[row];
@@ -114,6 +116,7 @@ __global__ void __launch_bounds__(256) k_permute(const uint16_t* __restrict__ x,
 // out = (x / rms) * w.  IEEE divide and square root, as the oracle.
 __global__ void __launch_bounds__(256) k_rmsnorm(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
                                                  int H, float eps, uint16_t* __restrict__ out) {
+    pdl_begin();
     __shared__ float sq[256];
     const int t = blockIdx.x, l = threadIdx.x;
     const uint16_t* row = x + (size_t)t * H;
@@ -140,6 +143,7 @@ __global__ void __launch_bounds__(256) k_combine(const uint16_t* __restrict__ y,
                                                  const int32_t* __restrict__ slot_of, const float* __restrict__ w,
                                                  const uint16_t* __restrict__ residual, int H, int K,
                                                  uint16_t* __restrict__ out) {
+    pdl_begin();
     const int t = blockIdx.x;
     for (int f = threadIdx.x * 8; f < H; f += blockDim.x * 8) {
         float acc[8];
@@ -201,29 +205,37 @@ __global__ void k_tile_rows(const uint16_t* __restrict__ x, int n, int cols, int
 
 cudaError_t launch_dispatch(const int32_t* ids, const uint16_t* x, int T, const Shape& sh, const DispatchBufs& d,
                             int permute, cudaStream_t st) {
-    note_launch();
-    k_dispatch<<<sh.E, kDispThreads, 0, st>>>(ids, T, sh.E, sh.K, d);
+    {
+        const cudaError_t le_ = launch_pdl(k_dispatch, dim3(sh.E), dim3(kDispThreads), 0, st, ids, T, sh.E, sh.K, d);
+        if (le_ != cudaSuccess) return le_;
+    }
     if (!permute) return cudaGetLastError();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    note_launch();
-    k_permute<<<d.atoms, 256, 0, st>>>(x, sh.H, d.src, d.seg + sh.E, d.atoms, d.xp);  // 8 rows per CTA
+    {
+        const cudaError_t le_ = launch_pdl(k_permute, dim3(d.atoms), dim3(256), 0, st, x, sh.H, d.src, d.seg + sh.E, d.atoms, d.xp);
+        if (le_ != cudaSuccess) return le_;
+    }  // 8 rows per CTA
     return cudaGetLastError();
 }
 
 cudaError_t launch_combine(const uint16_t* y, int y_ld, const int32_t* slot_of, const float* w,
                            const uint16_t* residual, int T, int H, int K, uint16_t* out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    note_launch();
-    k_combine<<<T, 256, 0, st>>>(y, y_ld, slot_of, w, residual, H, K, out);
+    {
+        const cudaError_t le_ = launch_pdl(k_combine, dim3(T), dim3(256), 0, st, y, y_ld, slot_of, w, residual, H, K, out);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps, uint16_t* out,
                            cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    note_launch();
-    k_rmsnorm<<<T, 256, 0, st>>>(x, w, H, eps, out);
+    {
+        const cudaError_t le_ = launch_pdl(k_rmsnorm, dim3(T), dim3(256), 0, st, x, w, H, eps, out);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 

@@ -63,6 +63,7 @@ __device__ __forceinline__ T* at(uint8_t* base, size_t off) {
 // per-destination counts and stamps.
 __global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids, const uint16_t* __restrict__ x,
                                                  int T, int E, EpArgs a) {
+    pdl_begin();
     __shared__ int s_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t e = *a.epoch + 1;
@@ -107,6 +108,7 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids
 // routing problem: ids_local[s*cap + i] = local expert of row i of source s
 // (-1 beyond the source's count) and a histogram per local expert.
 __global__ void __launch_bounds__(256) k_ep_recv(EpArgs a) {
+    pdl_begin();
     const uint32_t e = *a.epoch + 1;
     uint8_t* mine = a.peer[a.rank];
     if (!wait_stamps(at<uint32_t>(mine, a.off_rflag), a.world, e, a.err)) return;
@@ -135,6 +137,7 @@ __global__ void __launch_bounds__(256) k_ep_recv(EpArgs a) {
 // source.
 __global__ void __launch_bounds__(256) k_ep_return(const int32_t* __restrict__ slot_of, const uint16_t* __restrict__ y,
                                                    EpArgs a) {
+    pdl_begin();
     __shared__ int s_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t e = *a.epoch + 1;
@@ -158,6 +161,7 @@ __global__ void __launch_bounds__(256) k_ep_return(const int32_t* __restrict__ s
 
 // Wait until every rank has returned this rank's rows, then close the epoch.
 __global__ void k_ep_finish(EpArgs a) {
+    pdl_begin();
     const uint32_t e = *a.epoch + 1;
     wait_stamps(at<uint32_t>(a.peer[a.rank], a.off_retflag), a.world, e, a.err);
     if (threadIdx.x == 0) *a.epoch = e;
@@ -168,30 +172,38 @@ __global__ void k_ep_finish(EpArgs a) {
 cudaError_t launch_ep_send(const int32_t* ids, const uint16_t* x, int T, int E, const EpArgs& a, cudaStream_t st) {
     const int items = T * a.K;
     const int grid = items > 0 ? (items + 7) / 8 : 1;  // one CTA at least: it publishes the counts
-    note_launch();
-    k_ep_send<<<grid, 256, 0, st>>>(ids, x, T, E, a);
+    {
+        const cudaError_t le_ = launch_pdl(k_ep_send, dim3(grid), dim3(256), 0, st, ids, x, T, E, a);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
 cudaError_t launch_ep_recv(const EpArgs& a, cudaStream_t st) {
     const int n = a.world * a.cap;
     const int grid = (n + 255) / 256 < 296 ? (n + 255) / 256 : 296;
-    note_launch();
-    k_ep_recv<<<grid, 256, 0, st>>>(a);
+    {
+        const cudaError_t le_ = launch_pdl(k_ep_recv, dim3(grid), dim3(256), 0, st, a);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
 cudaError_t launch_ep_return(const int32_t* slot_of, const uint16_t* y, const EpArgs& a, cudaStream_t st) {
     const int n = a.world * a.cap;
     const int grid = (n + 7) / 8 < 1184 ? (n + 7) / 8 : 1184;
-    note_launch();
-    k_ep_return<<<grid, 256, 0, st>>>(slot_of, y, a);
+    {
+        const cudaError_t le_ = launch_pdl(k_ep_return, dim3(grid), dim3(256), 0, st, slot_of, y, a);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
 cudaError_t launch_ep_finish(const EpArgs& a, cudaStream_t st) {
-    note_launch();
-    k_ep_finish<<<1, 32, 0, st>>>(a);
+    {
+        const cudaError_t le_ = launch_pdl(k_ep_finish, dim3(1), dim3(32), 0, st, a);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 

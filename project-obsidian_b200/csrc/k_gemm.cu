@@ -133,6 +133,7 @@ __device__ __forceinline__ void trace_at(const GemmArgs& a, int role, int i) {
 
 template <int EPI, bool TRACE>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
+    pdl_begin();
     using C = Cfg<EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -477,8 +478,10 @@ static cudaError_t launch_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
     auto kern = a.trace ? k_gemm<EPI, true> : k_gemm<EPI, false>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return err;
-    note_launch();
-    kern<<<num_sms, kThreads, smem, st>>>(a);
+    {
+        const cudaError_t le_ = launch_pdl(kern, dim3(num_sms), dim3(kThreads), smem, st, a);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 

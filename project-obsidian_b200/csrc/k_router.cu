@@ -9,8 +9,8 @@
 // Top-k follows moe_routing_topk.metal:31-56 (softmax in fp32, repeated
 // argmax with the lowest index winning ties, renormalise), selecting on the
 // fp32 logits so the choice depends only on bit-exact values.  For T > 16 the
-// logits are produced as eight partial subtree sums [8][T][E] (more CTAs) and
-// combined in the fixed tree by the top-k kernel.
+// logits are produced as the 32 leaf sums [32][T][E] (more CTAs) and combined in
+// the fixed tree by the top-k kernel.
 #include "obs_internal.cuh"
 
 namespace obs {
@@ -20,10 +20,12 @@ namespace {
 // One warp per (expert, token chunk).  Lane l owns group(s) l*m..; its 64
 // dequantised weights per group stay in registers across the chunk's tokens.
 constexpr int kWarpTok = 8;
+constexpr int kLeaves = 32;  // lanes of the canonical order = leaf sums of the prefill form
 
 __global__ void __launch_bounds__(256) k_router_warp(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
                                                      const uint16_t* __restrict__ b, const uint16_t* __restrict__ x,
                                                      int T, int H, int E, float* __restrict__ logits) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int t0 = blockIdx.y * kWarpTok;
@@ -76,136 +78,124 @@ __global__ void __launch_bounds__(256) k_router_warp(const uint32_t* __restrict_
 }
 
 // ---------------------------------------------------------------- prefill form
-// CTA tile: 32 tokens x 64 experts x one eighth of the 32 lanes (a 4-leaf
-// subtree of the reduction tree).  Per group the CTA stages the group's
-// dequantised weights and activations (fp32) in shared memory, the next
-// group's global loads already in flight; every (token, expert) accumulator
-// chains its group in column order and folds the lane sums into a 2-deep
-// binary-counter stack, which evaluates exactly the adjacent pairwise tree of
-// the decode form on its 4 leaves.  The eight subtree sums meet as
-// (((S0+S1)+(S2+S3))+((S4+S5)+(S6+S7))) in the top-k kernel (or k_router_finish).
-constexpr int kTT = 32, kTE = 64, kPad = 68, kSplit = 8;
+// One CTA per (64 tokens, 128 experts, leaf): a leaf is lane l's share of the
+// canonical order, groups [l*m, (l+1)*m).  The CTA stages each group's
+// dequantised weights and activations (fp32) in shared memory; each of its 128
+// threads keeps an 8 x 8 register tile of (token, expert) accumulators (tokens
+// tt + 8i, experts te + 16j: rows read by a warp are consecutive, so the padded
+// rows are conflict-free) and chains the group's 64 columns in order with
+// fused multiply-adds.  The leaf sums land in parts[leaf][T][E]; top-k (or
+// k_router_finish) adds them in the adjacent pairwise tree, which is the decode
+// form's xor-butterfly (offsets 1, 2, 4, 8, 16).  16 FMAs per 128-bit shared load.
+constexpr int kRT = 64, kRE = 128, kRPad = 68, kLeafThreads = 128;
+constexpr size_t kLeafSmem = (size_t)(kRT + kRE) * kRPad * 4;  // 52,224 bytes
 
-struct RouterStage {
-    uint32_t q[4];
-    float sc[4], bi[4];
-    uint4 xv;
-};
-
-__device__ __forceinline__ void router_load(RouterStage& r, const uint32_t* __restrict__ w,
-                                            const uint16_t* __restrict__ s, const uint16_t* __restrict__ b,
-                                            const uint16_t* __restrict__ x, int T, int H, int E, int G, int t0,
-                                            int e0, int g, int tid) {
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const int i = tid + 256 * u, el = i >> 4, wd = i & 15, e = e0 + el;
-        r.q[u] = 0, r.sc[u] = 0.0f, r.bi[u] = 0.0f;
-        if (e < E) {
-            r.q[u] = __ldg(w + (size_t)e * (H / 4) + (size_t)g * 16 + wd);
-            r.sc[u] = bf2f(s[(size_t)e * G + g]);
-            r.bi[u] = bf2f(b[(size_t)e * G + g]);
-        }
-    }
-    const int tl = tid >> 3, v = tid & 7, t = t0 + tl;
-    r.xv = make_uint4(0, 0, 0, 0);
-    if (t < T) r.xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + (size_t)g * 64) + v);
-}
-
-__global__ void __launch_bounds__(256) k_router_tiled(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
-                                                      const uint16_t* __restrict__ b, const uint16_t* __restrict__ x,
-                                                      int T, int H, int E, float* __restrict__ parts) {
-    __shared__ __align__(16) float ws[kTE][kPad];
-    __shared__ __align__(16) float xs[kTT][kPad];
-    const int tid = threadIdx.x;
-    const int tt = tid & 15, te = tid >> 4;  // 16 x 16 threads; micro-tile 2 tokens x 4 experts
-    const int t0 = blockIdx.x * kTT, e0 = blockIdx.y * kTE, split = blockIdx.z;
+__global__ void __launch_bounds__(kLeafThreads) k_router_leaf(const uint32_t* __restrict__ w,
+                                                              const uint16_t* __restrict__ s,
+                                                              const uint16_t* __restrict__ b,
+                                                              const uint16_t* __restrict__ x, int T, int H, int E,
+                                                              float* __restrict__ parts) {
+    pdl_begin();
+    extern __shared__ __align__(16) float rsm[];
+    float(*xs)[kRPad] = reinterpret_cast<float(*)[kRPad]>(rsm);
+    float(*ws)[kRPad] = reinterpret_cast<float(*)[kRPad]>(rsm + kRT * kRPad);
+    const int tid = threadIdx.x, tt = tid & 7, te = tid >> 3;
+    const int t0 = blockIdx.x * kRT, e0 = blockIdx.y * kRE, leaf = blockIdx.z;
     const int G = H / kGroup, m = G / 32;
-    const int g0 = split * 4 * m, g1 = g0 + 4 * m;  // this eighth's groups (leaves split*4 .. +3)
-    float lane_acc[2][4], st0[2][4], st1[2][4];
+    float acc[8][8];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) lane_acc[i][j] = st0[i][j] = st1[i][j] = 0.0f;
-
-    RouterStage nxt;
-    router_load(nxt, w, s, b, x, T, H, E, G, t0, e0, g0, tid);
-    for (int g = g0; g < g1; ++g) {
-        __syncthreads();
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    for (int g = leaf * m; g < (leaf + 1) * m; ++g) {
+        __syncthreads();  // the previous group's tiles are consumed
+        // activations: 32 tokens x 64 columns bf16 -> fp32 (8 columns per uint4)
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = tid + 256 * u, el = i >> 4, wd = i & 15;
-            float f[4];
+        for (int u = 0; u < kRT * 8 / kLeafThreads; ++u) {
+            const int i = tid + kLeafThreads * u, r = i >> 3, c8 = i & 7, t = t0 + r;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (t < T) v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + (size_t)g * 64) + c8);
+            const uint32_t q[4] = {v.x, v.y, v.z, v.w};
+            float* d = &xs[r][c8 * 8];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) f[j] = __fmaf_rn((float)((nxt.q[u] >> (8 * j)) & 0xFFu), nxt.sc[u], nxt.bi[u]);
-            *reinterpret_cast<float4*>(&ws[el][wd * 4]) = make_float4(f[0], f[1], f[2], f[3]);
+            for (int c = 0; c < 4; ++c) d[2 * c] = __uint_as_float(q[c] << 16), d[2 * c + 1] = __uint_as_float(q[c] & 0xFFFF0000u);
         }
-        {
-            const uint32_t qs[4] = {nxt.xv.x, nxt.xv.y, nxt.xv.z, nxt.xv.w};
-            float* d = &xs[tid >> 3][(tid & 7) * 8];
+        // weights: 128 experts x 64 codes (16 per uint4), w = q * s + b (dequant_matvec_8bit.metal:26)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                d[2 * c] = __uint_as_float(qs[c] << 16);
-                d[2 * c + 1] = __uint_as_float(qs[c] & 0xFFFF0000u);
+        for (int u = 0; u < kRE * 4 / kLeafThreads; ++u) {
+            const int i = tid + kLeafThreads * u, r = i >> 2, c16 = i & 3, e = e0 + r;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            float sc = 0.0f, bi = 0.0f;
+            if (e < E) {
+                v = __ldg(reinterpret_cast<const uint4*>(w + (size_t)e * (H / 4) + (size_t)g * 16) + c16);
+                sc = bf2f(s[(size_t)e * G + g]);
+                bi = bf2f(b[(size_t)e * G + g]);
             }
+            const uint32_t q[4] = {v.x, v.y, v.z, v.w};
+            float* d = &ws[r][c16 * 16];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) d[4 * c + j] = __fmaf_rn((float)((q[c] >> (8 * j)) & 0xFFu), sc, bi);
         }
         __syncthreads();
-        if (g + 1 < g1) router_load(nxt, w, s, b, x, T, H, E, G, t0, e0, g + 1, tid);
-#pragma unroll 4
+#pragma unroll 2
         for (int j = 0; j < 64; j += 4) {
-            float4 xv[2], wv[4];
+            float4 xv[8], wv[8];
 #pragma unroll
-            for (int i = 0; i < 2; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[tt + 16 * i][j]);
+            for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[tt + 8 * i][j]);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) wv[i] = *reinterpret_cast<const float4*>(&ws[te + 16 * i][j]);
+            for (int i = 0; i < 8; ++i) wv[i] = *reinterpret_cast<const float4*>(&ws[te + 16 * i][j]);
+            // column by column: 64 independent FMAs per column, each chain in column order
 #pragma unroll
-            for (int a = 0; a < 2; ++a)
+            for (int a = 0; a < 8; ++a)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float acc = lane_acc[a][c];
-                    acc = __fmaf_rn(wv[c].x, xv[a].x, acc);
-                    acc = __fmaf_rn(wv[c].y, xv[a].y, acc);
-                    acc = __fmaf_rn(wv[c].z, xv[a].z, acc);
-                    acc = __fmaf_rn(wv[c].w, xv[a].w, acc);
-                    lane_acc[a][c] = acc;
-                }
-        }
-        if (((g - g0) % m) == m - 1) {
-            const int leaf = (g - g0) / m;  // 0..3 inside this subtree
+                for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].x, xv[a].x, acc[a][c]);
 #pragma unroll
-            for (int a = 0; a < 2; ++a)
+            for (int a = 0; a < 8; ++a)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float v = lane_acc[a][c];
-                    lane_acc[a][c] = 0.0f;
-                    if (leaf & 1) {
-                        v = __fadd_rn(st0[a][c], v);
-                        if (leaf & 2) v = __fadd_rn(st1[a][c], v);
-                        st1[a][c] = v;
-                    } else {
-                        st0[a][c] = v;
-                    }
-                }
+                for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].y, xv[a].y, acc[a][c]);
+#pragma unroll
+            for (int a = 0; a < 8; ++a)
+#pragma unroll
+                for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].z, xv[a].z, acc[a][c]);
+#pragma unroll
+            for (int a = 0; a < 8; ++a)
+#pragma unroll
+                for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].w, xv[a].w, acc[a][c]);
         }
     }
+    // leaf sums out through shared memory ([token][expert]) for coalesced stores
+    __syncthreads();
+    float(*os)[kRE + 4] = reinterpret_cast<float(*)[kRE + 4]>(rsm);
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
+    for (int a = 0; a < 8; ++a)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            int t = t0 + tt + 16 * a, e = e0 + te + 16 * c;
-            if (t < T && e < E) parts[((size_t)split * T + t) * E + e] = st1[a][c];
-        }
+        for (int c = 0; c < 8; ++c) os[tt + 8 * a][te + 16 * c] = acc[a][c];
+    __syncthreads();
+    float* pl = parts + (size_t)leaf * T * E;
+    for (int i = tid; i < kRT * kRE; i += kLeafThreads) {
+        const int r = i / kRE, c = i % kRE, t = t0 + r, e = e0 + c;
+        if (t < T && e < E) pl[(size_t)t * E + e] = os[r][c];
+    }
 }
 
-// logits = (((S0+S1)+(S2+S3))+((S4+S5)+(S6+S7))) of the eight subtree sums
-__device__ __forceinline__ float tree8(const float* __restrict__ p, size_t plane, size_t i) {
-    const float a = __fadd_rn(__fadd_rn(p[i], p[plane + i]), __fadd_rn(p[2 * plane + i], p[3 * plane + i]));
-    const float c = __fadd_rn(__fadd_rn(p[4 * plane + i], p[5 * plane + i]), __fadd_rn(p[6 * plane + i], p[7 * plane + i]));
-    return __fadd_rn(a, c);
+// logit = the adjacent pairwise tree over the 32 leaf sums
+__device__ __forceinline__ float tree32(const float* __restrict__ p, size_t plane, size_t i) {
+    float v[16];
+#pragma unroll
+    for (int l = 0; l < 16; ++l) v[l] = __fadd_rn(p[(2 * l) * plane + i], p[(2 * l + 1) * plane + i]);
+#pragma unroll
+    for (int n = 8; n > 0; n >>= 1)
+#pragma unroll
+        for (int l = 0; l < n; ++l) v[l] = __fadd_rn(v[2 * l], v[2 * l + 1]);
+    return v[0];
 }
 
 __global__ void k_router_finish(const float* __restrict__ parts, size_t n, float* __restrict__ logits) {
+    pdl_begin();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        logits[i] = tree8(parts, n, i);
+        logits[i] = tree32(parts, n, i);
 }
 
 // ---------------------------------------------------------------------- top-k
@@ -227,6 +217,7 @@ __global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, 
                                               const float* __restrict__ bias, int T, int E, int K, int norm,
                                               int32_t* __restrict__ ids, float* __restrict__ wout,
                                               int32_t* __restrict__ counts, float* __restrict__ logits_out) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= T) return;
@@ -239,7 +230,7 @@ __global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, 
         key[i] = 0;  // below every real key: never selected
         if (e < E) {
             const size_t idx = (size_t)t * E + e;
-            float l = nparts == kSplit ? tree8(logits, plane, idx) : logits[idx];
+            float l = nparts == kLeaves ? tree32(logits, plane, idx) : logits[idx];
             if (logits_out) logits_out[idx] = l;
             l = __fadd_rn(l, bias ? bias[e] : 0.0f);
             key[i] = order_key(l);
@@ -281,19 +272,27 @@ __global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, 
 
 }  // namespace
 
-int router_parts(int T) { return T <= 2 * kWarpTok ? 1 : kSplit; }
+int router_parts(int T) { return T <= 2 * kWarpTok ? 1 : kLeaves; }
 
 cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint16_t* x, int T, float* parts,
                                  cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (router_parts(T) == 1) {
         dim3 grid((sh.E + 7) / 8, (T + kWarpTok - 1) / kWarpTok);
-        note_launch();
-        k_router_warp<<<grid, 256, 0, st>>>(L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E, parts);
+        {
+            const cudaError_t le_ = launch_pdl(k_router_warp, dim3(grid), dim3(256), 0, st, L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E, parts);
+            if (le_ != cudaSuccess) return le_;
+        }
     } else {
-        dim3 grid((T + kTT - 1) / kTT, (sh.E + kTE - 1) / kTE, kSplit);
-        note_launch();
-        k_router_tiled<<<grid, 256, 0, st>>>(L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E, parts);
+        cudaError_t e = cudaFuncSetAttribute(k_router_leaf, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kLeafSmem);  // 52 KB of dynamic shared memory
+        if (e != cudaSuccess) return e;
+        dim3 grid((T + kRT - 1) / kRT, (sh.E + kRE - 1) / kRE, kLeaves);
+        {
+            const cudaError_t le_ = launch_pdl(k_router_leaf, dim3(grid), dim3(kLeafThreads), kLeafSmem, st, L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E,
+                                                              parts);
+            if (le_ != cudaSuccess) return le_;
+        }
     }
     return cudaGetLastError();
 }
@@ -301,8 +300,10 @@ cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint1
 cudaError_t launch_router_finish(const float* parts, int T, int E, float* logits, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     size_t n = (size_t)T * E;
-    note_launch();
-    k_router_finish<<<(int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096), 256, 0, st>>>(parts, n, logits);
+    {
+        const cudaError_t le_ = launch_pdl(k_router_finish, dim3((int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096)), dim3(256), 0, st, parts, n, logits);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 
@@ -310,8 +311,10 @@ cudaError_t launch_topk(const float* logits, int nparts, const float* bias, int 
                         int32_t* ids, float* w, int32_t* counts, float* logits_out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (E > kMaxE || K > kMaxK || K > 32) return cudaErrorInvalidValue;
-    note_launch();
-    k_topk<<<(T + 7) / 8, 256, 0, st>>>(logits, nparts, bias, T, E, K, norm, ids, w, counts, logits_out);
+    {
+        const cudaError_t le_ = launch_pdl(k_topk, dim3((T + 7) / 8), dim3(256), 0, st, logits, nparts, bias, T, E, K, norm, ids, w, counts, logits_out);
+        if (le_ != cudaSuccess) return le_;
+    }
     return cudaGetLastError();
 }
 

@@ -49,6 +49,17 @@ __device__ __forceinline__ size_t tiled_off(int row, int col, int atoms) {
 // the bf16 rounding of h).
 __device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
 
+// Programmatic dependent launch (griddepcontrol): every kernel of the layer
+// forward lets the next kernel of its stream be scheduled as soon as all of its
+// own CTAs have started, and waits for the previous kernel to complete (and its
+// memory to be visible) before touching anything that kernel wrote.  The next
+// kernel's launch latency overlaps this kernel's tail.  Both are no-ops for a
+// kernel launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ------------------------------------------------------------ time / waits
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;

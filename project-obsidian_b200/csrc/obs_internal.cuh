@@ -4,12 +4,33 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "obs_common.cuh"
 
 namespace obs {
 
 // Counts every kernel launch the library issues (obs_kernel_launches).
 void note_launch();
+
+// Launch with programmatic stream serialization (the kernel calls pdl_begin()
+// first): it may be scheduled while the previous kernel of the stream finishes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    note_launch();
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // One 128-row x 64-column block of a tiled 4-bit projection (4608 bytes):
 // words 0-3 of the 128 rows, words 4-7 of the 128 rows, 128 bf16 scales,
@@ -41,8 +62,8 @@ cudaError_t launch_retile(const uint32_t* w, const uint16_t* s, const uint16_t* 
 
 // --------------------------------------------------------------- k_router.cu
 // Router logits for T tokens: router_parts(T) partial planes [parts][T][E]
-// (1: final logits; 8: subtree sums that launch_topk / launch_router_finish
-// combine in the fixed tree).  `parts` must hold 8*T*E floats.
+// (1: final logits; 32: leaf sums that launch_topk / launch_router_finish
+// combine in the fixed tree).  `parts` must hold 32*T*E floats.
 int router_parts(int T);
 cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint16_t* x, int T, float* parts,
                                  cudaStream_t st);
