@@ -63,6 +63,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=32, help="config 2: tokens per decode step (1, 8, 32, 128)")
     ap.add_argument("--layers", type=int, default=48, help="configs 2 and 3: layers in the stack")
+    ap.add_argument("--tokens", type=int, default=0, help="configs 0 and 1: override T (a sweep point, not a BASELINE config)")
     return ap.parse_args()
 
 
@@ -405,7 +406,9 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.tokens:
+        cfg["T"], cfg["name"] = args.tokens, cfg["name"].split(",")[0] + f", T={args.tokens} tokens (sweep)"
     T = cfg["T"]
     ep = world > 1  # N GPUs: expert parallelism, E/N experts per GPU, each GPU routes its own T tokens
     path = obsmoe.PATH_DECODE if T <= 4 and not ep else obsmoe.PATH_PREFILL
@@ -525,6 +528,13 @@ def main():
         # gate+up weights of the U routed experts (this GPU's), the routed rows read, h written
         alg = U_mean * GATEUP_BYTES + R_mean * H * 2 + R_mean * I * 2
         kname = "k_gemm<kEpiSwiglu> (tcgen05 grouped gate/up GEMM + SwiGLU)"
+    elif prof["decode_fused"][1]:
+        top = "decode_fused"
+        # the whole decode layer in one launch: router weights, all three projections
+        # of the U routed experts, x read, out written
+        alg = ROUTER_BYTES + U_mean * EXPERT_BYTES + 2 * T * H * 2
+        kname = ("k_decode_fused (whole decode layer: router, top-k, 4-bit gate/up and down mat-vec, "
+                 "combine; one cooperative launch)")
     else:
         top = "decode_gateup"
         alg = U_mean * GATEUP_BYTES + T * H * 2 + T * K * I * 2

@@ -146,10 +146,11 @@ int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert, const uin
  * every kernel launch of the layer is bracketed by CUDA events on the
  * caller's stream.  obs_profile_read fills ms_total[OBS_N_STAGES] and
  * launches[OBS_N_STAGES] with the sums since the last read, then resets. */
-#define OBS_N_STAGES 8
+#define OBS_N_STAGES 9
 enum obs_stage {
     OBS_STAGE_ROUTER = 0, OBS_STAGE_TOPK = 1, OBS_STAGE_DISPATCH = 2, OBS_STAGE_GEMM_GATEUP = 3,
-    OBS_STAGE_GEMM_DOWN = 4, OBS_STAGE_COMBINE = 5, OBS_STAGE_DECODE_GATEUP = 6, OBS_STAGE_DECODE_DOWN = 7
+    OBS_STAGE_GEMM_DOWN = 4, OBS_STAGE_COMBINE = 5, OBS_STAGE_DECODE_GATEUP = 6, OBS_STAGE_DECODE_DOWN = 7,
+    OBS_STAGE_DECODE_FUSED = 8  /* the whole decode layer in one launch (T <= 4) */
 };
 int obs_profile_enable(obs_ctx* ctx, int enable);
 int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches);

@@ -14,7 +14,7 @@
 //
 // The kernels read either the context's tiled 4608-byte blocks or the
 // reference's MLX row-major layout directly.
-#include "obs_internal.cuh"
+#include "router_dev.cuh"
 
 namespace obs {
 namespace {
@@ -27,8 +27,13 @@ __device__ __forceinline__ float nib_f16th(uint32_t w, int j) {
     return __uint_as_float((m & 0x00780000u) | 0x3F800000u);
 }
 
-// Weight sources: 128 rows x 64 columns of one projection of one expert.
+// Weight sources: 128 rows x 64 columns of one block of one expert.
 // Lane l covers rows (l>>1) + 16 i (i < 8) and the 32 columns of half (l & 1).
+// The context's gate/up array is paired: the 128 features of gate/up row tile rt
+// are blocks 2rt and 2rt+1, and feature c of block h sits in row paired_row(c)
+// (gate) and paired_row(c) + 16 (up).  Each row's dot product is the same
+// arithmetic whichever block it sits in; only the final pairing re-indexes.
+__device__ __forceinline__ int paired_row(int c) { return 32 * (c >> 4) + (c & 15); }
 struct TiledSrc {  // the context's blocks; nibble order c0,c2,c4,c6,c1,c3,c5,c7
     const uint8_t* base;
     int n_rt, KT, stride, off;  // block (e, rt, kt) = base + (((e*n_rt + rt)*KT + kt)*stride + off) * 4608
@@ -129,7 +134,7 @@ __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const
         const int kt = ks * nkt + j;
         float xr[32];
         const float xs = load_x32(x + (size_t)t * H + kt * kGroup + (lane & 1) * 32, xr);
-        block_dot(proj ? usrc : gsrc, e, rt, kt, xr, xs, lane, acc);
+        block_dot(proj ? usrc : gsrc, e, Src::kNatural ? rt : 2 * rt + proj, kt, xr, xs, lane, acc);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -137,7 +142,7 @@ __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const
         if ((lane & 1) == 0) s_part[w][(lane >> 1) + 16 * i] = v;
     }
     __syncthreads();
-    // fixed-order sum of the 4 warps of each projection
+    // fixed-order sum of the 4 warps of each projection (paired blocks: of each block)
     const int pr = tid >> 7, row = tid & 127;
     const float v = ((s_part[pr][row] + s_part[pr + 2][row]) + s_part[pr + 4][row]) + s_part[pr + 6][row];
     float* part = d.part + (((size_t)p * n_rt + rt) * kSplitGU) * 2 * kRowTile;
@@ -159,7 +164,13 @@ __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const
     s_gu[pr][row] = sum;
     __syncthreads();
     if (tid < kRowTile) {
-        const float g = s_gu[0][tid], u = s_gu[1][tid];
+        float g, u;
+        if constexpr (Src::kNatural) {
+            g = s_gu[0][tid], u = s_gu[1][tid];
+        } else {
+            const int rr = paired_row(tid & 63);  // block 2rt + tid/64 holds feature tid
+            g = s_gu[tid >> 6][rr], u = s_gu[tid >> 6][rr + 16];
+        }
         d.h[(size_t)p * I + rt * kRowTile + tid] = f2bf(silu_mul(g, u));
     }
 }
@@ -221,12 +232,220 @@ __global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __
 
 int down_threads(int I) { return 32 * (I / kGroup < 16 ? I / kGroup : 16); }
 
+// ----------------------------------------------------------- fused decode layer
+// One cooperative launch runs the whole decode layer for T <= 4 tokens, so the
+// step pays one launch instead of four dependent ones.  One CTA of 16 warps per
+// SM; work units go round-robin over the CTAs first, so every SM works.
+//   A  router logits: one warp per (expert, 8-token chunk), canonical order;
+//      grid barrier;
+//   B  top-k: every CTA computes the routes of all T tokens itself (identical,
+//      deterministic), so no barrier follows;
+//   C  gate/up: each half-CTA (8 warps) runs one CTA of k_decode_gateup -- a
+//      (pair, row tile, split) unit, its shared-memory reduction, and, in the
+//      last split to arrive, the split sum and SwiGLU over 256 threads;
+//      grid barrier;
+//   D  down: each CTA runs one CTA of k_decode_down -- a (pair, row tile) unit,
+//      y, and in the last pair of a (token, row tile) the rank-order combine.
+// The arithmetic is that of the separate decode kernels, term for term, so the
+// two forms give identical outputs.  Barriers wait at most 2 s.
+constexpr int kFusedThreads = 512, kFusedWarps = kFusedThreads / 32;
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// every CTA of the grid; false (error flag set) after a timeout
+__device__ bool grid_sync(uint32_t* bar, uint32_t target, int* err) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(bar, 1u);
+        int ok = 1;
+        const uint64_t t0 = global_ns();
+        while (ld_acquire_gpu(bar) < target) {
+            if (global_ns() - t0 > kWaitLimitNs) {
+                ok = 0;
+                atomicExch(err, kDevTimeout);
+                break;
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+// load_x32 for data written earlier in this kernel (read through L2)
+__device__ __forceinline__ float load_x32_cg(const uint16_t* __restrict__ x, float (&xr)[32]) {
+    const uint4* p = reinterpret_cast<const uint4*>(x);
+    float sum = 0.0f;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        uint4 q = __ldcg(p + v);
+        uint32_t qs[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            xr[v * 8 + 2 * c] = __uint_as_float(qs[c] << 16);
+            xr[v * 8 + 2 * c + 1] = __uint_as_float(qs[c] & 0xFFFF0000u);
+            sum += xr[v * 8 + 2 * c] + xr[v * 8 + 2 * c + 1];
+        }
+    }
+    return sum;
+}
+
+__global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
+    const uint32_t* __restrict__ rw, const uint16_t* __restrict__ rs, const uint16_t* __restrict__ rb,
+    TiledSrc gsrc, TiledSrc dsrc, const uint16_t* __restrict__ x, const uint16_t* __restrict__ residual,
+    const float* __restrict__ bias, int T, int H, int I, int E, int K, int norm, FusedDecodeBufs f,
+    uint16_t* __restrict__ out) {
+    __shared__ int s_ids[kFusedMaxT * kMaxK];
+    __shared__ float s_wts[kFusedMaxT * kMaxK];
+    __shared__ float s_part[kFusedWarps][kRowTile];  // C: [half][8 warps]; D: [16 warps]
+    __shared__ float s_gu[2][2][kRowTile];            // C: [half][block][row]
+    __shared__ int s_last[2];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = gridDim.x, b = blockIdx.x;
+
+    // A: router logits; item i on warp i / G of CTA i % G
+    const int n_tc = (T + kWarpTok - 1) / kWarpTok;
+    for (int item = warp * G + b; item < E * n_tc; item += kFusedWarps * G)
+        router_warp_item(rw, rs, rb, x, T, H, E, item % E, (item / E) * kWarpTok, lane, f.logits);
+    if (!grid_sync(f.bar, G, f.err)) return;
+
+    // B: top-k of every token, in every CTA
+    if (warp < T) {
+        const int t = warp;
+        auto logit = [&](int e) { return __ldcg(f.logits + (size_t)t * E + e); };
+        int ik;
+        float wk;
+        topk_token(logit, bias, E, K, norm, lane, &ik, &wk);
+        if (lane < K) {
+            s_ids[t * K + lane] = ik;
+            s_wts[t * K + lane] = wk;
+            if (b == 0) f.ids[t * K + lane] = ik, f.wts[t * K + lane] = wk;
+        }
+    }
+    __syncthreads();
+
+    // C: gate/up -- half-CTA h takes units (pair p, row tile rt, split ks) like one
+    // CTA of k_decode_gateup: warp w8 = block half (w8 & 1) of paired blocks
+    // 2rt, 2rt+1, k-tiles ks*nkt + (w8 >> 1) + 4j
+    {
+        const int h = warp >> 3, w8 = warp & 7, t256 = tid & 255, half = w8 & 1;
+        const int n_rt = I / kRowTile, KT = H / kGroup, nkt = KT / kSplitGU, n_pairs = T * K;
+        const int units = n_pairs * n_rt * kSplitGU;
+        float* part = f.part_gu;  // [p][rt][ks][2][128]
+        for (int u = h * G + b; u < units; u += 2 * G) {
+            const int ks = u % kSplitGU, rt = (u / kSplitGU) % n_rt, p = u / (kSplitGU * n_rt);
+            const int t = p / K, e = checked_expert(s_ids[p], E, f.err);
+            float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int j = (w8 >> 1); j < nkt; j += 4) {
+                const int kt = ks * nkt + j;
+                float xr[32];
+                const float xs = load_x32(x + (size_t)t * H + kt * kGroup + (lane & 1) * 32, xr);
+                block_dot(gsrc, e, 2 * rt + half, kt, xr, xs, lane, acc);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float v = acc[i] + __shfl_xor_sync(0xffffffffu, acc[i], 1);
+                if ((lane & 1) == 0) s_part[h * 8 + w8][(lane >> 1) + 16 * i] = v;
+            }
+            named_bar_sync(1 + h, 256);
+            // fixed-order sum of the 4 warps of each block
+            const int pr = t256 >> 7, row = t256 & 127;
+            const float* sp = &s_part[h * 8][0];
+            const float v = ((sp[pr * kRowTile + row] + sp[(pr + 2) * kRowTile + row]) + sp[(pr + 4) * kRowTile + row]) +
+                            sp[(pr + 6) * kRowTile + row];
+            float* tp = part + (((size_t)p * n_rt + rt) * kSplitGU) * 2 * kRowTile;
+            tp[(size_t)ks * 2 * kRowTile + pr * kRowTile + row] = v;
+            __threadfence();
+            named_bar_sync(1 + h, 256);
+            if (t256 == 0) {
+                uint32_t* c = f.cnt_gu + (size_t)p * n_rt + rt;
+                const unsigned old = atomicAdd(c, 1u);
+                s_last[h] = (old == kSplitGU - 1);
+                if (s_last[h]) *c = 0;  // ready for the next call
+            }
+            named_bar_sync(1 + h, 256);
+            if (s_last[h]) {
+                __threadfence();
+                float sum = 0.0f;
+#pragma unroll
+                for (int jj = 0; jj < kSplitGU; ++jj) sum += __ldcg(tp + (size_t)jj * 2 * kRowTile + pr * kRowTile + row);
+                s_gu[h][pr][row] = sum;
+                named_bar_sync(1 + h, 256);
+                if (t256 < kRowTile) {
+                    const int rr = paired_row(t256 & 63);  // block 2rt + t/64 holds feature t
+                    const float g = s_gu[h][t256 >> 6][rr], uu = s_gu[h][t256 >> 6][rr + 16];
+                    f.h[(size_t)p * I + rt * kRowTile + t256] = f2bf(silu_mul(g, uu));
+                }
+            }
+            named_bar_sync(1 + h, 256);  // s_part / s_gu / s_last free for the next unit
+        }
+    }
+    if (!grid_sync(f.bar, 2 * G, f.err)) return;
+
+    // D: down -- CTA units (pair p, row tile rt) like one CTA of k_decode_down
+    {
+        const int n_rd = H / kRowTile, KTd = I / kGroup, nwd = KTd < 16 ? KTd : 16, n_pairs = T * K;
+        for (int u = b; u < n_pairs * n_rd; u += G) {
+            const int rt = u % n_rd, p = u / n_rd, t = p / K;
+            const int e = checked_expert(s_ids[p], E, f.err);
+            if (warp < nwd) {
+                float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                for (int kt = warp; kt < KTd; kt += nwd) {
+                    float xr[32];
+                    const float xs = load_x32_cg(f.h + (size_t)p * I + kt * kGroup + (lane & 1) * 32, xr);
+                    block_dot(dsrc, e, rt, kt, xr, xs, lane, acc);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float v = acc[i] + __shfl_xor_sync(0xffffffffu, acc[i], 1);
+                    if ((lane & 1) == 0) s_part[warp][(lane >> 1) + 16 * i] = v;
+                }
+            }
+            __syncthreads();
+            if (tid < kRowTile) {
+                float v = 0.0f;
+                for (int j = 0; j < nwd; ++j) v += s_part[j][tid];
+                f.y[(size_t)p * H + rt * kRowTile + tid] = f2bf(v);
+            }
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) {
+                uint32_t* c = f.cnt_dn + (size_t)t * n_rd + rt;
+                const unsigned old = atomicAdd(c, 1u);
+                s_last[0] = (old == (unsigned)K - 1);
+                if (s_last[0]) *c = 0;
+            }
+            __syncthreads();
+            if (s_last[0]) {
+                __threadfence();
+                if (tid < kRowTile) {
+                    // rank-order combine, same operation order as k_combine (forward.rs:225-232)
+                    const int fo = rt * kRowTile + tid;
+                    float a = residual ? bf2f(residual[(size_t)t * H + fo]) : 0.0f;
+                    for (int jk = 0; jk < K; ++jk) {
+                        const uint16_t yv = __ldcg(f.y + ((size_t)t * K + jk) * H + fo);
+                        a = __fmaf_rn(s_wts[t * K + jk], bf2f(yv), a);
+                    }
+                    out[(size_t)t * H + fo] = f2bf(a);
+                }
+            }
+            __syncthreads();  // s_part / s_last free for the next unit
+        }
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_decode_gateup(const LayerDev& L, const Shape& sh, const uint16_t* x, const int32_t* ids, int T,
                                  const DecodeBufs& d, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    const TiledSrc g{L.gateup, sh.I / kRowTile, sh.H / kGroup, 2, 0}, u{L.gateup, sh.I / kRowTile, sh.H / kGroup, 2, 1};
+    const TiledSrc g{L.gateup, sh.I / 64, sh.H / kGroup, 1, 0}, u = g;  // paired blocks
     dim3 grid(sh.I / kRowTile, kSplitGU, T * sh.K);
     {
         const cudaError_t le_ = launch_pdl(k_decode_gateup<TiledSrc>, dim3(grid), dim3(256), 0, st, g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
@@ -247,6 +466,29 @@ cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();
+}
+
+cudaError_t launch_decode_fused(const LayerDev& L, const Shape& sh, const uint16_t* x, const uint16_t* residual,
+                                const float* bias, int T, int norm, const FusedDecodeBufs& f, uint16_t* out,
+                                int num_sms, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (T > kFusedMaxT || sh.K > kMaxK || sh.E > kMaxE) return cudaErrorInvalidValue;
+    const TiledSrc g{L.gateup, sh.I / 64, sh.H / kGroup, 1, 0};  // paired blocks
+    const TiledSrc dn{L.down, sh.H / kRowTile, sh.I / kGroup, 1, 0};
+    cudaError_t e = cudaMemsetAsync(f.bar, 0, 4, st);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms);  // one CTA per SM: every CTA is resident (cooperative)
+    cfg.blockDim = dim3(kFusedThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    note_launch();
+    return cudaLaunchKernelEx(&cfg, k_decode_fused, L.router_w, L.router_s, L.router_b, g, dn, x, residual, bias, T,
+                              sh.H, sh.I, sh.E, sh.K, norm, f, out);
 }
 
 cudaError_t launch_decode_ffn_mlx(const uint32_t* gw, const uint16_t* gs, const uint16_t* gb, const uint32_t* uw,

@@ -100,25 +100,30 @@ __device__ __forceinline__ uint4 nib_order(uint4 v) {
     return make_uint4(nib_order(v.x), nib_order(v.y), nib_order(v.z), nib_order(v.w));
 }
 
-// Thread per (block, row): 8 packed words + scale + bias.  Group size 64 equals
-// the block width, so block kt uses scale/bias column kt.  Rows' first and
-// second 16-byte halves go to separate 2 KB planes of the block, so 16-byte
-// reads by consecutive rows are contiguous.
+// Thread per (block, source row): 8 packed words + scale + bias.  Group size 64
+// equals the block width, so block kt uses scale/bias column kt.  Rows' first
+// and second 16-byte halves go to separate 2 KB planes of the block, so 16-byte
+// reads by consecutive rows are contiguous.  Unpaired: 128-row tiles, block row
+// = tile row.  Paired (the gate/up array): 64-row tiles of each projection,
+// tile feature c -> block row 32*(c/16) + 16*proj + c%16, so TMEM lane quarter
+// q holds gate and up of the same 16 features.
 __global__ void k_retile(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
                          const uint16_t* __restrict__ b, int E, int out_f, int in_f, uint8_t* __restrict__ dst,
-                         int interleave, int p) {
-    const int n_rt = out_f / kRowTile, n_kt = in_f / kGroup;
+                         int paired, int proj) {
+    const int tile_rows = paired ? kRowTile / 2 : kRowTile;
+    const int n_rt = out_f / tile_rows, n_kt = in_f / kGroup;
     const size_t nblk = (size_t)E * n_rt * n_kt;
-    const size_t total = nblk * kRowTile;
+    const size_t total = nblk * tile_rows;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        int r = (int)(i % kRowTile);
-        size_t blk = i / kRowTile;
-        int kt = (int)(blk % n_kt);
-        int rt = (int)((blk / n_kt) % n_rt);
-        int e = (int)(blk / ((size_t)n_kt * n_rt));
-        size_t row = (size_t)e * out_f + (size_t)rt * kRowTile + r;
+        const int c = (int)(i % tile_rows);
+        const size_t blk = i / tile_rows;
+        const int kt = (int)(blk % n_kt);
+        const int rt = (int)((blk / n_kt) % n_rt);
+        const int e = (int)(blk / ((size_t)n_kt * n_rt));
+        const size_t row = (size_t)e * out_f + (size_t)rt * tile_rows + c;
+        const int r = paired ? 32 * (c >> 4) + 16 * proj + (c & 15) : c;
         const uint4* src = reinterpret_cast<const uint4*>(w + row * (in_f / 8) + (size_t)kt * 8);
-        uint8_t* d = dst + (blk * interleave + p) * (size_t)kBlockBytes;
+        uint8_t* d = dst + blk * (size_t)kBlockBytes;
         *reinterpret_cast<uint4*>(d + r * 16) = nib_order(src[0]);         // words 0-3
         *reinterpret_cast<uint4*>(d + 2048 + r * 16) = nib_order(src[1]);  // words 4-7
         uint16_t* ds = reinterpret_cast<uint16_t*>(d + kBlockWords * 4);
@@ -163,10 +168,10 @@ cudaError_t launch_synth_x(uint64_t seed, uint32_t layer, int row0, int T, int H
 }
 
 cudaError_t launch_retile(const uint32_t* w, const uint16_t* s, const uint16_t* b, int E, int out_f, int in_f,
-                          uint8_t* dst, int interleave, int p, cudaStream_t st) {
-    size_t total = (size_t)E * (out_f / kRowTile) * (in_f / kGroup) * kRowTile;
+                          uint8_t* dst, int paired, int proj, cudaStream_t st) {
+    const size_t total = (size_t)E * out_f * (in_f / kGroup);  // one thread per (source row, k-tile)
     note_launch();
-    k_retile<<<grid_for(total, 256), 256, 0, st>>>(w, s, b, E, out_f, in_f, dst, interleave, p);
+    k_retile<<<grid_for(total, 256), 256, 0, st>>>(w, s, b, E, out_f, in_f, dst, paired, proj);
     return cudaGetLastError();
 }
 

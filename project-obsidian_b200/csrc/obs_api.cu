@@ -24,7 +24,7 @@ using namespace obs;
 
 namespace {
 constexpr int kDecodeMaxT = 64;  // largest T the decode path's scratch covers
-constexpr int kBNTile = 64;      // GEMM token tile (gemm_tile_rows())
+constexpr int kBNTile = 128;     // GEMM token tile (gemm_tile_rows())
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 }  // namespace
@@ -48,6 +48,7 @@ struct obs_ctx {
     uint16_t* ybuf = nullptr;
     float* yf32 = nullptr;
     DecodeBufs dec{};
+    FusedDecodeBufs fused{};
     int* err_flag = nullptr;
     uint16_t* x_dev = nullptr;
     uint16_t* out_dev = nullptr;
@@ -140,7 +141,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     };
     if (cfg->group_size != 64) return bad("group_size must be 64");
     if (s.H <= 0 || s.H % 2048) return bad("hidden must be a multiple of 2048");
-    if (s.I <= 0 || s.I % kRowTile) return bad("inter must be a multiple of 128");
+    if (s.I <= 0 || s.I % 256) return bad("inter must be a multiple of 256");
     if (s.E <= 0 || s.E > 256) return bad("n_experts must be in 1..256");
     if (s.K <= 0 || s.K > 16 || s.K > s.E) return bad("top_k must be in 1..min(16, n_experts)");
     if (cfg->n_layers <= 0 || cfg->max_tokens <= 0) return bad("n_layers and max_tokens must be positive");
@@ -220,6 +221,10 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->bias_dev, (size_t)E * 4},
         {(void**)&ctx->xnorm_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->rtmp_dev, (size_t)T * s.H * 2},
+        {(void**)&ctx->fused.part_gu, (size_t)kFusedMaxT * K * (s.I / kRowTile) * kDecodeSplit * 2 * kRowTile * 4},
+        {(void**)&ctx->fused.cnt_gu, (size_t)kFusedMaxT * K * (s.I / kRowTile) * 4},
+        {(void**)&ctx->fused.cnt_dn, (size_t)kFusedMaxT * (s.H / kRowTile) * 4},
+        {(void**)&ctx->fused.bar, 16},
         {(void**)&ctx->ep.send_cnt, (size_t)kMaxWorld * 4},
         {(void**)&ctx->ep.done, 16},
         {(void**)&ctx->ep.epoch, 16},
@@ -242,6 +247,12 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         off += align_up(it.bytes ? it.bytes : 16, 1024);
     }
     ctx->dec.err = ctx->err_flag;
+    ctx->fused.logits = ctx->logits;
+    ctx->fused.ids = ctx->ids;
+    ctx->fused.wts = ctx->wts;
+    ctx->fused.h = ctx->dec.h;
+    ctx->fused.y = ctx->dec.y;
+    ctx->fused.err = ctx->err_flag;
     if (W > 1) {
         // this rank's shared buffer (layout in k_ep.cu), zeroed: stamps and counts start at 0
         EpArgs& a = ctx->ep;
@@ -350,8 +361,8 @@ static int load_impl(obs_ctx* ctx, int layer, const obs_layer_weights* w, int on
             step(cudaMemcpy(ss, ps + (size_t)e0 * out_f * (in_f / 64), ng, kind));
             step(cudaMemcpy(sb, pb + (size_t)e0 * out_f * (in_f / 64), ng, kind));
         }
-        if (proj < 2) step(launch_retile(sw, ss, sb, EL, out_f, in_f, L.gateup, 2, proj, 0));
-        else step(launch_retile(sw, ss, sb, EL, out_f, in_f, L.down, 1, 0, 0));
+        if (proj < 2) step(launch_retile(sw, ss, sb, EL, out_f, in_f, L.gateup, 1, proj, 0));
+        else step(launch_retile(sw, ss, sb, EL, out_f, in_f, L.down, 0, 0, 0));
         step(cudaDeviceSynchronize());
     }
     cudaFree(stage);
@@ -449,13 +460,12 @@ static GemmArgs gemm_gateup(obs_ctx* ctx, const LayerDev& L, const uint16_t* x) 
     const Shape& s = ctx->sh;
     GemmArgs g{};
     g.wblocks = L.gateup;
-    g.wstride = 2;
-    g.woff = 0;
+    g.paired = 1;
     g.act = ctx->disp.xp;  // the routed rows, permuted and tiled by the dispatch
     g.atoms = ctx->disp.atoms;
     g.tiles = ctx->disp.tiles;
     g.n_tiles = ctx->disp.n_tiles;
-    g.n_rt = s.I / kRowTile;
+    g.n_rt = s.I / 64;
     g.n_kt = s.H / kGroup;
     g.bn = kBNTile;
     g.out = ctx->hbuf;
@@ -471,8 +481,7 @@ static GemmArgs gemm_down(obs_ctx* ctx, const LayerDev& L) {
     const Shape& s = ctx->sh;
     GemmArgs g{};
     g.wblocks = L.down;
-    g.wstride = 1;
-    g.woff = 0;
+    g.paired = 0;
     g.act = ctx->hbuf;
     g.atoms = ctx->disp.atoms;
     g.tiles = ctx->disp.tiles;
@@ -545,13 +554,13 @@ extern "C" int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert
     CU(launch_tile_rows(x, n, in_f, ctx->disp.atoms, ctx->disp.xp, st), "tile rows");
     GemmArgs g{};
     g.wblocks = proj == 2 ? L.down : L.gateup;
-    g.wstride = proj == 2 ? 1 : 2;
-    g.woff = proj == 2 ? 0 : proj;
+    g.paired = proj < 2;  // the paired array computes gate and up together; the epilogue keeps one
+    g.proj_sel = proj;
     g.act = ctx->disp.xp;
     g.atoms = ctx->disp.atoms;
     g.tiles = ctx->disp.tiles;
     g.n_tiles = ctx->disp.n_tiles;
-    g.n_rt = out_f / kRowTile;
+    g.n_rt = proj == 2 ? out_f / kRowTile : out_f / 64;
     g.n_kt = in_f / kGroup;
     g.bn = kBNTile;
     g.out = y;
@@ -663,6 +672,14 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
     const Shape& s = ctx->sh;
     const LayerDev& L = ctx->layers[layer];
     cudaStream_t st = as_stream(stream);
+    if (path == OBS_PATH_DECODE && T <= kFusedMaxT) {
+        // router, top-k, experts and combine in one cooperative launch
+        prof_begin(ctx, OBS_STAGE_DECODE_FUSED, st);
+        CU(launch_decode_fused(L, s, x, residual, logit_bias, T, ctx->cfg.norm_topk, ctx->fused, out, ctx->num_sms, st),
+           "fused decode");
+        prof_end(ctx, st);
+        return OBS_OK;
+    }
     prof_begin(ctx, OBS_STAGE_ROUTER, st);
     CU(launch_router_logits(L, s, x, T, ctx->logits, st), "router");
     prof_end(ctx, st);

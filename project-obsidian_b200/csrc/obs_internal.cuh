@@ -34,13 +34,14 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 
 // One 128-row x 64-column block of a tiled 4-bit projection (4608 bytes):
 // words 0-3 of the 128 rows, words 4-7 of the 128 rows, 128 bf16 scales,
-// 128 bf16 biases.
-// gate and up are interleaved per block (gate, up) so one copy brings both.
+// 128 bf16 biases.  The gate/up array is "paired": each block holds 64 gate
+// and the same 64 up features, so one MMA chain yields both halves of SwiGLU.
 struct LayerDev {
     uint32_t* router_w;   // [E, H/4]   reference layout
     uint16_t* router_s;   // [E, H/64]
     uint16_t* router_b;
-    uint8_t* gateup;      // [E][I/128][H/64][2] blocks
+    uint8_t* gateup;      // [E][I/64][H/64] paired blocks: rows 32q+i = gate (i < 16) / up (i >= 16)
+                          // of feature 64*rt + 16q + (i & 15)
     uint8_t* down;        // [E][H/128][I/64] blocks
     bool loaded;
 };
@@ -56,9 +57,13 @@ cudaError_t launch_synth_proj(uint64_t seed, uint32_t layer, int proj, int e0, i
                               uint32_t* w, uint16_t* s, uint16_t* b, cudaStream_t st);
 cudaError_t launch_synth_x(uint64_t seed, uint32_t layer, int row0, int T, int H, float eps, uint16_t* x,
                            cudaStream_t st);
-// reference layout -> tiled blocks.  interleave = 2 writes block p of each pair.
+// Re-tile one projection [E][out_f][in_f] (reference layout) into 4608-byte
+// blocks [E][tiles][in_f/64].  paired = 0: 128-row tiles, row r of the block =
+// row r of the tile.  paired = 1 (gate proj 0 / up proj 1 into the gate/up
+// array): 64-row tiles, feature c of the tile goes to block row
+// 32*(c/16) + 16*proj + c%16.
 cudaError_t launch_retile(const uint32_t* w, const uint16_t* s, const uint16_t* b, int E, int out_f, int in_f,
-                          uint8_t* dst, int interleave, int p, cudaStream_t st);
+                          uint8_t* dst, int paired, int proj, cudaStream_t st);
 
 // --------------------------------------------------------------- k_router.cu
 // Router logits for T tokens: router_parts(T) partial planes [parts][T][E]
@@ -124,6 +129,24 @@ struct DecodeBufs {
     uint32_t* cnt_dn;   // [T][n_rt_dn]
     int* err;           // device error flag (expert id out of range)
 };
+// The fused decode layer (router -> top-k -> gate/up -> SwiGLU -> down ->
+// combine in one cooperative launch) for T <= kFusedMaxT tokens.
+constexpr int kFusedMaxT = 4;
+struct FusedDecodeBufs {
+    float* logits;      // [T][E]
+    int32_t* ids;       // [T][K]
+    float* wts;         // [T][K]
+    float* part_gu;     // [T*K][n_rt_gu][kDecodeSplit][2][128] gate/up split partials
+    uint32_t* cnt_gu;   // [T*K][n_rt_gu]  self-resetting arrival counters
+    uint32_t* cnt_dn;   // [T][n_rt_dn]
+    uint32_t* bar;      // grid barrier arrivals (zeroed before each launch)
+    uint16_t* h;        // [T*K][I]
+    uint16_t* y;        // [T*K][H]
+    int* err;
+};
+cudaError_t launch_decode_fused(const LayerDev& L, const Shape& sh, const uint16_t* x, const uint16_t* residual,
+                                const float* bias, int T, int norm, const FusedDecodeBufs& f, uint16_t* out,
+                                int num_sms, cudaStream_t st);
 cudaError_t launch_decode_gateup(const LayerDev& L, const Shape& sh, const uint16_t* x, const int32_t* ids,
                                  int T, const DecodeBufs& d, cudaStream_t st);
 cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t* ids, const float* w,
@@ -133,15 +156,15 @@ cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t
 // ----------------------------------------------------------------- k_gemm.cu
 enum GemmEpi : int { kEpiSwiglu = 0, kEpiBf16 = 1, kEpiF32 = 2 };
 struct GemmArgs {
-    const uint8_t* wblocks;   // tiled weight blocks of the projection(s)
-    int wstride;              // blocks per k-tile step (2 for the gate/up array, 1 for down)
-    int woff;                 // block offset inside a step (0 gate, 1 up)
+    const uint8_t* wblocks;   // tiled weight blocks [E][n_rt][n_kt] of 4608 bytes
+    int paired;               // 1: the gate/up array (each 128-row block = 64 gate + 64 up rows)
+    int proj_sel;             // kEpiF32 on the paired array: 0 stores the gate rows, 1 the up rows
     const uint16_t* act;      // tiled activations (B operand): 8-row atoms of 1024 B per k-group
     int atoms;                // row atoms of the activation layout
     const int4* tiles;        // token tiles {expert, row0, nrows, 0}
     const int32_t* n_tiles;   // device count of token tiles
-    int n_rt;                 // weight row tiles per expert
-    int n_kt;                 // k-tiles (in / 64)
+    int n_rt;                 // weight row tiles per expert (I/64 for the paired array, H/128 for down)
+    int n_kt;                 // k-tiles (in / 64), a multiple of 4
     int bn;                   // max token rows per tile (<= 128)
     void* out;                // kEpiSwiglu: tiled bf16 H; kEpiBf16: bf16 [rows, out_ld]; kEpiF32: fp32
     int out_ld;               // row stride of row-major outputs (elements)

@@ -35,7 +35,8 @@ EXPORTS = (
     "obs_rmsnorm", "obs_moe_stack_forward",
 )
 EP_HANDLE_BYTES = 64
-STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down")
+STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down",
+          "decode_fused")
 
 
 class ObsError(RuntimeError):

@@ -326,18 +326,19 @@ def test_errors(small):
     ctx.close()
 
 
-@pytest.mark.parametrize("path,T", [(obsmoe.PATH_PREFILL, 100), (obsmoe.PATH_DECODE, 3)])
-def test_forward_replays_from_a_cuda_graph(small, path, T):
+@pytest.mark.parametrize("path,T,launches", [(obsmoe.PATH_PREFILL, 100, 3), (obsmoe.PATH_DECODE, 3, 1),
+                                            (obsmoe.PATH_DECODE, 6, 3)])
+def test_forward_replays_from_a_cuda_graph(small, path, T, launches):
     """The layer forward issues only stream-ordered work, so it can be captured
-    in a CUDA graph; replays give the eager result bit for bit and launch the
-    same kernels."""
+    in a CUDA graph (the fused decode layer of T <= 4 is one cooperative launch);
+    replays give the eager result bit for bit."""
     torch = small.torch
     x = dev(torch, small.x(T, row0=21))
     eager = torch.empty((T, 2048), dtype=torch.int16, device="cuda")
     n0 = obsmoe.kernel_launches()
     small.ctx.moe_forward(0, x, eager, T, path=path)
     per_forward = obsmoe.kernel_launches() - n0
-    assert per_forward >= 3
+    assert per_forward >= launches
     out = torch.full((T, 2048), -1, dtype=torch.int16, device="cuda")
     cap = torch.cuda.Stream()
     cap.wait_stream(torch.cuda.current_stream())
