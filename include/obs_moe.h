@@ -156,10 +156,17 @@ int obs_profile_enable(obs_ctx* ctx, int enable);
 int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches);
 /* Pipeline trace of the gate/up grouped GEMM (diagnostics): while set, the
  * GEMM's CTA 0 writes %globaltimer (ns) into trace[role * n_steps + i] for
- * k-step (or item) i of each role: 0 weight copy issued, 1 token tile ready,
- * 2 dequant start, 3 dequant done, 4 MMA start, 5 MMA committed, 6 epilogue
- * start, 7 epilogue done, 8 dequant stores done, 9 MMA fences passed.
- * trace = NULL switches it off.  Device memory of 10 * n_steps uint64. */
+ * entry i of each role: 0 weight copy issued (per four k-groups), 1 token-tile
+ * copies issued (per k-step), 2 dequant start, 3 dequant done, 8 dequant TMEM
+ * stores done (per k-step, steps 0 mod 4, lane quarter 0), 10-12 dequant done
+ * for lane quarters 1-3, 4 MMA pair ready, 9 MMA fence passed, 5 MMA pair
+ * committed (per pair of k-steps), 6 epilogue start, 7 epilogue done (per
+ * item), 13 token tile landed (per k-step).
+ * When 14 * n_steps >= 8 * (SM count), the fused decode layer (T <= 4) writes
+ * instead, for every CTA b, trace[8b + k]: k = 0 start, 1 router done, 2 first
+ * grid barrier passed, 3 top-k done, 4 gate/up done, 5 second barrier passed,
+ * 6 down + combine done.
+ * trace = NULL switches it off.  Device memory of 14 * n_steps uint64. */
 int obs_trace_enable(obs_ctx* ctx, uint64_t* trace, int n_steps);
 /* No counterpart in the reference.  *count = the number of kernel launches the
  * library has issued in this process so far (all contexts and devices); the

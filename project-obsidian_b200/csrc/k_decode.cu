@@ -308,12 +308,19 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
     __shared__ int s_last[2];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, b = blockIdx.x;
+    // phase timeline (diagnostics): start, A done, barrier 1, B done, C done, barrier 2, D done
+    auto mark = [&](int k) {
+        if (f.trace && tid == 0) f.trace[8 * b + k] = global_ns();
+    };
+    mark(0);
 
     // A: router logits; item i on warp i / G of CTA i % G
     const int n_tc = (T + kWarpTok - 1) / kWarpTok;
     for (int item = warp * G + b; item < E * n_tc; item += kFusedWarps * G)
         router_warp_item(rw, rs, rb, x, T, H, E, item % E, (item / E) * kWarpTok, lane, f.logits);
+    mark(1);
     if (!grid_sync(f.bar, G, f.err)) return;
+    mark(2);
 
     // B: top-k of every token, in every CTA
     if (warp < T) {
@@ -329,6 +336,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
         }
     }
     __syncthreads();
+    mark(3);
 
     // C: gate/up -- half-CTA h takes units (pair p, row tile rt, split ks) like one
     // CTA of k_decode_gateup: warp w8 = block half (w8 & 1) of paired blocks
@@ -386,7 +394,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
             named_bar_sync(1 + h, 256);  // s_part / s_gu / s_last free for the next unit
         }
     }
+    mark(4);
     if (!grid_sync(f.bar, 2 * G, f.err)) return;
+    mark(5);
 
     // D: down -- CTA units (pair p, row tile rt) like one CTA of k_decode_down
     {
@@ -438,6 +448,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
             __syncthreads();  // s_part / s_last free for the next unit
         }
     }
+    mark(6);
 }
 
 }  // namespace

@@ -29,16 +29,22 @@
 //               gate/up epilogue;
 //   warp 2      MMA issuer (the warp runs converged, one elected lane issues):
 //               tcgen05.mma kind::f16, A in TMEM, B in shared memory, K = 16,
-//               eight per step, fp32 accumulators in TMEM.  At N = 128 one MMA
-//               takes longer than one thread needs to issue the next;
-//   warp 3      idle (keeps the dequant warps on TMEM lane quarters warp % 4);
+//               eight per step, fp32 accumulators in TMEM.  One thread issues an
+//               MMA every ~40 cycles and each mbarrier wait costs it more than a
+//               hundred, so it waits once per pair of steps (16 MMAs), on a
+//               barrier that says both steps' A and B stages are ready, and
+//               frees both with one commit;
+//   warp 3      idle (keeps the dequant warps on TMEM lane quarters warp % 4;
+//               in trace builds it records when token tiles land);
 //   warps 4-19  four dequant quads (one warp per lane quarter); quad j owns the
 //               MMA steps j mod 4 and A stage j, so each warp has four step
 //               periods for its share: read the packed words of its 32 rows x
 //               two k-groups from the W stage, unpack two codes per bf16x2
 //               register, q = (0x4300 | n) - 128, w = fma.rn.bf16x2(q, s, b)
-//               (the correctly rounded bf16 of q*s + b), and write them with
-//               tcgen05.st into the A stage (one weight row per TMEM lane);
+//               (the correctly rounded bf16 of q*s + b), write them with
+//               tcgen05.st into the A stage (one weight row per TMEM lane), wait
+//               for the step's token tile to land, and arrive on the pair's
+//               ready barrier;
 //   warps 20-23 epilogue: tcgen05.ld, SwiGLU (or plain), results staged in
 //               shared memory in the global layout and written back with bulk
 //               copies or 16-byte stores (fp32 debug output: direct stores).
@@ -78,12 +84,13 @@ struct Cfg {
     static constexpr int STG_OFF = B_OFF + SB * B_STAGE;
     static constexpr int W_OFF = STG_OFF + STG;
     static constexpr int BAR_OFF = W_OFF + SW * W_STAGE;
-    static constexpr int N_BARS = 2 * SW + 2 * SB + 2 * SA + 4;
+    static constexpr int N_BARS = 2 * SW + SB + 2 * 2 + 4;
     static constexpr int SMEM = BAR_OFF + N_BARS * 8 + 32 + 1024;  // + alignment slack
 };
 static_assert(Cfg::SMEM <= 232448, "smem");
 static_assert(Cfg::A_TMEM + Cfg::SA * Cfg::A_COLS <= Cfg::TMEM_COLS, "tmem");
 static_assert(kWK == 2 * kKS, "a W stage holds two MMA steps");
+static_assert(Cfg::SB == kQuads && Cfg::SA == kQuads, "quad j owns A stage j and B stage j");
 
 __device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
     uint32_t d;
@@ -140,19 +147,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     auto full_w = [&](int s) { return bar_base + 8 * s; };
     auto empty_w = [&](int s) { return bar_base + 8 * (C::SW + s); };
     auto full_b = [&](int s) { return bar_base + 8 * (2 * C::SW + s); };
-    auto empty_b = [&](int s) { return bar_base + 8 * (2 * C::SW + C::SB + s); };
-    auto aready = [&](int s) { return bar_base + 8 * (2 * C::SW + 2 * C::SB + s); };
-    auto aempty = [&](int s) { return bar_base + 8 * (2 * C::SW + 2 * C::SB + C::SA + s); };
-    auto accfull = [&](int b) { return bar_base + 8 * (2 * C::SW + 2 * C::SB + 2 * C::SA + b); };
-    auto accempty = [&](int b) { return bar_base + 8 * (2 * C::SW + 2 * C::SB + 2 * C::SA + 2 + b); };
+    // pair slot ps = (step / 2) % 2 covers the A and B stages 2ps, 2ps + 1
+    auto aready = [&](int ps) { return bar_base + 8 * (2 * C::SW + C::SB + ps); };
+    auto sfree = [&](int ps) { return bar_base + 8 * (2 * C::SW + C::SB + 2 + ps); };
+    auto accfull = [&](int b) { return bar_base + 8 * (2 * C::SW + C::SB + 4 + b); };
+    auto accempty = [&](int b) { return bar_base + 8 * (2 * C::SW + C::SB + 6 + b); };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         // a W stage is read by the two quads of its two MMA steps (four warps each)
         for (int s = 0; s < C::SW; ++s) mbar_init(full_w(s), 1), mbar_init(empty_w(s), 8);
-        // B and A stages are freed, and accumulators filled, by commits of the issuer
-        for (int s = 0; s < C::SB; ++s) mbar_init(full_b(s), 1), mbar_init(empty_b(s), 1);
-        for (int s = 0; s < C::SA; ++s) mbar_init(aready(s), 4), mbar_init(aempty(s), 1);
+        // a pair of steps is ready when its two quads (eight warps) have written A and
+        // seen B land; one issuer commit frees its A and B stages
+        for (int s = 0; s < C::SB; ++s) mbar_init(full_b(s), 1);
+        for (int ps = 0; ps < 2; ++ps) mbar_init(aready(ps), 8), mbar_init(sfree(ps), 1);
         for (int b = 0; b < 2; ++b) mbar_init(accfull(b), 1), mbar_init(accempty(b), kEpThreads);
         *abort_flag = 0;
         fence_mbar_init();
@@ -200,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(a.act) + (size_t)(tl.y >> 3) * 1024;
             const uint32_t bbytes = (uint32_t)tl.z * 128u;
             for (int ks = 0; ks < KS; ++ks) {
-                if (!wait_all(empty_b(s), ph ^ 1, abort_flag)) break;
+                if (!wait_all(sfree(s >> 1), ph ^ 1, abort_flag)) break;
                 if (elect_one()) {
                     mbar_arrive_expect_tx(full_b(s), kKS * bbytes);
 #pragma unroll
@@ -220,7 +228,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         // ---------------------------------------------------------- MMA issuer
         // The whole warp runs the loop (waits, descriptor arithmetic) and one
         // elected lane issues: a loop run by lane 0 alone issues far slower.
-        int sa = 0, pha = 0, sb = 0, phb = 0, it = 0, step = 0;
+        // One wait, one fence and one commit per pair of steps (16 MMAs): every
+        // mbarrier wait costs the issuing thread more than a hundred cycles.
+        int pair = 0, it = 0;
         const uint64_t b_desc0 = sw128_desc(sbase + C::B_OFF);
         const bool tr = TRACE && lane == 0;
         for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, ++it) {
@@ -231,37 +241,50 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             tc_fence_after();
             const uint32_t dbase = tmem + buf * C::ACC_COLS;
             bool ok = true;
-            for (int ks = 0; ks < KS; ++ks) {
-                if (!__all_sync(0xffffffffu, mbar_wait(aready(sa), pha, abort_flag) &&
-                                                  mbar_wait(full_b(sb), phb, abort_flag))) {
+            for (int pi = 0; pi < KS / 2; ++pi, ++pair) {
+                const int ps = pair & 1;
+                if (!wait_all(aready(ps), (pair >> 1) & 1, abort_flag)) {
                     ok = false;
                     break;
                 }
-                if (tr) trace_at<TRACE>(a, kTrMmaStart, step);
+                if (tr) trace_at<TRACE>(a, kTrMmaStart, pair);
                 tc_fence_after();
-                if (tr) trace_at<TRACE>(a, kTrMmaFenced, step);
+                if (tr) trace_at<TRACE>(a, kTrMmaFenced, pair);
                 // descriptors: plain adds on precomputed bases (the start address field
-                // advances 16 bytes per unit; stages stay below 256 KB).  k-slice kk of the
-                // step: A columns kk*8, B group kk/4, 32 bytes per slice.
-                const uint32_t abase = tmem + C::A_TMEM + sa * C::A_COLS;
-                const uint64_t bdesc = b_desc0 + (uint64_t)(sb * (C::B_STAGE >> 4));
+                // advances 16 bytes per unit; stages stay below 256 KB).  k-slice kk of
+                // step stage sa: A columns kk*8, B group kk/4, 32 bytes per slice.
                 if (elect_one()) {
 #pragma unroll
-                    for (int kk = 0; kk < 4 * kKS; ++kk)
-                        tc_mma_f16_ts(dbase, abase + kk * 8, bdesc + (kk >> 2) * (C::B_GROUP >> 4) + 2 * (kk & 3),
-                                      idesc, (ks | kk) != 0 ? 1u : 0u);
-                    tc_commit(empty_b(sb));  // the step's MMAs are done: B stage sb ...
-                    tc_commit(aempty(sa));   // ... and A stage sa are free
+                    for (int h = 0; h < 2; ++h) {
+                        const int sa = 2 * ps + h;
+                        const uint32_t abase = tmem + C::A_TMEM + sa * C::A_COLS;
+                        const uint64_t bdesc = b_desc0 + (uint64_t)(sa * (C::B_STAGE >> 4));
+#pragma unroll
+                        for (int kk = 0; kk < 4 * kKS; ++kk)
+                            tc_mma_f16_ts(dbase, abase + kk * 8, bdesc + (kk >> 2) * (C::B_GROUP >> 4) + 2 * (kk & 3),
+                                          idesc, (pi | h | kk) != 0 ? 1u : 0u);
+                    }
+                    tc_commit(sfree(ps));  // the pair's MMAs are done: its A and B stages are free
                 }
                 __syncwarp();
-                if (tr) trace_at<TRACE>(a, kTrMmaIssued, step);
-                ++step;
-                if (++sa == C::SA) sa = 0, pha ^= 1;
-                if (++sb == C::SB) sb = 0, phb ^= 1;
+                if (tr) trace_at<TRACE>(a, kTrMmaIssued, pair);
             }
             if (!ok) break;
             if (elect_one()) tc_commit(accfull(buf));
             __syncwarp();
+        }
+    } else if (TRACE && warp == kWarpMma + 1) {
+        // ---------------------------------------- trace observer (CTA 0 only)
+        // records when each token-tile stage lands; bounded waits, never aborts
+        const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+        const int total = blockIdx.x == 0 ? min(my_items * KS, a.trace_n) : 0;
+        for (int i = 0; i < total && !*abort_flag; ++i) {
+            const uint64_t t0 = global_ns();
+            bool got = false;
+            while (!(got = mbar_try_wait(full_b(i % C::SB), (i / C::SB) & 1)) && global_ns() - t0 < kWaitLimitNs) {
+            }
+            if (!got) break;
+            if (lane == 0) trace_at<TRACE>(a, kTrBLanded, i);
         }
     } else if (warp >= kWarpDq && warp < kWarpEp) {
         // ------------------------------------------------------------ dequant
@@ -273,6 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         const int r = q * 32 + lane;    // weight row of the tile = TMEM lane
         const uint32_t at = tmem + ((uint32_t)(q * 32) << 16) + C::A_TMEM + j * C::A_COLS;
         const bool tr = TRACE && dw == 0 && lane == 0;
+        const bool trq = TRACE && dw > 0 && dw < 4 && lane == 0;  // the other quarters of quad 0
         const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
         const int total = my_items * KS;
         uint32_t ws[8 * kKS], s2v[kKS], b2v[kKS];
@@ -303,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         bool ok = j >= total || load_w(j);
         for (int step = j; step < total && ok; step += kQuads) {
             // A stage j was last read by the MMAs of step (step - 4)
-            if (!wait_all(aempty(j), ((step / kQuads) & 1) ^ 1, abort_flag)) break;
+            if (!wait_all(sfree(j >> 1), ((step / kQuads) & 1) ^ 1, abort_flag)) break;
             tc_fence_after();
 #pragma unroll
             for (int g = 0; g < kKS; ++g) {
@@ -314,10 +338,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             }
             if (tr) trace_at<TRACE>(a, kTrDqStored, step);
             tc_wait_st();
+            // the step's token tile (B stage j) must have landed before the pair is ready
+            if (!wait_all(full_b(j), (step / kQuads) & 1, abort_flag)) break;
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(aready(j));
+            if (lane == 0) mbar_arrive(aready(j >> 1));
             if (tr) trace_at<TRACE>(a, kTrDqDone, step);
+            if (trq) trace_at<TRACE>(a, kTrDqDoneQ1 + dw - 1, step);
             // the quad's next step is four steps away: its load is off the critical loop
             if (step + kQuads < total && !load_w(step + kQuads)) ok = false;
         }

@@ -827,5 +827,7 @@ extern "C" int obs_trace_enable(obs_ctx* ctx, uint64_t* trace, int n_steps) {
     if (trace && n_steps <= 0) return fail(ctx, OBS_ERR_INVALID, "n_steps must be positive");
     ctx->trace = trace;
     ctx->trace_n = trace ? n_steps : 0;
+    // the fused decode layer records the phase timeline of every CTA when the buffer holds it
+    ctx->fused.trace = trace && (size_t)n_steps * kTrRoles >= (size_t)8 * ctx->num_sms ? trace : nullptr;
     return OBS_OK;
 }

@@ -143,6 +143,7 @@ struct FusedDecodeBufs {
     uint16_t* h;        // [T*K][I]
     uint16_t* y;        // [T*K][H]
     int* err;
+    uint64_t* trace;    // optional: thread 0 of CTA b writes %globaltimer at 7 points to trace[8b .. 8b+6]
 };
 cudaError_t launch_decode_fused(const LayerDev& L, const Shape& sh, const uint16_t* x, const uint16_t* residual,
                                 const float* bias, int T, int norm, const FusedDecodeBufs& f, uint16_t* out,
@@ -176,17 +177,19 @@ struct GemmArgs {
 };
 // trace roles (rows of the trace buffer, trace_n entries each)
 enum TraceRole : int {
-    kTrWIssue = 0,     // weight producer issued the copy of k-step i
-    kTrBSignal = 1,    // token-tile producer signalled k-step i full
+    kTrWIssue = 0,     // weight producer issued the copy of W stage i (four k-groups)
+    kTrBSignal = 1,    // token-tile producer issued the copies of k-step i
     kTrDqStart = 2,    // dequant warp 0 passed its waits for k-step i
-    kTrDqDone = 3,     // dequant warp 0 arrived "A ready" for k-step i
-    kTrMmaStart = 4,   // MMA thread passed its waits for k-step i
-    kTrMmaIssued = 5,  // MMA thread committed k-step i
+    kTrDqDone = 3,     // dequant warp 0 arrived "pair ready" for k-step i
+    kTrMmaStart = 4,   // MMA thread passed its wait for pair i (k-steps 2i, 2i+1)
+    kTrMmaIssued = 5,  // MMA thread committed pair i
     kTrEpStart = 6,    // epilogue passed accfull of item i
     kTrEpDone = 7,     // epilogue released the accumulator of item i
-    kTrDqStored = 8,   // dequant warp 0 finished its shared-memory stores of k-step i
-    kTrMmaFenced = 9,  // MMA thread passed its fences for k-step i
-    kTrRoles = 10
+    kTrDqStored = 8,   // dequant warp 0 finished its TMEM stores of k-step i
+    kTrMmaFenced = 9,  // MMA thread passed its fence for pair i
+    kTrDqDoneQ1 = 10,  // as kTrDqDone, for the dequant warps of TMEM lane quarters 1, 2, 3
+    kTrBLanded = 13,   // the token tile of k-step i has landed in shared memory (observer warp)
+    kTrRoles = 14
 };
 cudaError_t launch_gemm(const GemmArgs& a, int epi, int num_sms, cudaStream_t st);
 size_t gemm_smem_bytes(int epi);

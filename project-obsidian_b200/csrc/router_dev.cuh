@@ -78,7 +78,9 @@ __device__ __forceinline__ float key_value(uint32_t k) {
 
 // One warp, one token (moe_routing_topk.metal:31-56): softmax in fp32, K
 // rounds of argmax (lowest index on ties), renormalise.  logit(e) returns the
-// token's logit of expert e; lane k < K ends with (*id, *wt) of rank k.
+// token's logit of expert e; lane k < K ends with (*id, *wt) of rank k.  The
+// rounds only select; lane k then forms its own probability
+// exp(l_k - max) / sum, and the renormalising sum adds them in rank order.
 template <class LogitFn>
 __device__ __forceinline__ void topk_token(LogitFn logit, const float* __restrict__ bias, int E, int K, int norm,
                                            int lane, int* id, float* wt) {
@@ -102,7 +104,7 @@ __device__ __forceinline__ void topk_token(LogitFn logit, const float* __restric
         if (lane + 32 * i < E) se += expf(key_value(key[i]) - mx);
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
-    float wk = 0.0f, wsum = 0.0f;
+    uint32_t kk = 0;
     int ik = 0;
 #pragma unroll
     for (int k = 0; k < kMaxK; ++k) {
@@ -115,12 +117,13 @@ __device__ __forceinline__ void topk_token(LogitFn logit, const float* __restric
         const uint32_t best = __reduce_max_sync(0xffffffffu, kb);
         const int bi = (int)__reduce_min_sync(0xffffffffu, kb == best ? (uint32_t)ib : 0x7fffffffu);
         if ((bi & 31) == lane) key[bi >> 5] = 0;
-        const float p = expf(key_value(best) - mx) / se;
-        wsum += p;
-        if (lane == k) wk = p, ik = bi;
+        if (lane == k) kk = best, ik = bi;
     }
+    const float p = lane < K ? expf(key_value(kk) - mx) / se : 0.0f;
+    float wsum = 0.0f;
+    for (int k = 0; k < K; ++k) wsum += __shfl_sync(0xffffffffu, p, k);
     *id = ik;
-    *wt = (norm && wsum > 0.0f) ? wk / wsum : wk;
+    *wt = (norm && wsum > 0.0f) ? p / wsum : p;
 }
 
 }  // namespace obs
