@@ -33,14 +33,14 @@ __global__ void __launch_bounds__(256) k_router_warp(const uint32_t* __restrict_
 // ---------------------------------------------------------------- prefill form
 // One CTA per (64 tokens, 128 experts, leaf): a leaf is lane l's share of the
 // canonical order, groups [l*m, (l+1)*m).  The CTA stages each group's
-// dequantised weights and activations (fp32) in shared memory; each of its 128
-// threads keeps an 8 x 8 register tile of (token, expert) accumulators (tokens
-// tt + 8i, experts te + 16j: rows read by a warp are consecutive, so the padded
-// rows are conflict-free) and chains the group's 64 columns in order with
-// fused multiply-adds.  The leaf sums land in parts[leaf][T][E]; top-k (or
-// k_router_finish) adds them in the adjacent pairwise tree, which is the decode
-// form's xor-butterfly (offsets 1, 2, 4, 8, 16).  16 FMAs per 128-bit shared load.
-constexpr int kRT = 64, kRE = 128, kRPad = 68, kLeafThreads = 128;
+// dequantised weights and activations (fp32) in shared memory; each of its 256
+// threads keeps a 4 x 8 register tile of (token, expert) accumulators (tokens
+// tt + 16i, experts te + 16j; a warp's activation reads cover 16 rows and its
+// weight reads two, served by broadcast) and chains the group's 64 columns in
+// order with fused multiply-adds.  The leaf sums land in parts[leaf][T][E];
+// top-k (or k_router_finish) adds them in the adjacent pairwise tree, which is
+// the decode form's xor-butterfly (offsets 1, 2, 4, 8, 16).
+constexpr int kRT = 64, kRE = 128, kRPad = 68, kLeafThreads = 256;
 constexpr size_t kLeafSmem = (size_t)(kRT + kRE) * kRPad * 4;  // 52,224 bytes
 
 __global__ void __launch_bounds__(kLeafThreads) k_router_leaf(const uint32_t* __restrict__ w,
@@ -52,12 +52,12 @@ __global__ void __launch_bounds__(kLeafThreads) k_router_leaf(const uint32_t* __
     extern __shared__ __align__(16) float rsm[];
     float(*xs)[kRPad] = reinterpret_cast<float(*)[kRPad]>(rsm);
     float(*ws)[kRPad] = reinterpret_cast<float(*)[kRPad]>(rsm + kRT * kRPad);
-    const int tid = threadIdx.x, tt = tid & 7, te = tid >> 3;
+    const int tid = threadIdx.x, tt = tid & 15, te = tid >> 4;
     const int t0 = blockIdx.x * kRT, e0 = blockIdx.y * kRE, leaf = blockIdx.z;
     const int G = H / kGroup, m = G / 32;
-    float acc[8][8];
+    float acc[4][8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
     for (int g = leaf * m; g < (leaf + 1) * m; ++g) {
@@ -94,26 +94,26 @@ __global__ void __launch_bounds__(kLeafThreads) k_router_leaf(const uint32_t* __
         __syncthreads();
 #pragma unroll 2
         for (int j = 0; j < 64; j += 4) {
-            float4 xv[8], wv[8];
+            float4 xv[4], wv[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[tt + 8 * i][j]);
+            for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[tt + 16 * i][j]);
 #pragma unroll
             for (int i = 0; i < 8; ++i) wv[i] = *reinterpret_cast<const float4*>(&ws[te + 16 * i][j]);
-            // column by column: 64 independent FMAs per column, each chain in column order
+            // column by column: 32 independent FMAs per column, each chain in column order
 #pragma unroll
-            for (int a = 0; a < 8; ++a)
+            for (int a = 0; a < 4; ++a)
 #pragma unroll
                 for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].x, xv[a].x, acc[a][c]);
 #pragma unroll
-            for (int a = 0; a < 8; ++a)
+            for (int a = 0; a < 4; ++a)
 #pragma unroll
                 for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].y, xv[a].y, acc[a][c]);
 #pragma unroll
-            for (int a = 0; a < 8; ++a)
+            for (int a = 0; a < 4; ++a)
 #pragma unroll
                 for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].z, xv[a].z, acc[a][c]);
 #pragma unroll
-            for (int a = 0; a < 8; ++a)
+            for (int a = 0; a < 4; ++a)
 #pragma unroll
                 for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].w, xv[a].w, acc[a][c]);
         }
@@ -122,9 +122,9 @@ __global__ void __launch_bounds__(kLeafThreads) k_router_leaf(const uint32_t* __
     __syncthreads();
     float(*os)[kRE + 4] = reinterpret_cast<float(*)[kRE + 4]>(rsm);
 #pragma unroll
-    for (int a = 0; a < 8; ++a)
+    for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int c = 0; c < 8; ++c) os[tt + 8 * a][te + 16 * c] = acc[a][c];
+        for (int c = 0; c < 8; ++c) os[tt + 16 * a][te + 16 * c] = acc[a][c];
     __syncthreads();
     float* pl = parts + (size_t)leaf * T * E;
     for (int i = tid; i < kRT * kRE; i += kLeafThreads) {
@@ -152,22 +152,33 @@ __global__ void k_router_finish(const float* __restrict__ parts, size_t n, float
 }
 
 // ---------------------------------------------------------------------- top-k
-// One warp per token (body in router_dev.cuh).
+// Two tokens per CTA: every thread forms logits (the leaf tree when the router
+// left 32 partial planes; its 32 loads are independent and coalesced across
+// the CTA) into shared memory, then one warp per token selects (body in
+// router_dev.cuh).  Enough CTAs to fill the GPU at prefill sizes.
+constexpr int kTopkTok = 2;
+
 __global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, int nparts,
                                               const float* __restrict__ bias, int T, int E, int K, int norm,
                                               int32_t* __restrict__ ids, float* __restrict__ wout,
                                               int32_t* __restrict__ counts, float* __restrict__ logits_out) {
     pdl_begin();
-    const int lane = threadIdx.x & 31;
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (t >= T) return;
+    __shared__ float s_l[kTopkTok][kMaxE];
+    const int t0 = blockIdx.x * kTopkTok;
     const size_t plane = (size_t)T * E;
-    auto logit = [&](int e) {
-        const size_t idx = (size_t)t * E + e;
-        const float l = nparts == kLeaves ? tree32(logits, plane, idx) : logits[idx];
-        if (logits_out) logits_out[idx] = l;
-        return l;
-    };
+    for (int i = threadIdx.x; i < kTopkTok * E; i += blockDim.x) {
+        const int tt = i / E, e = i - tt * E, t = t0 + tt;
+        if (t < T) {
+            const size_t idx = (size_t)t * E + e;
+            const float l = nparts == kLeaves ? tree32(logits, plane, idx) : logits[idx];
+            s_l[tt][e] = l;
+            if (logits_out) logits_out[idx] = l;
+        }
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = t0 + warp;
+    if (warp >= kTopkTok || t >= T) return;
+    auto logit = [&](int e) { return s_l[warp][e]; };
     int ik;
     float wk;
     topk_token(logit, bias, E, K, norm, lane, &ik, &wk);
@@ -220,7 +231,8 @@ cudaError_t launch_topk(const float* logits, int nparts, const float* bias, int 
     if (T <= 0) return cudaSuccess;
     if (E > kMaxE || K > kMaxK || K > 32) return cudaErrorInvalidValue;
     {
-        const cudaError_t le_ = launch_pdl(k_topk, dim3((T + 7) / 8), dim3(256), 0, st, logits, nparts, bias, T, E, K, norm, ids, w, counts, logits_out);
+        const cudaError_t le_ = launch_pdl(k_topk, dim3((T + kTopkTok - 1) / kTopkTok), dim3(256), 0, st, logits, nparts,
+                                           bias, T, E, K, norm, ids, w, counts, logits_out);
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();
