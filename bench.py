@@ -15,8 +15,8 @@ T=512 tokens.  Config 0 (decode of one token) is selectable with --config 0.
             from L2.
 * e2e       the same metric through obs_moe_forward_host: pinned host input,
             host->device copy, the layer, device->host copy of the output.
-* roofline  the dominant kernel (the gate/up grouped GEMM at T=512, the decode
-            gate/up mat-vec at T=1), algorithmic bytes per launch / its mean
+* roofline  the dominant kernel (the gate/up grouped GEMM at T=512, the fused
+            decode layer at T=1), algorithmic bytes per launch / its mean
             CUDA-event duration on the launching stream, against the measured
             HBM copy bandwidth in MEASURED_PEAKS.json.
 * cpu_baseline  the C oracle (oracle/, all host threads) on the same layer.
@@ -24,7 +24,9 @@ T=512 tokens.  Config 0 (decode of one token) is selectable with --config 0.
 --impl reference runs the reference's own kernels (shaders/*.metal compiled
 for the CPU into oracle/_ref) on the host cores over a bounded token sample.
 Multi-GPU (torchrun): every rank runs its own T-token batch against its own
-copy of the layers (replicas; weak scaling), timed on the device, max over ranks.
+copy of the layers (data-parallel replicas; weak scaling), timed on the device,
+max over ranks.  --ep instead splits the experts E/N per GPU and exchanges the
+routed rows over NVLink peer memory (expert parallelism).
 """
 from __future__ import annotations
 
@@ -64,6 +66,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=32, help="config 2: tokens per decode step (1, 8, 32, 128)")
     ap.add_argument("--layers", type=int, default=48, help="configs 2 and 3: layers in the stack")
     ap.add_argument("--tokens", type=int, default=0, help="configs 0 and 1: override T (a sweep point, not a BASELINE config)")
+    ap.add_argument("--ep", action="store_true",
+                    help="N > 1: expert parallelism (E/N experts per GPU) instead of N data-parallel replicas")
     return ap.parse_args()
 
 
@@ -163,13 +167,16 @@ def run_stack(args, rank, world, local):
 
         import torch.distributed as dist
 
+        # NCCL carries only barriers and small reductions here; no NVLink multicast
+        # (NVLS) objects next to the peer buffers the expert exchange writes into
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     cfg = CONFIGS[args.config]
     nl = args.layers
     T = args.batch if args.config == 2 else cfg["T"]
     decode = args.config == 2
     path = obsmoe.PATH_AUTO if decode else obsmoe.PATH_PREFILL
-    ep = world > 1
+    ep = world > 1 and args.ep  # default for N > 1: data-parallel replicas, every GPU holds all experts
     shape = obsmoe.MoeShape(H, I, E, K, n_layers=nl, max_tokens=max(T, 16),
                             ep_world=world if ep else 1, ep_rank=rank if ep else 0)
     ctx = obsmoe.MoeContext(shape, local)
@@ -309,7 +316,8 @@ def run_stack(args, rank, world, local):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; BASELINE config distributions; weights generated on the device)",
         "config": {"workload": cfg["name"], "layers": nl, "T": T, "E": E, "K": K, "H": H, "I": I,
-                   "parallelism": f"expert parallel x{world} (NVLink peer all-to-all)" if ep else "single GPU",
+                   "parallelism": (f"expert parallel x{world} (NVLink peer all-to-all)" if ep else
+                                   f"data parallel x{world} (replicas)" if world > 1 else "single GPU"),
                    "l2": f"inputs larger than L2: {nl} resident layers ({nl * 340} MB) per step",
                    "path": "decode (mat-vec)" if decode and T <= 4 and not ep else "prefill (tcgen05 grouped GEMM)",
                    "zipf_beta": beta, "load_max_over_mean_layer0": imbalance,
@@ -334,6 +342,8 @@ def run_stack(args, rank, world, local):
         line["cpu_baseline"] = {"value": Ts / dt, "unit": "tokens/s", "cores": n, "kind": "port",
                                 "sample": f"{Ts} tokens through {nlo} layers of oracle/obs_oracle.c, "
                                           f"time scaled to {nl} layers"}
+    if dist is not None:
+        dist.barrier()  # no rank frees its peer-mapped buffer while another may still use it
     ctx.close()
     if dist is not None:
         dist.barrier()
@@ -405,12 +415,17 @@ def main():
 
         import torch.distributed as dist
 
+        # NCCL carries only barriers and small reductions here; no NVLink multicast
+        # (NVLS) objects next to the peer buffers the expert exchange writes into
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     cfg = dict(CONFIGS[args.config])
     if args.tokens:
         cfg["T"], cfg["name"] = args.tokens, cfg["name"].split(",")[0] + f", T={args.tokens} tokens (sweep)"
     T = cfg["T"]
-    ep = world > 1  # N GPUs: expert parallelism, E/N experts per GPU, each GPU routes its own T tokens
+    # N GPUs: each routes its own T tokens; by default every GPU holds all experts
+    # (data-parallel replicas), with --ep E/N experts per GPU and an NVLink exchange
+    ep = world > 1 and args.ep
     path = obsmoe.PATH_DECODE if T <= 4 and not ep else obsmoe.PATH_PREFILL
     shape = obsmoe.MoeShape(H, I, E, K, n_layers=N_ROT, max_tokens=max(T, 16),
                             ep_world=world if ep else 1, ep_rank=rank if ep else 0)
@@ -550,7 +565,8 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; BASELINE config distributions; weights generated on the device)",
         "config": {"workload": cfg["name"], "T": T, "E": E, "K": K, "H": H, "I": I, "weights": "4-bit g64 (router 8-bit)",
-                   "parallelism": f"expert parallel x{world} (NVLink peer all-to-all)" if ep else "single GPU",
+                   "parallelism": (f"expert parallel x{world} (NVLink peer all-to-all)" if ep else
+                                   f"data parallel x{world} (replicas)" if world > 1 else "single GPU"),
                    "l2": f"inputs larger than L2: steps rotate over {N_ROT} resident layers ({N_ROT * 340} MB)",
                    "path": "prefill (tcgen05 grouped GEMM)" if path == obsmoe.PATH_PREFILL else "decode (mat-vec)"},
         "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": hbm, "unit": "GB/s",
@@ -571,6 +587,8 @@ def main():
 
         Lh = O.synth_layer(0, 0, E=E, H=H, I=I, K=K)
         line["cpu_baseline"] = cpu_baseline(Lh, xs[0].cpu().numpy().view(np.uint16), T)
+    if dist is not None:
+        dist.barrier()  # no rank frees its peer-mapped buffer while another may still use it
     ctx.close()
     if dist is not None:
         dist.barrier()

@@ -71,19 +71,23 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids
     if (item < T * a.K) {
         int id = ids[item];
         if (id < 0 || id >= E) {
-            if (lane == 0) atomicExch(a.err, 1);
+            if (lane == 0) atomicExch(a.err, kDevBadRoute);
             id = 0;
         }
         const int dest = id / a.E_local, le = id - dest * a.E_local;
         int slot = 0;
         if (lane == 0) slot = atomicAdd(a.send_cnt + dest, 1);
         slot = __shfl_sync(0xffffffffu, slot, 0);
-        uint8_t* pb = a.peer[dest];
-        const size_t row = (size_t)a.rank * a.cap + slot;
-        const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(item / a.K) * a.H);
-        uint4* dst = at<uint4>(pb, a.off_rx + row * a.H * 2);
-        for (int c = lane; c < a.H / 8; c += 32) dst[c] = __ldg(src + c);
-        if (lane == 0) *at<int2>(pb, a.off_meta + row * 8) = make_int2(le, item);
+        if (slot < a.cap) {
+            uint8_t* pb = a.peer[dest];
+            const size_t row = (size_t)a.rank * a.cap + slot;
+            const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(item / a.K) * a.H);
+            uint4* dst = at<uint4>(pb, a.off_rx + row * a.H * 2);
+            for (int c = lane; c < a.H / 8; c += 32) dst[c] = __ldg(src + c);
+            if (lane == 0) *at<int2>(pb, a.off_meta + row * 8) = make_int2(le, item);
+        } else if (lane == 0) {
+            atomicExch(a.err, kDevBadSlot);  // more rows than the source's region holds: refused
+        }
     }
     __threadfence_system();
     __syncthreads();
@@ -95,7 +99,7 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids
     __threadfence_system();
     if (threadIdx.x < a.world) {
         const int d = threadIdx.x;
-        const int n = ld_volatile(a.send_cnt + d);
+        const int n = min(ld_volatile(a.send_cnt + d), a.cap);
         *at<int32_t>(a.peer[d], a.off_cnt + (size_t)a.rank * 4) = n;
         __threadfence_system();
         st_release_sys(at<uint32_t>(a.peer[d], a.off_rflag + (size_t)a.rank * 4), e);
@@ -115,13 +119,13 @@ __global__ void __launch_bounds__(256) k_ep_recv(EpArgs a) {
     const int n = a.world * a.cap;
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
         const int s = j / a.cap, i = j - s * a.cap;
-        const int cnt = ld_volatile(at<int32_t>(mine, a.off_cnt) + s);
+        const int cnt = min(ld_volatile(at<int32_t>(mine, a.off_cnt) + s), a.cap);
         int le = -1, item = -1;
         if (i < cnt) {
             const int2 m = *at<int2>(mine, a.off_meta + (size_t)j * 8);
             le = m.x, item = m.y;
-            if (le < 0 || le >= a.E_local) {
-                atomicExch(a.err, 1);
+            if (le < 0 || le >= a.E_local || item < 0 || item >= a.cap) {
+                atomicExch(a.err, kDevBadRoute);
                 le = -1;
             } else {
                 atomicAdd(a.counts + le, 1);
@@ -144,8 +148,12 @@ __global__ void __launch_bounds__(256) k_ep_return(const int32_t* __restrict__ s
     const int n = a.world * a.cap;
     for (int j = blockIdx.x * 8 + warp; j < n; j += gridDim.x * 8) {
         if (a.ids_local[j] < 0) continue;
-        const int s = j / a.cap, item = a.src_item[j];
-        const uint4* src = reinterpret_cast<const uint4*>(y + (size_t)slot_of[j] * a.H);
+        const int s = j / a.cap, item = a.src_item[j], slot = slot_of[j];
+        if (slot < 0 || slot >= a.rows_cap || item < 0 || item >= a.cap) {  // refused, recorded
+            if (lane == 0) atomicExch(a.err, kDevBadSlot);
+            continue;
+        }
+        const uint4* src = reinterpret_cast<const uint4*>(y + (size_t)slot * a.H);
         uint4* dst = at<uint4>(a.peer[s], a.off_ret + (size_t)item * a.H * 2);
         for (int c = lane; c < a.H / 8; c += 32) dst[c] = src[c];
     }

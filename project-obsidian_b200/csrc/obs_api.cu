@@ -258,6 +258,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         EpArgs& a = ctx->ep;
         a.world = W, a.rank = ctx->ep_rank, a.cap = T * K, a.H = s.H, a.K = K, a.E_local = EL;
         a.counts = ctx->disp.counts;
+        a.rows_cap = ctx->R_cap;
         a.err = ctx->err_flag;
         size_t o = 0;
         a.off_rx = o, o += align_up((size_t)W * a.cap * s.H * 2, 256);
@@ -468,6 +469,7 @@ static GemmArgs gemm_gateup(obs_ctx* ctx, const LayerDev& L, const uint16_t* x) 
     g.n_rt = s.I / 64;
     g.n_kt = s.H / kGroup;
     g.bn = kBNTile;
+    g.n_experts = ctx->E_local;
     g.out = ctx->hbuf;
     g.out_atoms = ctx->disp.atoms;
     g.row_limit = ctx->R_cap;
@@ -489,6 +491,7 @@ static GemmArgs gemm_down(obs_ctx* ctx, const LayerDev& L) {
     g.n_rt = s.H / kRowTile;
     g.n_kt = s.I / kGroup;
     g.bn = kBNTile;
+    g.n_experts = ctx->E_local;
     g.out = ctx->ybuf;
     g.out_ld = s.H;
     g.row_limit = ctx->R_cap;
@@ -563,6 +566,7 @@ extern "C" int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert
     g.n_rt = proj == 2 ? out_f / kRowTile : out_f / 64;
     g.n_kt = in_f / kGroup;
     g.bn = kBNTile;
+    g.n_experts = s.E;
     g.out = y;
     g.out_ld = out_f;
     g.row_limit = n;
@@ -784,6 +788,9 @@ extern "C" int obs_check_device(obs_ctx* ctx, void* stream) {
     if (flag) {
         CU(cudaMemset(ctx->err_flag, 0, 4), "clear flag");
         if (flag == kDevTimeout) return fail(ctx, OBS_ERR_TIMEOUT, "a device-side wait gave up (timeout)");
+        if (flag == kDevBadTile) return fail(ctx, OBS_ERR_INVALID, "device refused a GEMM tile outside its buffers");
+        if (flag == kDevBadSlot)
+            return fail(ctx, OBS_ERR_INVALID, "device refused an expert-parallel row slot outside its buffers");
         return fail(ctx, OBS_ERR_INVALID, "device reported an invalid route (expert id out of range)");
     }
     return OBS_OK;

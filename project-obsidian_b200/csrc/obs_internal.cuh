@@ -112,6 +112,7 @@ struct EpArgs {
     int32_t* ids_local;  // [world * cap] local expert of each received row, -1 = empty
     int32_t* src_item;   // [world * cap] source item t*K+k of each received row
     int32_t* counts;     // [E_local] received rows per local expert (zeroed before k_ep_recv)
+    int rows_cap;        // rows of the expert-output buffer k_ep_return reads (slot_of bound)
     int* err;
 };
 cudaError_t launch_ep_send(const int32_t* ids, const uint16_t* x, int T, int E, const EpArgs& a, cudaStream_t st);
@@ -167,6 +168,7 @@ struct GemmArgs {
     int n_rt;                 // weight row tiles per expert (I/64 for the paired array, H/128 for down)
     int n_kt;                 // k-tiles (in / 64), a multiple of 4
     int bn;                   // max token rows per tile (<= 128)
+    int n_experts;            // experts in wblocks (tile expert ids are checked against it)
     void* out;                // kEpiSwiglu: tiled bf16 H; kEpiBf16: bf16 [rows, out_ld]; kEpiF32: fp32
     int out_ld;               // row stride of row-major outputs (elements)
     int out_atoms;            // row atoms of the tiled output
