@@ -11,6 +11,7 @@
 
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <utility>
@@ -821,6 +822,13 @@ extern "C" int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches
 namespace obs {
 static std::atomic<uint64_t> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("OBS_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
 }  // namespace obs
 
 extern "C" int obs_kernel_launches(uint64_t* count) {

@@ -13,6 +13,10 @@ namespace obs {
 // Counts every kernel launch the library issues (obs_kernel_launches).
 void note_launch();
 
+// Programmatic dependent launch on/off (environment OBS_PDL=0 turns it off for
+// the process; read once).
+bool pdl_enabled();
+
 // Launch with programmatic stream serialization (the kernel calls pdl_begin()
 // first): it may be scheduled while the previous kernel of the stream finishes.
 template <typename... KArgs, typename... Args>
@@ -27,7 +31,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
     note_launch();
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
