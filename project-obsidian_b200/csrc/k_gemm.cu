@@ -84,7 +84,7 @@ struct Cfg {
     static constexpr int STG_OFF = B_OFF + SB * B_STAGE;
     static constexpr int W_OFF = STG_OFF + STG;
     static constexpr int BAR_OFF = W_OFF + SW * W_STAGE;
-    static constexpr int N_BARS = 2 * SW + SB + 2 * 2 + 4;
+    static constexpr int N_BARS = 2 * SW + SB + 2 * 2 + 4 + 1;
     static constexpr int SMEM = BAR_OFF + N_BARS * 8 + 32 + 1024;  // + alignment slack
 };
 static_assert(Cfg::SMEM <= 232448, "smem");
@@ -109,8 +109,11 @@ __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t s2, uint32_t b
     for (int j = 0; j < 4; ++j) out[j] = bf2_fma(bf2_sub(((w >> (4 * j)) & 0x000F000Fu) | magic, magic), s2, b2);
 }
 
-__device__ __forceinline__ bool wait_all(uint32_t bar, uint32_t parity, volatile int* abort) {
-    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort));
+// which wait timed out (recorded in the context's second error word)
+enum WaitCode : int { kWtEmptyW = 11, kWtSfreeB, kWtAccEmpty, kWtAReady, kWtFullW, kWtSfreeA, kWtFullB, kWtAccFull };
+
+__device__ __forceinline__ bool wait_all(uint32_t bar, uint32_t parity, volatile int* abort, int code) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, code));
 }
 
 // After giving up, a producer waits (bounded) until the newest copy it issued
@@ -152,6 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     auto sfree = [&](int ps) { return bar_base + 8 * (2 * C::SW + C::SB + 2 + ps); };
     auto accfull = [&](int b) { return bar_base + 8 * (2 * C::SW + C::SB + 4 + b); };
     auto accempty = [&](int b) { return bar_base + 8 * (2 * C::SW + C::SB + 6 + b); };
+    const uint32_t mma_done = bar_base + 8 * (2 * C::SW + C::SB + 8);  // the issuer's last commit
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
@@ -162,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         for (int s = 0; s < C::SB; ++s) mbar_init(full_b(s), 1);
         for (int ps = 0; ps < 2; ++ps) mbar_init(aready(ps), 8), mbar_init(sfree(ps), 1);
         for (int b = 0; b < 2; ++b) mbar_init(accfull(b), 1), mbar_init(accempty(b), kEpThreads);
+        mbar_init(mma_done, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -205,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const int rt = item % a.n_rt;
             const uint8_t* wsrc = a.wblocks + ((size_t)tl.x * a.n_rt + rt) * a.n_kt * kBlockBytes;
             for (int w = 0; w < a.n_kt / kWK; ++w) {
-                if (!wait_all(empty_w(s), ph ^ 1, abort_flag)) break;
+                if (!wait_all(empty_w(s), ph ^ 1, abort_flag, kWtEmptyW)) break;
                 if (elect_one()) {
                     mbar_arrive_expect_tx(full_w(s), C::W_STAGE);
                     bulk_g2s_hint(sbase + C::W_OFF + s * C::W_STAGE, wsrc + (size_t)w * C::W_STAGE, C::W_STAGE,
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(a.act) + (size_t)(tl.y >> 3) * 1024;
             const uint32_t bbytes = (uint32_t)tl.z * 128u;
             for (int ks = 0; ks < KS; ++ks) {
-                if (!wait_all(sfree(s >> 1), ph ^ 1, abort_flag)) break;
+                if (!wait_all(sfree(s >> 1), ph ^ 1, abort_flag, kWtSfreeB)) break;
                 if (elect_one()) {
                     mbar_arrive_expect_tx(full_b(s), kKS * bbytes);
 #pragma unroll
@@ -257,13 +262,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const int4 tl = a.tiles[item / a.n_rt];
             const uint32_t idesc = idesc_bf16(128, tl.z);
             const int buf = it & 1;
-            if (!wait_all(accempty(buf), ((it >> 1) & 1) ^ 1, abort_flag)) break;
+            if (!wait_all(accempty(buf), ((it >> 1) & 1) ^ 1, abort_flag, kWtAccEmpty)) break;
             tc_fence_after();
             const uint32_t dbase = tmem + buf * C::ACC_COLS;
             bool ok = true;
             for (int pi = 0; pi < KS / 2; ++pi, ++pair) {
                 const int ps = pair & 1;
-                if (!wait_all(aready(ps), (pair >> 1) & 1, abort_flag)) {
+                if (!wait_all(aready(ps), (pair >> 1) & 1, abort_flag, kWtAReady)) {
                     ok = false;
                     break;
                 }
@@ -293,6 +298,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             if (elect_one()) tc_commit(accfull(buf));
             __syncwarp();
         }
+        // Every MMA this thread issued has finished before the CTA frees its tensor
+        // memory, also when a role gave up mid-item (bounded; no abort check).
+        if (elect_one()) tc_commit(mma_done);
+        __syncwarp();
+        {
+            const uint64_t t0 = global_ns();
+            while (!mbar_try_wait(mma_done, 0) && global_ns() - t0 < kWaitLimitNs) {
+            }
+        }
+        __syncwarp();
     } else if (TRACE && warp == kWarpMma + 1) {
         // ---------------------------------------- trace observer (CTA 0 only)
         // records when each token-tile stage lands; bounded waits, never aborts
@@ -323,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         // read the packed words (and the row's scales and biases) of step i, release its half of the W stage
         auto load_w = [&](int i) -> bool {
             const int wi = i >> 1, ls = wi % C::SW;
-            if (!wait_all(full_w(ls), (wi / C::SW) & 1, abort_flag)) return false;
+            if (!wait_all(full_w(ls), (wi / C::SW) & 1, abort_flag, kWtFullW)) return false;
             if (tr) trace_at<TRACE>(a, kTrDqStart, i);
 #pragma unroll
             for (int g = 0; g < kKS; ++g) {
@@ -347,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         bool ok = j >= total || load_w(j);
         for (int step = j; step < total && ok; step += kQuads) {
             // A stage j was last read by the MMAs of step (step - 4)
-            if (!wait_all(sfree(j >> 1), ((step / kQuads) & 1) ^ 1, abort_flag)) break;
+            if (!wait_all(sfree(j >> 1), ((step / kQuads) & 1) ^ 1, abort_flag, kWtSfreeA)) break;
             tc_fence_after();
 #pragma unroll
             for (int g = 0; g < kKS; ++g) {
@@ -359,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             if (tr) trace_at<TRACE>(a, kTrDqStored, step);
             tc_wait_st();
             // the step's token tile (B stage j) must have landed before the pair is ready
-            if (!wait_all(full_b(j), (step / kQuads) & 1, abort_flag)) break;
+            if (!wait_all(full_b(j), (step / kQuads) & 1, abort_flag, kWtFullB)) break;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(aready(j >> 1));
@@ -380,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const int4 tl = a.tiles[item / a.n_rt];
             const int rt = item % a.n_rt;
             const int buf = it & 1;
-            if (!wait_all(accfull(buf), (it >> 1) & 1, abort_flag)) break;
+            if (!wait_all(accfull(buf), (it >> 1) & 1, abort_flag, kWtAccFull)) break;
             if (et == 0) trace_at<TRACE>(a, kTrEpStart, it);
             tc_fence_after();
             const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + buf * C::ACC_COLS;
@@ -466,7 +481,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     __syncthreads();
     tc_fence_after();
     if (warp == kWarpMma) tmem_dealloc(tmem, C::TMEM_COLS);
-    if (tid == 0 && *abort_flag) atomicExch(a.err, kDevTimeout);
+    if (tid == 0 && *abort_flag) {
+        atomicExch(a.err + 1, *abort_flag);  // which wait gave up first
+        atomicExch(a.err, kDevTimeout);
+    }
 }
 
 }  // namespace

@@ -784,11 +784,16 @@ extern "C" int obs_check_device(obs_ctx* ctx, void* stream) {
     OBS_CHECK_CTX(ctx);
     CU(cudaStreamSynchronize(as_stream(stream)), "stream sync");
     CU(cudaGetLastError(), "pending error");
-    int flag = 0;
-    CU(cudaMemcpy(&flag, ctx->err_flag, 4, cudaMemcpyDeviceToHost), "read flag");
+    int words[2] = {0, 0};
+    CU(cudaMemcpy(words, ctx->err_flag, 8, cudaMemcpyDeviceToHost), "read flag");
+    const int flag = words[0];
     if (flag) {
-        CU(cudaMemset(ctx->err_flag, 0, 4), "clear flag");
-        if (flag == kDevTimeout) return fail(ctx, OBS_ERR_TIMEOUT, "a device-side wait gave up (timeout)");
+        CU(cudaMemset(ctx->err_flag, 0, 8), "clear flag");
+        if (flag == kDevTimeout) {
+            char msg[96];
+            snprintf(msg, sizeof msg, "a device-side wait gave up (timeout; GEMM wait code %d)", words[1]);
+            return fail(ctx, OBS_ERR_TIMEOUT, msg);
+        }
         if (flag == kDevBadTile) return fail(ctx, OBS_ERR_INVALID, "device refused a GEMM tile outside its buffers");
         if (flag == kDevBadSlot)
             return fail(ctx, OBS_ERR_INVALID, "device refused an expert-parallel row slot outside its buffers");

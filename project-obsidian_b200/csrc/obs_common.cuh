@@ -99,8 +99,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait: gives up after kWaitLimitNs or when another role of the CTA
-// has already given up (*abort != 0); on giving up sets *abort and returns false.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+// has already given up (*abort != 0); the wait that times out stores `code`
+// (non-zero: which wait it was) in *abort; returns false on giving up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code = 1) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
@@ -108,7 +109,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         if ((i & 63) == 0) {
             if (*abort) return false;
             if (global_ns() - t0 > kWaitLimitNs) {
-                *abort = 1;
+                *abort = code;
                 return false;
             }
         }
