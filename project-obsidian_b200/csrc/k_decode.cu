@@ -256,7 +256,10 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     return v;
 }
 
-// every CTA of the grid; false (error flag set) after a timeout
+// every CTA of the grid; false (error flag set) after a timeout.  The arrival
+// counter only grows (launch n's barriers wait for (2n+1)G and (2n+2)G arrivals,
+// n the generation read at the start), so no launch needs it cleared; the
+// comparison is wrap-safe.
 __device__ bool grid_sync(uint32_t* bar, uint32_t target, int* err) {
     __shared__ int s_ok;
     __syncthreads();
@@ -265,7 +268,7 @@ __device__ bool grid_sync(uint32_t* bar, uint32_t target, int* err) {
         atomicAdd(bar, 1u);
         int ok = 1;
         const uint64_t t0 = global_ns();
-        while (ld_acquire_gpu(bar) < target) {
+        while ((int)(ld_acquire_gpu(bar) - target) < 0) {
             if (global_ns() - t0 > kWaitLimitNs) {
                 ok = 0;
                 atomicExch(err, kDevTimeout);
@@ -276,6 +279,24 @@ __device__ bool grid_sync(uint32_t* bar, uint32_t target, int* err) {
     }
     __syncthreads();
     return s_ok != 0;
+}
+
+// load_x32 from shared memory (or any generic address)
+__device__ __forceinline__ float load_x32_gen(const uint16_t* x, float (&xr)[32]) {
+    const uint4* p = reinterpret_cast<const uint4*>(x);
+    float sum = 0.0f;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        uint4 q = p[v];
+        uint32_t qs[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            xr[v * 8 + 2 * c] = __uint_as_float(qs[c] << 16);
+            xr[v * 8 + 2 * c + 1] = __uint_as_float(qs[c] & 0xFFFF0000u);
+            sum += xr[v * 8 + 2 * c] + xr[v * 8 + 2 * c + 1];
+        }
+    }
+    return sum;
 }
 
 // load_x32 for data written earlier in this kernel (read through L2)
@@ -298,9 +319,11 @@ __device__ __forceinline__ float load_x32_cg(const uint16_t* __restrict__ x, flo
 
 __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
     const uint32_t* __restrict__ rw, const uint16_t* __restrict__ rs, const uint16_t* __restrict__ rb,
-    TiledSrc gsrc, TiledSrc dsrc, const uint16_t* __restrict__ x, const uint16_t* __restrict__ residual,
-    const float* __restrict__ bias, int T, int H, int I, int E, int K, int norm, FusedDecodeBufs f,
-    uint16_t* __restrict__ out) {
+    TiledSrc gsrc, TiledSrc dsrc, const uint16_t* __restrict__ x_in, const uint16_t* __restrict__ residual,
+    const float* __restrict__ bias, int T, int H, int I, int E, int K, int norm, int normalize, float eps,
+    FusedDecodeBufs f, uint16_t* __restrict__ out) {
+    extern __shared__ __align__(16) uint16_t s_x[];  // [T][H] the layer input, this CTA's copy
+    __shared__ float s_sq[2][256];
     __shared__ int s_ids[kFusedMaxT * kMaxK];
     __shared__ float s_wts[kFusedMaxT * kMaxK];
     __shared__ float s_part[kFusedWarps][kRowTile];  // C: [half][8 warps]; D: [16 warps]
@@ -313,13 +336,47 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
         if (f.trace && tid == 0) f.trace[8 * b + k] = global_ns();
     };
     mark(0);
+    // barrier generation of this launch (advanced by CTA 0 after the last barrier)
+    const uint32_t gen = *reinterpret_cast<volatile uint32_t*>(f.bar + 1);
+
+    // 0: the layer input into shared memory; with `normalize`, the MoE input
+    // RMSNorm of rmsnorm.metal:9-37 in k_rmsnorm's order (256 threads per row,
+    // strided rounded squares, halving tree, IEEE divide and square root)
+    for (int t0 = 0; t0 < T; t0 += 2) {
+        const int t = t0 + (tid >> 8), l = tid & 255;
+        const uint16_t* row = x_in + (size_t)t * H;
+        if (normalize) {
+            float ps = 0.0f;
+            if (t < T)
+                for (int i = l; i < H; i += 256) {
+                    const float v = bf2f(row[i]);
+                    ps = __fadd_rn(ps, __fmul_rn(v, v));
+                }
+            s_sq[tid >> 8][l] = ps;
+            __syncthreads();
+            for (int st = 128; st > 0; st >>= 1) {
+                if (l < st) s_sq[tid >> 8][l] = __fadd_rn(s_sq[tid >> 8][l], s_sq[tid >> 8][l + st]);
+                __syncthreads();
+            }
+            if (t < T) {
+                const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(s_sq[tid >> 8][0], (float)H), eps));
+                for (int i = l; i < H; i += 256) s_x[(size_t)t * H + i] = f2bf(__fdiv_rn(bf2f(row[i]), rms));
+            }
+            __syncthreads();
+        } else if (t < T) {
+            for (int i = l * 8; i < H; i += 256 * 8)
+                *reinterpret_cast<uint4*>(s_x + (size_t)t * H + i) = __ldg(reinterpret_cast<const uint4*>(row + i));
+        }
+    }
+    __syncthreads();
+    const uint16_t* x = s_x;
 
     // A: router logits; item i on warp i / G of CTA i % G
     const int n_tc = (T + kWarpTok - 1) / kWarpTok;
     for (int item = warp * G + b; item < E * n_tc; item += kFusedWarps * G)
-        router_warp_item(rw, rs, rb, x, T, H, E, item % E, (item / E) * kWarpTok, lane, f.logits);
+        router_warp_item<true>(rw, rs, rb, x, T, H, E, item % E, (item / E) * kWarpTok, lane, f.logits);
     mark(1);
-    if (!grid_sync(f.bar, G, f.err)) return;
+    if (!grid_sync(f.bar, (2 * gen + 1) * G, f.err)) return;
     mark(2);
 
     // B: top-k of every token, in every CTA
@@ -353,7 +410,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
             for (int j = (w8 >> 1); j < nkt; j += 4) {
                 const int kt = ks * nkt + j;
                 float xr[32];
-                const float xs = load_x32(x + (size_t)t * H + kt * kGroup + (lane & 1) * 32, xr);
+                const float xs = load_x32_gen(x + (size_t)t * H + kt * kGroup + (lane & 1) * 32, xr);
                 block_dot(gsrc, e, 2 * rt + half, kt, xr, xs, lane, acc);
             }
 #pragma unroll
@@ -395,8 +452,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
         }
     }
     mark(4);
-    if (!grid_sync(f.bar, 2 * G, f.err)) return;
+    if (!grid_sync(f.bar, (2 * gen + 2) * G, f.err)) return;
     mark(5);
+    // every CTA read `gen` before the first barrier: the next launch may use the next one
+    if (b == 0 && tid == 0) *reinterpret_cast<volatile uint32_t*>(f.bar + 1) = gen + 1;
 
     // D: down -- CTA units (pair p, row tile rt) like one CTA of k_decode_down
     {
@@ -480,17 +539,19 @@ cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t
 }
 
 cudaError_t launch_decode_fused(const LayerDev& L, const Shape& sh, const uint16_t* x, const uint16_t* residual,
-                                const float* bias, int T, int norm, const FusedDecodeBufs& f, uint16_t* out,
-                                int num_sms, cudaStream_t st) {
+                                const float* bias, int T, int norm, int normalize, float eps,
+                                const FusedDecodeBufs& f, uint16_t* out, int num_sms, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    if (T > kFusedMaxT || sh.K > kMaxK || sh.E > kMaxE) return cudaErrorInvalidValue;
+    if (T > kFusedMaxT || sh.K > kMaxK || sh.E > kMaxE || sh.H % 2048) return cudaErrorInvalidValue;
     const TiledSrc g{L.gateup, sh.I / 64, sh.H / kGroup, 1, 0};  // paired blocks
     const TiledSrc dn{L.down, sh.H / kRowTile, sh.I / kGroup, 1, 0};
-    cudaError_t e = cudaMemsetAsync(f.bar, 0, 4, st);
+    const size_t smem = (size_t)T * sh.H * 2;  // the layer input rows
+    cudaError_t e = cudaFuncSetAttribute(k_decode_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);  // one CTA per SM: every CTA is resident (cooperative)
     cfg.blockDim = dim3(kFusedThreads);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
@@ -499,7 +560,7 @@ cudaError_t launch_decode_fused(const LayerDev& L, const Shape& sh, const uint16
     cfg.numAttrs = 1;
     note_launch();
     return cudaLaunchKernelEx(&cfg, k_decode_fused, L.router_w, L.router_s, L.router_b, g, dn, x, residual, bias, T,
-                              sh.H, sh.I, sh.E, sh.K, norm, f, out);
+                              sh.H, sh.I, sh.E, sh.K, norm, normalize, eps, f, out);
 }
 
 cudaError_t launch_decode_ffn_mlx(const uint32_t* gw, const uint16_t* gs, const uint16_t* gb, const uint32_t* uw,

@@ -680,7 +680,8 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
     if (path == OBS_PATH_DECODE && T <= kFusedMaxT) {
         // router, top-k, experts and combine in one cooperative launch
         prof_begin(ctx, OBS_STAGE_DECODE_FUSED, st);
-        CU(launch_decode_fused(L, s, x, residual, logit_bias, T, ctx->cfg.norm_topk, ctx->fused, out, ctx->num_sms, st),
+        CU(launch_decode_fused(L, s, x, residual, logit_bias, T, ctx->cfg.norm_topk, 0, 0.0f, ctx->fused, out,
+                               ctx->num_sms, st),
            "fused decode");
         prof_end(ctx, st);
         return OBS_OK;
@@ -747,10 +748,23 @@ extern "C" int obs_moe_stack_forward(obs_ctx* ctx, int layer0, int n_layers, uin
     cudaStream_t st = as_stream(stream);
     uint16_t* r = resid;
     uint16_t* other = ctx->rtmp_dev;
+    const int eff = path == OBS_PATH_AUTO ? (T <= ctx->decode_max ? OBS_PATH_DECODE : OBS_PATH_PREFILL) : path;
+    const bool fused = ctx->ep_world <= 1 && eff == OBS_PATH_DECODE && T > 0 && T <= kFusedMaxT;
     for (int l = layer0; l < layer0 + n_layers; ++l) {
-        if (T > 0) CU(launch_rmsnorm(r, nullptr, T, ctx->sh.H, ctx->cfg.rms_eps, ctx->xnorm_dev, st), "rmsnorm");
-        rc = obs_moe_forward(ctx, l, ctx->xnorm_dev, other, r, T, logit_bias, path, stream);
-        if (rc) return rc;
+        if (fused) {
+            // RMSNorm, router, top-k, experts and the residual combine of the layer in one launch
+            rc = check_layer(ctx, l, true);
+            if (rc) return rc;
+            prof_begin(ctx, OBS_STAGE_DECODE_FUSED, st);
+            CU(launch_decode_fused(ctx->layers[l], ctx->sh, r, r, logit_bias, T, ctx->cfg.norm_topk, 1,
+                                   ctx->cfg.rms_eps, ctx->fused, other, ctx->num_sms, st),
+               "fused decode");
+            prof_end(ctx, st);
+        } else {
+            if (T > 0) CU(launch_rmsnorm(r, nullptr, T, ctx->sh.H, ctx->cfg.rms_eps, ctx->xnorm_dev, st), "rmsnorm");
+            rc = obs_moe_forward(ctx, l, ctx->xnorm_dev, other, r, T, logit_bias, path, stream);
+            if (rc) return rc;
+        }
         std::swap(r, other);
     }
     if (r != resid && T > 0)
@@ -789,6 +803,8 @@ extern "C" int obs_check_device(obs_ctx* ctx, void* stream) {
     const int flag = words[0];
     if (flag) {
         CU(cudaMemset(ctx->err_flag, 0, 8), "clear flag");
+        // a wait that gave up leaves the fused decode layer's barrier counts behind: start over
+        CU(cudaMemset(ctx->fused.bar, 0, 8), "reset barrier");
         if (flag == kDevTimeout) {
             char msg[96];
             snprintf(msg, sizeof msg, "a device-side wait gave up (timeout; GEMM wait code %d)", words[1]);

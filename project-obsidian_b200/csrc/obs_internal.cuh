@@ -144,15 +144,17 @@ struct FusedDecodeBufs {
     float* part_gu;     // [T*K][n_rt_gu][kDecodeSplit][2][128] gate/up split partials
     uint32_t* cnt_gu;   // [T*K][n_rt_gu]  self-resetting arrival counters
     uint32_t* cnt_dn;   // [T][n_rt_dn]
-    uint32_t* bar;      // grid barrier arrivals (zeroed before each launch)
+    uint32_t* bar;      // [0] grid barrier arrivals (only grows), [1] launch generation
     uint16_t* h;        // [T*K][I]
     uint16_t* y;        // [T*K][H]
     int* err;
     uint64_t* trace;    // optional: thread 0 of CTA b writes %globaltimer at 7 points to trace[8b .. 8b+6]
 };
+// normalize = 1: x is the residual stream and the kernel applies the MoE input
+// RMSNorm (eps) itself, bit-identical to launch_rmsnorm.
 cudaError_t launch_decode_fused(const LayerDev& L, const Shape& sh, const uint16_t* x, const uint16_t* residual,
-                                const float* bias, int T, int norm, const FusedDecodeBufs& f, uint16_t* out,
-                                int num_sms, cudaStream_t st);
+                                const float* bias, int T, int norm, int normalize, float eps,
+                                const FusedDecodeBufs& f, uint16_t* out, int num_sms, cudaStream_t st);
 cudaError_t launch_decode_gateup(const LayerDev& L, const Shape& sh, const uint16_t* x, const int32_t* ids,
                                  int T, const DecodeBufs& d, cudaStream_t st);
 cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t* ids, const float* w,

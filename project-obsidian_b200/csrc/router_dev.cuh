@@ -12,7 +12,9 @@ constexpr int kMaxE = 256, kMaxK = 16;
 // One warp: logits of expert e for tokens t0 .. t0+7 in the canonical order
 // (dequant_matvec_8bit.metal:8-31): lane l chains fma(w, x, acc) over its
 // groups l*m .. (l+1)*m-1 in column order, the lanes meet in the adjacent
-// pairwise tree (xor-butterfly offsets 1, 2, 4, 8, 16).
+// pairwise tree (xor-butterfly offsets 1, 2, 4, 8, 16).  kGenericX: x may live
+// in shared memory (plain loads instead of the read-only path).
+template <bool kGenericX = false>
 __device__ __forceinline__ void router_warp_item(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
                                                  const uint16_t* __restrict__ b, const uint16_t* __restrict__ x,
                                                  int T, int H, int E, int e, int t0, int lane,
@@ -43,7 +45,7 @@ __device__ __forceinline__ void router_warp_item(const uint32_t* __restrict__ w,
                 float a = acc[i];
 #pragma unroll
                 for (int v = 0; v < 8; ++v) {
-                    uint4 q = __ldg(xr + v);
+                    uint4 q = kGenericX ? xr[v] : __ldg(xr + v);
                     uint32_t qs[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
