@@ -319,7 +319,7 @@ def run_stack(args, rank, world, local):
                    "parallelism": (f"expert parallel x{world} (NVLink peer all-to-all)" if ep else
                                    f"data parallel x{world} (replicas)" if world > 1 else "single GPU"),
                    "l2": f"inputs larger than L2: {nl} resident layers ({nl * 340} MB) per step",
-                   "path": "decode (mat-vec)" if decode and T <= 4 and not ep else "prefill (tcgen05 grouped GEMM)",
+                   "path": "decode (mat-vec)" if decode and T <= 2 and not ep else "prefill (tcgen05 grouped GEMM)",
                    "zipf_beta": beta, "load_max_over_mean_layer0": imbalance,
                    "load_max_over_mean_all_layers": float(load.max() / load.mean())},
         "roofline": roof, "distinct_experts_per_layer": float(np.mean(U)),
@@ -426,7 +426,7 @@ def main():
     # N GPUs: each routes its own T tokens; by default every GPU holds all experts
     # (data-parallel replicas), with --ep E/N experts per GPU and an NVLink exchange
     ep = world > 1 and args.ep
-    path = obsmoe.PATH_DECODE if T <= 4 and not ep else obsmoe.PATH_PREFILL
+    path = obsmoe.PATH_DECODE if T <= 2 and not ep else obsmoe.PATH_PREFILL
     shape = obsmoe.MoeShape(H, I, E, K, n_layers=N_ROT, max_tokens=max(T, 16),
                             ep_world=world if ep else 1, ep_rank=rank if ep else 0)
     ctx = obsmoe.MoeContext(shape, local)

@@ -64,7 +64,7 @@ typedef struct obs_config {
     int32_t n_layers;          /* layers whose weights the context holds */
     int32_t max_tokens;        /* largest T of one call (sizes the scratch) */
     int32_t norm_topk;         /* renormalise the top-k weights (norm_topk_prob) */
-    int32_t decode_max_tokens; /* OBS_PATH_AUTO threshold; <= 0 picks 4 */
+    int32_t decode_max_tokens; /* OBS_PATH_AUTO threshold; <= 0 picks 2 */
     float rms_eps;             /* RMSNorm epsilon of the fused input norm */
     int32_t ep_world;          /* expert parallelism: ranks sharing the experts (<= 1: off, max 8) */
     int32_t ep_rank;           /* this context's rank: it holds experts [rank*E/world, (rank+1)*E/world) */

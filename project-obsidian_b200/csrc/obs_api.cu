@@ -57,7 +57,7 @@ struct obs_ctx {
     float* bias_dev = nullptr;
     uint16_t* xnorm_dev = nullptr;  // the layer stack's normalised input
     uint16_t* rtmp_dev = nullptr;   // the layer stack's other residual buffer
-    int R_cap = 0, max_tiles = 0, decode_max = 4;
+    int R_cap = 0, max_tiles = 0, decode_max = 2;
     uint64_t* trace = nullptr;  // obs_trace_enable
     int trace_n = 0;
     // expert parallelism (ep_world > 1): this rank holds experts [e0, e0 + E_local)
@@ -153,7 +153,8 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     if (ctx->ep_rank < 0 || ctx->ep_rank >= ctx->ep_world) return bad("ep_rank must be in [0, ep_world)");
     ctx->E_local = s.E / ctx->ep_world;
     ctx->e0 = ctx->ep_rank * ctx->E_local;
-    ctx->decode_max = cfg->decode_max_tokens > 0 ? cfg->decode_max_tokens : 4;
+    // measured on B200: the mat-vec (fused) layer wins up to 2 tokens, the grouped GEMM from 3
+    ctx->decode_max = cfg->decode_max_tokens > 0 ? cfg->decode_max_tokens : 2;
     if (ctx->decode_max > kDecodeMaxT) ctx->decode_max = kDecodeMaxT;
     ctx->device = device;
     cudaError_t e = cudaSetDevice(device);
