@@ -98,6 +98,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait that lets the thread sleep (up to hint_ns) until the phase completes,
+// instead of returning at once: a waiting warp then takes no issue slots from
+// the warps doing work on the same scheduler
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+constexpr uint32_t kWaitSleepNs = 20000;
+
 // Bounded wait: gives up after kWaitLimitNs or when another role of the CTA
 // has already given up (*abort != 0); the wait that times out stores `code`
 // (non-zero: which wait it was) in *abort; returns false on giving up.
@@ -105,13 +120,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63) == 0) {
-            if (*abort) return false;
-            if (global_ns() - t0 > kWaitLimitNs) {
-                *abort = code;
-                return false;
-            }
+        if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
+        if (*abort) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort = code;
+            return false;
         }
     }
 }
