@@ -4,18 +4,18 @@
 // (shaders/matmul_dequant_4bit.metal:21-66; host src/forward.rs:313-321,
 // per-expert calls :219-222) and the ew_swiglu between them (ops.metal:18-22).
 //
-// One persistent CTA per SM walks work items (token tile of <= 128 rows, weight
+// One persistent CTA per SM walks work items (token tile of <= BN rows, weight
 // row tile).  The MMA is M = 128 weight rows x N = the tile's token rows, so a
-// dequantised weight row feeds up to 128 tokens: the 4-bit -> bf16 unpack (four
-// ALU / fp16-pipe instructions per pair of weights) costs less than the tensor
-// work it feeds once a tile holds more than ~96 tokens.  Tensor memory holds
-// two accumulator buffers of N = 128 fp32 columns (the epilogue drains one
-// while the next item accumulates) and four dequantised A stages.  To fit the
-// SwiGLU pair into one accumulator, the gate/up weight array is "paired": each
-// 128-row block holds 64 gate rows and the matching 64 up rows, interleaved by
-// TMEM lane quarter (rows 32q + i: gate feature 16q + i for i < 16, up feature
-// 16q + i - 16 for i >= 16), so one MMA chain yields gate and up of 64 features
-// and the epilogue pairs them with one shuffle across lanes i and i + 16.
+// dequantised weight row feeds up to BN tokens.  Two instances: BN = 128 (large
+// batches: the 4-bit -> bf16 unpack, four ALU / fp16-pipe instructions per pair
+// of weights, is then cheap per token) and BN = 64 (everything else: the two
+// accumulator buffers of 64 columns leave TMEM room for six A stages, so the
+// dequant warps run one more pair of steps ahead of the MMAs).  To fit the SwiGLU
+// pair into one accumulator, the gate/up weight array is "paired": each 128-row
+// block holds 64 gate rows and the matching 64 up rows, interleaved by TMEM lane
+// quarter (rows 32q + i: gate feature 16q + i for i < 16, up feature 16q + i - 16
+// for i >= 16), so one MMA chain yields gate and up of 64 features and the
+// epilogue pairs them with one shuffle across lanes i and i + 16.
 //
 // The reduction dimension is walked in MMA steps of two k-groups (K = 128).
 // Twenty-four warps:
@@ -37,8 +37,8 @@
 //   warp 3      idle (keeps the dequant warps on TMEM lane quarters warp % 4;
 //               in trace builds it records when token tiles land);
 //   warps 4-19  four dequant quads (one warp per lane quarter); quad j owns the
-//               MMA steps j mod 4 and A stage j, so each warp has four step
-//               periods for its share: read the packed words of its 32 rows x
+//               MMA steps j mod 4 (A and B stage: step mod SA), so each warp has
+//               four step periods for its share: read the packed words of its 32 rows x
 //               two k-groups from the W stage, unpack two codes per bf16x2
 //               register, q = (0x4300 | n) - 128, w = fma.rn.bf16x2(q, s, b)
 //               (the correctly rounded bf16 of q*s + b), write them with
@@ -59,7 +59,6 @@
 namespace obs {
 namespace {
 
-constexpr int kBN = 128;   // token rows per tile (tcgen05 N)
 constexpr int kKS = 2;     // k-groups (K = 64 each) per MMA step
 constexpr int kWK = 4;     // k-groups per weight copy (one W stage = two MMA steps)
 constexpr int kQuads = 4;  // dequant quads; quad j owns MMA steps j mod 4
@@ -68,29 +67,34 @@ constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2, kWarpDq = 4, kWarpEp = kWarp
 constexpr int kThreads = 32 * (kWarpEp + kEpWarps);  // 768
 constexpr int kEpThreads = 32 * kEpWarps;
 
+// BN = token rows per tile (tcgen05 N).  TMEM holds two accumulator buffers of BN
+// fp32 columns and the A stages (64 columns each) in the rest: four stages (two
+// pair slots) at BN = 128, six (three pair slots) at BN = 64, so with small tiles
+// the dequant warps can run one more pair ahead of the MMAs.  Step s uses A and
+// B stage s % SA; pair slot p covers stages 2p, 2p+1.
+template <int BN>
 struct Cfg {
+    static constexpr int NPS = BN >= 128 ? 2 : 3;      // pair slots
+    static constexpr int SA = 2 * NPS, SB = SA;        // A stages (TMEM), B stages (shared memory)
     static constexpr int W_STAGE = kWK * kBlockBytes;  // 18432
-    static constexpr int SW = 3;                       // W stages (six MMA steps ahead)
-    static constexpr int B_GROUP = kBN * 128;          // one k-group of the token tile (SW128 K-major)
-    static constexpr int B_STAGE = kKS * B_GROUP;      // 32 KB
-    static constexpr int SB = 4;                       // B stages (the activations' L2 latency)
-    static constexpr int ACC_COLS = kBN;               // one accumulator buffer (fp32 columns)
+    static constexpr int SW = BN >= 128 ? 3 : 5;       // W stages (two MMA steps each)
+    static constexpr int B_GROUP = BN * 128;           // one k-group of the token tile (SW128 K-major)
+    static constexpr int B_STAGE = kKS * B_GROUP;
+    static constexpr int ACC_COLS = BN;                // one accumulator buffer (fp32 columns)
     static constexpr int A_COLS = kKS * 32;            // one A stage: 64 bf16 per row and k-group = 32 columns
-    static constexpr int SA = kQuads;
     static constexpr int A_TMEM = 2 * ACC_COLS;        // first A stage column
     static constexpr int TMEM_COLS = 512;
-    static constexpr int STG = kBN * 256;              // epilogue staging: 128 rows x 128 features bf16
+    static constexpr int STG = BN * 256;               // epilogue staging: BN rows x 128 features bf16
     static constexpr int B_OFF = 0;                    // 1024-aligned tiles first
     static constexpr int STG_OFF = B_OFF + SB * B_STAGE;
     static constexpr int W_OFF = STG_OFF + STG;
     static constexpr int BAR_OFF = W_OFF + SW * W_STAGE;
-    static constexpr int N_BARS = 2 * SW + SB + 2 * 2 + 4 + 1;
+    static constexpr int N_BARS = 2 * SW + SB + 2 * NPS + 4 + 1;
     static constexpr int SMEM = BAR_OFF + N_BARS * 8 + 32 + 1024;  // + alignment slack
+    static_assert(SMEM <= 232448, "smem");
+    static_assert(A_TMEM + SA * A_COLS <= TMEM_COLS, "tmem");
 };
-static_assert(Cfg::SMEM <= 232448, "smem");
-static_assert(Cfg::A_TMEM + Cfg::SA * Cfg::A_COLS <= Cfg::TMEM_COLS, "tmem");
 static_assert(kWK == 2 * kKS, "a W stage holds two MMA steps");
-static_assert(Cfg::SB == kQuads && Cfg::SA == kQuads, "quad j owns A stage j and B stage j");
 
 __device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
     uint32_t d;
@@ -136,10 +140,10 @@ __device__ __forceinline__ void trace_at(const GemmArgs& a, int role, int i) {
         if (blockIdx.x == 0 && i < a.trace_n) a.trace[(size_t)role * a.trace_n + i] = global_ns();
 }
 
-template <int EPI, bool TRACE>
+template <int EPI, int BN, bool TRACE>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     pdl_begin();
-    using C = Cfg;
+    using C = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
@@ -150,12 +154,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     auto full_w = [&](int s) { return bar_base + 8 * s; };
     auto empty_w = [&](int s) { return bar_base + 8 * (C::SW + s); };
     auto full_b = [&](int s) { return bar_base + 8 * (2 * C::SW + s); };
-    // pair slot ps = (step / 2) % 2 covers the A and B stages 2ps, 2ps + 1
-    auto aready = [&](int ps) { return bar_base + 8 * (2 * C::SW + C::SB + ps); };
-    auto sfree = [&](int ps) { return bar_base + 8 * (2 * C::SW + C::SB + 2 + ps); };
-    auto accfull = [&](int b) { return bar_base + 8 * (2 * C::SW + C::SB + 4 + b); };
-    auto accempty = [&](int b) { return bar_base + 8 * (2 * C::SW + C::SB + 6 + b); };
-    const uint32_t mma_done = bar_base + 8 * (2 * C::SW + C::SB + 8);  // the issuer's last commit
+    // pair slot ps = (step / 2) % NPS covers the A and B stages 2ps, 2ps + 1
+    constexpr int PB = 2 * C::SW + C::SB;
+    auto aready = [&](int ps) { return bar_base + 8 * (PB + ps); };
+    auto sfree = [&](int ps) { return bar_base + 8 * (PB + C::NPS + ps); };
+    auto accfull = [&](int b) { return bar_base + 8 * (PB + 2 * C::NPS + b); };
+    auto accempty = [&](int b) { return bar_base + 8 * (PB + 2 * C::NPS + 2 + b); };
+    const uint32_t mma_done = bar_base + 8 * (PB + 2 * C::NPS + 4);  // the issuer's last commit
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
@@ -164,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         // a pair of steps is ready when its two quads (eight warps) have written A and
         // seen B land; one issuer commit frees its A and B stages
         for (int s = 0; s < C::SB; ++s) mbar_init(full_b(s), 1);
-        for (int ps = 0; ps < 2; ++ps) mbar_init(aready(ps), 8), mbar_init(sfree(ps), 1);
+        for (int ps = 0; ps < C::NPS; ++ps) mbar_init(aready(ps), 8), mbar_init(sfree(ps), 1);
         for (int b = 0; b < 2; ++b) mbar_init(accfull(b), 1), mbar_init(accempty(b), kEpThreads);
         mbar_init(mma_done, 1);
         *abort_flag = 0;
@@ -267,8 +272,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const uint32_t dbase = tmem + buf * C::ACC_COLS;
             bool ok = true;
             for (int pi = 0; pi < KS / 2; ++pi, ++pair) {
-                const int ps = pair & 1;
-                if (!wait_all(aready(ps), (pair >> 1) & 1, abort_flag, kWtAReady)) {
+                const int ps = pair % C::NPS;
+                if (!wait_all(aready(ps), (pair / C::NPS) & 1, abort_flag, kWtAReady)) {
                     ok = false;
                     break;
                 }
@@ -323,13 +328,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         }
     } else if (warp >= kWarpDq && warp < kWarpEp) {
         // ------------------------------------------------------------ dequant
-        // Quad j (warps 4j+4 .. 4j+7) owns the MMA steps i = j mod 4 and A stage j.
-        // Step i reads half (i & 1) of W stage i / 2: k-groups 2(i&1), 2(i&1)+1.
+        // Quad j (warps 4j+4 .. 4j+7) owns the MMA steps i = j mod 4; step i writes
+        // A stage i % SA and reads half (i & 1) of W stage i / 2: k-groups 2(i&1), 2(i&1)+1.
         const int dw = warp - kWarpDq;  // 0..15
         const int j = dw >> 2;          // quad
         const int q = warp & 3;         // TMEM lane quarter this warp may write
         const int r = q * 32 + lane;    // weight row of the tile = TMEM lane
-        const uint32_t at = tmem + ((uint32_t)(q * 32) << 16) + C::A_TMEM + j * C::A_COLS;
+        const uint32_t at0 = tmem + ((uint32_t)(q * 32) << 16) + C::A_TMEM;
         const bool tr = TRACE && dw == 0 && lane == 0;
         const bool trq = TRACE && dw > 0 && dw < 4 && lane == 0;  // the other quarters of quad 0
         const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -361,8 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         };
         bool ok = j >= total || load_w(j);
         for (int step = j; step < total && ok; step += kQuads) {
-            // A stage j was last read by the MMAs of step (step - 4)
-            if (!wait_all(sfree(j >> 1), ((step / kQuads) & 1) ^ 1, abort_flag, kWtSfreeA)) break;
+            // A stage x was last read by the MMAs of step (step - SA), in pair slot x / 2
+            const int x = step % C::SA, use = step / C::SA;
+            const uint32_t at = at0 + x * C::A_COLS;
+            if (!wait_all(sfree(x >> 1), (use & 1) ^ 1, abort_flag, kWtSfreeA)) break;
             tc_fence_after();
 #pragma unroll
             for (int g = 0; g < kKS; ++g) {
@@ -373,11 +380,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             }
             if (tr) trace_at<TRACE>(a, kTrDqStored, step);
             tc_wait_st();
-            // the step's token tile (B stage j) must have landed before the pair is ready
-            if (!wait_all(full_b(j), (step / kQuads) & 1, abort_flag, kWtFullB)) break;
+            // the step's token tile (B stage x) must have landed before the pair is ready
+            if (!wait_all(full_b(x), use & 1, abort_flag, kWtFullB)) break;
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(aready(j >> 1));
+            if (lane == 0) mbar_arrive(aready(x >> 1));
             if (tr) trace_at<TRACE>(a, kTrDqDone, step);
             if (trq) trace_at<TRACE>(a, kTrDqDoneQ1 + dw - 1, step);
             // the quad's next step is four steps away: its load is off the critical loop
@@ -489,13 +496,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
 
 }  // namespace
 
-size_t gemm_smem_bytes(int) { return Cfg::SMEM; }
-int gemm_tile_rows() { return kBN; }
+size_t gemm_smem_bytes(int) { return Cfg<128>::SMEM; }
+int gemm_tile_rows() { return 128; }
 
-template <int EPI>
+template <int EPI, int BN>
 static cudaError_t launch_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
-    const int smem = Cfg::SMEM;
-    auto kern = a.trace ? k_gemm<EPI, true> : k_gemm<EPI, false>;
+    const int smem = Cfg<BN>::SMEM;
+    auto kern = a.trace ? k_gemm<EPI, BN, true> : k_gemm<EPI, BN, false>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return err;
     {
@@ -505,13 +512,16 @@ static cudaError_t launch_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// a.bn (the dispatch's tile size) picks the instance: 64-token tiles leave TMEM
+// for three pair slots of A stages, 128-token tiles for two
 cudaError_t launch_gemm(const GemmArgs& a, int epi, int num_sms, cudaStream_t st) {
-    if (a.bn > kBN || a.bn % kSegAlign || a.n_kt % kWK || a.n_kt <= 0 || !a.act || (epi == kEpiSwiglu && !a.paired))
+    if (a.bn > 128 || a.bn % kSegAlign || a.n_kt % kWK || a.n_kt <= 0 || !a.act || (epi == kEpiSwiglu && !a.paired))
         return cudaErrorInvalidValue;
+    const bool small = a.bn <= 64;
     switch (epi) {
-        case kEpiSwiglu: return launch_t<kEpiSwiglu>(a, num_sms, st);
-        case kEpiBf16: return launch_t<kEpiBf16>(a, num_sms, st);
-        case kEpiF32: return launch_t<kEpiF32>(a, num_sms, st);
+        case kEpiSwiglu: return small ? launch_t<kEpiSwiglu, 64>(a, num_sms, st) : launch_t<kEpiSwiglu, 128>(a, num_sms, st);
+        case kEpiBf16: return small ? launch_t<kEpiBf16, 64>(a, num_sms, st) : launch_t<kEpiBf16, 128>(a, num_sms, st);
+        case kEpiF32: return small ? launch_t<kEpiF32, 64>(a, num_sms, st) : launch_t<kEpiF32, 128>(a, num_sms, st);
     }
     return cudaErrorInvalidValue;
 }
