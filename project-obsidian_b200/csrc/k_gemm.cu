@@ -6,11 +6,11 @@
 //
 // One persistent CTA per SM walks work items (token tile of <= BN rows, weight
 // row tile).  The MMA is M = 128 weight rows x N = the tile's token rows, so a
-// dequantised weight row feeds up to BN tokens.  Two instances: BN = 128 (large
-// batches: the 4-bit -> bf16 unpack, four ALU / fp16-pipe instructions per pair
-// of weights, is then cheap per token) and BN = 64 (everything else: the two
-// accumulator buffers of 64 columns leave TMEM room for six A stages, so the
-// dequant warps run one more pair of steps ahead of the MMAs).  To fit the SwiGLU
+// dequantised weight row feeds up to BN tokens.  The template has two forms:
+// BN = 64, the one launched (the two accumulator buffers of 64 columns leave TMEM
+// room for six A stages, so the dequant warps run three pairs of steps ahead of
+// the MMAs), and BN = 128 (halves the 4-bit -> bf16 unpack per token), withdrawn
+// after an unexplained device fault on workloads with many 65-127-row tiles.  To fit the SwiGLU
 // pair into one accumulator, the gate/up weight array is "paired": each 128-row
 // block holds 64 gate rows and the matching 64 up rows, interleaved by TMEM lane
 // quarter (rows 32q + i: gate feature 16q + i for i < 16, up feature 16q + i - 16
@@ -22,11 +22,14 @@
 //   warp 0      weight producer: one 1-D bulk async copy of four k-groups
 //               (18 KB, contiguous by construction of the HBM layout) per W
 //               stage (= two MMA steps);
-//   warp 1      token-tile producer: bulk copies (L2 evict-last: every row tile
-//               re-reads them) of the tile's rows of the tiled activations
+//   warps 1, 3  token-tile producers: bulk copies (L2 evict-last: every row
+//               tile re-reads them) of the tile's rows of the tiled activations
 //               (128-byte-swizzled K-major 8-row atoms): for gate/up the routed
 //               input rows the dispatch permuted, for down the H rows of the
-//               gate/up epilogue;
+//               gate/up epilogue.  Warp 1 copies the first k-group of each MMA
+//               step, warp 3 the second: one thread takes ~200 ns to issue an
+//               8 KB bulk copy, so a single producer issuing both (~400 ns per
+//               step) held the MMAs back at large batches;
 //   warp 2      MMA issuer (the warp runs converged, one elected lane issues):
 //               tcgen05.mma kind::f16, A in TMEM, B in shared memory, K = 16,
 //               eight per step, fp32 accumulators in TMEM.  One thread issues an
@@ -34,14 +37,13 @@
 //               hundred, so it waits once per pair of steps (16 MMAs), on a
 //               barrier that says both steps' A and B stages are ready, and
 //               frees both with one commit;
-//   warp 3      idle (keeps the dequant warps on TMEM lane quarters warp % 4;
-//               in trace builds it records when token tiles land);
 //   warps 4-19  four dequant quads (one warp per lane quarter); quad j owns the
 //               MMA steps j mod 4 (A and B stage: step mod SA), so each warp has
 //               four step periods for its share: read the packed words of its 32 rows x
 //               two k-groups from the W stage, unpack two codes per bf16x2
-//               register, q = (0x4300 | n) - 128, w = fma.rn.bf16x2(q, s, b)
-//               (the correctly rounded bf16 of q*s + b), write them with
+//               register, w = fma.rn.bf16x2(n as a subnormal, s * 2^133, b)
+//               (the correctly rounded bf16 of n*s + b; scales outside that
+//               form's range take q = (0x4300 | n) - 128 first), write them with
 //               tcgen05.st into the A stage (one weight row per TMEM lane), wait
 //               for the step's token tile to land, and arrive on the pair's
 //               ready barrier;
@@ -63,7 +65,7 @@ constexpr int kKS = 2;     // k-groups (K = 64 each) per MMA step
 constexpr int kWK = 4;     // k-groups per weight copy (one W stage = two MMA steps)
 constexpr int kQuads = 4;  // dequant quads; quad j owns MMA steps j mod 4
 constexpr int kDqWarps = 4 * kQuads, kEpWarps = 4;
-constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2, kWarpDq = 4, kWarpEp = kWarpDq + kDqWarps;
+constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2, kWarpB2 = 3, kWarpDq = 4, kWarpEp = kWarpDq + kDqWarps;
 constexpr int kThreads = 32 * (kWarpEp + kEpWarps);  // 768
 constexpr int kEpThreads = 32 * kEpWarps;
 
@@ -111,6 +113,22 @@ __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t s2, uint32_t b
     const uint32_t magic = 0x43004300u;  // bf16x2 (128, 128)
 #pragma unroll
     for (int j = 0; j < 4; ++j) out[j] = bf2_fma(bf2_sub(((w >> (4 * j)) & 0x000F000Fu) | magic, magic), s2, b2);
+}
+
+// The same in one instruction per pair: the masked code n, read as a bf16 bit
+// pattern, is the subnormal n * 2^-133, and s2 carries the scale times 2^133
+// (its exponent field raised by 133, exact), so the product is exactly n * s and
+// fma.rn gives round(n * s + b), bit for bit the value above.  Valid for scales
+// with exponent field 1..121 (2^-126 <= |s| < 2^-5); the caller falls back to
+// dequant_word for any other group.
+__device__ __forceinline__ void dequant_word_sub(uint32_t w, uint32_t s2x, uint32_t b2, uint32_t* out) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = bf2_fma((w >> (4 * j)) & 0x000F000Fu, s2x, b2);
+}
+constexpr uint32_t kSubExpShift = 133u << 7;  // + 133 in a bf16 exponent field
+__device__ __forceinline__ bool sub_form_ok(uint32_t s_bits) {
+    const uint32_t ex = (s_bits >> 7) & 0xFFu;
+    return ex >= 1u && ex <= 121u;
 }
 
 // which wait timed out (recorded in the context's second error word)
@@ -168,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         for (int s = 0; s < C::SW; ++s) mbar_init(full_w(s), 1), mbar_init(empty_w(s), 8);
         // a pair of steps is ready when its two quads (eight warps) have written A and
         // seen B land; one issuer commit frees its A and B stages
-        for (int s = 0; s < C::SB; ++s) mbar_init(full_b(s), 1);
+        for (int s = 0; s < C::SB; ++s) mbar_init(full_b(s), kKS);  // one arrival per k-group producer
         for (int ps = 0; ps < C::NPS; ++ps) mbar_init(aready(ps), 8), mbar_init(sfree(ps), 1);
         for (int b = 0; b < 2; ++b) mbar_init(accfull(b), 1), mbar_init(accempty(b), kEpThreads);
         mbar_init(mma_done, 1);
@@ -229,8 +247,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         }
         if (*abort_flag && lane == 0) drain_ring(full_w(0), C::SW, issued);
         __syncwarp();
-    } else if (warp == kWarpB) {
-        // ----------------------------------------------- token-tile producer
+    } else if (warp == kWarpB || warp == kWarpB2) {
+        // ------------------------------------- token-tile producers (k-group g)
+        const int g = warp == kWarpB ? 0 : 1;
+        static_assert(kKS == 2, "one producer warp per k-group of an MMA step");
         const uint64_t pol = policy_evict_last();
         int s = 0, ph = 0, issued = 0;
         for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
@@ -240,18 +260,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             for (int ks = 0; ks < KS; ++ks) {
                 if (!wait_all(sfree(s >> 1), ph ^ 1, abort_flag, kWtSfreeB)) break;
                 if (elect_one()) {
-                    mbar_arrive_expect_tx(full_b(s), kKS * bbytes);
-#pragma unroll
-                    for (int g = 0; g < kKS; ++g)
-                        bulk_g2s_hint(sbase + C::B_OFF + s * C::B_STAGE + g * C::B_GROUP,
-                                      xsrc + (size_t)(ks * kKS + g) * a.atoms * 1024, bbytes, full_b(s), pol);
+                    mbar_arrive_expect_tx(full_b(s), bbytes);
+                    bulk_g2s_hint(sbase + C::B_OFF + s * C::B_STAGE + g * C::B_GROUP,
+                                  xsrc + (size_t)(ks * kKS + g) * a.atoms * 1024, bbytes, full_b(s), pol);
                 }
                 __syncwarp();
-                if (lane == 0) trace_at<TRACE>(a, kTrBSignal, issued);
+                if (g == 0 && lane == 0) trace_at<TRACE>(a, kTrBSignal, issued);
                 ++issued;
                 if (++s == C::SB) s = 0, ph ^= 1;
             }
         }
+        // (a phase the other producer never fed ends the drain at its time limit)
         if (*abort_flag && lane == 0) drain_ring(full_b(0), C::SB, issued);
         __syncwarp();
     } else if (warp == kWarpMma) {
@@ -313,19 +332,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             }
         }
         __syncwarp();
-    } else if (TRACE && warp == kWarpMma + 1) {
-        // ---------------------------------------- trace observer (CTA 0 only)
-        // records when each token-tile stage lands; bounded waits, never aborts
-        const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-        const int total = blockIdx.x == 0 ? min(my_items * KS, a.trace_n) : 0;
-        for (int i = 0; i < total && !*abort_flag; ++i) {
-            const uint64_t t0 = global_ns();
-            bool got = false;
-            while (!(got = mbar_try_wait(full_b(i % C::SB), (i / C::SB) & 1)) && global_ns() - t0 < kWaitLimitNs) {
-            }
-            if (!got) break;
-            if (lane == 0) trace_at<TRACE>(a, kTrBLanded, i);
-        }
     } else if (warp >= kWarpDq && warp < kWarpEp) {
         // ------------------------------------------------------------ dequant
         // Quad j (warps 4j+4 .. 4j+7) owns the MMA steps i = j mod 4; step i writes
@@ -340,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
         const int total = my_items * KS;
         uint32_t ws[8 * kKS], s2v[kKS], b2v[kKS];
+        bool subf[kKS];  // this row's group takes the subnormal form (s2v then holds s * 2^133)
         // read the packed words (and the row's scales and biases) of step i, release its half of the W stage
         auto load_w = [&](int i) -> bool {
             const int wi = i >> 1, ls = wi % C::SW;
@@ -350,7 +357,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                 const uint8_t* blk = smem + C::W_OFF + ls * C::W_STAGE + ((i & 1) * kKS + g) * kBlockBytes;
                 const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
                 const uint32_t sv = sb[r], bv = sb[kRowTile + r];
-                s2v[g] = sv | (sv << 16);
+                subf[g] = sub_form_ok(sv);
+                const uint32_t sx = subf[g] ? sv + kSubExpShift : sv;
+                s2v[g] = sx | (sx << 16);
                 b2v[g] = bv | (bv << 16);
                 // word w of row r lives in plane w/4 of the block
 #pragma unroll
@@ -371,11 +380,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const uint32_t at = at0 + x * C::A_COLS;
             if (!wait_all(sfree(x >> 1), (use & 1) ^ 1, abort_flag, kWtSfreeA)) break;
             tc_fence_after();
+            if (tr) trace_at<TRACE>(a, kTrDqAFree, step);
 #pragma unroll
             for (int g = 0; g < kKS; ++g) {
                 uint32_t v[32];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) dequant_word(ws[8 * g + c], s2v[g], b2v[g], &v[4 * c]);
+                if (__all_sync(0xffffffffu, subf[g])) {
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) dequant_word_sub(ws[8 * g + c], s2v[g], b2v[g], &v[4 * c]);
+                } else {  // a scale outside the subnormal form's range: per-row choice
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        if (subf[g]) dequant_word_sub(ws[8 * g + c], s2v[g], b2v[g], &v[4 * c]);
+                        else dequant_word(ws[8 * g + c], s2v[g], b2v[g], &v[4 * c]);
+                    }
+                }
                 tmem_st32(at + g * 32, v);
             }
             if (tr) trace_at<TRACE>(a, kTrDqStored, step);
@@ -496,8 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
 
 }  // namespace
 
-size_t gemm_smem_bytes(int) { return Cfg<128>::SMEM; }
-int gemm_tile_rows() { return 128; }
+size_t gemm_smem_bytes(int) { return Cfg<64>::SMEM; }
+int gemm_tile_rows() { return 64; }
 
 template <int EPI, int BN>
 static cudaError_t launch_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
@@ -512,16 +531,15 @@ static cudaError_t launch_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-// a.bn (the dispatch's tile size) picks the instance: 64-token tiles leave TMEM
-// for three pair slots of A stages, 128-token tiles for two
+// Only the 64-token form is launched: the 128-token form (Cfg<128>) ended in an
+// unexplained device fault on workloads with many 65-127-row tiles and is withdrawn.
 cudaError_t launch_gemm(const GemmArgs& a, int epi, int num_sms, cudaStream_t st) {
-    if (a.bn > 128 || a.bn % kSegAlign || a.n_kt % kWK || a.n_kt <= 0 || !a.act || (epi == kEpiSwiglu && !a.paired))
+    if (a.bn > 64 || a.bn % kSegAlign || a.n_kt % kWK || a.n_kt <= 0 || !a.act || (epi == kEpiSwiglu && !a.paired))
         return cudaErrorInvalidValue;
-    const bool small = a.bn <= 64;
     switch (epi) {
-        case kEpiSwiglu: return small ? launch_t<kEpiSwiglu, 64>(a, num_sms, st) : launch_t<kEpiSwiglu, 128>(a, num_sms, st);
-        case kEpiBf16: return small ? launch_t<kEpiBf16, 64>(a, num_sms, st) : launch_t<kEpiBf16, 128>(a, num_sms, st);
-        case kEpiF32: return small ? launch_t<kEpiF32, 64>(a, num_sms, st) : launch_t<kEpiF32, 128>(a, num_sms, st);
+        case kEpiSwiglu: return launch_t<kEpiSwiglu, 64>(a, num_sms, st);
+        case kEpiBf16: return launch_t<kEpiBf16, 64>(a, num_sms, st);
+        case kEpiF32: return launch_t<kEpiF32, 64>(a, num_sms, st);
     }
     return cudaErrorInvalidValue;
 }

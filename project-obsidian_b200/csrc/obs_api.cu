@@ -25,14 +25,11 @@ using namespace obs;
 
 namespace {
 constexpr int kDecodeMaxT = 64;  // largest T the decode path's scratch covers
-constexpr int kBNTile = 128;     // GEMM token tile for many rows per expert
-constexpr int kBNSmall = 64;     // ... and for few: leaves TMEM for a deeper A ring
-
-// token tile of a dispatch of `rows` routed rows over `experts` experts: 128-row
-// tiles only where experts average >= 192 rows (nearly every tile is then full);
-// 64-row tiles otherwise.  Workloads whose tiles were mostly 65-127 rows on the
-// 128-row kernel ended in a device fault whose cause is not yet found.
-static int tile_rows_for(long rows, int experts) { return rows >= 192L * experts ? kBNTile : kBNSmall; }
+// GEMM token tile (rows of one expert per work item).  The grouped GEMM kernel
+// also has a 128-row form, withdrawn: on workloads whose tiles were mostly 65-127
+// rows it ended in a device fault whose cause is not found, so only the 64-row
+// form runs.
+constexpr int kBNTile = 64;
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 }  // namespace
@@ -202,7 +199,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     const int T = cfg->max_tokens, K = s.K, E = s.E, W = ctx->ep_world, EL = ctx->E_local;
     // rows the grouped GEMMs may see: every rank's routed rows for this rank's experts, padded
     ctx->R_cap = (int)align_up((size_t)W * T * K + (size_t)EL * (kSegAlign - 1), 128);
-    ctx->max_tiles = ctx->R_cap / kBNSmall + EL + 1;  // enough for either tile size
+    ctx->max_tiles = ctx->R_cap / kBNTile + EL + 1;
     const int DT = ctx->decode_max > 0 ? kDecodeMaxT : 0;
     struct Item { void** p; size_t bytes; };
     std::vector<Item> items = {
@@ -462,7 +459,6 @@ static int dispatch_from_ids(obs_ctx* ctx, const int32_t* ids, const uint16_t* x
     CU(cudaMemsetAsync(ctx->disp.counts, 0, s.E * 4, st), "memset");
     if (T) CU(cudaMemsetAsync(ctx->disp.slot_of, 0, (size_t)T * s.K * 4, st), "memset");
     CU(launch_histogram(ids, T * s.K, s.E, ctx->disp.counts, ctx->err_flag, st), "histogram");
-    ctx->disp.bn = tile_rows_for((long)T * s.K, s.E);
     CU(launch_dispatch(ids, x, T, s, ctx->disp, permute, st), "dispatch");
     return OBS_OK;
 }
@@ -644,7 +640,6 @@ static int forward_ep(obs_ctx* ctx, const LayerDev& L, const uint16_t* x, uint16
     CU(cudaMemsetAsync(ctx->disp.counts, 0, ctx->E_local * 4, st), "memset");
     CU(launch_ep_recv(a, st), "ep receive");
     const Shape sl{s.H, s.I, ctx->E_local, 1};  // received rows: one local expert each
-    ctx->disp.bn = tile_rows_for((long)a.world * a.cap, ctx->E_local);
     CU(launch_dispatch(a.ids_local, reinterpret_cast<const uint16_t*>(ctx->ep_buf + a.off_rx), a.world * a.cap, sl,
                        ctx->disp, 1, st),
        "dispatch");
@@ -720,7 +715,6 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
        "topk");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_DISPATCH, st);
-    ctx->disp.bn = tile_rows_for((long)T * s.K, s.E);
     CU(launch_dispatch(ctx->ids, x, T, s, ctx->disp, 1, st), "dispatch");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_GEMM_GATEUP, st);

@@ -186,7 +186,7 @@ struct GemmArgs {
 // trace roles (rows of the trace buffer, trace_n entries each)
 enum TraceRole : int {
     kTrWIssue = 0,     // weight producer issued the copy of W stage i (four k-groups)
-    kTrBSignal = 1,    // token-tile producer issued the copies of k-step i
+    kTrBSignal = 1,    // token-tile producer of the first k-group issued its copy for k-step i
     kTrDqStart = 2,    // dequant warp 0 passed its waits for k-step i
     kTrDqDone = 3,     // dequant warp 0 arrived "pair ready" for k-step i
     kTrMmaStart = 4,   // MMA thread passed its wait for pair i (k-steps 2i, 2i+1)
@@ -196,7 +196,7 @@ enum TraceRole : int {
     kTrDqStored = 8,   // dequant warp 0 finished its TMEM stores of k-step i
     kTrMmaFenced = 9,  // MMA thread passed its fence for pair i
     kTrDqDoneQ1 = 10,  // as kTrDqDone, for the dequant warps of TMEM lane quarters 1, 2, 3
-    kTrBLanded = 13,   // the token tile of k-step i has landed in shared memory (observer warp)
+    kTrDqAFree = 13,   // dequant warp 0 passed the wait for its A stage of k-step i
     kTrRoles = 14
 };
 cudaError_t launch_gemm(const GemmArgs& a, int epi, int num_sms, cudaStream_t st);

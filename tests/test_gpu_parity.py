@@ -207,6 +207,67 @@ def test_gemm_dequant_bit_exact(small, proj):
     assert np.array_equal(got.view(np.uint32), ref[:, c0:c0 + n].T.copy().view(np.uint32))
 
 
+# bf16 bit patterns of scales at and around the edges of the GEMM's one-instruction unpack
+# (exponent field 1..121): zero, subnormal, smallest normal, just under and at 2^-5,
+# large, and negative ones on both sides
+EDGE_SCALES = np.array([0x0000, 0x0001, 0x007F, 0x0080, 0x3CFF, 0x3D00, 0x3DCC, 0x3F80, 0x4040,
+                        0x8080, 0xBC23, 0xBD00, 0xBF00, 0x3C23, 0x3B80, 0x3A00], np.uint16)
+
+
+@pytest.fixture(scope="module")
+def edge(cuda):
+    """The small layer with every weight group's scale drawn from EDGE_SCALES (mixed within
+    each 32-row warp), so both unpack forms and the per-row choice between them run."""
+    env = Env.__new__(Env)
+    env.torch = cuda
+    env.shape = obsmoe.MoeShape(2048, 256, 16, 4, n_layers=1, max_tokens=256)
+    env.ctx = obsmoe.MoeContext(env.shape, 0)
+    L = O.synth_layer(5, 0, E=16, H=2048, I=256, K=4)
+    rng = np.random.default_rng(17)
+    for name in ("gate_s", "up_s", "down_s"):
+        a = getattr(L, name)
+        setattr(L, name, EDGE_SCALES[rng.integers(0, len(EDGE_SCALES), a.shape)].astype(a.dtype))
+    env.L = L
+    env.seed = 5
+    env.ctx.load_layer(0, L)
+    yield env
+    env.ctx.check_device()
+    env.ctx.close()
+
+
+@pytest.mark.parametrize("proj", [0, 1, 2])
+def test_gemm_dequant_bit_exact_edge_scales(edge, proj):
+    """As above, on scales outside the one-instruction unpack's range (and zero / subnormal)."""
+    torch = edge.torch
+    L = edge.L
+    in_f = 256 if proj == 2 else 2048
+    w, s, b = [(L.gate_w, L.gate_s, L.gate_b), (L.up_w, L.up_s, L.up_b), (L.down_w, L.down_s, L.down_b)][proj]
+    for e in (2, 11):
+        ref = O.bf16_to_f32(O.dequant4_bf16(w[e], s[e], b[e]))
+        for c0 in range(0, in_f, 256):
+            eye = np.zeros((256, in_f), np.float32)
+            eye[np.arange(256), c0 + np.arange(256)] = 1.0
+            y = empty(torch, (256, ref.shape[0]), np.float32)
+            edge.ctx.matmul_raw_f32(0, proj, e, dev(torch, O.f32_to_bf16(eye)), 256, y)
+            got = host(y, np.float32)
+            assert np.array_equal(got.view(np.uint32), ref[:, c0:c0 + 256].T.copy().view(np.uint32)), (e, c0)
+
+
+@pytest.mark.parametrize("path,T", [(obsmoe.PATH_DECODE, 3), (obsmoe.PATH_PREFILL, 100)])
+def test_expert_ffn_edge_scales_vs_oracle(edge, path, T):
+    """Both FFN paths with edge-case scales against the oracle."""
+    torch = edge.torch
+    x = edge.x(T, row0=3)
+    rng = np.random.default_rng(T + 1)
+    ids = np.stack([rng.permutation(16)[:4] for _ in range(T)]).astype(np.int32)
+    y = empty(torch, (T * 4, 2048), np.uint16)
+    edge.ctx.expert_ffn(0, dev(torch, x), dev(torch, ids), T, y, path=path)
+    wmode = 0 if path == obsmoe.PATH_DECODE else 1
+    _, _, ry = O.moe_ffn_combine(edge.L, x, ids, np.full((T, 4), 0.25, np.float32), wmode=wmode, want_y=True)
+    got = O.bf16_to_f32(host(y, np.uint16)).reshape(T, 4, 2048)
+    assert rel_err(got, O.bf16_to_f32(ry)) < REL_SAME
+
+
 @pytest.mark.parametrize("n", [1, 16, 100, 256])
 def test_gemm_random_vs_oracle(small, n):
     torch = small.torch
