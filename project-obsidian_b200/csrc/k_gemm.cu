@@ -445,21 +445,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                 if (et == 0) bulk_wait_read0();
                 named_bar_sync(1, kEpThreads);
                 uint8_t* stg = smem + C::STG_OFF;
-                const int cx = fp >> 3, cb = (fp & 7) << 1;  // 16-byte chunk and byte of column fp
+                // lane pair (f, f^1) stores features (f & ~1, +1) as one 4-byte word
+                const int odd = lane & 1;
+                const int cx = fp >> 3, cb = (fp & 6) << 1;  // 16-byte chunk and byte of the feature pair
                 for (int j0 = 0; j0 < tl.z; j0 += 16) {
                     float v[16];
                     tmem_ld16(tq + j0, v);
                     tc_wait_ld();
-                    // lanes i and i+16 swap halves: lane i forms tokens j0..j0+7, lane i+16 j0+8..j0+15
+                    // SwiGLU: lanes i (gate) and i+16 (up) split the 16 tokens, lane i taking
+                    // {0-3, 8-11} and lane i+16 {4-7, 12-15} (k-th of each: tk + 4 * hi)
+                    float h[8];
 #pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) {
-                        const float mine = hi ? v[jj + 8] : v[jj];
-                        const float other = __shfl_xor_sync(0xffffffffu, hi ? v[jj] : v[jj + 8], 16);
-                        const float hv = hi ? silu_mul(other, mine) : silu_mul(mine, other);
-                        const int t = j0 + jj + 8 * hi;
-                        // one k-tile plane of H, swizzled like the global layout
-                        *reinterpret_cast<uint16_t*>(stg + (t >> 3) * 1024 + (t & 7) * 128 + ((cx ^ (t & 7)) << 4) + cb) =
-                            f2bf(hv);
+                    for (int k = 0; k < 8; ++k) {
+                        const int tk = (k & 3) + ((k >> 2) << 3);
+                        const float mine = v[tk + 4 * hi];
+                        const float other = __shfl_xor_sync(0xffffffffu, v[tk + 4 * (hi ^ 1)], 16);
+                        h[k] = hi ? silu_mul(other, mine) : silu_mul(mine, other);
+                    }
+                    // tokens a and a + 2 of each half: the even lane of a pair keeps token a, the
+                    // odd lane token a + 2, and they swap the other.  One store instruction then
+                    // writes tokens a, a+2, a+4, a+6, whose swizzled chunks use disjoint banks.
+#pragma unroll
+                    for (int p = 0; p < 4; ++p) {
+                        const int ka = (p & 1) + ((p >> 1) << 2);  // h index of token a; a + 2 is ka + 2
+                        const float keep = odd ? h[ka + 2] : h[ka];
+                        const float recv = __shfl_xor_sync(0xffffffffu, odd ? h[ka] : h[ka + 2], 1);
+                        const int t = j0 + (ka & 3) + ((ka >> 2) << 3) + 4 * hi + 2 * odd;
+                        *reinterpret_cast<uint32_t*>(stg + (t >> 3) * 1024 + (t & 7) * 128 + ((cx ^ (t & 7)) << 4) + cb) =
+                            odd ? pack_bf2(recv, keep) : pack_bf2(keep, recv);
                     }
                 }
                 tc_fence_before();
@@ -475,17 +488,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                     trace_at<TRACE>(a, kTrEpDone, it);
                 }
             } else {
-                // row-major Y: 256 bytes per token row at a 2*out_ld stride
+                // row-major Y: 256 bytes per token row at a 2*out_ld stride.  Staging rows
+                // are 256 bytes with the 16-byte chunks of odd rows swapped in fours
+                // (chunk c at c ^ 4), so the two tokens of one store use disjoint banks.
                 named_bar_sync(1, kEpThreads);  // the previous item's rows have been copied out
                 uint8_t* stg = smem + C::STG_OFF;
-                const int f = q * 32 + lane;
+                const int odd = lane & 1;
+                const int fb = (q * 32 + (lane & ~1)) * 2;  // byte of the feature pair in a row
                 for (int j0 = 0; j0 < tl.z; j0 += 16) {
                     float g[16];
                     tmem_ld16(tq + j0, g);
                     tc_wait_ld();
+                    // lane pair (f, f^1): the even lane stores token t, the odd lane token t + 1
 #pragma unroll
-                    for (int jj = 0; jj < 16; ++jj)
-                        *reinterpret_cast<uint16_t*>(stg + (j0 + jj) * 256 + f * 2) = f2bf(g[jj]);
+                    for (int jj = 0; jj < 16; jj += 2) {
+                        const float keep = odd ? g[jj + 1] : g[jj];
+                        const float recv = __shfl_xor_sync(0xffffffffu, odd ? g[jj] : g[jj + 1], 1);
+                        const int t = j0 + jj + odd;
+                        *reinterpret_cast<uint32_t*>(stg + t * 256 + (fb ^ (odd << 6))) =
+                            odd ? pack_bf2(recv, keep) : pack_bf2(keep, recv);
+                    }
                 }
                 tc_fence_before();
                 mbar_arrive(accempty(buf));
@@ -496,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                 for (int i = et; i < nstore * 16; i += kEpThreads) {
                     const int jr = i >> 4, c = i & 15;
                     *reinterpret_cast<uint4*>(yb + (size_t)jr * a.out_ld * 2 + c * 16) =
-                        *reinterpret_cast<const uint4*>(stg + jr * 256 + c * 16);
+                        *reinterpret_cast<const uint4*>(stg + jr * 256 + ((c ^ ((jr & 1) << 2)) << 4));
                 }
                 if (et == 0) trace_at<TRACE>(a, kTrEpDone, it);
             }
