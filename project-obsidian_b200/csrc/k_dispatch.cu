@@ -93,16 +93,16 @@ __global__ void __launch_bounds__(256) k_permute(const uint16_t* __restrict__ x,
     if (row >= *seg_end) return;
     const int t = src[row];
     const int chunks = H / 8;
-    for (int c0 = lane; c0 < chunks; c0 += 32 * 4) {
-        uint4 v[4];
+    for (int c0 = lane; c0 < chunks; c0 += 32 * 8) {  // H = 2048: the whole row in flight at once
+        uint4 v[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 8; ++u) {
             const int c = c0 + 32 * u;
             v[u] = make_uint4(0, 0, 0, 0);
             if (t >= 0 && c < chunks) v[u] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H) + c);
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 8; ++u) {
             const int c = c0 + 32 * u;
             if (c < chunks) *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(xp) + tiled_off(row, c * 8, atoms)) = v[u];
         }
@@ -139,12 +139,22 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const uint16_t* __restrict__ x,
 }
 
 // out[t] = bf16(residual[t] + sum_k w[t,k] * y[slot_of[t,k]]), rank order, fp32
+constexpr int kCombineMaxK = 16;  // the context accepts top_k <= 16
+
 __global__ void __launch_bounds__(256) k_combine(const uint16_t* __restrict__ y, int y_ld,
                                                  const int32_t* __restrict__ slot_of, const float* __restrict__ w,
                                                  const uint16_t* __restrict__ residual, int H, int K,
                                                  uint16_t* __restrict__ out) {
     pdl_begin();
     const int t = blockIdx.x;
+    // the token's K slots and weights once per CTA, so every row load below is independent
+    __shared__ int s_slot[kCombineMaxK];
+    __shared__ float s_w[kCombineMaxK];
+    if (threadIdx.x < K) {
+        s_slot[threadIdx.x] = slot_of ? slot_of[(size_t)t * K + threadIdx.x] : t * K + threadIdx.x;  // nullptr: item order
+        s_w[threadIdx.x] = w[(size_t)t * K + threadIdx.x];
+    }
+    __syncthreads();
     for (int f = threadIdx.x * 8; f < H; f += blockDim.x * 8) {
         float acc[8];
         if (residual) {
@@ -156,15 +166,22 @@ __global__ void __launch_bounds__(256) k_combine(const uint16_t* __restrict__ y,
 #pragma unroll
             for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
         }
-        for (int k = 0; k < K; ++k) {
-            const int slot = slot_of ? slot_of[(size_t)t * K + k] : t * K + k;  // nullptr: rows in item order
-            float wk = w[(size_t)t * K + k];
-            uint4 v = __ldg(reinterpret_cast<const uint4*>(y + (size_t)slot * y_ld + f));
-            uint32_t vs[4] = {v.x, v.y, v.z, v.w};
+        // ranks in order, eight rows in flight at a time
+        for (int k0 = 0; k0 < K; k0 += 8) {
+            uint4 v[8];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                acc[2 * c] = __fmaf_rn(wk, __uint_as_float(vs[c] << 16), acc[2 * c]);
-                acc[2 * c + 1] = __fmaf_rn(wk, __uint_as_float(vs[c] & 0xFFFF0000u), acc[2 * c + 1]);
+            for (int kk = 0; kk < 8; ++kk)
+                if (k0 + kk < K) v[kk] = __ldg(reinterpret_cast<const uint4*>(y + (size_t)s_slot[k0 + kk] * y_ld + f));
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                if (k0 + kk >= K) break;
+                const float wk = s_w[k0 + kk];
+                const uint32_t vs[4] = {v[kk].x, v[kk].y, v[kk].z, v[kk].w};
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    acc[2 * c] = __fmaf_rn(wk, __uint_as_float(vs[c] << 16), acc[2 * c]);
+                    acc[2 * c + 1] = __fmaf_rn(wk, __uint_as_float(vs[c] & 0xFFFF0000u), acc[2 * c + 1]);
+                }
             }
         }
         uint4 o = make_uint4(pack_bf2(acc[0], acc[1]), pack_bf2(acc[2], acc[3]), pack_bf2(acc[4], acc[5]),
@@ -222,6 +239,7 @@ cudaError_t launch_dispatch(const int32_t* ids, const uint16_t* x, int T, const 
 cudaError_t launch_combine(const uint16_t* y, int y_ld, const int32_t* slot_of, const float* w,
                            const uint16_t* residual, int T, int H, int K, uint16_t* out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
+    if (K > kCombineMaxK) return cudaErrorInvalidValue;
     {
         const cudaError_t le_ = launch_pdl(k_combine, dim3(T), dim3(256), 0, st, y, y_ld, slot_of, w, residual, H, K, out);
         if (le_ != cudaSuccess) return le_;

@@ -21,10 +21,19 @@ namespace {
 // dequantised weights per group stay in registers across the chunk's tokens.
 constexpr int kLeaves = 32;  // lanes of the canonical order = leaf sums of the prefill form
 
+// the expert histogram of this forward starts at zero (written by the first CTA,
+// after the previous kernel of the stream has completed)
+__device__ __forceinline__ void zero_on_first_cta(int32_t* counts, int E) {
+    if (counts && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+        for (int i = threadIdx.x; i < E; i += blockDim.x) counts[i] = 0;
+}
+
 __global__ void __launch_bounds__(256) k_router_warp(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
                                                      const uint16_t* __restrict__ b, const uint16_t* __restrict__ x,
-                                                     int T, int H, int E, float* __restrict__ logits) {
+                                                     int T, int H, int E, float* __restrict__ logits,
+                                                     int32_t* __restrict__ zero_counts) {
     pdl_begin();
+    zero_on_first_cta(zero_counts, E);
     const int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (e >= E) return;
     router_warp_item(w, s, b, x, T, H, E, e, blockIdx.y * kWarpTok, threadIdx.x & 31, logits);
@@ -47,8 +56,10 @@ __global__ void __launch_bounds__(kLeafThreads) k_router_leaf(const uint32_t* __
                                                               const uint16_t* __restrict__ s,
                                                               const uint16_t* __restrict__ b,
                                                               const uint16_t* __restrict__ x, int T, int H, int E,
-                                                              float* __restrict__ parts) {
+                                                              float* __restrict__ parts,
+                                                              int32_t* __restrict__ zero_counts) {
     pdl_begin();
+    zero_on_first_cta(zero_counts, E);
     extern __shared__ __align__(16) float rsm[];
     float(*xs)[kRPad] = reinterpret_cast<float(*)[kRPad]>(rsm);
     float(*ws)[kRPad] = reinterpret_cast<float(*)[kRPad]>(rsm + kRT * kRPad);
@@ -194,12 +205,12 @@ __global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, 
 int router_parts(int T) { return T <= 2 * kWarpTok ? 1 : kLeaves; }
 
 cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint16_t* x, int T, float* parts,
-                                 cudaStream_t st) {
+                                 cudaStream_t st, int32_t* zero_counts) {
     if (T <= 0) return cudaSuccess;
     if (router_parts(T) == 1) {
         dim3 grid((sh.E + 7) / 8, (T + kWarpTok - 1) / kWarpTok);
         {
-            const cudaError_t le_ = launch_pdl(k_router_warp, dim3(grid), dim3(256), 0, st, L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E, parts);
+            const cudaError_t le_ = launch_pdl(k_router_warp, dim3(grid), dim3(256), 0, st, L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E, parts, zero_counts);
             if (le_ != cudaSuccess) return le_;
         }
     } else {
@@ -209,7 +220,7 @@ cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint1
         dim3 grid((T + kRT - 1) / kRT, (sh.E + kRE - 1) / kRE, kLeaves);
         {
             const cudaError_t le_ = launch_pdl(k_router_leaf, dim3(grid), dim3(kLeafThreads), kLeafSmem, st, L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E,
-                                                              parts);
+                                                              parts, zero_counts);
             if (le_ != cudaSuccess) return le_;
         }
     }

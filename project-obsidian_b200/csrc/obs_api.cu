@@ -692,7 +692,9 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
         return OBS_OK;
     }
     prof_begin(ctx, OBS_STAGE_ROUTER, st);
-    CU(launch_router_logits(L, s, x, T, ctx->logits, st), "router");
+    // the grouped-GEMM path's expert histogram is zeroed by the router kernel
+    CU(launch_router_logits(L, s, x, T, ctx->logits, st, path == OBS_PATH_DECODE ? nullptr : ctx->disp.counts),
+       "router");
     prof_end(ctx, st);
     if (path == OBS_PATH_DECODE) {
         prof_begin(ctx, OBS_STAGE_TOPK, st);
@@ -708,7 +710,6 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
         prof_end(ctx, st);
         return OBS_OK;
     }
-    CU(cudaMemsetAsync(ctx->disp.counts, 0, s.E * 4, st), "memset");
     prof_begin(ctx, OBS_STAGE_TOPK, st);
     CU(launch_topk(ctx->logits, router_parts(T), logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids,
                    ctx->wts, ctx->disp.counts, nullptr, st),

@@ -74,8 +74,11 @@ cudaError_t launch_retile(const uint32_t* w, const uint16_t* s, const uint16_t* 
 // (1: final logits; 32: leaf sums that launch_topk / launch_router_finish
 // combine in the fixed tree).  `parts` must hold 32*T*E floats.
 int router_parts(int T);
+// zero_counts (optional, E ints): zeroed by the router kernel once the previous
+// kernel of the stream has completed, so the expert histogram needs no memset
+// node between router and top-k (a memset breaks the dependent-launch chain).
 cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint16_t* x, int T, float* parts,
-                                 cudaStream_t st);
+                                 cudaStream_t st, int32_t* zero_counts = nullptr);
 cudaError_t launch_router_finish(const float* parts, int T, int E, float* logits, cudaStream_t st);
 // logits_out (optional) receives the combined logits.
 cudaError_t launch_topk(const float* logits, int nparts, const float* bias, int T, int E, int K, int norm,
