@@ -327,8 +327,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
     __shared__ int s_ids[kFusedMaxT * kMaxK];
     __shared__ float s_wts[kFusedMaxT * kMaxK];
     __shared__ float s_part[kFusedWarps][kRowTile];  // C: [half][8 warps]; D: [16 warps]
-    __shared__ float s_gu[2][2][kRowTile];            // C: [half][block][row]
-    __shared__ int s_last[2];
+    __shared__ int s_last[1];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, b = blockIdx.x;
     // phase timeline (diagnostics): start, A done, barrier 1, B done, C done, barrier 2, D done
@@ -419,36 +418,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
                 if ((lane & 1) == 0) s_part[h * 8 + w8][(lane >> 1) + 16 * i] = v;
             }
             named_bar_sync(1 + h, 256);
-            // fixed-order sum of the 4 warps of each block
+            // fixed-order sum of the 4 warps of each block; the split partials meet in
+            // phase D, after the grid barrier has published them
             const int pr = t256 >> 7, row = t256 & 127;
             const float* sp = &s_part[h * 8][0];
             const float v = ((sp[pr * kRowTile + row] + sp[(pr + 2) * kRowTile + row]) + sp[(pr + 4) * kRowTile + row]) +
                             sp[(pr + 6) * kRowTile + row];
             float* tp = part + (((size_t)p * n_rt + rt) * kSplitGU) * 2 * kRowTile;
             tp[(size_t)ks * 2 * kRowTile + pr * kRowTile + row] = v;
-            __threadfence();
-            named_bar_sync(1 + h, 256);
-            if (t256 == 0) {
-                uint32_t* c = f.cnt_gu + (size_t)p * n_rt + rt;
-                const unsigned old = atomicAdd(c, 1u);
-                s_last[h] = (old == kSplitGU - 1);
-                if (s_last[h]) *c = 0;  // ready for the next call
-            }
-            named_bar_sync(1 + h, 256);
-            if (s_last[h]) {
-                __threadfence();
-                float sum = 0.0f;
-#pragma unroll
-                for (int jj = 0; jj < kSplitGU; ++jj) sum += __ldcg(tp + (size_t)jj * 2 * kRowTile + pr * kRowTile + row);
-                s_gu[h][pr][row] = sum;
-                named_bar_sync(1 + h, 256);
-                if (t256 < kRowTile) {
-                    const int rr = paired_row(t256 & 63);  // block 2rt + t/64 holds feature t
-                    const float g = s_gu[h][t256 >> 6][rr], uu = s_gu[h][t256 >> 6][rr + 16];
-                    f.h[(size_t)p * I + rt * kRowTile + t256] = f2bf(silu_mul(g, uu));
-                }
-            }
-            named_bar_sync(1 + h, 256);  // s_part / s_gu / s_last free for the next unit
+            named_bar_sync(1 + h, 256);  // s_part free for the next unit
         }
     }
     mark(4);
@@ -460,14 +438,34 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
     // D: down -- CTA units (pair p, row tile rt) like one CTA of k_decode_down
     {
         const int n_rd = H / kRowTile, KTd = I / kGroup, nwd = KTd < 16 ? KTd : 16, n_pairs = T * K;
+        const int n_rt = I / kRowTile;
+        uint16_t* s_h = s_x + (size_t)T * H;  // [I] this unit's SwiGLU input row, bf16
+        int p_h = -1;                          // the pair s_h holds
         for (int u = b; u < n_pairs * n_rd; u += G) {
             const int rt = u % n_rd, p = u / n_rd, t = p / K;
             const int e = checked_expert(s_ids[p], E, f.err);
+            if (p != p_h) {
+                // h of pair p: gate and up summed over the k-splits in split order, then
+                // SwiGLU (the last-split step of k_decode_gateup, term for term)
+                for (int i = tid; i < I; i += kFusedThreads) {
+                    const int rg = i / kRowTile, tt = i % kRowTile, pr = tt >> 6, rr = paired_row(tt & 63);
+                    const float* tp = f.part_gu + (((size_t)p * n_rt + rg) * kSplitGU) * 2 * kRowTile + pr * kRowTile;
+                    float g = 0.0f, uu = 0.0f;
+#pragma unroll
+                    for (int jj = 0; jj < kSplitGU; ++jj) {
+                        g += __ldcg(tp + (size_t)jj * 2 * kRowTile + rr);
+                        uu += __ldcg(tp + (size_t)jj * 2 * kRowTile + rr + 16);
+                    }
+                    s_h[i] = f2bf(silu_mul(g, uu));
+                }
+                __syncthreads();
+                p_h = p;
+            }
             if (warp < nwd) {
                 float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                 for (int kt = warp; kt < KTd; kt += nwd) {
                     float xr[32];
-                    const float xs = load_x32_cg(f.h + (size_t)p * I + kt * kGroup + (lane & 1) * 32, xr);
+                    const float xs = load_x32_gen(s_h + kt * kGroup + (lane & 1) * 32, xr);
                     block_dot(dsrc, e, rt, kt, xr, xs, lane, acc);
                 }
 #pragma unroll
@@ -545,7 +543,7 @@ cudaError_t launch_decode_fused(const LayerDev& L, const Shape& sh, const uint16
     if (T > kFusedMaxT || sh.K > kMaxK || sh.E > kMaxE || sh.H % 2048) return cudaErrorInvalidValue;
     const TiledSrc g{L.gateup, sh.I / 64, sh.H / kGroup, 1, 0};  // paired blocks
     const TiledSrc dn{L.down, sh.H / kRowTile, sh.I / kGroup, 1, 0};
-    const size_t smem = (size_t)T * sh.H * 2;  // the layer input rows
+    const size_t smem = (size_t)T * sh.H * 2 + (size_t)sh.I * 2;  // the layer input rows, one SwiGLU row
     cudaError_t e = cudaFuncSetAttribute(k_decode_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
