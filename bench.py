@@ -13,8 +13,10 @@ T=512 tokens.  Config 0 (decode of one token) is selectable with --config 0.
             Steps rotate over 4 resident layers (1.36 GB of weights, far more
             than the 126 MB L2), so no step reads the previous step's weights
             from L2.
-* e2e       the same metric through obs_moe_forward_host: pinned host input,
-            host->device copy, the layer, device->host copy of the output.
+* e2e       the same metric through the host entry points (obs_moe_forward_host_async
+            + obs_moe_host_join): every step copies its input from pinned host memory
+            and its output back; successive steps pipeline (step i+1's input copy and
+            step i-1's output copy overlap step i), as a serving loop would.
 * roofline  the dominant kernel (the gate/up grouped GEMM at T=512, the fused
             decode layer at T=1), algorithmic bytes per launch / its mean
             CUDA-event duration on the launching stream, against the measured
@@ -499,19 +501,25 @@ def main():
     value = world * T * args.steps / (ms / 1e3)
 
     # ---------------------------------------------------------------- e2e
+    # every step copies its input in from pinned host memory and its output back, through the
+    # pipelined host entry: step i+1's input copy and step i-1's output copy overlap step i
     xh = [torch.empty((T, H), dtype=torch.int16).pin_memory() for _ in range(N_ROT)]
     for l in range(N_ROT):
         xh[l].copy_(xs[l].cpu())
-    oh = torch.empty((T, H), dtype=torch.int16).pin_memory()
+    oh = [torch.empty((T, H), dtype=torch.int16).pin_memory() for _ in range(2)]
     for i in range(3):
-        ctx.moe_forward_host(i % N_ROT, xh[i % N_ROT], oh, T, path=path, stream=stream)
+        ctx.moe_forward_host_async(i % N_ROT, xh[i % N_ROT], oh[i % 2], T, path=path, stream=stream)
+    ctx.host_join(stream)
+    stream.synchronize()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
-        ctx.moe_forward_host(i % N_ROT, xh[i % N_ROT], oh, T, path=path, stream=stream)
+        ctx.moe_forward_host_async(i % N_ROT, xh[i % N_ROT], oh[i % 2], T, path=path, stream=stream)
+    ctx.host_join(stream)  # the last step's result is in host memory before e1
     e1.record(stream)
+    stream.synchronize()
     barrier()
     ems_t = torch.tensor([e0.elapsed_time(e1)], device="cuda")
     if dist is not None:

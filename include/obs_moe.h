@@ -117,6 +117,21 @@ int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint16_t* out,
 int obs_moe_forward_host(obs_ctx* ctx, int layer, const uint16_t* x_host, uint16_t* out_host,
                          const uint16_t* residual_host, int T, const float* logit_bias_host,
                          int path, void* stream);
+/* The host entry without the wait, for callers that pipeline successive layers
+ * or batches (the reference's forward.rs:421-441 / :164-232 call, issued ahead):
+ * the input copy runs on an internal stream into one of two staging slots
+ * (alternating per call), the forward on `stream`, the output copy on a second
+ * internal stream, so call i+1's input and call i-1's output overlap call i's
+ * forward.  x_host (and residual, bias) must stay unchanged, and out_host
+ * unread, until obs_moe_host_join's stream has passed; pinned host memory is
+ * needed for the copies to be asynchronous.  Successive calls use the same
+ * `stream`.  Single-GPU contexts only. */
+int obs_moe_forward_host_async(obs_ctx* ctx, int layer, const uint16_t* x_host, uint16_t* out_host,
+                               const uint16_t* residual_host, int T, const float* logit_bias_host,
+                               int path, void* stream);
+/* Make `stream` wait (on the device) for every output copy issued by
+ * obs_moe_forward_host_async so far; synchronise `stream` to read the results. */
+int obs_moe_host_join(obs_ctx* ctx, void* stream);
 
 /* ----------------------------------- stage entry points (tests, debugging) */
 /* gate_gpu / dequant_matvec_8bit (forward.rs:386-397): router logits fp32

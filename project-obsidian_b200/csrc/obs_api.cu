@@ -59,6 +59,17 @@ struct obs_ctx {
     uint16_t* out_dev = nullptr;
     uint16_t* res_dev = nullptr;
     float* bias_dev = nullptr;
+    // obs_moe_forward_host_async: two staging slots of its own, an input and an
+    // output copy stream (created on first use), and per slot the events that order them
+    struct HostSlot {
+        uint16_t *x = nullptr, *out = nullptr, *res = nullptr;
+        float* bias = nullptr;
+        cudaEvent_t in_done = nullptr, computed = nullptr, out_done = nullptr;
+        bool used = false;
+    } hs[2];
+    cudaStream_t hs_in = nullptr, hs_out = nullptr;
+    int hs_next = 0;
+    bool hs_ready = false;
     uint16_t* xnorm_dev = nullptr;  // the layer stack's normalised input
     uint16_t* rtmp_dev = nullptr;   // the layer stack's other residual buffer
     int R_cap = 0, max_tiles = 0, decode_max = 2;
@@ -225,6 +236,14 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->out_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->res_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->bias_dev, (size_t)E * 4},
+        {(void**)&ctx->hs[0].x, (size_t)T * s.H * 2},
+        {(void**)&ctx->hs[0].out, (size_t)T * s.H * 2},
+        {(void**)&ctx->hs[0].res, (size_t)T * s.H * 2},
+        {(void**)&ctx->hs[0].bias, (size_t)E * 4},
+        {(void**)&ctx->hs[1].x, (size_t)T * s.H * 2},
+        {(void**)&ctx->hs[1].out, (size_t)T * s.H * 2},
+        {(void**)&ctx->hs[1].res, (size_t)T * s.H * 2},
+        {(void**)&ctx->hs[1].bias, (size_t)E * 4},
         {(void**)&ctx->xnorm_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->rtmp_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->fused.part_gu, (size_t)kFusedMaxT * K * (s.I / kRowTile) * kDecodeSplit * 2 * kRowTile * 4},
@@ -301,6 +320,12 @@ extern "C" int obs_destroy(obs_ctx* ctx) {
     if (!ctx) return OBS_OK;
     cudaSetDevice(ctx->device);
     for (auto e : ctx->ev_pool) cudaEventDestroy(e);
+    if (ctx->hs_ready) {
+        cudaStreamSynchronize(ctx->hs_out);
+        for (auto& h : ctx->hs) cudaEventDestroy(h.in_done), cudaEventDestroy(h.computed), cudaEventDestroy(h.out_done);
+        cudaStreamDestroy(ctx->hs_in);
+        cudaStreamDestroy(ctx->hs_out);
+    }
     if (ctx->ep_connected)
         for (int r = 0; r < ctx->ep_world; ++r)
             if (r != ctx->ep_rank && ctx->ep.peer[r]) cudaIpcCloseMemHandle(ctx->ep.peer[r]);
@@ -797,6 +822,62 @@ extern "C" int obs_moe_forward_host(obs_ctx* ctx, int layer, const uint16_t* x_h
     if (rc) return rc;
     CU(cudaMemcpyAsync(out_host, ctx->out_dev, bytes, cudaMemcpyDeviceToHost, st), "d2h out");
     CU(cudaStreamSynchronize(st), "sync");
+    return OBS_OK;
+}
+
+extern "C" int obs_moe_forward_host_async(obs_ctx* ctx, int layer, const uint16_t* x_host, uint16_t* out_host,
+                                          const uint16_t* residual_host, int T, const float* bias_host, int path,
+                                          void* stream) {
+    OBS_CHECK_CTX(ctx);
+    int rc = check_T(ctx, T);
+    if (rc) return rc;
+    if (T == 0) return OBS_OK;
+    if (!x_host || !out_host) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    if (ctx->ep_world > 1) return fail(ctx, OBS_ERR_UNSUPPORTED, "the asynchronous host entry is single-GPU only");
+    CU(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (!ctx->hs_ready) {
+        CU(cudaStreamCreateWithFlags(&ctx->hs_in, cudaStreamNonBlocking), "copy stream");
+        CU(cudaStreamCreateWithFlags(&ctx->hs_out, cudaStreamNonBlocking), "copy stream");
+        for (auto& h : ctx->hs) {
+            CU(cudaEventCreateWithFlags(&h.in_done, cudaEventDisableTiming), "event");
+            CU(cudaEventCreateWithFlags(&h.computed, cudaEventDisableTiming), "event");
+            CU(cudaEventCreateWithFlags(&h.out_done, cudaEventDisableTiming), "event");
+        }
+        ctx->hs_ready = true;
+    }
+    const Shape& s = ctx->sh;
+    cudaStream_t st = as_stream(stream);
+    auto& h = ctx->hs[ctx->hs_next];
+    const size_t bytes = (size_t)T * s.H * 2;
+    // input: after this slot's previous forward has read its staging buffers
+    if (h.used) CU(cudaStreamWaitEvent(ctx->hs_in, h.computed, 0), "wait");
+    CU(cudaMemcpyAsync(h.x, x_host, bytes, cudaMemcpyHostToDevice, ctx->hs_in), "h2d x");
+    if (residual_host) CU(cudaMemcpyAsync(h.res, residual_host, bytes, cudaMemcpyHostToDevice, ctx->hs_in), "h2d");
+    if (bias_host) CU(cudaMemcpyAsync(h.bias, bias_host, s.E * 4, cudaMemcpyHostToDevice, ctx->hs_in), "h2d");
+    CU(cudaEventRecord(h.in_done, ctx->hs_in), "record");
+    // forward on the caller's stream: after the input landed and the slot's previous result left
+    CU(cudaStreamWaitEvent(st, h.in_done, 0), "wait");
+    if (h.used) CU(cudaStreamWaitEvent(st, h.out_done, 0), "wait");
+    rc = obs_moe_forward(ctx, layer, h.x, h.out, residual_host ? h.res : nullptr, T, bias_host ? h.bias : nullptr,
+                         path, stream);
+    if (rc) return rc;
+    CU(cudaEventRecord(h.computed, st), "record");
+    // output: after the forward
+    CU(cudaStreamWaitEvent(ctx->hs_out, h.computed, 0), "wait");
+    CU(cudaMemcpyAsync(out_host, h.out, bytes, cudaMemcpyDeviceToHost, ctx->hs_out), "d2h out");
+    CU(cudaEventRecord(h.out_done, ctx->hs_out), "record");
+    h.used = true;
+    ctx->hs_next ^= 1;
+    return OBS_OK;
+}
+
+extern "C" int obs_moe_host_join(obs_ctx* ctx, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    if (!ctx->hs_ready) return OBS_OK;
+    CU(cudaSetDevice(ctx->device), "cudaSetDevice");
+    cudaStream_t st = as_stream(stream);
+    for (auto& h : ctx->hs)
+        if (h.used) CU(cudaStreamWaitEvent(st, h.out_done, 0), "wait");
     return OBS_OK;
 }
 

@@ -29,7 +29,7 @@ _STATUS = {1: "INVALID", 2: "CUDA", 3: "NOMEM", 4: "STATE", 5: "TIMEOUT", 6: "NC
 EXPORTS = (
     "obs_abi_version", "obs_create", "obs_destroy", "obs_last_error", "obs_memory_bytes",
     "obs_load_layer", "obs_synth_layer", "obs_synth_activations", "obs_moe_forward",
-    "obs_moe_forward_host", "obs_gate", "obs_route", "obs_dispatch", "obs_expert_ffn",
+    "obs_moe_forward_host", "obs_moe_forward_host_async", "obs_moe_host_join", "obs_gate", "obs_route", "obs_dispatch", "obs_expert_ffn",
     "obs_expert_gemm_f32", "obs_check_device", "obs_profile_enable", "obs_profile_read",
     "obs_trace_enable", "obs_decode_ffn_static", "obs_kernel_launches", "obs_ep_handle", "obs_ep_connect",
     "obs_rmsnorm", "obs_moe_stack_forward",
@@ -81,6 +81,8 @@ def lib() -> C.CDLL:
         L.obs_synth_activations.argtypes = [i64, C.c_uint32, i32, i32, i32, C.c_float, vp, vp]
         L.obs_moe_forward.argtypes = [vp, i32, vp, vp, vp, i32, vp, i32, vp]
         L.obs_moe_forward_host.argtypes = [vp, i32, vp, vp, vp, i32, vp, i32, vp]
+        L.obs_moe_forward_host_async.argtypes = [vp, i32, vp, vp, vp, i32, vp, i32, vp]
+        L.obs_moe_host_join.argtypes = [vp, vp]
         L.obs_gate.argtypes = [vp, i32, vp, vp, i32, vp]
         L.obs_route.argtypes = [vp, vp, vp, i32, vp, vp, vp]
         L.obs_dispatch.argtypes = [vp, vp, i32, vp, vp, vp, vp]
@@ -235,6 +237,18 @@ class MoeContext:
         self._chk(lib().obs_moe_forward_host(self._h, layer, _ptr(x_host), _ptr(out_host),
                                              _ptr(residual_host), T, _ptr(bias_host), path,
                                              _stream(stream)))
+
+    def moe_forward_host_async(self, layer, x_host, out_host, T, residual_host=None, bias_host=None,
+                               path=PATH_AUTO, stream=None):
+        """moe_forward_host without the wait: copies in and out on internal streams, two staging
+        slots, so successive calls overlap (host_join, then synchronise, before reading out_host)."""
+        self._chk(lib().obs_moe_forward_host_async(self._h, layer, _ptr(x_host), _ptr(out_host),
+                                                   _ptr(residual_host), T, _ptr(bias_host), path,
+                                                   _stream(stream)))
+
+    def host_join(self, stream=None):
+        """Make `stream` wait for every output copy moe_forward_host_async has issued."""
+        self._chk(lib().obs_moe_host_join(self._h, _stream(stream)))
 
     def profile(self, enable: bool):
         self._chk(lib().obs_profile_enable(self._h, int(enable)))

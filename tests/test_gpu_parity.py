@@ -364,6 +364,30 @@ def test_host_entry_matches_device(small):
     assert np.array_equal(oh.numpy().view(np.uint16), dev_out)
 
 
+def test_host_async_matches_sync(small):
+    """Five pipelined asynchronous host calls (alternating staging slots, some with a residual,
+    both paths) give the synchronous host entry's results bit for bit."""
+    torch = small.torch
+    cases = [(40, obsmoe.PATH_PREFILL, False), (17, obsmoe.PATH_PREFILL, True), (3, obsmoe.PATH_DECODE, False),
+             (100, obsmoe.PATH_PREFILL, True), (1, obsmoe.PATH_AUTO, True)]
+    ins, want = [], []
+    for i, (T, path, with_res) in enumerate(cases):
+        xh = torch.from_numpy(small.x(T, row0=11 * i).view(np.int16)).pin_memory()
+        rh = torch.from_numpy(small.x(T, row0=5 + 7 * i, seed=9).view(np.int16)).pin_memory() if with_res else None
+        oh = torch.empty((T, 2048), dtype=torch.int16).pin_memory()
+        small.ctx.moe_forward_host(0, xh, oh, T, residual_host=rh, path=path)
+        ins.append((T, path, xh, rh))
+        want.append(oh.numpy().copy())
+    stream = torch.cuda.Stream()
+    outs = [torch.full((T, 2048), -1, dtype=torch.int16).pin_memory() for (T, _, _, _) in ins]
+    for (T, path, xh, rh), oh in zip(ins, outs):
+        small.ctx.moe_forward_host_async(0, xh, oh, T, residual_host=rh, path=path, stream=stream)
+    small.ctx.host_join(stream)
+    stream.synchronize()
+    for oh, w in zip(outs, want):
+        assert np.array_equal(oh.numpy(), w)
+
+
 def test_deterministic(small):
     x = small.x(100, row0=1)
     a = run_forward(small, x, obsmoe.PATH_PREFILL)
