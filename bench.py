@@ -507,8 +507,15 @@ def main():
     for l in range(N_ROT):
         xh[l].copy_(xs[l].cpu())
     oh = [torch.empty((T, H), dtype=torch.int16).pin_memory() for _ in range(2)]
+
+    def host_step(i):
+        if ep:  # the pipelined entry is single-GPU: expert parallelism copies in and out per call
+            ctx.moe_forward_host(i % N_ROT, xh[i % N_ROT], oh[i % 2], T, path=path, stream=stream)
+        else:
+            ctx.moe_forward_host_async(i % N_ROT, xh[i % N_ROT], oh[i % 2], T, path=path, stream=stream)
+
     for i in range(3):
-        ctx.moe_forward_host_async(i % N_ROT, xh[i % N_ROT], oh[i % 2], T, path=path, stream=stream)
+        host_step(i)
     ctx.host_join(stream)
     stream.synchronize()
     barrier()
@@ -516,7 +523,7 @@ def main():
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
-        ctx.moe_forward_host_async(i % N_ROT, xh[i % N_ROT], oh[i % 2], T, path=path, stream=stream)
+        host_step(i)
     ctx.host_join(stream)  # the last step's result is in host memory before e1
     e1.record(stream)
     stream.synchronize()
