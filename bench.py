@@ -47,6 +47,10 @@ EXPERT_BYTES = 2_654_208        # one expert: 3 projections of 4-bit codes + bf1
 GATEUP_BYTES = 2 * 884_736      # the gate and up projections of one expert
 ROUTER_BYTES = 278_528
 N_ROT = 4                       # resident layers the steps rotate over
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of the same
+# workload (profiles/k_gemm_config1_T512.md, profiles/k_decode_fused_config0_T1.md); other
+# workloads report null
+NCU_TRAFFIC = {("gemm_gateup", 512): 246_949_888 + 4_585_472, ("decode_fused", 1): 21_645_056}
 CONFIGS = {
     0: dict(T=1, name="config0: Qwen3-30B-A3B MoE layer, decode of 1 token"),
     1: dict(T=512, name="config1: Qwen3-30B-A3B MoE layer, batched prefill of T=512 tokens"),
@@ -586,7 +590,8 @@ def main():
                    "path": "prefill (tcgen05 grouped GEMM)" if path == obsmoe.PATH_PREFILL else "decode (mat-vec)"},
         "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                     "algorithmic_bytes_per_launch": alg, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg,
+                     "traffic": NCU_TRAFFIC.get((top, T)) if world == 1 else None,
                      "kernel_us": k_avg_s * 1e6},
         "layer_hbm_gbs": layer_bytes / (ms / args.steps / 1e3) / 1e9,
         "layer_tflops": 2 * T * K * 4_718_592 / (ms / args.steps / 1e3) / 1e12,
