@@ -48,8 +48,7 @@ GATEUP_BYTES = 2 * 884_736      # the gate and up projections of one expert
 ROUTER_BYTES = 278_528
 N_ROT = 4                       # resident layers the steps rotate over
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of the same
-# workload (profiles/k_gemm_config1_T512.md, profiles/k_decode_fused_config0_T1.md); other
-# workloads report null
+# workload (the committed profile summaries); other workloads report null
 NCU_TRAFFIC = {("gemm_gateup", 512): 246_949_888 + 4_585_472, ("decode_fused", 1): 21_645_056}
 CONFIGS = {
     0: dict(T=1, name="config0: Qwen3-30B-A3B MoE layer, decode of 1 token"),

@@ -57,7 +57,7 @@ typedef struct obs_ctx obs_ctx;
  * (src/model.rs:7-23). */
 typedef struct obs_config {
     int32_t hidden;            /* H: multiple of 2048 */
-    int32_t inter;             /* I: moe_intermediate_size, multiple of 128 */
+    int32_t inter;             /* I: moe_intermediate_size, multiple of 256 */
     int32_t n_experts;         /* E: <= 256 */
     int32_t top_k;             /* K: <= 16 */
     int32_t group_size;        /* must be 64 */
@@ -190,6 +190,27 @@ int obs_kernel_launches(uint64_t* count);
 /* Waits for the stream and reports any device-side error flag (bounded waits
  * that gave up) raised since the last check; clears the flags. */
 int obs_check_device(obs_ctx* ctx, void* stream);
+/* No counterpart in the reference (its waits are host-side and unbounded,
+ * src/router.rs:47-48).  Every device-side wait of the context's kernels (GEMM
+ * pipeline barriers, the fused decode layer's grid barriers, expert-parallel
+ * peer stamps) gives up after limit_ns, records a timeout and returns, so a
+ * stalled peer or pipeline ends in OBS_ERR_TIMEOUT from obs_check_device with
+ * the GPU still answering.  limit_ns in [1 ms, 60 s]; 0 restores the default
+ * 2 s.  Applies to work issued after the call. */
+int obs_set_wait_limit(obs_ctx* ctx, uint64_t limit_ns);
+/* Failure-path check without a failure: launches one bounded device wait on a
+ * stamp that nothing writes -- the wait an expert-parallel receive runs for a
+ * peer that never sends (same device code) -- which gives up after the wait
+ * limit; obs_check_device then returns OBS_ERR_TIMEOUT and the context stays
+ * usable. */
+int obs_probe_wait(obs_ctx* ctx, void* stream);
+/* ABI self-description for bindings in other languages: writes
+ *   sizeof(obs_config), the offsets of its 12 fields in declaration order,
+ *   sizeof(obs_layer_weights), the offsets of its 12 fields in declaration order
+ * (26 values) into out[0 .. n), and returns 26.  A binding compares these with
+ * its own struct layout (the reference passes its parameter structs by value
+ * as #[repr(C)], src/forward.rs:22-28, src/router.rs:8-14). */
+int obs_struct_layout(int32_t* out, int n);
 
 /* ----------------------------------------------------- the layer stack */
 /* The MoE input norm, rmsnorm.metal:9-37 (Model::rmsnorm, forward.rs:421):

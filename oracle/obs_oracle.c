@@ -331,6 +331,10 @@ static void dequant_proj(const orc_experts* ex, int proj, int e, int wmode, floa
     }
 }
 
+/* One expert's slots in blocks of ORC_NB tokens: each weight row is read once
+ * per block (the per-(row, token) dot product is unchanged, so the results do
+ * not depend on the block size). */
+#define ORC_NB 8
 static void* ffn_worker(void* arg) {
     ffn_job* J = (ffn_job*)arg;
     const orc_experts* ex = J->ex;
@@ -338,8 +342,8 @@ static void* ffn_worker(void* arg) {
     float* wg = (float*)malloc(sizeof(float) * (size_t)I * H);
     float* wu = (float*)malloc(sizeof(float) * (size_t)I * H);
     float* wd = (float*)malloc(sizeof(float) * (size_t)H * I);
-    float* xf = (float*)malloc(sizeof(float) * (size_t)H);
-    float* hf = (float*)malloc(sizeof(float) * (size_t)I);
+    float* xf = (float*)malloc(sizeof(float) * (size_t)H * ORC_NB);
+    float* hf = (float*)malloc(sizeof(float) * (size_t)I * ORC_NB);
     for (;;) {
         pthread_mutex_lock(&J->mu);
         int e = J->next_e++;
@@ -349,18 +353,24 @@ static void* ffn_worker(void* arg) {
         dequant_proj(ex, 0, e, J->wmode, wg);
         dequant_proj(ex, 1, e, J->wmode, wu);
         dequant_proj(ex, 2, e, J->wmode, wd);
-        for (int slot = J->offsets[e]; slot < J->offsets[e + 1]; ++slot) {
-            int t = J->src_token[slot];
-            for (int i = 0; i < H; ++i) xf[i] = orc_bf16_to_f32(J->x[(size_t)t * H + i]);
-            for (int i = 0; i < I; ++i) {
-                float g = dot8(wg + (size_t)i * H, xf, H);
-                float u = dot8(wu + (size_t)i * H, xf, H);
-                uint16_t hb = orc_f32_to_bf16(silu_mul(g, u));
-                hf[i] = orc_bf16_to_f32(hb);
-                if (J->h_slots) J->h_slots[(size_t)slot * I + i] = hb;
+        for (int s0 = J->offsets[e]; s0 < J->offsets[e + 1]; s0 += ORC_NB) {
+            int nb = J->offsets[e + 1] - s0 < ORC_NB ? J->offsets[e + 1] - s0 : ORC_NB;
+            for (int bt = 0; bt < nb; ++bt) {
+                int t = J->src_token[s0 + bt];
+                for (int i = 0; i < H; ++i) xf[(size_t)bt * H + i] = orc_bf16_to_f32(J->x[(size_t)t * H + i]);
             }
+            for (int i = 0; i < I; ++i)
+                for (int bt = 0; bt < nb; ++bt) {
+                    float g = dot8(wg + (size_t)i * H, xf + (size_t)bt * H, H);
+                    float u = dot8(wu + (size_t)i * H, xf + (size_t)bt * H, H);
+                    uint16_t hb = orc_f32_to_bf16(silu_mul(g, u));
+                    hf[(size_t)bt * I + i] = orc_bf16_to_f32(hb);
+                    if (J->h_slots) J->h_slots[(size_t)(s0 + bt) * I + i] = hb;
+                }
             for (int o = 0; o < H; ++o)
-                J->y_slots[(size_t)slot * H + o] = orc_f32_to_bf16(dot8(wd + (size_t)o * I, hf, I));
+                for (int bt = 0; bt < nb; ++bt)
+                    J->y_slots[(size_t)(s0 + bt) * H + o] =
+                        orc_f32_to_bf16(dot8(wd + (size_t)o * I, hf + (size_t)bt * I, I));
         }
     }
     free(wg); free(wu); free(wd); free(xf); free(hf);

@@ -305,6 +305,27 @@ def ref_lib():
     return _REF
 
 
+def ref_route(L: Layer, x, norm=True):
+    """The reference's router on the CPU, token by token as forward.rs:386-397 and
+    router.rs:25-56 run it: dequant_matvec_8bit (logits rounded to f16) then
+    moe_routing_topk.  Returns (logits f16 [T, E], ids [T, K], weights f16 [T, K])."""
+    R = ref_lib()
+    if R is None:
+        raise RuntimeError("oracle/_ref not built")
+    x = np.ascontiguousarray(x, np.uint16)
+    T = x.shape[0]
+    s16 = bf16_to_f32(L.router_s).astype(np.float16)
+    b16 = bf16_to_f32(L.router_b).astype(np.float16)
+    x16 = bf16_to_f32(x).astype(np.float16)
+    logits = np.empty((T, L.E), np.float16)
+    ids = np.empty((T, L.K), np.int32)
+    w = np.empty((T, L.K), np.float16)
+    for t in range(T):
+        R.ref_dequant_matvec_8bit(L.router_w, s16, b16, np.ascontiguousarray(x16[t]), logits[t], L.H, L.E)
+        R.ref_moe_routing_topk(np.ascontiguousarray(logits[t]), L.E, L.K, int(norm), ids[t], w[t])
+    return logits, ids, w
+
+
 class _RefLayer(C.Structure):
     _fields_ = [("E", C.c_int), ("H", C.c_int), ("I", C.c_int), ("K", C.c_int),
                 ("router_w", C.c_void_p), ("gate_w", C.c_void_p), ("up_w", C.c_void_p),

@@ -83,8 +83,13 @@ __device__ __forceinline__ void block_dot(const Src& src, int e, int rt, int kt,
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int j = 0; j < 8; ++j)  // nibble j holds column j (MLX) or nib_col(j) (tiled)
-                f = __fmaf_rn(nib_f16th(ws[c], j), xr[c * 8 + (Src::kNatural ? j : nib_col(j))], f);
+            for (int j = 0; j < 8; ++j) {
+                // columns in the order (0,2,4,6,1,3,5,7) of every word for both layouts, so
+                // the two give bit-identical sums: the tiled word holds that column at nibble j,
+                // the MLX word at nibble nib_col(j)
+                const int col = nib_col(j);
+                f = __fmaf_rn(nib_f16th(ws[c], Src::kNatural ? col : j), xr[c * 8 + col], f);
+            }
         // s * sum q x + b * sum x, with sum q x = 16 (f - sum x)
         acc[i] = __fmaf_rn(16.0f * sc[i], f - xsum, __fmaf_rn(bi[i], xsum, acc[i]));
     }
@@ -201,10 +206,10 @@ __global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __
         if ((lane & 1) == 0) s_part[w][(lane >> 1) + 16 * i] = v;
     }
     __syncthreads();
-    if (tid < kRowTile) {
+    for (int r = tid; r < kRowTile; r += blockDim.x) {  // blockDim may be below 128 (inter = 128)
         float v = 0.0f;
-        for (int j = 0; j < nwarps; ++j) v += s_part[j][tid];
-        d.y[(size_t)p * H + rt * kRowTile + tid] = f2bf(v);
+        for (int j = 0; j < nwarps; ++j) v += s_part[j][r];
+        d.y[(size_t)p * H + rt * kRowTile + r] = f2bf(v);
     }
     if (!do_combine) return;
     __threadfence();
@@ -218,9 +223,9 @@ __global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    if (tid < kRowTile) {
+    for (int r = tid; r < kRowTile; r += blockDim.x) {
         // rank-order combine, same operation order as k_combine (forward.rs:225-232)
-        const int f = rt * kRowTile + tid;
+        const int f = rt * kRowTile + r;
         float a = residual ? bf2f(residual[(size_t)t * H + f]) : 0.0f;
         for (int j = 0; j < K; ++j) {
             const uint16_t yv = __ldcg(d.y + ((size_t)t * K + j) * H + f);
@@ -260,7 +265,7 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
 // counter only grows (launch n's barriers wait for (2n+1)G and (2n+2)G arrivals,
 // n the generation read at the start), so no launch needs it cleared; the
 // comparison is wrap-safe.
-__device__ bool grid_sync(uint32_t* bar, uint32_t target, int* err) {
+__device__ bool grid_sync(uint32_t* bar, uint32_t target, int* err, uint64_t limit_ns) {
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -269,7 +274,7 @@ __device__ bool grid_sync(uint32_t* bar, uint32_t target, int* err) {
         int ok = 1;
         const uint64_t t0 = global_ns();
         while ((int)(ld_acquire_gpu(bar) - target) < 0) {
-            if (global_ns() - t0 > kWaitLimitNs) {
+            if (global_ns() - t0 > limit_ns) {
                 ok = 0;
                 atomicExch(err, kDevTimeout);
                 break;
@@ -375,7 +380,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
     for (int item = warp * G + b; item < E * n_tc; item += kFusedWarps * G)
         router_warp_item<true>(rw, rs, rb, x, T, H, E, item % E, (item / E) * kWarpTok, lane, f.logits);
     mark(1);
-    if (!grid_sync(f.bar, (2 * gen + 1) * G, f.err)) return;
+    if (!grid_sync(f.bar, (2 * gen + 1) * G, f.err, f.wait_ns)) return;
     mark(2);
 
     // B: top-k of every token, in every CTA
@@ -430,7 +435,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
         }
     }
     mark(4);
-    if (!grid_sync(f.bar, (2 * gen + 2) * G, f.err)) return;
+    if (!grid_sync(f.bar, (2 * gen + 2) * G, f.err, f.wait_ns)) return;
     mark(5);
     // every CTA read `gen` before the first barrier: the next launch may use the next one
     if (b == 0 && tid == 0) *reinterpret_cast<volatile uint32_t*>(f.bar + 1) = gen + 1;

@@ -35,14 +35,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 __device__ __forceinline__ int ld_volatile(const int32_t* p) { return *reinterpret_cast<const volatile int32_t*>(p); }
 
 // threads [0, world) wait until stamp[t] == e (bounded); false on timeout
-__device__ bool wait_stamps(const uint32_t* stamps, int world, uint32_t e, int* err) {
+__device__ bool wait_stamps(const uint32_t* stamps, int world, uint32_t e, int* err, uint64_t limit_ns) {
     __shared__ int s_bad;
     if (threadIdx.x == 0) s_bad = 0;
     __syncthreads();
     if (threadIdx.x < world) {
         const uint64_t t0 = global_ns();
         while (ld_acquire_sys(stamps + threadIdx.x) != e) {
-            if (global_ns() - t0 > kWaitLimitNs) {
+            if (global_ns() - t0 > limit_ns) {
                 s_bad = 1;
                 atomicExch(err, kDevTimeout);
                 break;
@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(256) k_ep_recv(EpArgs a) {
     pdl_begin();
     const uint32_t e = *a.epoch + 1;
     uint8_t* mine = a.peer[a.rank];
-    if (!wait_stamps(at<uint32_t>(mine, a.off_rflag), a.world, e, a.err)) return;
+    if (!wait_stamps(at<uint32_t>(mine, a.off_rflag), a.world, e, a.err, a.wait_ns)) return;
     const int n = a.world * a.cap;
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
         const int s = j / a.cap, i = j - s * a.cap;
@@ -167,11 +167,18 @@ __global__ void __launch_bounds__(256) k_ep_return(const int32_t* __restrict__ s
     if (threadIdx.x == 0) a.done[1] = 0;
 }
 
+// The failure path of the peer waits, without peers: one wait on a stamp that
+// nothing writes runs out after limit_ns and records the timeout, exactly as a
+// k_ep_recv whose peer never sends would (obs_probe_wait).
+__global__ void k_probe_wait(const uint32_t* stamp, uint64_t limit_ns, int* err) {
+    wait_stamps(stamp, 1, 1u, err, limit_ns);
+}
+
 // Wait until every rank has returned this rank's rows, then close the epoch.
 __global__ void k_ep_finish(EpArgs a) {
     pdl_begin();
     const uint32_t e = *a.epoch + 1;
-    wait_stamps(at<uint32_t>(a.peer[a.rank], a.off_retflag), a.world, e, a.err);
+    wait_stamps(at<uint32_t>(a.peer[a.rank], a.off_retflag), a.world, e, a.err, a.wait_ns);
     if (threadIdx.x == 0) *a.epoch = e;
 }
 
@@ -204,6 +211,12 @@ cudaError_t launch_ep_return(const int32_t* slot_of, const uint16_t* y, const Ep
         const cudaError_t le_ = launch_pdl(k_ep_return, dim3(grid), dim3(256), 0, st, slot_of, y, a);
         if (le_ != cudaSuccess) return le_;
     }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_probe_wait(const uint32_t* stamp, uint64_t limit_ns, int* err, cudaStream_t st) {
+    note_launch();
+    k_probe_wait<<<1, 32, 0, st>>>(stamp, limit_ns, err);
     return cudaGetLastError();
 }
 

@@ -134,18 +134,19 @@ __device__ __forceinline__ bool sub_form_ok(uint32_t s_bits) {
 // which wait timed out (recorded in the context's second error word)
 enum WaitCode : int { kWtEmptyW = 11, kWtSfreeB, kWtAccEmpty, kWtAReady, kWtFullW, kWtSfreeA, kWtFullB, kWtAccFull };
 
-__device__ __forceinline__ bool wait_all(uint32_t bar, uint32_t parity, volatile int* abort, int code) {
-    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, code));
+__device__ __forceinline__ bool wait_all(uint32_t bar, uint32_t parity, volatile int* abort, int code,
+                                         uint64_t limit_ns) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, code, limit_ns));
 }
 
 // After giving up, a producer waits (bounded) until the newest copy it issued
 // into each stage of its ring has landed, so no copy targets freed memory.
-__device__ __forceinline__ void drain_ring(uint32_t bar0, int stages, int issued) {
+__device__ __forceinline__ void drain_ring(uint32_t bar0, int stages, int issued, uint64_t limit_ns) {
     for (int st = 0; st < stages && st < issued; ++st) {
         const int last = st + (issued - 1 - st) / stages * stages;
         const uint32_t par = (last / stages) & 1;
         const uint64_t t0 = global_ns();
-        while (!mbar_try_wait(bar0 + 8 * st, par) && global_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(bar0 + 8 * st, par) && global_ns() - t0 < limit_ns) {
         }
     }
 }
@@ -233,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const int rt = item % a.n_rt;
             const uint8_t* wsrc = a.wblocks + ((size_t)tl.x * a.n_rt + rt) * a.n_kt * kBlockBytes;
             for (int w = 0; w < a.n_kt / kWK; ++w) {
-                if (!wait_all(empty_w(s), ph ^ 1, abort_flag, kWtEmptyW)) break;
+                if (!wait_all(empty_w(s), ph ^ 1, abort_flag, kWtEmptyW, a.wait_ns)) break;
                 if (elect_one()) {
                     mbar_arrive_expect_tx(full_w(s), C::W_STAGE);
                     bulk_g2s_hint(sbase + C::W_OFF + s * C::W_STAGE, wsrc + (size_t)w * C::W_STAGE, C::W_STAGE,
@@ -245,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                 if (++s == C::SW) s = 0, ph ^= 1;
             }
         }
-        if (*abort_flag && lane == 0) drain_ring(full_w(0), C::SW, issued);
+        if (*abort_flag && lane == 0) drain_ring(full_w(0), C::SW, issued, a.wait_ns);
         __syncwarp();
     } else if (warp == kWarpB || warp == kWarpB2) {
         // ------------------------------------- token-tile producers (k-group g)
@@ -258,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(a.act) + (size_t)(tl.y >> 3) * 1024;
             const uint32_t bbytes = (uint32_t)tl.z * 128u;
             for (int ks = 0; ks < KS; ++ks) {
-                if (!wait_all(sfree(s >> 1), ph ^ 1, abort_flag, kWtSfreeB)) break;
+                if (!wait_all(sfree(s >> 1), ph ^ 1, abort_flag, kWtSfreeB, a.wait_ns)) break;
                 if (elect_one()) {
                     mbar_arrive_expect_tx(full_b(s), bbytes);
                     bulk_g2s_hint(sbase + C::B_OFF + s * C::B_STAGE + g * C::B_GROUP,
@@ -271,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             }
         }
         // (a phase the other producer never fed ends the drain at its time limit)
-        if (*abort_flag && lane == 0) drain_ring(full_b(0), C::SB, issued);
+        if (*abort_flag && lane == 0) drain_ring(full_b(0), C::SB, issued, a.wait_ns);
         __syncwarp();
     } else if (warp == kWarpMma) {
         // ---------------------------------------------------------- MMA issuer
@@ -286,13 +287,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const int4 tl = a.tiles[item / a.n_rt];
             const uint32_t idesc = idesc_bf16(128, tl.z);
             const int buf = it & 1;
-            if (!wait_all(accempty(buf), ((it >> 1) & 1) ^ 1, abort_flag, kWtAccEmpty)) break;
+            if (!wait_all(accempty(buf), ((it >> 1) & 1) ^ 1, abort_flag, kWtAccEmpty, a.wait_ns)) break;
             tc_fence_after();
             const uint32_t dbase = tmem + buf * C::ACC_COLS;
             bool ok = true;
             for (int pi = 0; pi < KS / 2; ++pi, ++pair) {
                 const int ps = pair % C::NPS;
-                if (!wait_all(aready(ps), (pair / C::NPS) & 1, abort_flag, kWtAReady)) {
+                if (!wait_all(aready(ps), (pair / C::NPS) & 1, abort_flag, kWtAReady, a.wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -328,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         __syncwarp();
         {
             const uint64_t t0 = global_ns();
-            while (!mbar_try_wait(mma_done, 0) && global_ns() - t0 < kWaitLimitNs) {
+            while (!mbar_try_wait(mma_done, 0) && global_ns() - t0 < a.wait_ns) {
             }
         }
         __syncwarp();
@@ -350,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
         // read the packed words (and the row's scales and biases) of step i, release its half of the W stage
         auto load_w = [&](int i) -> bool {
             const int wi = i >> 1, ls = wi % C::SW;
-            if (!wait_all(full_w(ls), (wi / C::SW) & 1, abort_flag, kWtFullW)) return false;
+            if (!wait_all(full_w(ls), (wi / C::SW) & 1, abort_flag, kWtFullW, a.wait_ns)) return false;
             if (tr) trace_at<TRACE>(a, kTrDqStart, i);
 #pragma unroll
             for (int g = 0; g < kKS; ++g) {
@@ -378,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             // A stage x was last read by the MMAs of step (step - SA), in pair slot x / 2
             const int x = step % C::SA, use = step / C::SA;
             const uint32_t at = at0 + x * C::A_COLS;
-            if (!wait_all(sfree(x >> 1), (use & 1) ^ 1, abort_flag, kWtSfreeA)) break;
+            if (!wait_all(sfree(x >> 1), (use & 1) ^ 1, abort_flag, kWtSfreeA, a.wait_ns)) break;
             tc_fence_after();
             if (tr) trace_at<TRACE>(a, kTrDqAFree, step);
 #pragma unroll
@@ -400,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             if (tr) trace_at<TRACE>(a, kTrDqStored, step);
             tc_wait_st();
             // the step's token tile (B stage x) must have landed before the pair is ready
-            if (!wait_all(full_b(x), use & 1, abort_flag, kWtFullB)) break;
+            if (!wait_all(full_b(x), use & 1, abort_flag, kWtFullB, a.wait_ns)) break;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(aready(x >> 1));
@@ -421,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
             const int4 tl = a.tiles[item / a.n_rt];
             const int rt = item % a.n_rt;
             const int buf = it & 1;
-            if (!wait_all(accfull(buf), (it >> 1) & 1, abort_flag, kWtAccFull)) break;
+            if (!wait_all(accfull(buf), (it >> 1) & 1, abort_flag, kWtAccFull, a.wait_ns)) break;
             if (et == 0) trace_at<TRACE>(a, kTrEpStart, it);
             tc_fence_after();
             const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + buf * C::ACC_COLS;

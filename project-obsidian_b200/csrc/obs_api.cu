@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstddef>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -73,6 +74,8 @@ struct obs_ctx {
     uint16_t* xnorm_dev = nullptr;  // the layer stack's normalised input
     uint16_t* rtmp_dev = nullptr;   // the layer stack's other residual buffer
     int R_cap = 0, max_tiles = 0, decode_max = 2;
+    uint64_t wait_ns = kDefaultWaitNs;  // limit of every bounded device wait (obs_set_wait_limit)
+    uint32_t* probe_stamp = nullptr;    // a stamp nothing writes (obs_probe_wait)
     uint64_t* trace = nullptr;  // obs_trace_enable
     int trace_n = 0;
     // expert parallelism (ep_world > 1): this rank holds experts [e0, e0 + E_local)
@@ -250,6 +253,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->fused.cnt_gu, (size_t)kFusedMaxT * K * (s.I / kRowTile) * 4},
         {(void**)&ctx->fused.cnt_dn, (size_t)kFusedMaxT * (s.H / kRowTile) * 4},
         {(void**)&ctx->fused.bar, 16},
+        {(void**)&ctx->probe_stamp, 16},
         {(void**)&ctx->ep.send_cnt, (size_t)kMaxWorld * 4},
         {(void**)&ctx->ep.done, 16},
         {(void**)&ctx->ep.epoch, 16},
@@ -278,6 +282,8 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     ctx->fused.h = ctx->dec.h;
     ctx->fused.y = ctx->dec.y;
     ctx->fused.err = ctx->err_flag;
+    ctx->fused.wait_ns = ctx->wait_ns;
+    ctx->ep.wait_ns = ctx->wait_ns;
     if (W > 1) {
         // this rank's shared buffer (layout in k_ep.cu), zeroed: stamps and counts start at 0
         EpArgs& a = ctx->ep;
@@ -507,6 +513,7 @@ static GemmArgs gemm_gateup(obs_ctx* ctx, const LayerDev& L, const uint16_t* x) 
     g.err = ctx->err_flag;
     g.trace = ctx->trace;
     g.trace_n = ctx->trace_n;
+    g.wait_ns = ctx->wait_ns;
     return g;
 }
 
@@ -527,6 +534,7 @@ static GemmArgs gemm_down(obs_ctx* ctx, const LayerDev& L) {
     g.out_ld = s.H;
     g.row_limit = ctx->R_cap;
     g.err = ctx->err_flag;
+    g.wait_ns = ctx->wait_ns;
     return g;
 }
 
@@ -602,6 +610,7 @@ extern "C" int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert
     g.out_ld = out_f;
     g.row_limit = n;
     g.err = ctx->err_flag;
+    g.wait_ns = ctx->wait_ns;
     CU(launch_gemm(g, kEpiF32, ctx->num_sms, st), "gemm f32");
     CU(cudaStreamSynchronize(st), "sync");  // the host tile list must outlive its copy
     return OBS_OK;
@@ -903,6 +912,45 @@ extern "C" int obs_check_device(obs_ctx* ctx, void* stream) {
         return fail(ctx, OBS_ERR_INVALID, "device reported an invalid route (expert id out of range)");
     }
     return OBS_OK;
+}
+
+extern "C" int obs_set_wait_limit(obs_ctx* ctx, uint64_t limit_ns) {
+    OBS_CHECK_CTX(ctx);
+    if (limit_ns == 0) limit_ns = kDefaultWaitNs;
+    if (limit_ns < 1000000ull || limit_ns > 60000000000ull)
+        return fail(ctx, OBS_ERR_INVALID, "wait limit must lie in [1 ms, 60 s] (0: the default 2 s)");
+    ctx->wait_ns = limit_ns;
+    ctx->fused.wait_ns = limit_ns;
+    ctx->ep.wait_ns = limit_ns;
+    return OBS_OK;
+}
+
+extern "C" int obs_probe_wait(obs_ctx* ctx, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    CU(cudaSetDevice(ctx->device), "cudaSetDevice");
+    CU(launch_probe_wait(ctx->probe_stamp, ctx->wait_ns, ctx->err_flag, as_stream(stream)), "probe wait");
+    return OBS_OK;
+}
+
+extern "C" int obs_struct_layout(int32_t* out, int n) {
+    if (!out && n) return OBS_ERR_INVALID;
+#define OBS_OFF(T, f) (int32_t) offsetof(T, f)
+    const int32_t v[] = {
+        (int32_t)sizeof(obs_config),
+        OBS_OFF(obs_config, hidden), OBS_OFF(obs_config, inter), OBS_OFF(obs_config, n_experts),
+        OBS_OFF(obs_config, top_k), OBS_OFF(obs_config, group_size), OBS_OFF(obs_config, n_layers),
+        OBS_OFF(obs_config, max_tokens), OBS_OFF(obs_config, norm_topk), OBS_OFF(obs_config, decode_max_tokens),
+        OBS_OFF(obs_config, rms_eps), OBS_OFF(obs_config, ep_world), OBS_OFF(obs_config, ep_rank),
+        (int32_t)sizeof(obs_layer_weights),
+        OBS_OFF(obs_layer_weights, router_w), OBS_OFF(obs_layer_weights, router_s), OBS_OFF(obs_layer_weights, router_b),
+        OBS_OFF(obs_layer_weights, gate_w), OBS_OFF(obs_layer_weights, gate_s), OBS_OFF(obs_layer_weights, gate_b),
+        OBS_OFF(obs_layer_weights, up_w), OBS_OFF(obs_layer_weights, up_s), OBS_OFF(obs_layer_weights, up_b),
+        OBS_OFF(obs_layer_weights, down_w), OBS_OFF(obs_layer_weights, down_s), OBS_OFF(obs_layer_weights, down_b),
+    };
+#undef OBS_OFF
+    const int total = (int)(sizeof(v) / sizeof(v[0]));
+    for (int i = 0; i < n && i < total; ++i) out[i] = v[i];
+    return total;
 }
 
 extern "C" int obs_profile_enable(obs_ctx* ctx, int enable) {

@@ -66,7 +66,10 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legal wait
+// Default limit of every bounded device-side wait (2 s: far above any legal
+// wait); a context can lower it at run time (obs_set_wait_limit), which the
+// kernels receive as an argument.
+constexpr uint64_t kDefaultWaitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -113,16 +116,17 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 }
 constexpr uint32_t kWaitSleepNs = 20000;
 
-// Bounded wait: gives up after kWaitLimitNs or when another role of the CTA
-// has already given up (*abort != 0); the wait that times out stores `code`
+// Bounded wait: gives up after limit_ns or when another role of the CTA has
+// already given up (*abort != 0); the wait that times out stores `code`
 // (non-zero: which wait it was) in *abort; returns false on giving up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code = 1) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code,
+                                          uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
         if (*abort) return false;
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit_ns) {
             *abort = code;
             return false;
         }

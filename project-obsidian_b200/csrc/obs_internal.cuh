@@ -121,11 +121,15 @@ struct EpArgs {
     int32_t* counts;     // [E_local] received rows per local expert (zeroed before k_ep_recv)
     int rows_cap;        // rows of the expert-output buffer k_ep_return reads (slot_of bound)
     int* err;
+    uint64_t wait_ns;    // limit of the bounded waits for peers
 };
 cudaError_t launch_ep_send(const int32_t* ids, const uint16_t* x, int T, int E, const EpArgs& a, cudaStream_t st);
 cudaError_t launch_ep_recv(const EpArgs& a, cudaStream_t st);
 cudaError_t launch_ep_return(const int32_t* slot_of, const uint16_t* y, const EpArgs& a, cudaStream_t st);
 cudaError_t launch_ep_finish(const EpArgs& a, cudaStream_t st);
+// One bounded wait on a stamp that nothing writes (obs_probe_wait): gives up
+// after limit_ns and records kDevTimeout in *err.
+cudaError_t launch_probe_wait(const uint32_t* stamp, uint64_t limit_ns, int* err, cudaStream_t st);
 
 // --------------------------------------------------------------- k_decode.cu
 constexpr int kDecodeSplit = 8;  // k-splits of the decode gate/up mat-vec
@@ -152,6 +156,7 @@ struct FusedDecodeBufs {
     uint16_t* y;        // [T*K][H]
     int* err;
     uint64_t* trace;    // optional: thread 0 of CTA b writes %globaltimer at 7 points to trace[8b .. 8b+6]
+    uint64_t wait_ns;   // limit of the grid-barrier waits
 };
 // normalize = 1: x is the residual stream and the kernel applies the MoE input
 // RMSNorm (eps) itself, bit-identical to launch_rmsnorm.
@@ -185,6 +190,7 @@ struct GemmArgs {
     int* err;                 // device error flag
     uint64_t* trace;          // optional: CTA 0 records %globaltimer per role and k-step
     int trace_n;              // k-steps recorded per role
+    uint64_t wait_ns;         // limit of every mbarrier wait
 };
 // trace roles (rows of the trace buffer, trace_n entries each)
 enum TraceRole : int {

@@ -32,7 +32,7 @@ EXPORTS = (
     "obs_moe_forward_host", "obs_moe_forward_host_async", "obs_moe_host_join", "obs_gate", "obs_route", "obs_dispatch", "obs_expert_ffn",
     "obs_expert_gemm_f32", "obs_check_device", "obs_profile_enable", "obs_profile_read",
     "obs_trace_enable", "obs_decode_ffn_static", "obs_kernel_launches", "obs_ep_handle", "obs_ep_connect",
-    "obs_rmsnorm", "obs_moe_stack_forward",
+    "obs_rmsnorm", "obs_moe_stack_forward", "obs_set_wait_limit", "obs_probe_wait", "obs_struct_layout",
 )
 EP_HANDLE_BYTES = 64
 STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down",
@@ -97,6 +97,9 @@ def lib() -> C.CDLL:
         L.obs_ep_connect.argtypes = [vp, vp]
         L.obs_rmsnorm.argtypes = [vp, vp, vp, i32, vp, vp]
         L.obs_moe_stack_forward.argtypes = [vp, i32, i32, vp, i32, vp, i32, vp]
+        L.obs_set_wait_limit.argtypes = [vp, i64]
+        L.obs_probe_wait.argtypes = [vp, vp]
+        L.obs_struct_layout.argtypes = [C.POINTER(C.c_int32), i32]
         L.obs_decode_ffn_static.argtypes = [C.POINTER(LayerWeights), i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp]
         for name in EXPORTS:
             if name not in ("obs_last_error", "obs_abi_version"):
@@ -267,6 +270,14 @@ class MoeContext:
     def check_device(self, stream=None):
         self._chk(lib().obs_check_device(self._h, _stream(stream)))
 
+    def set_wait_limit(self, limit_ns: int):
+        """Limit of every bounded device-side wait (0: the default 2 s)."""
+        self._chk(lib().obs_set_wait_limit(self._h, limit_ns))
+
+    def probe_wait(self, stream=None):
+        """One bounded device wait on a stamp nothing writes: it runs out after the wait limit."""
+        self._chk(lib().obs_probe_wait(self._h, _stream(stream)))
+
 
 def decode_ffn_static(w, n_experts, hidden, inter, top_k, x, ids, weights, T, out, residual=None, stream=None):
     """obs_decode_ffn_static: the decode FFN + combine with no context and no
@@ -277,6 +288,14 @@ def decode_ffn_static(w, n_experts, hidden, inter, top_k, x, ids, weights, T, ou
                                      _ptr(weights), _ptr(residual), T, _ptr(out), _stream(stream))
     if rc != OBS_OK:
         raise ObsError(rc, lib().obs_last_error(None).decode())
+
+
+def struct_layout() -> list[int]:
+    """sizeof and field offsets of obs_config and obs_layer_weights, as the library was compiled."""
+    n = lib().obs_struct_layout(None, 0)
+    buf = (C.c_int32 * n)()
+    lib().obs_struct_layout(buf, n)
+    return list(buf)
 
 
 def kernel_launches() -> int:

@@ -54,3 +54,59 @@ def test_null_context_is_an_error():
     lib = obsmoe.lib()
     assert lib.obs_moe_forward(None, 0, None, None, None, 1, None, 0, None) == 1
     assert lib.obs_destroy(None) == 0
+
+
+# ------------------------------------------------------------ struct layouts
+RUST_TYPES = {"i32": (4, 4), "u32": (4, 4), "f32": (4, 4), "u64": (8, 8), "usize": (8, 8)}
+
+
+def rust_block():
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    return text[text.index("```rust"):text.index("```", text.index("```rust") + 7)]
+
+
+def rust_struct_layout(name):
+    """repr(C) layout of a struct of the INTEGRATION.md Rust binding: (size, [(field, offset)])."""
+    body = re.search(r"pub struct %s \{(.*?)\n\}" % name, rust_block(), flags=re.S).group(1)
+    fields = re.findall(r"pub (\w+): ([^,]+),", body)
+    off, align_max, out = 0, 1, []
+    for fname, ty in fields:
+        ty = ty.strip()
+        size, align = (8, 8) if ty.startswith("*") else RUST_TYPES[ty]
+        off = (off + align - 1) // align * align
+        out.append((fname, off))
+        off += size
+        align_max = max(align_max, align)
+    return (off + align_max - 1) // align_max * align_max, out
+
+
+def header_struct_fields(name):
+    src = open(os.path.join(ROOT, "include", "obs_moe.h")).read()
+    body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (name, name), src, flags=re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    return re.findall(r"(\w+)\s*;", body.replace(",", ";"))
+
+
+def test_struct_layout_of_library_ctypes_and_rust_agree():
+    v = obsmoe.struct_layout()
+    assert len(v) == 26
+    cfg_fields = header_struct_fields("obs_config")
+    lw_fields = header_struct_fields("obs_layer_weights")
+    assert len(cfg_fields) == 12 and len(lw_fields) == 12
+    # the library as compiled
+    lib_cfg = (v[0], list(zip(cfg_fields, v[1:13])))
+    lib_lw = (v[13], list(zip(lw_fields, v[14:26])))
+    # the ctypes binding
+    ct_cfg = (C.sizeof(obsmoe.Config), [(f, getattr(obsmoe.Config, f).offset) for f, _ in obsmoe.Config._fields_])
+    ct_lw = (C.sizeof(obsmoe.LayerWeights),
+             [(f, getattr(obsmoe.LayerWeights, f).offset) for f, _ in obsmoe.LayerWeights._fields_])
+    assert ct_cfg == lib_cfg
+    assert ct_lw == lib_lw
+    # the Rust binding a maintainer of the reference would add
+    assert rust_struct_layout("ObsConfig") == lib_cfg
+    assert rust_struct_layout("ObsLayerWeights") == lib_lw
+
+
+def test_rust_binding_declares_every_export():
+    declared = set(re.findall(r"pub fn (obs_\w+)\(", rust_block()))
+    assert declared == header_entry_points()
