@@ -1,34 +1,43 @@
 """Benchmark of the B200 MoE hot path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 3]
 
-A step is one MoE layer forward (router -> top-k -> dispatch -> 4-bit SwiGLU
-experts -> combine) over one batch of seeded synthetic tokens.  The default
-workload is BASELINE config 1: one Qwen3-30B-A3B MoE layer (E=128, top-8,
-H=2048, I=768, 4-bit group-64 experts, 8-bit router), batched prefill of
-T=512 tokens.  Config 0 (decode of one token) is selectable with --config 0.
+The default workload is BASELINE config 3, the largest single-GPU configuration:
+a 48-layer Qwen3-30B-A3B MoE stack (E=128, top-8, H=2048, I=768, 4-bit
+group-64 experts, 8-bit router; 16.3 GB of weights resident in HBM), prefill of
+T=4096 tokens per GPU with a Zipf(1.1) expert bias on the router logits (the
+hottest expert gets ~10x the mean load).  A step is one pass of the batch
+through all 48 layers, r <- r + MoE_l(RMSNorm(r)) (obs_moe_stack_forward),
+replayed from one CUDA graph.  Configs 0 (one-layer decode of 1 token), 1
+(one-layer prefill of 512 tokens) and 2 (48-layer decode of B tokens) are
+selectable with --config; on one GPU the default line also carries configs 0
+and 1 (`config0`, `config1`), each timed for about half a second.
 
 * value     tokens/s of the whole job, inputs resident in HBM, device-timed
-            (CUDA events, barrier + synchronize both sides, max over ranks).
-            Steps rotate over 4 resident layers (1.36 GB of weights, far more
-            than the 126 MB L2), so no step reads the previous step's weights
-            from L2.
-* e2e       the same metric through the host entry points (obs_moe_forward_host_async
-            + obs_moe_host_join): every step copies its input from pinned host memory
-            and its output back; successive steps pipeline (step i+1's input copy and
-            step i-1's output copy overlap step i), as a serving loop would.
-* roofline  the dominant kernel (the gate/up grouped GEMM at T=512, the fused
-            decode layer at T=1), algorithmic bytes per launch / its mean
-            CUDA-event duration on the launching stream, against the measured
-            HBM copy bandwidth in MEASURED_PEAKS.json.
-* cpu_baseline  the C oracle (oracle/, all host threads) on the same layer.
+            (CUDA events on the launching stream, barrier + synchronize on both
+            sides, max over ranks).  The 48 resident layers (16.3 GB) are far
+            larger than the 126 MB L2.
+* e2e       the same metric with every step's input copied in from pinned host
+            memory and its result copied back inside the timed region.
+* roofline  the dominant kernel: for prefill the gate/up grouped GEMM
+            (k_gemm<kEpiSwiglu>), algorithmic FLOPs per launch (6,291,456 per
+            routed row) over its mean CUDA-event duration in an eager pass of
+            one step, against the measured sustained bf16 peak (the kernel runs
+            inside a seconds-long step; the burst fraction is also given); the
+            whole-stack fraction beside it.  For decode the fused decode layer
+            against the measured HBM copy bandwidth.
+* cpu_baseline  the C oracle (oracle/, all host threads) on a bounded sample.
 
---impl reference runs the reference's own kernels (shaders/*.metal compiled
-for the CPU into oracle/_ref) on the host cores over a bounded token sample.
-Multi-GPU (torchrun): every rank runs its own T-token batch against its own
-copy of the layers (data-parallel replicas; weak scaling), timed on the device,
-max over ranks.  --ep instead splits the experts E/N per GPU and exchanges the
-routed rows over NVLink peer memory (expert parallelism).
+Multi-GPU (torchrun): every rank routes its own batch (weak scaling) and the
+experts are split E/N per GPU (expert parallelism: routed rows travel to the
+rank holding their expert and back over NVLink peer memory); the line reports
+all-to-all bytes per GPU per layer and the per-GPU load.  --replicas instead
+runs N independent replicas that each hold every expert.
+
+--impl reference times the reference's own kernels (shaders/*.metal compiled
+for the CPU into oracle/_ref, strung as src/forward.rs:164-232) on the host
+cores, on the same config: each step is a 256-token slice of the same batch
+through one layer with the same expert bias, scaled to the stack's layers.
 """
 from __future__ import annotations
 
@@ -46,10 +55,14 @@ H, I, E, K = 2048, 768, 128, 8
 EXPERT_BYTES = 2_654_208        # one expert: 3 projections of 4-bit codes + bf16 scales/biases
 GATEUP_BYTES = 2 * 884_736      # the gate and up projections of one expert
 ROUTER_BYTES = 278_528
-N_ROT = 4                       # resident layers the steps rotate over
+GATEUP_FLOPS_PER_ROW = 2 * 2 * I * H   # gate + up of one routed (token, expert) row
+LAYER_FLOPS = 2 * K * 4_718_592        # per token and layer (router excluded)
+N_ROT = 4                       # resident layers the single-layer configs rotate over
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of the same
 # workload (the committed profile summaries); other workloads report null
-NCU_TRAFFIC = {("gemm_gateup", 512): 246_949_888 + 4_585_472, ("decode_fused", 1): 21_645_056}
+NCU_TRAFFIC = {("gemm_gateup", 512): 246_949_888 + 4_585_472, ("decode_fused", 1): 21_645_056,
+               # layer 0 of config 3 (T=4096, Zipf bias) captured in a 2-layer stack: the same launch
+               ("gemm_gateup_cfg3", 4096): 462_567_680 + 38_029_568}
 CONFIGS = {
     0: dict(T=1, name="config0: Qwen3-30B-A3B MoE layer, decode of 1 token"),
     1: dict(T=512, name="config1: Qwen3-30B-A3B MoE layer, batched prefill of T=512 tokens"),
@@ -57,32 +70,39 @@ CONFIGS = {
     3: dict(T=4096, name="config3: 48-layer MoE stack, prefill of T=4096 tokens, Zipf(1.1) expert bias",
             stack=True),
 }
-LAYER_FLOPS = 2 * K * 4_718_592  # per token and layer (router excluded)
+EXTRA_SECONDS = 0.5   # timed region of the extra config 0 / config 1 measurements
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
+    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="config 3 on one GPU: skip the config 0/1 keys")
     ap.add_argument("--batch", type=int, default=32, help="config 2: tokens per decode step (1, 8, 32, 128)")
     ap.add_argument("--layers", type=int, default=48, help="configs 2 and 3: layers in the stack")
-    ap.add_argument("--tokens", type=int, default=0, help="configs 0 and 1: override T (a sweep point, not a BASELINE config)")
-    ap.add_argument("--ep", action="store_true",
-                    help="N > 1: expert parallelism (E/N experts per GPU) instead of N data-parallel replicas")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="configs 0 and 1: override T (a sweep point, not a BASELINE config)")
+    ap.add_argument("--decode-max", type=int, default=0,
+                    help="largest T the decode (mat-vec) path takes under OBS_PATH_AUTO (0: the library's default)")
+    ap.add_argument("--ref-tokens", type=int, default=256, help="reference arm: tokens per step (a slice of T)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: N data-parallel replicas (every GPU holds all experts) instead of expert parallelism")
     return ap.parse_args()
 
 
 def peaks():
+    """(HBM GB/s, bf16 TF/s burst, bf16 TF/s sustained, source)."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), \
+            "measured"
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 class Clocks:
@@ -134,137 +154,154 @@ class Clocks:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def cpu_baseline(L_host, x_host, T):
-    """The C oracle on the host cores (all threads), the same layer and tokens."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
+class Ranks:
+    """The process group (NCCL) of a multi-GPU run: barriers, max over ranks and
+    gathering the host-side statistics -- the data path never goes through it."""
 
-    n = os.cpu_count() or 1
-    t0 = time.perf_counter()
-    O.moe_layer(L_host, x_host, nthreads=n)
-    dt = time.perf_counter() - t0
-    return {"value": T / dt, "unit": "tokens/s", "cores": n, "kind": "port",
-            "sample": f"the full {T}-token layer once through oracle/obs_oracle.c ({dt:.2f} s)"}
+    def __init__(self, world):
+        self.dist = None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            # no NVLink multicast (NVLS) objects next to the peer buffers the expert exchange writes into
+            os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+            self.dist = dist
+
+    def barrier(self):
+        import torch
+
+        if self.dist is not None:
+            self.dist.barrier()
+        torch.cuda.synchronize()
+
+    def max(self, v: float) -> float:
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        if self.dist is not None:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather(self, obj):
+        if self.dist is None:
+            return [obj]
+        out = [None] * self.dist.get_world_size()
+        self.dist.all_gather_object(out, obj)
+        return out
+
+    def close(self):
+        if self.dist is not None:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
 
 
-def zipf_bias(beta, seed=11):
-    """Config 3's per-expert logit bias: beta * log(r_e^-1.1) over a seeded rank
-    permutation r (1 = hottest)."""
+def zipf_bias_device(beta):
+    import torch
+
+    import synthetic
+
+    return torch.from_numpy(synthetic.zipf_bias(beta, E)).cuda()
+
+
+def calibrate_beta(ctx, r0, T):
+    """beta of config 3's Zipf bias so the hottest expert of layer 0 gets ~10x the mean load."""
     import numpy as np
+    import torch
 
-    r = np.random.default_rng(seed).permutation(E) + 1
-    return (beta * -1.1 * np.log(r)).astype(np.float32)
+    logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    xn = torch.empty_like(r0)
+    ctx.rmsnorm(r0, xn, T)
+    ctx.gate_gpu(0, xn, logits, T)
+    best = None
+    for b in np.linspace(0.0, 8.0, 81):
+        ctx.route(logits, T, ids, wts, bias=zipf_bias_device(float(b)))
+        load = np.bincount(ids.cpu().numpy().ravel(), minlength=E)
+        ratio = load.max() / load.mean()
+        if best is None or abs(ratio - 10.0) < abs(best[1] - 10.0):
+            best = (float(b), float(ratio))
+    return best
 
 
-def run_stack(args, rank, world, local):
-    """Configs 2 and 3: a stack of MoE layers on a residual stream,
-    r <- r + MoE_l(RMSNorm(r)) for every layer (obs_moe_stack_forward); a step is
-    one pass of the batch through all layers, captured in one CUDA graph."""
+def run_stack(args, rank, world, local, ranks):
+    """Configs 2 and 3: a stack of MoE layers on a residual stream; a step is one
+    pass of the batch through every layer, captured in one CUDA graph."""
     import numpy as np
     import torch
 
     import obsmoe
 
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        # NCCL carries only barriers and small reductions here; no NVLink multicast
-        # (NVLS) objects next to the peer buffers the expert exchange writes into
-        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     cfg = CONFIGS[args.config]
     nl = args.layers
     T = args.batch if args.config == 2 else cfg["T"]
     decode = args.config == 2
     path = obsmoe.PATH_AUTO if decode else obsmoe.PATH_PREFILL
-    ep = world > 1 and args.ep  # default for N > 1: data-parallel replicas, every GPU holds all experts
-    shape = obsmoe.MoeShape(H, I, E, K, n_layers=nl, max_tokens=max(T, 16),
+    ep = world > 1 and not args.replicas
+    shape = obsmoe.MoeShape(H, I, E, K, n_layers=nl, max_tokens=max(T, 16), decode_max_tokens=args.decode_max,
                             ep_world=world if ep else 1, ep_rank=rank if ep else 0)
     ctx = obsmoe.MoeContext(shape, local)
+    decode_max = args.decode_max if args.decode_max > 0 else 2
     if ep:
-        handles = [None] * world
-        dist.all_gather_object(handles, ctx.ep_handle())
-        ctx.ep_connect(handles)
+        ctx.ep_connect(ranks.gather(ctx.ep_handle()))
     for l in range(nl):
         ctx.synth_layer(l, 0)
     r0 = torch.empty((T, H), dtype=torch.int16, device="cuda")
     obsmoe.synth_activations(rank, 0, 0, T, H, r0)
     stream = torch.cuda.current_stream()
-    bias, beta, imbalance = None, None, None
+    bias, beta, imbalance0 = None, None, None
     if args.config == 3:
-        # calibrate beta so the hottest expert gets ~10x the mean load (layer 0's routing)
-        logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
-        ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
-        wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
-        xn = torch.empty_like(r0)
-        ctx.rmsnorm(r0, xn, T)
-        ctx.gate_gpu(0, xn, logits, T)
-        best = None
-        for b in np.linspace(0.0, 8.0, 81):
-            bt = torch.from_numpy(zipf_bias(b)).cuda()
-            ctx.route(logits, T, ids, wts, bias=bt)
-            load = np.bincount(ids.cpu().numpy().ravel(), minlength=E)
-            ratio = load.max() / load.mean()
-            if best is None or abs(ratio - 10.0) < abs(best[1] - 10.0):
-                best = (float(b), float(ratio))
-        beta, imbalance = best
-        bias = torch.from_numpy(zipf_bias(beta)).cuda()
+        beta, imbalance0 = calibrate_beta(ctx, r0, T)
+        beta = ranks.gather(beta)[0]  # every rank uses rank 0's bias
+        bias = zipf_bias_device(beta)
     r = torch.empty_like(r0)
 
-    def step():
+    def step(s=stream):
         r.copy_(r0)
-        ctx.moe_stack_forward(0, nl, r, T, bias=bias, path=path, stream=stream)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
+        ctx.moe_stack_forward(0, nl, r, T, bias=bias, path=path, stream=s)
 
     step()
-    barrier()
+    ranks.barrier()
     ctx.check_device()
     n0 = obsmoe.kernel_launches()
     step()
+    ranks.barrier()
     launches_per_step = obsmoe.kernel_launches() - n0
     cap = torch.cuda.Stream()
     cap.wait_stream(stream)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.stream(cap):
         with torch.cuda.graph(g, stream=cap):
-            r.copy_(r0)
-            ctx.moe_stack_forward(0, nl, r, T, bias=bias, path=path, stream=cap)
+            step(cap)
     stream.wait_stream(cap)
-    barrier()
+    ranks.barrier()
     for _ in range(max(args.warmup, 3)):
         g.replay()
-    barrier()
+    ranks.barrier()
     ctx.check_device()
+    # ---------------------------------------------------------------- timed region
     clocks = Clocks(local)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
+    ranks.barrier()
     ev0.record(stream)
     for _ in range(args.steps):
         g.replay()
     ev1.record(stream)
-    barrier()
-    ms = ev0.elapsed_time(ev1)
+    ranks.barrier()
     clk = clocks.stop()
+    ms = ranks.max(ev0.elapsed_time(ev1))
     ctx.check_device()
-    ms_t = torch.tensor([ms], device="cuda")
-    if dist is not None:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms = float(ms_t.item())
     step_s = ms / args.steps / 1e3
     value = world * T / step_s
 
-    # e2e: the residual batch from pinned host memory, the stack, the result back
+    # ---------------------------------------------------------------- e2e
+    # every step: the residual batch in from pinned host memory, the stack, the result back
     rh = r0.cpu().pin_memory()
     oh = torch.empty_like(rh).pin_memory()
-    barrier()
+    ranks.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
@@ -272,72 +309,101 @@ def run_stack(args, rank, world, local):
         ctx.moe_stack_forward(0, nl, r, T, bias=bias, path=path, stream=stream)
         oh.copy_(r, non_blocking=True)
     e1.record(stream)
-    barrier()
-    ems_t = torch.tensor([e0.elapsed_time(e1)], device="cuda")
-    if dist is not None:
-        dist.all_reduce(ems_t, op=dist.ReduceOp.MAX)
-    e2e_value = world * T * args.steps / (float(ems_t.item()) / 1e3)
+    ranks.barrier()
+    e2e_value = world * T * args.steps / (ranks.max(e0.elapsed_time(e1)) / 1e3)
 
-    # per-layer routing of this step (distinct experts), replayed eagerly layer by layer
-    hbm, bf16, peak_kind = peaks()
+    # ------------------------------------------- stage times: one eager step, events per launch
+    ctx.profile(True)
+    step()
+    ranks.barrier()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    stage_us = {k: round(v[0] / max(v[1], 1) * 1e3, 2) for k, v in prof.items() if v[1]}
+
+    # ---------------------------------- per-layer routing of this step (the same inputs), eagerly
     logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
     ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
     wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
     xn = torch.empty_like(r0)
     rr = r0.clone()
-    U, loads = [], []
+    U, loads, local_rows, sent_rows = [], [], [], []
+    EL = E // world if ep else E
     for l in range(nl):
         ctx.rmsnorm(rr, xn, T)
         ctx.gate_gpu(l, xn, logits, T)
         ctx.route(logits, T, ids, wts, bias=bias)
-        every = ids.cpu().numpy().ravel()
-        if ep:
-            parts = [None] * world
-            dist.all_gather_object(parts, every)
-            every = np.concatenate(parts)
+        mine = ids.cpu().numpy().ravel()
+        if ep:  # rows this rank sends to another rank (and gets back), per layer
+            sent_rows.append(int(np.sum(mine // EL != rank)))
+        every = np.concatenate(ranks.gather(mine)) if ep else mine
         U.append(len(np.unique(every)))
-        loads.append(np.bincount(every, minlength=E))
+        cnt = np.bincount(every, minlength=E)
+        loads.append(cnt)
+        local_rows.append(int(cnt[rank * EL:(rank + 1) * EL].sum()) if ep else int(cnt.sum()))
         ctx.moe_stack_forward(l, 1, rr, T, bias=bias, path=path, stream=stream)
     torch.cuda.synchronize()
     load = np.sum(loads, axis=0)
+    hbm, bf16, bf16_sus, peak_kind = peaks()
     if decode:
         # HBM roofline: every routed expert's weights, the router and the activations, per layer
         per_gpu_bytes = (sum(U) * EXPERT_BYTES / world + nl * ROUTER_BYTES + nl * 2 * T * H * 2 * 2)
         achieved = per_gpu_bytes / step_s / 1e9
         roof = {"bound": "hbm", "kernel": f"whole {nl}-layer decode step (router, top-k, 4-bit mat-vecs, combine, "
                 f"RMSNorm per layer)", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "peak_source": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
                 "algorithmic_bytes_per_launch": per_gpu_bytes, "traffic": None}
     else:
-        flops = nl * T * LAYER_FLOPS  # per GPU (weak scaling: each GPU's T tokens)
-        achieved = flops / step_s / 1e12
-        roof = {"bound": "tensor", "kernel": f"whole {nl}-layer prefill step (grouped tcgen05 GEMMs dominate)",
-                "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops)",
-                "algorithmic_flops_per_launch": flops, "traffic": None}
+        # the gate/up grouped GEMM: FLOPs of the rows it processed in this step / its event time
+        gu_ms, gu_n = prof["gemm_gateup"]
+        gu_flops = float(np.mean(local_rows)) * GATEUP_FLOPS_PER_ROW  # per launch (one per layer)
+        gu_s = gu_ms / max(gu_n, 1) / 1e3
+        achieved = gu_flops / gu_s / 1e12
+        stack_tf = nl * T * LAYER_FLOPS / step_s / 1e12
+        roof = {"bound": "tensor",
+                "kernel": "k_gemm<kEpiSwiglu> (tcgen05 grouped gate/up GEMM + SwiGLU), mean over the step's layers",
+                "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s", "frac": achieved / bf16_sus,
+                "peak_source": f"{peak_kind} sustained bf16 (MEASURED_PEAKS.json bf16_tflops_sustained: the kernel "
+                               f"runs inside a {step_s * 1e3:.0f} ms step)",
+                "frac_of_burst_peak": achieved / bf16, "burst_peak": bf16,
+                "algorithmic_flops_per_launch": gu_flops, "kernel_us": gu_s * 1e6,
+                "traffic": NCU_TRAFFIC.get(("gemm_gateup_cfg3", T)) if world == 1 else None,
+                "whole_stack": {"achieved": stack_tf, "frac": stack_tf / bf16_sus,
+                                "flops_per_step": nl * T * LAYER_FLOPS}}
     line = {
         "metric": "MoE stack tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; BASELINE config distributions; weights generated on the device)",
         "config": {"workload": cfg["name"], "layers": nl, "T": T, "E": E, "K": K, "H": H, "I": I,
-                   "parallelism": (f"expert parallel x{world} (NVLink peer all-to-all)" if ep else
+                   "parallelism": (f"expert parallel x{world} (NVLink peer stores)" if ep else
                                    f"data parallel x{world} (replicas)" if world > 1 else "single GPU"),
                    "l2": f"inputs larger than L2: {nl} resident layers ({nl * 340} MB) per step",
-                   "path": "decode (mat-vec)" if decode and T <= 2 and not ep else "prefill (tcgen05 grouped GEMM)",
-                   "zipf_beta": beta, "load_max_over_mean_layer0": imbalance,
-                   "load_max_over_mean_all_layers": float(load.max() / load.mean())},
-        "roofline": roof, "distinct_experts_per_layer": float(np.mean(U)),
+                   "path": "decode (mat-vec)" if decode and T <= decode_max and not ep else
+                           "prefill (tcgen05 grouped GEMM)",
+                   "zipf_beta": beta},
+        "roofline": roof, "stage_us": stage_us, "distinct_experts_per_layer": float(np.mean(U)),
+        "load": {"expert_max_over_mean_layer0": imbalance0,
+                 "expert_max_over_mean_all_layers": float(load.max() / load.mean())},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2},
         "gpu_launches": launches_per_step * args.steps, "clocks": clk,
     }
+    if ep:
+        rows_per_gpu = ranks.gather(float(np.mean(local_rows)))
+        sent = ranks.gather(float(np.mean(sent_rows)))
+        line["ep"] = {"experts_per_gpu": EL,
+                      "rows_per_gpu_per_layer": rows_per_gpu,
+                      "gpu_rows_max_over_mean": float(max(rows_per_gpu) / np.mean(rows_per_gpu)),
+                      "a2a_bytes_per_gpu_per_layer": {"dispatch": [s * H * 2 for s in sent],
+                                                      "combine": [s * H * 2 for s in sent],
+                                                      "row_bytes": H * 2},
+                      "note": "rows to another GPU travel once per (token, expert) pair out and back"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
 
-        # bounded sample: 2 layers and at most 32 tokens through the C oracle, scaled to the stack
-        nlo, Ts = 2, min(T, 32)
+        # bounded sample: 2 layers and at most 64 tokens through the C oracle, scaled to the stack
+        nlo, Ts = 2, min(T, 64)
         Ls = [O.synth_layer(0, l, E=E, H=H, I=I, K=K) for l in range(nlo)]
         rs = r0[:Ts].cpu().numpy().view(np.uint16)
         n = os.cpu_count() or 1
@@ -347,98 +413,31 @@ def run_stack(args, rank, world, local):
         line["cpu_baseline"] = {"value": Ts / dt, "unit": "tokens/s", "cores": n, "kind": "port",
                                 "sample": f"{Ts} tokens through {nlo} layers of oracle/obs_oracle.c, "
                                           f"time scaled to {nl} layers"}
-    if dist is not None:
-        dist.barrier()  # no rank frees its peer-mapped buffer while another may still use it
+    ranks.barrier()  # no rank frees its peer-mapped buffer while another may still use it
+    del g
     ctx.close()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line))
+    return line
 
 
-def run_reference(args, rank, world):
-    """The reference's own kernels on the host cores (oracle/_ref)."""
-    cfg = CONFIGS[args.config]
-    T = cfg["T"] if cfg["T"] is not None else args.batch
-    if rank != 0:
-        return
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-
-    if O.ref_lib() is None:
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libobs_refshaders.so was not built"}))
-        return
-    n = os.cpu_count() or 1
-    Ts = min(T, 64)  # bounded sample: one step is Ts tokens of the workload
-    L = O.synth_layer(0, 0, E=E, H=H, I=I, K=K)
-    x = O.synth_x(0, 0, Ts, H)
-    for _ in range(args.warmup):
-        O.ref_moe_prefill(L, x, nthreads=n)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        O.ref_moe_prefill(L, x, nthreads=n)
-    dt = time.perf_counter() - t0
-    value = Ts * args.steps / dt
-    sample = (f"{Ts} of the {T} tokens per step through the reference's shaders/*.metal kernels compiled "
-              f"for the CPU (oracle/_ref), strung as src/forward.rs:164-232, {n} threads")
-    metric = "MoE layer tokens/s"
-    if cfg.get("stack"):  # one layer timed, scaled to the stack's layer count
-        value /= args.layers
-        metric = "MoE stack tokens/s"
-        sample += f"; one layer per step, time scaled to {args.layers} layers"
-    print(json.dumps({
-        "impl": "reference", "metric": metric, "value": value, "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded, BASELINE config distributions)",
-        "config": {"workload": cfg["name"], "T": T, "E": E, "K": K, "H": H, "I": I, "sample_tokens": Ts},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": n, "kind": "reference", "sample": sample},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }))
-
-
-def main():
-    args = parse()
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
-        return run_reference(args, rank, world)
-    if CONFIGS[args.config].get("stack"):
-        return run_stack(args, rank, world, local)
-
+def run_layer(args, cfg_id, rank, world, local, ranks, steps, warmup, tokens=0, cpu=True):
+    """Configs 0 and 1: one MoE layer per step, steps rotating over N_ROT resident
+    layers, each replayed from a CUDA graph of its forward."""
     import numpy as np
     import torch
 
     import obsmoe
 
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        # NCCL carries only barriers and small reductions here; no NVLink multicast
-        # (NVLS) objects next to the peer buffers the expert exchange writes into
-        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-    cfg = dict(CONFIGS[args.config])
-    if args.tokens:
-        cfg["T"], cfg["name"] = args.tokens, cfg["name"].split(",")[0] + f", T={args.tokens} tokens (sweep)"
+    cfg = dict(CONFIGS[cfg_id])
+    if tokens:
+        cfg["T"], cfg["name"] = tokens, cfg["name"].split(",")[0] + f", T={tokens} tokens (sweep)"
     T = cfg["T"]
-    # N GPUs: each routes its own T tokens; by default every GPU holds all experts
-    # (data-parallel replicas), with --ep E/N experts per GPU and an NVLink exchange
-    ep = world > 1 and args.ep
+    ep = world > 1 and not args.replicas
     path = obsmoe.PATH_DECODE if T <= 2 and not ep else obsmoe.PATH_PREFILL
     shape = obsmoe.MoeShape(H, I, E, K, n_layers=N_ROT, max_tokens=max(T, 16),
                             ep_world=world if ep else 1, ep_rank=rank if ep else 0)
     ctx = obsmoe.MoeContext(shape, local)
     if ep:
-        handles = [None] * world
-        dist.all_gather_object(handles, ctx.ep_handle())
-        ctx.ep_connect(handles)
+        ctx.ep_connect(ranks.gather(ctx.ep_handle()))
     for l in range(N_ROT):
         ctx.synth_layer(l, 0)  # layer l of seed 0 (config 2's per-layer seeding)
     xs = [torch.empty((T, H), dtype=torch.int16, device="cuda") for _ in range(N_ROT)]
@@ -451,16 +450,9 @@ def main():
         l = i % N_ROT
         ctx.moe_forward(l, xs[l], out, T, path=path, stream=stream)
 
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    for i in range(max(args.warmup, 3)):
+    for i in range(max(warmup, 3)):
         step(i)
     ctx.check_device()
-    # one CUDA graph per resident layer: a step replays the layer's whole
-    # forward (router .. combine) without host launch gaps
     n0 = obsmoe.kernel_launches()
     step(0)
     launches_per_step = obsmoe.kernel_launches() - n0
@@ -474,34 +466,30 @@ def main():
                 ctx.moe_forward(l, xs[l], out, T, path=path, stream=cap)
             graphs.append(g)
     stream.wait_stream(cap)
-    for i in range(max(args.warmup, 3)):
+    for i in range(max(warmup, 3)):
         graphs[i % N_ROT].replay()
-    barrier()
+    ranks.barrier()
     ctx.check_device()
     # ------------------------------------------------------------ timed region
     clocks = Clocks(local)
-    barrier()
+    ranks.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for i in range(args.steps):
+    for i in range(steps):
         graphs[i % N_ROT].replay()
     ev1.record(stream)
-    barrier()
-    ms = ev0.elapsed_time(ev1)
+    ranks.barrier()
     clk = clocks.stop()
+    ms = ranks.max(ev0.elapsed_time(ev1))
     ctx.check_device()
     # stage times from a separate, eager pass (events between the stages)
     ctx.profile(True)
-    for i in range(args.steps):
+    for i in range(min(steps, 200)):
         step(i)
     torch.cuda.synchronize()
     prof = ctx.profile_read()
     ctx.profile(False)
-    ms_t = torch.tensor([ms], device="cuda")
-    if dist is not None:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms = float(ms_t.item())
-    value = world * T * args.steps / (ms / 1e3)
+    value = world * T * steps / (ms / 1e3)
 
     # ---------------------------------------------------------------- e2e
     # every step copies its input in from pinned host memory and its output back, through the
@@ -521,24 +509,20 @@ def main():
         host_step(i)
     ctx.host_join(stream)
     stream.synchronize()
-    barrier()
+    ranks.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
+    for i in range(steps):
         host_step(i)
     ctx.host_join(stream)  # the last step's result is in host memory before e1
     e1.record(stream)
     stream.synchronize()
-    barrier()
-    ems_t = torch.tensor([e0.elapsed_time(e1)], device="cuda")
-    if dist is not None:
-        dist.all_reduce(ems_t, op=dist.ReduceOp.MAX)
-    e2e_value = world * T * args.steps / (float(ems_t.item()) / 1e3)
+    ranks.barrier()
+    e2e_value = world * T * steps / (ranks.max(e0.elapsed_time(e1)) / 1e3)
 
     # ------------------------------------------------ roofline of the top kernel
-    hbm, bf16, peak_kind = peaks()
-    # distinct experts per step (U), from the same routing the timed steps used
+    hbm, _, _, peak_kind = peaks()
     ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
     wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
     logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
@@ -549,9 +533,7 @@ def main():
         ctx.route(logits, T, ids, wts, stream=stream)
         mine = ids.cpu().numpy().ravel()
         if ep:  # this GPU's experts see every rank's rows routed to them
-            every = [None] * world
-            dist.all_gather_object(every, mine)
-            mine = np.concatenate(every)
+            mine = np.concatenate(ranks.gather(mine))
         local_ids = mine[(mine >= e_lo) & (mine < e_hi)]
         U.append(len(np.unique(local_ids)))
         R.append(len(local_ids))
@@ -579,39 +561,133 @@ def main():
     layer_bytes = U_mean * EXPERT_BYTES + ROUTER_BYTES + 2 * T * H * 2
     line = {
         "metric": "MoE layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
+        "steps": steps, "warmup": max(warmup, 3), "ms_per_step": ms / steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; BASELINE config distributions; weights generated on the device)",
-        "config": {"workload": cfg["name"], "T": T, "E": E, "K": K, "H": H, "I": I, "weights": "4-bit g64 (router 8-bit)",
-                   "parallelism": (f"expert parallel x{world} (NVLink peer all-to-all)" if ep else
+        "config": {"workload": cfg["name"], "T": T, "E": E, "K": K, "H": H, "I": I,
+                   "weights": "4-bit g64 (router 8-bit)",
+                   "parallelism": (f"expert parallel x{world} (NVLink peer stores)" if ep else
                                    f"data parallel x{world} (replicas)" if world > 1 else "single GPU"),
                    "l2": f"inputs larger than L2: steps rotate over {N_ROT} resident layers ({N_ROT * 340} MB)",
                    "path": "prefill (tcgen05 grouped GEMM)" if path == obsmoe.PATH_PREFILL else "decode (mat-vec)"},
         "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "frac": achieved / hbm, "peak_source": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
                      "algorithmic_bytes_per_launch": alg,
                      "traffic": NCU_TRAFFIC.get((top, T)) if world == 1 else None,
                      "kernel_us": k_avg_s * 1e6},
-        "layer_hbm_gbs": layer_bytes / (ms / args.steps / 1e3) / 1e9,
-        "layer_tflops": 2 * T * K * 4_718_592 / (ms / args.steps / 1e3) / 1e12,
+        "layer_hbm_gbs": layer_bytes / (ms / steps / 1e3) / 1e9,
+        "layer_tflops": 2 * T * K * 4_718_592 / (ms / steps / 1e3) / 1e12,
         "stage_us": stage_us, "distinct_experts": U_mean,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2},
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": launches_per_step * steps,
         "clocks": clk,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
 
         Lh = O.synth_layer(0, 0, E=E, H=H, I=I, K=K)
-        line["cpu_baseline"] = cpu_baseline(Lh, xs[0].cpu().numpy().view(np.uint16), T)
-    if dist is not None:
-        dist.barrier()  # no rank frees its peer-mapped buffer while another may still use it
+        xh0 = xs[0].cpu().numpy().view(np.uint16)
+        n = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        O.moe_layer(Lh, xh0, nthreads=n)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": T / dt, "unit": "tokens/s", "cores": n, "kind": "port",
+                                "sample": f"the full {T}-token layer once through oracle/obs_oracle.c ({dt:.2f} s)"}
+    ranks.barrier()
+    del graphs
     ctx.close()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    return line
+
+
+def extra_summary(line):
+    """The keys of a config 0 / config 1 line that the default line carries."""
+    keep = ("value", "unit", "ms_per_step", "steps", "roofline", "stage_us", "e2e", "gpu_launches", "clocks",
+            "layer_hbm_gbs", "layer_tflops", "distinct_experts")
+    out = {k: line[k] for k in keep if k in line}
+    out["workload"] = line["config"]["workload"]
+    out["path"] = line["config"]["path"]
+    return out
+
+
+def run_reference(args, rank, world):
+    """The reference's own kernels on the host cores (oracle/_ref), on the same config."""
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    import synthetic
+
+    cfg = CONFIGS[args.config]
+    T = cfg["T"] if cfg["T"] is not None else args.batch
+    if O.ref_lib() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libobs_refshaders.so was not built"}))
+        return
+    n = os.cpu_count() or 1
+    Ts = min(T, args.ref_tokens)
+    L = O.synth_layer(0, 0, E=E, H=H, I=I, K=K)
+    # the same inputs as our arm: rank 0's residual batch; the layer input is its RMSNorm
+    r = O.synth_x(0, 0, T, H)
+    x = O.rmsnorm_layer(r)
+    bias = synthetic.zipf_bias(synthetic.CONFIG3_BETA, E) if args.config == 3 else None
+
+    def ref_step(i):
+        lo = (i * Ts) % T
+        O.ref_moe_prefill(L, x[lo:lo + Ts], residual=r[lo:lo + Ts], bias=bias, nthreads=n)
+
+    for i in range(args.warmup):
+        ref_step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        ref_step(i)
+    dt = time.perf_counter() - t0
+    value = Ts * args.steps / dt
+    metric = "MoE layer tokens/s"
+    sample = (f"{Ts} of the {T} tokens per step (slice i*{Ts} mod {T}; each token's work is independent of "
+              f"the others') through the reference's shaders/*.metal kernels compiled for the CPU (oracle/_ref), "
+              f"strung as src/forward.rs:164-232, {n} threads")
+    config = {"workload": cfg["name"], "T": T, "E": E, "K": K, "H": H, "I": I}
+    if cfg.get("stack"):  # one layer per step, time scaled to the stack's layers
+        value /= args.layers
+        metric = "MoE stack tokens/s"
+        config["layers"] = args.layers
+        sample += f"; one layer per step, time scaled to {args.layers} layers"
+    if bias is not None:
+        sample += "; the Zipf expert bias added to the reference's logits before its top-k kernel"
+    print(json.dumps({
+        "impl": "reference", "metric": metric, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded, BASELINE config distributions)",
+        "config": config,
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": n, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    import torch
+
+    torch.cuda.set_device(local)
+    ranks = Ranks(world)
+    if CONFIGS[args.config].get("stack"):
+        line = run_stack(args, rank, world, local, ranks)
+        if args.config == 3 and world == 1 and not args.no_extras:
+            # the decode target (config 0) and config 1, each timed for ~EXTRA_SECONDS
+            line["config0"] = extra_summary(run_layer(args, 0, rank, world, local, ranks,
+                                                      steps=int(EXTRA_SECONDS / 27e-6), warmup=20, cpu=False))
+            line["config1"] = extra_summary(run_layer(args, 1, rank, world, local, ranks,
+                                                      steps=int(EXTRA_SECONDS / 130e-6), warmup=10, cpu=False))
+    else:
+        line = run_layer(args, args.config, rank, world, local, ranks, args.steps, args.warmup, tokens=args.tokens)
+    ranks.close()
     if rank == 0:
         print(json.dumps(line))
 

@@ -299,7 +299,7 @@ def ref_lib():
         R.ref_ew_scaled_add.argtypes = [_f16p, _f16p, C.c_float, C.c_int]
         R.ref_rmsnorm.argtypes = [_f16p, _f16p, _f16p, C.c_int, C.c_int, C.c_float]
         R.ref_moe_prefill.restype = C.c_int
-        R.ref_moe_prefill.argtypes = [C.c_void_p, _u16p, C.c_void_p, C.c_int, C.c_int, _f16p,
+        R.ref_moe_prefill.argtypes = [C.c_void_p, _u16p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, _f16p,
                                       _i32p, _f32p]
         _REF = R
     return _REF
@@ -334,7 +334,7 @@ class _RefLayer(C.Structure):
                 ("up_b", C.c_void_p), ("down_s", C.c_void_p), ("down_b", C.c_void_p)]
 
 
-def ref_moe_prefill(L: Layer, x, residual=None, nthreads=None):
+def ref_moe_prefill(L: Layer, x, residual=None, nthreads=None, bias=None):
     """The reference's batched-prefill MoE section on the CPU: (out f16, ids, w)."""
     R = ref_lib()
     if R is None:
@@ -351,5 +351,7 @@ def ref_moe_prefill(L: Layer, x, residual=None, nthreads=None):
                    L.up_s.ctypes.data, L.up_b.ctypes.data, L.down_s.ctypes.data,
                    L.down_b.ctypes.data)
     res = None if residual is None else np.ascontiguousarray(residual, np.uint16)
-    R.ref_moe_prefill(C.byref(st), x, None if res is None else res.ctypes.data, T, nthreads, out, ids, w)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    R.ref_moe_prefill(C.byref(st), x, None if res is None else res.ctypes.data, None if b is None else b.ctypes.data,
+                      T, nthreads, out, ids, w)
     return out, ids, w

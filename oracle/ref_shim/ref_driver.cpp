@@ -127,6 +127,9 @@ void ref_ew_scaled_add(half* acc, const half* y, float scale, int n) {
 // Inputs in the repository's bf16 host format; converted to f16 on entry the
 // way the reference's loaders do.  out [T,H] f16 = x1 after the rank-order
 // scaled adds, x1 starting from `residual` (or zeros).  ids/weights per token.
+// logit_bias (fp32 [E], may be NULL) is added to the f16 logits the router
+// mat-vec wrote before its top-k kernel runs: the skewed-load configuration of
+// the benchmark, which the reference's router has no input for.
 struct RefLayer {
     int E, H, I, K;
     const uint32_t *router_w, *gate_w, *up_w, *down_w;
@@ -134,7 +137,7 @@ struct RefLayer {
 };
 
 int ref_moe_prefill(const RefLayer* L, const uint16_t* x_bf16, const uint16_t* residual_bf16,
-                    int T, int nthreads, half* out, int* ids_out, float* w_out) {
+                    const float* logit_bias, int T, int nthreads, half* out, int* ids_out, float* w_out) {
     const int E = L->E, H = L->H, I = L->I, K = L->K, G = H / 64, GI = I / 64;
     std::vector<half> x = to_f16(x_bf16, (size_t)T * H);
     std::vector<half> rs = to_f16(L->router_s, (size_t)E * G), rb = to_f16(L->router_b, (size_t)E * G);
@@ -145,6 +148,8 @@ int ref_moe_prefill(const RefLayer* L, const uint16_t* x_bf16, const uint16_t* r
         std::vector<half> logits(E), w(K);
         ref_dequant_matvec_8bit(L->router_w, rs.data(), rb.data(), x.data() + (size_t)t * H,
                                 logits.data(), H, E);
+        if (logit_bias)
+            for (int e = 0; e < E; ++e) logits[e] = (half)((float)logits[e] + logit_bias[e]);
         ref_moe_routing_topk(logits.data(), E, K, 1, ids.data() + (size_t)t * K, w.data());
         for (int k = 0; k < K; ++k) wts[(size_t)t * K + k] = (float)w[k];  // router.rs:91-92
     });

@@ -118,7 +118,10 @@ __device__ __forceinline__ void topk_token(LogitFn logit, const float* __restric
             if (key[i] > kb) kb = key[i], ib = lane + 32 * i;
         const uint32_t best = __reduce_max_sync(0xffffffffu, kb);
         const int bi = (int)__reduce_min_sync(0xffffffffu, kb == best ? (uint32_t)ib : 0x7fffffffu);
-        if ((bi & 31) == lane) key[bi >> 5] = 0;
+        // clear the winner's key (compile-time indices: key[] stays in registers)
+#pragma unroll
+        for (int i = 0; i < kMaxE / 32; ++i)
+            if (bi == lane + 32 * i) key[i] = 0;
         if (lane == k) kk = best, ik = bi;
     }
     const float p = lane < K ? expf(key_value(kk) - mx) / se : 0.0f;

@@ -137,7 +137,7 @@ class MoeShape:
     n_layers: int = 1
     max_tokens: int = 512
     norm_topk: bool = True
-    decode_max_tokens: int = 2
+    decode_max_tokens: int = 0   # <= 0: the library's default
     rms_eps: float = 1e-6
     ep_world: int = 1    # expert parallelism: ranks sharing the experts
     ep_rank: int = 0

@@ -24,6 +24,7 @@ pytestmark = pytest.mark.gpu
 
 E, H, I, K = 128, 2048, 768, 8
 T3 = 4096
+DECODE_MAX = 8
 
 
 @pytest.fixture(scope="module")
@@ -93,7 +94,8 @@ def test_config3_token_permutation_is_bit_exact(cfg3):
 @pytest.fixture(scope="module")
 def cfg2(cuda):
     torch = cuda
-    ctx = obsmoe.MoeContext(obsmoe.MoeShape(H, I, E, K, n_layers=2, max_tokens=128), 0)
+    # OBS_PATH_AUTO takes the decode mat-vec up to DECODE_MAX tokens and the grouped GEMM above
+    ctx = obsmoe.MoeContext(obsmoe.MoeShape(H, I, E, K, n_layers=2, max_tokens=128, decode_max_tokens=DECODE_MAX), 0)
     Ls = [O.synth_layer(0, l) for l in range(2)]
     for l, L in enumerate(Ls):
         ctx.load_layer(l, L)
@@ -113,7 +115,7 @@ def test_config2_batched_decode_vs_oracle(cfg2, B):
     for path in paths:
         got = stack_forward(torch, ctx, r0, B, None, path)
         # the decode mat-vec keeps fp32 weights (wmode 0), the grouped GEMM rounds them to bf16 (wmode 1)
-        gemm = path == obsmoe.PATH_PREFILL or (path == obsmoe.PATH_AUTO and B > ctx.shape.decode_max_tokens)
+        gemm = path == obsmoe.PATH_PREFILL or (path == obsmoe.PATH_AUTO and B > DECODE_MAX)
         same = ref1 if gemm else ref0
         print(f"B={B} path={path}: normwise {rel_err(got, ref0):.2e}, same-arithmetic {rel_err(got, same):.2e}, "
               f"elementwise {elem_err(got, same):.2e}")
@@ -123,14 +125,15 @@ def test_config2_batched_decode_vs_oracle(cfg2, B):
 
 
 @pytest.mark.parametrize("T,path", [(1, obsmoe.PATH_AUTO), (4, obsmoe.PATH_DECODE), (8, obsmoe.PATH_AUTO),
-                                    (100, obsmoe.PATH_PREFILL)])
+                                    (12, obsmoe.PATH_AUTO), (100, obsmoe.PATH_PREFILL)])
 def test_stack_two_full_layers_vs_oracle(cfg2, T, path):
     torch, ctx, Ls = cfg2
     r0 = O.synth_x(0, 7, T, H)
     got = stack_forward(torch, ctx, r0, T, None, path, n_layers=2)
-    gemm = path == obsmoe.PATH_PREFILL or (path == obsmoe.PATH_AUTO and T > ctx.shape.decode_max_tokens)
+    gemm = path == obsmoe.PATH_PREFILL or (path == obsmoe.PATH_AUTO and T > DECODE_MAX)
     same = O.moe_stack(Ls, r0, wmode=1 if gemm else 0)
     ref = O.moe_stack(Ls, r0, wmode=0)
     print(f"stack T={T} path={path}: normwise {rel_err(got, ref):.2e}, same-arithmetic {rel_err(got, same):.2e}")
     assert rel_err(got, ref) < REL
-    assert rel_err(got, same) < REL_SAME
+    # the second layer's input carries the first layer's rounding differences: the per-layer bound twice
+    assert rel_err(got, same) < 2 * REL_SAME

@@ -1,6 +1,6 @@
 """The fused decode layer (one cooperative launch for T <= 4) against the
 separate decode kernels (router, top-k, gate/up mat-vec, down mat-vec, combine
-as five launches, taken for T = 5).  Every output row depends on its own input
+as four launches, taken for T = 5).  Every output row depends on its own input
 row only, so rows [r, r+T) of a fused call on x[r:r+T] must equal the same rows
 of the separate kernels' call on all of x, bit for bit: same router order, same
 split-K chains, same combine order.  Also checked against the oracle."""
