@@ -333,8 +333,10 @@ def run_stack(args, rank, world, local, ranks):
         ctx.gate_gpu(l, xn, logits, T)
         ctx.route(logits, T, ids, wts, bias=bias)
         mine = ids.cpu().numpy().ravel()
-        if ep:  # rows this rank sends to another rank (and gets back), per layer
-            sent_rows.append(int(np.sum(mine // EL != rank)))
+        if ep:  # rows this rank sends to other ranks: once per (token, rank); outputs back per (token, expert)
+            dest = (mine // EL).reshape(T, K)
+            sent_rows.append((sum(int(np.sum(np.any(dest == d, axis=1))) for d in range(world) if d != rank),
+                              int(np.sum(dest != rank))))
         every = np.concatenate(ranks.gather(mine)) if ep else mine
         U.append(len(np.unique(every)))
         cnt = np.bincount(every, minlength=E)
@@ -390,14 +392,16 @@ def run_stack(args, rank, world, local, ranks):
     }
     if ep:
         rows_per_gpu = ranks.gather(float(np.mean(local_rows)))
-        sent = ranks.gather(float(np.mean(sent_rows)))
+        sent = ranks.gather([float(np.mean([r[0] for r in sent_rows])), float(np.mean([r[1] for r in sent_rows]))])
         line["ep"] = {"experts_per_gpu": EL,
                       "rows_per_gpu_per_layer": rows_per_gpu,
                       "gpu_rows_max_over_mean": float(max(rows_per_gpu) / np.mean(rows_per_gpu)),
-                      "a2a_bytes_per_gpu_per_layer": {"dispatch": [s * H * 2 for s in sent],
-                                                      "combine": [s * H * 2 for s in sent],
+                      "a2a_bytes_per_gpu_per_layer": {"dispatch": [s[0] * H * 2 for s in sent],
+                                                      "combine": [s[1] * H * 2 for s in sent],
                                                       "row_bytes": H * 2},
-                      "note": "rows to another GPU travel once per (token, expert) pair out and back"}
+                      "note": "over NVLink: a token row goes to another GPU once per (token, GPU) however many of "
+                              "its experts live there; outputs come back once per (token, expert) pair; rows and "
+                              "outputs that stay on their GPU do not move"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O

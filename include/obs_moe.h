@@ -95,6 +95,24 @@ int obs_memory_bytes(const obs_ctx* ctx, size_t* weights, size_t* scratch);
  * src_on_device != 0 if the pointers are device memory.  Synchronous. */
 int obs_load_layer(obs_ctx* ctx, int layer, const obs_layer_weights* w, int src_on_device);
 
+/* Replaces ExpertIndex::open + read_experts_parallel (src/disk_io.rs:24-102)
+ * for one layer file of the reference's expert splitter
+ * (tools/split_experts.py:63-75): layer_{il}_experts.safetensors with tensors
+ * e{N}.{gate_proj,up_proj,down_proj}.{weight (U32 [out, in/8]), scales, biases
+ * (F16 or BF16 [out, in/64])}.  The whole file is read once, stacked and loaded
+ * like obs_load_layer (F16 scales/biases are rounded to bf16, exactly for every
+ * value the splitter wrote from a bf16 checkpoint).  The router gate is not in
+ * these files (src/weight_loader.rs:19-71 loads it from the model's shards):
+ * router_w/_s/_b are its host arrays in obs_layer_weights' layout.  The file's
+ * shapes must equal the context's.  Synchronous. */
+int obs_load_layer_safetensors(obs_ctx* ctx, int layer, const char* path, const uint32_t* router_w,
+                               const uint16_t* router_s, const uint16_t* router_b);
+/* Reads only the header of such a file (no GPU needed) and reports its expert
+ * count, hidden and intermediate sizes after checking that every expert has
+ * all nine tensors with consistent dtypes and shapes; errors through
+ * obs_last_error(NULL). */
+int obs_expert_file_info(const char* path, int32_t* n_experts, int32_t* hidden, int32_t* inter);
+
 /* Seeded synthetic layer generated on the device (bench/test support): the
  * same values oracle/obs_oracle.c produces on the host for (seed, layer). */
 int obs_synth_layer(obs_ctx* ctx, int layer, uint64_t seed);

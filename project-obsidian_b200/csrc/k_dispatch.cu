@@ -84,14 +84,17 @@ __global__ void __launch_bounds__(kDispThreads) k_dispatch(const int32_t* __rest
 // The routed rows (slot order) into the tiled activation layout the grouped
 // GEMM reads with bulk copies: one warp per slot row, 16-byte chunks (coalesced
 // 512-byte reads of the source row, 128-byte runs per k-group in the
-// destination); padding rows (src = -1) are written as zeros.
+// destination); padding rows (src = -1) are written as zeros.  Token t's row is
+// x[t], or row_src[t] when given (expert parallelism: received rows live in
+// the exchange buffer, the rank's own in x).
 __global__ void __launch_bounds__(256) k_permute(const uint16_t* __restrict__ x, int H, const int32_t* __restrict__ src,
                                                  const int32_t* __restrict__ seg_end, int atoms,
-                                                 uint16_t* __restrict__ xp) {
+                                                 uint16_t* __restrict__ xp, const uint16_t* const* __restrict__ row_src) {
     pdl_begin();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= *seg_end) return;
     const int t = src[row];
+    const uint16_t* xrow = t >= 0 ? (row_src ? row_src[t] : x + (size_t)t * H) : nullptr;
     const int chunks = H / 8;
     for (int c0 = lane; c0 < chunks; c0 += 32 * 8) {  // H = 2048: the whole row in flight at once
         uint4 v[8];
@@ -99,7 +102,7 @@ __global__ void __launch_bounds__(256) k_permute(const uint16_t* __restrict__ x,
         for (int u = 0; u < 8; ++u) {
             const int c = c0 + 32 * u;
             v[u] = make_uint4(0, 0, 0, 0);
-            if (t >= 0 && c < chunks) v[u] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H) + c);
+            if (t >= 0 && c < chunks) v[u] = __ldg(reinterpret_cast<const uint4*>(xrow) + c);
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
@@ -138,21 +141,30 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const uint16_t* __restrict__ x,
     }
 }
 
-// out[t] = bf16(residual[t] + sum_k w[t,k] * y[slot_of[t,k]]), rank order, fp32
+// out[t] = bf16(residual[t] + sum_k w[t,k] * y[slot_of[t,k]]), rank order, fp32.
+// slot_of == nullptr: y is in item order (row t*K + k).  local != nullptr
+// (expert parallelism): an item whose entry is s + 1 > 0 was computed on this
+// rank and is read from row s of y_local instead; the entry is cleared for the
+// next forward.
 constexpr int kCombineMaxK = 16;  // the context accepts top_k <= 16
 
 __global__ void __launch_bounds__(256) k_combine(const uint16_t* __restrict__ y, int y_ld,
                                                  const int32_t* __restrict__ slot_of, const float* __restrict__ w,
                                                  const uint16_t* __restrict__ residual, int H, int K,
-                                                 uint16_t* __restrict__ out) {
+                                                 uint16_t* __restrict__ out, const uint16_t* __restrict__ y_local,
+                                                 int32_t* __restrict__ local) {
     pdl_begin();
     const int t = blockIdx.x;
-    // the token's K slots and weights once per CTA, so every row load below is independent
-    __shared__ int s_slot[kCombineMaxK];
+    // the token's K rows and weights once per CTA, so every row load below is independent
+    __shared__ const uint16_t* s_row[kCombineMaxK];
     __shared__ float s_w[kCombineMaxK];
     if (threadIdx.x < K) {
-        s_slot[threadIdx.x] = slot_of ? slot_of[(size_t)t * K + threadIdx.x] : t * K + threadIdx.x;  // nullptr: item order
-        s_w[threadIdx.x] = w[(size_t)t * K + threadIdx.x];
+        const size_t item = (size_t)t * K + threadIdx.x;
+        const int slot = slot_of ? slot_of[item] : (int)item;  // nullptr: item order
+        const int ls = local ? local[item] : 0;
+        s_row[threadIdx.x] = ls > 0 ? y_local + (size_t)(ls - 1) * y_ld : y + (size_t)slot * y_ld;
+        if (ls > 0) local[item] = 0;
+        s_w[threadIdx.x] = w[item];
     }
     __syncthreads();
     for (int f = threadIdx.x * 8; f < H; f += blockDim.x * 8) {
@@ -171,7 +183,7 @@ __global__ void __launch_bounds__(256) k_combine(const uint16_t* __restrict__ y,
             uint4 v[8];
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
-                if (k0 + kk < K) v[kk] = __ldg(reinterpret_cast<const uint4*>(y + (size_t)s_slot[k0 + kk] * y_ld + f));
+                if (k0 + kk < K) v[kk] = __ldg(reinterpret_cast<const uint4*>(s_row[k0 + kk] + f));
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
                 if (k0 + kk >= K) break;
@@ -221,7 +233,7 @@ __global__ void k_tile_rows(const uint16_t* __restrict__ x, int n, int cols, int
 }  // namespace
 
 cudaError_t launch_dispatch(const int32_t* ids, const uint16_t* x, int T, const Shape& sh, const DispatchBufs& d,
-                            int permute, cudaStream_t st) {
+                            int permute, cudaStream_t st, const uint16_t* const* row_src) {
     {
         const cudaError_t le_ = launch_pdl(k_dispatch, dim3(sh.E), dim3(kDispThreads), 0, st, ids, T, sh.E, sh.K, d);
         if (le_ != cudaSuccess) return le_;
@@ -230,18 +242,21 @@ cudaError_t launch_dispatch(const int32_t* ids, const uint16_t* x, int T, const 
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     {
-        const cudaError_t le_ = launch_pdl(k_permute, dim3(d.atoms), dim3(256), 0, st, x, sh.H, d.src, d.seg + sh.E, d.atoms, d.xp);
+        const cudaError_t le_ =
+            launch_pdl(k_permute, dim3(d.atoms), dim3(256), 0, st, x, sh.H, d.src, d.seg + sh.E, d.atoms, d.xp, row_src);
         if (le_ != cudaSuccess) return le_;
     }  // 8 rows per CTA
     return cudaGetLastError();
 }
 
 cudaError_t launch_combine(const uint16_t* y, int y_ld, const int32_t* slot_of, const float* w,
-                           const uint16_t* residual, int T, int H, int K, uint16_t* out, cudaStream_t st) {
+                           const uint16_t* residual, int T, int H, int K, uint16_t* out, cudaStream_t st,
+                           const uint16_t* y_local, int32_t* local) {
     if (T <= 0) return cudaSuccess;
     if (K > kCombineMaxK) return cudaErrorInvalidValue;
     {
-        const cudaError_t le_ = launch_pdl(k_combine, dim3(T), dim3(256), 0, st, y, y_ld, slot_of, w, residual, H, K, out);
+        const cudaError_t le_ =
+            launch_pdl(k_combine, dim3(T), dim3(256), 0, st, y, y_ld, slot_of, w, residual, H, K, out, y_local, local);
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();

@@ -2,23 +2,33 @@
 //
 // The reference runs every expert on one device (src/forward.rs:164-247); on a
 // multi-GPU box the experts are split across G ranks (rank g holds experts
-// [g*E/G, (g+1)*E/G)) and the routed token rows travel to the rank that holds
-// their expert and back.  Each rank owns one device buffer (opened by its peers
-// through CUDA IPC) laid out identically on every rank:
-//   recv_x  [G][cap][H] bf16   rows sent to this rank, one region per source
-//   meta    [G][cap] int2      (local expert, source item t*K+k) of each row
-//   cnt     [G] int32          rows in each source region
-//   rflag   [G] uint32         epoch stamp: source s finished writing
-//   ret_y   [cap][H] bf16      this rank's expert outputs, indexed by item t*K+k
-//   retflag [G] uint32         epoch stamp: rank d finished returning
-// cap = max_tokens * top_k.  A forward writes peers' memory directly with plain
-// stores (k_ep_send, k_ep_return), then a system-scope fence and a release store
-// of the epoch stamp; readers spin (bounded, 2 s) on acquire loads of the stamps.
-// The epoch lives in device memory (incremented by the last kernel of each
-// forward), so a captured CUDA graph replays correctly.  Buffer reuse needs no
-// extra handshake: a source writes forward e+1's rows to a peer only after its
-// own forward e finished, which waited for that peer's returns of e, which that
-// peer issued after it had consumed the received rows of e.
+// [g*E/G, (g+1)*E/G)) and the routed token rows travel to the ranks that hold
+// their experts and the expert outputs travel back.  A token row is sent to a
+// rank once, however many of its K experts live there, with the list of those
+// experts (local id and rank-order position k) as metadata; the outputs come
+// back once per (token, expert) pair, since each pair's output is distinct --
+// written by the down GEMM's epilogue straight into the source rank's memory,
+// so the return all-to-all overlaps the GEMM tile by tile.  Rows and outputs
+// that stay on their rank are not copied at all.
+//
+// Each rank owns one device buffer (opened by its peers through CUDA IPC) laid
+// out identically on every rank:
+//   recv_x  [G][cap_rows][H] bf16  rows sent to this rank, one region per source
+//   meta    [G][cap_rows][16] int16  per row: (k << 8 | local expert) of each of
+//                                  the token's experts here, -1 elsewhere
+//   mtok    [G][cap_rows] int32    the row's token index at its source
+//   cnt     [G] int32              rows in each source region
+//   rflag   [G] uint32             epoch stamp: source s finished writing
+//   ret_y   [cap_items][H] bf16    this rank's expert outputs, indexed by item t*K+k
+//   retflag [G] uint32             epoch stamp: rank d finished returning
+// cap_rows = max_tokens, cap_items = max_tokens * top_k.  A forward writes
+// peers' memory directly with plain stores, then a system-scope fence and a
+// release store of the epoch stamp; readers spin (bounded) on acquire loads of
+// the stamps.  The epoch lives in device memory (incremented by the last kernel
+// of each forward), so a captured CUDA graph replays correctly.  Buffer reuse
+// needs no extra handshake: a source writes forward e+1's rows to a peer only
+// after its own forward e finished, which waited for that peer's returns of e,
+// which that peer issued after it had consumed the received rows of e.
 #include "obs_internal.cuh"
 
 namespace obs {
@@ -58,35 +68,45 @@ __device__ __forceinline__ T* at(uint8_t* base, size_t off) {
     return reinterpret_cast<T*>(base + off);
 }
 
-// One warp per routed item (t, k): copy row x[t] into the owning rank's region
-// for this source, with its metadata.  The last CTA to finish publishes the
-// per-destination counts and stamps.
+// One warp per token: for every rank that holds one or more of the token's K
+// experts, one copy of row x[t] into that rank's region for this source, with
+// the (k, local expert) list and the token index -- for this rank itself only
+// the list and the index: the permute reads the row from x.  The last CTA to
+// finish publishes the per-destination counts and stamps.
 __global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids, const uint16_t* __restrict__ x,
                                                  int T, int E, EpArgs a) {
     pdl_begin();
     __shared__ int s_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t e = *a.epoch + 1;
-    const int item = blockIdx.x * 8 + warp;
-    if (item < T * a.K) {
-        int id = ids[item];
-        if (id < 0 || id >= E) {
-            if (lane == 0) atomicExch(a.err, kDevBadRoute);
+    const int t = blockIdx.x * 8 + warp;
+    if (t < T) {
+        int id = lane < a.K ? ids[(size_t)t * a.K + lane] : 0;
+        if (lane < a.K && (id < 0 || id >= E)) {
+            atomicExch(a.err, kDevBadRoute);
             id = 0;
         }
-        const int dest = id / a.E_local, le = id - dest * a.E_local;
-        int slot = 0;
-        if (lane == 0) slot = atomicAdd(a.send_cnt + dest, 1);
-        slot = __shfl_sync(0xffffffffu, slot, 0);
-        if (slot < a.cap) {
-            uint8_t* pb = a.peer[dest];
-            const size_t row = (size_t)a.rank * a.cap + slot;
-            const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(item / a.K) * a.H);
-            uint4* dst = at<uint4>(pb, a.off_rx + row * a.H * 2);
-            for (int c = lane; c < a.H / 8; c += 32) dst[c] = __ldg(src + c);
-            if (lane == 0) *at<int2>(pb, a.off_meta + row * 8) = make_int2(le, item);
-        } else if (lane == 0) {
-            atomicExch(a.err, kDevBadSlot);  // more rows than the source's region holds: refused
+        const int dest = lane < a.K ? id / a.E_local : -1;
+        const int le = lane < a.K ? id - dest * a.E_local : 0;
+        const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * a.H);
+        for (int d = 0; d < a.world; ++d) {
+            if (!__any_sync(0xffffffffu, dest == d)) continue;
+            int slot = 0;
+            if (lane == 0) slot = atomicAdd(a.send_cnt + d, 1);
+            slot = __shfl_sync(0xffffffffu, slot, 0);
+            if (slot < a.cap_rows) {
+                uint8_t* pb = a.peer[d];
+                const size_t row = (size_t)a.rank * a.cap_rows + slot;
+                if (d != a.rank) {
+                    uint4* dst = at<uint4>(pb, a.off_rx + row * a.H * 2);
+                    for (int c = lane; c < a.H / 8; c += 32) dst[c] = __ldg(src + c);
+                }
+                if (lane < 16)
+                    at<int16_t>(pb, a.off_meta + row * 32)[lane] = (int16_t)(dest == d ? (lane << 8) | le : -1);
+                if (lane == 0) at<int32_t>(pb, a.off_mtok + row * 4)[0] = t;
+            } else if (lane == 0) {
+                atomicExch(a.err, kDevBadSlot);  // more rows than the source's region holds: refused
+            }
         }
     }
     __threadfence_system();
@@ -99,7 +119,7 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids
     __threadfence_system();
     if (threadIdx.x < a.world) {
         const int d = threadIdx.x;
-        const int n = min(ld_volatile(a.send_cnt + d), a.cap);
+        const int n = min(ld_volatile(a.send_cnt + d), a.cap_rows);
         *at<int32_t>(a.peer[d], a.off_cnt + (size_t)a.rank * 4) = n;
         __threadfence_system();
         st_release_sys(at<uint32_t>(a.peer[d], a.off_rflag + (size_t)a.rank * 4), e);
@@ -109,26 +129,36 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids
 }
 
 // Wait for every source's stamp, then turn the received rows into a local
-// routing problem: ids_local[s*cap + i] = local expert of row i of source s
-// (-1 beyond the source's count) and a histogram per local expert.
-__global__ void __launch_bounds__(256) k_ep_recv(EpArgs a) {
+// routing problem of W*cap_rows "tokens" with K slots each:
+// ids_local[row*K + k] = local expert of slot k of the row (-1: none, or beyond
+// the source's count), src_item = the source's item t*K + k, and a histogram per
+// local expert.  The rows this rank sent itself are read from x: row_src[row] is
+// the row to permute, x[t] for its own region, recv_x[row] otherwise.
+__global__ void __launch_bounds__(256) k_ep_recv(const uint16_t* __restrict__ x, EpArgs a) {
     pdl_begin();
     const uint32_t e = *a.epoch + 1;
     uint8_t* mine = a.peer[a.rank];
     if (!wait_stamps(at<uint32_t>(mine, a.off_rflag), a.world, e, a.err, a.wait_ns)) return;
-    const int n = a.world * a.cap;
+    const int n = a.world * a.cap_rows * a.K;
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
-        const int s = j / a.cap, i = j - s * a.cap;
-        const int cnt = min(ld_volatile(at<int32_t>(mine, a.off_cnt) + s), a.cap);
+        const int row = j / a.K, kk = j - row * a.K;
+        const int s = row / a.cap_rows, i = row - s * a.cap_rows;
+        const int cnt = min(ld_volatile(at<int32_t>(mine, a.off_cnt) + s), a.cap_rows);
         int le = -1, item = -1;
         if (i < cnt) {
-            const int2 m = *at<int2>(mine, a.off_meta + (size_t)j * 8);
-            le = m.x, item = m.y;
-            if (le < 0 || le >= a.E_local || item < 0 || item >= a.cap) {
-                atomicExch(a.err, kDevBadRoute);
-                le = -1;
-            } else {
-                atomicAdd(a.counts + le, 1);
+            const int code = at<int16_t>(mine, a.off_meta + (size_t)row * 32)[kk];
+            const int t = at<int32_t>(mine, a.off_mtok + (size_t)row * 4)[0];
+            if (kk == 0 && t >= 0 && t < a.cap_rows)
+                a.row_src[row] = s == a.rank ? x + (size_t)t * a.H
+                                             : at<uint16_t>(mine, a.off_rx + (size_t)row * a.H * 2);
+            if (code >= 0) {
+                const int l = code & 0xFF, k = code >> 8;
+                if (l >= a.E_local || k >= a.K || t < 0 || t >= a.cap_rows) {
+                    atomicExch(a.err, kDevBadRoute);
+                } else {
+                    le = l, item = t * a.K + k;
+                    atomicAdd(a.counts + le, 1);
+                }
             }
         }
         a.ids_local[j] = le;
@@ -136,35 +166,45 @@ __global__ void __launch_bounds__(256) k_ep_recv(EpArgs a) {
     }
 }
 
-// One warp per received row: its expert output (local slot slot_of[j]) goes back
-// to the source rank's ret_y at the row's item index.  The last CTA stamps every
-// source.
-__global__ void __launch_bounds__(256) k_ep_return(const int32_t* __restrict__ slot_of, const uint16_t* __restrict__ y,
-                                                   EpArgs a) {
+// Every output row (slot) of the down GEMM gets its destination before the
+// GEMM runs.  The slots below the dispatch's padded end are of two disjoint
+// kinds: padding rows (src < 0), which stay in this rank's y, and exactly one
+// received (row, k) pair each, whose output goes to its source rank's ret_y row
+// (item t*K + k) over NVLink -- or, for this rank's own items, stays in y and is
+// noted in local_slot for the combine.
+__global__ void __launch_bounds__(256) k_ep_rowptr(const int32_t* __restrict__ slot_of,
+                                                   const int32_t* __restrict__ src, const int32_t* __restrict__ seg_end,
+                                                   uint16_t* y, uint16_t** __restrict__ row_ptr, EpArgs a) {
     pdl_begin();
-    __shared__ int s_last;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t e = *a.epoch + 1;
-    const int n = a.world * a.cap;
-    for (int j = blockIdx.x * 8 + warp; j < n; j += gridDim.x * 8) {
-        if (a.ids_local[j] < 0) continue;
-        const int s = j / a.cap, item = a.src_item[j], slot = slot_of[j];
-        if (slot < 0 || slot >= a.rows_cap || item < 0 || item >= a.cap) {  // refused, recorded
-            if (lane == 0) atomicExch(a.err, kDevBadSlot);
+    const int total = min(*seg_end, a.rows_cap), n = a.world * a.cap_rows * a.K;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total + n; i += gridDim.x * blockDim.x) {
+        if (i < total) {
+            if (src[i] < 0) row_ptr[i] = y + (size_t)i * a.H;
             continue;
         }
-        const uint4* src = reinterpret_cast<const uint4*>(y + (size_t)slot * a.H);
-        uint4* dst = at<uint4>(a.peer[s], a.off_ret + (size_t)item * a.H * 2);
-        for (int c = lane; c < a.H / 8; c += 32) dst[c] = src[c];
+        const int j = i - total;
+        if (a.ids_local[j] < 0) continue;
+        const int s = j / (a.K * a.cap_rows), item = a.src_item[j], slot = slot_of[j];
+        if (slot < 0 || slot >= total || item < 0 || item >= a.cap_items) {  // refused, recorded
+            atomicExch(a.err, kDevBadSlot);
+            continue;
+        }
+        if (s == a.rank) {
+            row_ptr[slot] = y + (size_t)slot * a.H;
+            a.local_slot[item] = slot + 1;
+        } else {
+            row_ptr[slot] = at<uint16_t>(a.peer[s], a.off_ret + (size_t)item * a.H * 2);
+        }
     }
+}
+
+// The down GEMM wrote every output row to its destination and fenced its stores
+// system-wide: stamp every source.
+__global__ void k_ep_returned(EpArgs a) {
+    pdl_begin();
+    const uint32_t e = *a.epoch + 1;
     __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(a.done + 1, 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence_system();  // pairs with the other CTAs' fences: their row stores precede the stamps
     if (threadIdx.x < a.world) st_release_sys(at<uint32_t>(a.peer[threadIdx.x], a.off_retflag + (size_t)a.rank * 4), e);
-    if (threadIdx.x == 0) a.done[1] = 0;
 }
 
 // The failure path of the peer waits, without peers: one wait on a stamp that
@@ -185,8 +225,8 @@ __global__ void k_ep_finish(EpArgs a) {
 }  // namespace
 
 cudaError_t launch_ep_send(const int32_t* ids, const uint16_t* x, int T, int E, const EpArgs& a, cudaStream_t st) {
-    const int items = T * a.K;
-    const int grid = items > 0 ? (items + 7) / 8 : 1;  // one CTA at least: it publishes the counts
+    if (a.K > 16) return cudaErrorInvalidValue;  // 16 metadata slots per row
+    const int grid = T > 0 ? (T + 7) / 8 : 1;   // one warp per token; one CTA at least: it publishes the counts
     {
         const cudaError_t le_ = launch_pdl(k_ep_send, dim3(grid), dim3(256), 0, st, ids, x, T, E, a);
         if (le_ != cudaSuccess) return le_;
@@ -194,21 +234,31 @@ cudaError_t launch_ep_send(const int32_t* ids, const uint16_t* x, int T, int E, 
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_recv(const EpArgs& a, cudaStream_t st) {
-    const int n = a.world * a.cap;
+cudaError_t launch_ep_recv(const uint16_t* x, const EpArgs& a, cudaStream_t st) {
+    const int n = a.world * a.cap_rows * a.K;
     const int grid = (n + 255) / 256 < 296 ? (n + 255) / 256 : 296;
     {
-        const cudaError_t le_ = launch_pdl(k_ep_recv, dim3(grid), dim3(256), 0, st, a);
+        const cudaError_t le_ = launch_pdl(k_ep_recv, dim3(grid), dim3(256), 0, st, x, a);
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_return(const int32_t* slot_of, const uint16_t* y, const EpArgs& a, cudaStream_t st) {
-    const int n = a.world * a.cap;
-    const int grid = (n + 7) / 8 < 1184 ? (n + 7) / 8 : 1184;
+cudaError_t launch_ep_rowptr(const int32_t* slot_of, const int32_t* src, const int32_t* seg_end, uint16_t* y,
+                             uint16_t** row_ptr, const EpArgs& a, cudaStream_t st) {
+    const int n = a.rows_cap + a.world * a.cap_rows * a.K;
+    const int grid = (n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184;
     {
-        const cudaError_t le_ = launch_pdl(k_ep_return, dim3(grid), dim3(256), 0, st, slot_of, y, a);
+        const cudaError_t le_ =
+            launch_pdl(k_ep_rowptr, dim3(grid), dim3(256), 0, st, slot_of, src, seg_end, y, row_ptr, a);
+        if (le_ != cudaSuccess) return le_;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_returned(const EpArgs& a, cudaStream_t st) {
+    {
+        const cudaError_t le_ = launch_pdl(k_ep_returned, dim3(1), dim3(32), 0, st, a);
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();

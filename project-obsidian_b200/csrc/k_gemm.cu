@@ -518,13 +518,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                 const int nstore = min(tl.z, a.row_limit - tl.y);
                 for (int i = et; i < nstore * 16; i += kEpThreads) {
                     const int jr = i >> 4, c = i & 15;
-                    *reinterpret_cast<uint4*>(yb + (size_t)jr * a.out_ld * 2 + c * 16) =
+                    // with row_ptr (expert parallelism) the row goes straight to its destination, for a
+                    // row computed for another rank that rank's return buffer over NVLink
+                    uint8_t* yrow = a.row_ptr ? reinterpret_cast<uint8_t*>(a.row_ptr[tl.y + jr]) + rt * kRowTile * 2
+                                              : yb + (size_t)jr * a.out_ld * 2;
+                    *reinterpret_cast<uint4*>(yrow + c * 16) =
                         *reinterpret_cast<const uint4*>(stg + jr * 256 + ((c ^ ((jr & 1) << 2)) << 4));
                 }
                 if (et == 0) trace_at<TRACE>(a, kTrEpDone, it);
             }
         }
         if (et == 0) bulk_wait0();  // results are in global memory before the CTA exits
+        if (a.row_ptr) __threadfence_system();  // peer stores ordered before the stamp kernel's
     }
     tc_fence_before();
     __syncthreads();

@@ -81,6 +81,7 @@ struct obs_ctx {
     // expert parallelism (ep_world > 1): this rank holds experts [e0, e0 + E_local)
     int ep_world = 1, ep_rank = 0, E_local = 0, e0 = 0;
     uint8_t* ep_buf = nullptr;  // this rank's buffer, opened by its peers through CUDA IPC
+    uint16_t** ep_row_ptr = nullptr;  // [R_cap] destination of each down-GEMM output row
     size_t ep_bytes = 0;
     bool ep_connected = false;
     EpArgs ep{};
@@ -137,6 +138,12 @@ extern "C" const char* obs_last_error(const obs_ctx* ctx) { return ctx ? ctx->er
 namespace obs {
 // message of a context-free entry point, read back with obs_last_error(NULL)
 void set_thread_error(const char* msg) { g_create_err = msg ? msg : ""; }
+}  // namespace obs
+
+static int fail(obs_ctx* c, int code, const std::string& msg);
+namespace obs {
+void ctx_shape(const obs_ctx* ctx, int* E, int* H, int* I) { *E = ctx->sh.E, *H = ctx->sh.H, *I = ctx->sh.I; }
+int ctx_fail(obs_ctx* ctx, int code, const char* msg) { return fail(ctx, code, msg ? msg : ""); }
 }  // namespace obs
 
 static size_t layer_weight_bytes(const Shape& s, int E_local) {
@@ -257,8 +264,11 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->ep.send_cnt, (size_t)kMaxWorld * 4},
         {(void**)&ctx->ep.done, 16},
         {(void**)&ctx->ep.epoch, 16},
-        {(void**)&ctx->ep.ids_local, W > 1 ? (size_t)W * T * K * 4 : 0},
+        {(void**)&ctx->ep.ids_local, W > 1 ? (size_t)W * T * K * 4 : 0},  // [W * cap_rows * K]
         {(void**)&ctx->ep.src_item, W > 1 ? (size_t)W * T * K * 4 : 0},
+        {(void**)&ctx->ep.local_slot, W > 1 ? (size_t)T * K * 4 : 0},
+        {(void**)&ctx->ep_row_ptr, W > 1 ? (size_t)ctx->R_cap * 8 : 0},
+        {(void**)&ctx->ep.row_src, W > 1 ? (size_t)W * T * 8 : 0},
     };
     size_t total = 0;
     for (auto& it : items) total += align_up(it.bytes ? it.bytes : 16, 1024);
@@ -287,16 +297,18 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     if (W > 1) {
         // this rank's shared buffer (layout in k_ep.cu), zeroed: stamps and counts start at 0
         EpArgs& a = ctx->ep;
-        a.world = W, a.rank = ctx->ep_rank, a.cap = T * K, a.H = s.H, a.K = K, a.E_local = EL;
+        a.world = W, a.rank = ctx->ep_rank, a.H = s.H, a.K = K, a.E_local = EL;
+        a.cap_rows = T, a.cap_items = T * K;
         a.counts = ctx->disp.counts;
         a.rows_cap = ctx->R_cap;
         a.err = ctx->err_flag;
         size_t o = 0;
-        a.off_rx = o, o += align_up((size_t)W * a.cap * s.H * 2, 256);
-        a.off_meta = o, o += align_up((size_t)W * a.cap * 8, 256);
+        a.off_rx = o, o += align_up((size_t)W * a.cap_rows * s.H * 2, 256);
+        a.off_meta = o, o += align_up((size_t)W * a.cap_rows * 32, 256);
+        a.off_mtok = o, o += align_up((size_t)W * a.cap_rows * 4, 256);
         a.off_cnt = o, o += 256;
         a.off_rflag = o, o += 256;
-        a.off_ret = o, o += align_up((size_t)a.cap * s.H * 2, 256);
+        a.off_ret = o, o += align_up((size_t)a.cap_items * s.H * 2, 256);
         a.off_retflag = o, o += 256;
         ctx->ep_bytes = o;
         e = cudaMalloc(&ctx->ep_buf, o);
@@ -672,24 +684,31 @@ static int forward_ep(obs_ctx* ctx, const LayerDev& L, const uint16_t* x, uint16
     prof_begin(ctx, OBS_STAGE_DISPATCH, st);
     CU(launch_ep_send(ctx->ids, x, T, s.E, a, st), "ep send");
     CU(cudaMemsetAsync(ctx->disp.counts, 0, ctx->E_local * 4, st), "memset");
-    CU(launch_ep_recv(a, st), "ep receive");
-    const Shape sl{s.H, s.I, ctx->E_local, 1};  // received rows: one local expert each
-    CU(launch_dispatch(a.ids_local, reinterpret_cast<const uint16_t*>(ctx->ep_buf + a.off_rx), a.world * a.cap, sl,
-                       ctx->disp, 1, st),
-       "dispatch");
+    CU(launch_ep_recv(x, a, st), "ep receive");
+    // the received rows as a local routing problem: row j of source s (j < its count) with up to K
+    // local experts; the other entries are -1
+    const Shape sl{s.H, s.I, ctx->E_local, s.K};
+    CU(launch_dispatch(a.ids_local, nullptr, a.world * a.cap_rows, sl, ctx->disp, 1, st, a.row_src), "dispatch");
+    CU(launch_ep_rowptr(ctx->disp.slot_of, ctx->disp.src, ctx->disp.seg + ctx->E_local, ctx->ybuf, ctx->ep_row_ptr, a,
+                        st),
+       "ep row destinations");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_GEMM_GATEUP, st);
     CU(launch_gemm(gemm_gateup(ctx, L, x), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_GEMM_DOWN, st);
-    CU(launch_gemm(gemm_down(ctx, L), kEpiBf16, ctx->num_sms, st), "gemm down");
+    // the down GEMM's epilogue stores each output row at its destination: the return
+    // all-to-all runs inside the GEMM, tile by tile, over NVLink
+    GemmArgs gd = gemm_down(ctx, L);
+    gd.row_ptr = ctx->ep_row_ptr;
+    CU(launch_gemm(gd, kEpiBf16, ctx->num_sms, st), "gemm down");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_COMBINE, st);
-    CU(launch_ep_return(ctx->disp.slot_of, ctx->ybuf, a, st), "ep return");
+    CU(launch_ep_returned(a, st), "ep returned");
     CU(launch_ep_finish(a, st), "ep finish");
     if (T > 0)
         CU(launch_combine(reinterpret_cast<const uint16_t*>(ctx->ep_buf + a.off_ret), s.H, nullptr, ctx->wts, residual,
-                          T, s.H, s.K, out, st),
+                          T, s.H, s.K, out, st, ctx->ybuf, a.local_slot),
            "combine");
     prof_end(ctx, st);
     return OBS_OK;

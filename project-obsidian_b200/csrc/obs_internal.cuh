@@ -96,10 +96,13 @@ struct DispatchBufs {
     int atoms;          // R_cap / 8
     int bn;             // token rows per GEMM tile
 };
+// row_src (optional): the row of token t is row_src[t] instead of x + t*H
 cudaError_t launch_dispatch(const int32_t* ids, const uint16_t* x, int T, const Shape& sh, const DispatchBufs& d,
-                            int permute, cudaStream_t st);
+                            int permute, cudaStream_t st, const uint16_t* const* row_src = nullptr);
+// y_local / local (expert parallelism): items computed on this rank, read from y_local (see k_combine)
 cudaError_t launch_combine(const uint16_t* y, int y_ld, const int32_t* slot_of, const float* w,
-                           const uint16_t* residual, int T, int H, int K, uint16_t* out, cudaStream_t st);
+                           const uint16_t* residual, int T, int H, int K, uint16_t* out, cudaStream_t st,
+                           const uint16_t* y_local = nullptr, int32_t* local = nullptr);
 cudaError_t launch_gather_rows(const uint16_t* y, const int32_t* slot_of, int rows, int H, uint16_t* out,
                                cudaStream_t st);
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps, uint16_t* out,
@@ -111,21 +114,32 @@ cudaError_t launch_tile_rows(const uint16_t* x, int n, int cols, int atoms, uint
 constexpr int kMaxWorld = 8;
 struct EpArgs {
     uint8_t* peer[kMaxWorld];  // every rank's EP buffer (this rank's included), same layout
-    int world, rank, cap, H, K, E_local;
-    size_t off_rx, off_meta, off_cnt, off_rflag, off_ret, off_retflag;
+    int world, rank, H, K, E_local;
+    int cap_rows;        // rows of one source region: a token goes to a rank at most once (max_tokens)
+    int cap_items;       // (token, rank) items of one source (max_tokens * K)
+    size_t off_rx, off_meta, off_mtok, off_cnt, off_rflag, off_ret, off_retflag;
     int32_t* send_cnt;   // [world] rows sent to each rank (reset by the sender's last CTA)
     uint32_t* done;      // [2] CTA completion counters of k_ep_send / k_ep_return
     uint32_t* epoch;     // [1] completed forwards
-    int32_t* ids_local;  // [world * cap] local expert of each received row, -1 = empty
-    int32_t* src_item;   // [world * cap] source item t*K+k of each received row
-    int32_t* counts;     // [E_local] received rows per local expert (zeroed before k_ep_recv)
+    int32_t* ids_local;  // [world * cap_rows * K] local expert of each received (row, k), -1 = none
+    int32_t* src_item;   // [world * cap_rows * K] source item t*K+k of each received (row, k)
+    int32_t* counts;     // [E_local] received (row, k) pairs per local expert (zeroed before k_ep_recv)
+    int32_t* local_slot; // [cap_items] 1 + this rank's output slot of each of its own items computed here,
+                         // 0 otherwise (set by k_ep_rowptr, cleared by the combine)
+    const uint16_t** row_src;  // [world * cap_rows] where each received row's data is (k_ep_recv)
     int rows_cap;        // rows of the expert-output buffer k_ep_return reads (slot_of bound)
     int* err;
     uint64_t wait_ns;    // limit of the bounded waits for peers
 };
 cudaError_t launch_ep_send(const int32_t* ids, const uint16_t* x, int T, int E, const EpArgs& a, cudaStream_t st);
-cudaError_t launch_ep_recv(const EpArgs& a, cudaStream_t st);
-cudaError_t launch_ep_return(const int32_t* slot_of, const uint16_t* y, const EpArgs& a, cudaStream_t st);
+cudaError_t launch_ep_recv(const uint16_t* x, const EpArgs& a, cudaStream_t st);
+// The destination of every output slot of the down GEMM: the source rank's return
+// buffer (over NVLink) for rows received from another rank, this rank's y for its
+// own rows (noted in local_slot) and for padding rows.
+cudaError_t launch_ep_rowptr(const int32_t* slot_of, const int32_t* src, const int32_t* seg_end, uint16_t* y,
+                             uint16_t** row_ptr, const EpArgs& a, cudaStream_t st);
+// After a down GEMM that wrote its rows through row_ptr: stamps every source.
+cudaError_t launch_ep_returned(const EpArgs& a, cudaStream_t st);
 cudaError_t launch_ep_finish(const EpArgs& a, cudaStream_t st);
 // One bounded wait on a stamp that nothing writes (obs_probe_wait): gives up
 // after limit_ns and records kDevTimeout in *err.
@@ -191,6 +205,7 @@ struct GemmArgs {
     uint64_t* trace;          // optional: CTA 0 records %globaltimer per role and k-step
     int trace_n;              // k-steps recorded per role
     uint64_t wait_ns;         // limit of every mbarrier wait
+    uint16_t* const* row_ptr; // kEpiBf16, optional: destination of each output row (slot), row-major H wide
 };
 // trace roles (rows of the trace buffer, trace_n entries each)
 enum TraceRole : int {

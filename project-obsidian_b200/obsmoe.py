@@ -33,6 +33,7 @@ EXPORTS = (
     "obs_expert_gemm_f32", "obs_check_device", "obs_profile_enable", "obs_profile_read",
     "obs_trace_enable", "obs_decode_ffn_static", "obs_kernel_launches", "obs_ep_handle", "obs_ep_connect",
     "obs_rmsnorm", "obs_moe_stack_forward", "obs_set_wait_limit", "obs_probe_wait", "obs_struct_layout",
+    "obs_load_layer_safetensors", "obs_expert_file_info",
 )
 EP_HANDLE_BYTES = 64
 STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down",
@@ -97,6 +98,9 @@ def lib() -> C.CDLL:
         L.obs_ep_connect.argtypes = [vp, vp]
         L.obs_rmsnorm.argtypes = [vp, vp, vp, i32, vp, vp]
         L.obs_moe_stack_forward.argtypes = [vp, i32, i32, vp, i32, vp, i32, vp]
+        L.obs_load_layer_safetensors.argtypes = [vp, i32, C.c_char_p, vp, vp, vp]
+        L.obs_expert_file_info.argtypes = [C.c_char_p, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                                           C.POINTER(C.c_int32)]
         L.obs_set_wait_limit.argtypes = [vp, i64]
         L.obs_probe_wait.argtypes = [vp, vp]
         L.obs_struct_layout.argtypes = [C.POINTER(C.c_int32), i32]
@@ -184,6 +188,12 @@ class MoeContext:
         """Copy one layer in the reference format (attributes router_w ... down_b)."""
         lw = LayerWeights(*[_ptr(getattr(w, n)) for n, _ in LayerWeights._fields_])
         self._chk(lib().obs_load_layer(self._h, layer, C.byref(lw), int(on_device)))
+
+    def load_layer_file(self, layer: int, path: str, router_w, router_s, router_b):
+        """One layer from the reference splitter's safetensors file (experts) plus the router
+        arrays (host numpy arrays in the MLX layout)."""
+        self._chk(lib().obs_load_layer_safetensors(self._h, layer, os.fsencode(path), _ptr(router_w), _ptr(router_s),
+                                                   _ptr(router_b)))
 
     def synth_layer(self, layer: int, seed: int = 0):
         self._chk(lib().obs_synth_layer(self._h, layer, seed))
@@ -288,6 +298,15 @@ def decode_ffn_static(w, n_experts, hidden, inter, top_k, x, ids, weights, T, ou
                                      _ptr(weights), _ptr(residual), T, _ptr(out), _stream(stream))
     if rc != OBS_OK:
         raise ObsError(rc, lib().obs_last_error(None).decode())
+
+
+def expert_file_info(path: str) -> tuple[int, int, int]:
+    """(n_experts, hidden, inter) of a splitter expert file, read from its header alone."""
+    e, h, i = C.c_int32(), C.c_int32(), C.c_int32()
+    rc = lib().obs_expert_file_info(os.fsencode(path), C.byref(e), C.byref(h), C.byref(i))
+    if rc != OBS_OK:
+        raise ObsError(rc, lib().obs_last_error(None).decode())
+    return e.value, h.value, i.value
 
 
 def struct_layout() -> list[int]:

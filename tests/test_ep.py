@@ -28,7 +28,7 @@ def run_ranks(n):
     return r.returncode
 
 
-@pytest.mark.parametrize("n", [2, 4])
+@pytest.mark.parametrize("n", [2, 4, 8])
 def test_ep_forward_equals_single_gpu(cuda, n):
     if cuda.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs")
