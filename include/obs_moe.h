@@ -78,6 +78,15 @@ typedef struct obs_layer_weights {
     const uint32_t* down_w;   const uint16_t* down_s;   const uint16_t* down_b;
 } obs_layer_weights;
 
+/* The model's ends (the embedding, the final norm and the lm_head), MLX 4-bit
+ * group-64 like the layers: embed/lm W uint32 [vocab, H/8], s/b bf16
+ * [vocab, H/64]; norm_w bf16 [H] (model.norm.weight).  Host or device memory. */
+typedef struct obs_head_weights {
+    const uint32_t* embed_w; const uint16_t* embed_s; const uint16_t* embed_b;
+    const uint32_t* lm_w;    const uint16_t* lm_s;    const uint16_t* lm_b;
+    const uint16_t* norm_w;
+} obs_head_weights;
+
 /* ---------------------------------------------------------------- context */
 int obs_abi_version(void);
 /* Replaces ObsidianExecutor::new (src/executor.rs:39-58) and the expert pools
@@ -120,6 +129,24 @@ int obs_synth_layer(obs_ctx* ctx, int layer, uint64_t seed);
  * RMSNormed with eps, written to x [T, H] bf16 on `stream`. */
 int obs_synth_activations(uint64_t seed, uint32_t layer, int row0, int T, int H, float eps,
                           uint16_t* x, void* stream);
+
+/* ------------------------------------------------------- the model's ends */
+/* Copies the embedding, the final norm weight and the lm_head into the
+ * context's HBM (they replace the embed_tokens / model.norm / lm_head tensors
+ * Weights::load_non_expert keeps, src/weight_loader.rs:19-71).  Synchronous. */
+int obs_load_head(obs_ctx* ctx, int vocab, const obs_head_weights* w, int src_on_device);
+/* Model::embed (src/forward.rs:445-462) on the device: x[t] = the dequantised
+ * embedding row of tokens[t] (w = fma(q, s, b) in fp32, rounded to bf16).
+ * tokens int32 [T], x bf16 [T, H], device memory. */
+int obs_embed(obs_ctx* ctx, const int32_t* tokens, int T, uint16_t* x, void* stream);
+/* The end of run_one_token (src/forward.rs:553-566): RMSNorm with model.norm's
+ * weight, the 4-bit lm_head mat-vec over the vocabulary, and the greedy next
+ * token -- the first maximum, as the reference's strict '>' scan -- for T <= 16
+ * rows of the residual stream x (bf16 [T, H]).  ids int32 [T]; logits fp32
+ * [T, vocab] or NULL.  The logits follow one canonical fp32 order (lane l of 32
+ * chains fma(fma(q, s, b), x, acc) over its 64-column groups, then the adjacent
+ * pairwise tree), so the ids are bit-exact with the CPU oracle's. */
+int obs_lm_head(obs_ctx* ctx, const uint16_t* x, int T, int32_t* ids, float* logits, void* stream);
 
 /* ------------------------------------------------------ the MoE layer path */
 /* out = [residual +] sum_k w_k * expert_k(x): router -> top-k -> dispatch ->
@@ -224,8 +251,9 @@ int obs_set_wait_limit(obs_ctx* ctx, uint64_t limit_ns);
 int obs_probe_wait(obs_ctx* ctx, void* stream);
 /* ABI self-description for bindings in other languages: writes
  *   sizeof(obs_config), the offsets of its 12 fields in declaration order,
- *   sizeof(obs_layer_weights), the offsets of its 12 fields in declaration order
- * (26 values) into out[0 .. n), and returns 26.  A binding compares these with
+ *   sizeof(obs_layer_weights), the offsets of its 12 fields in declaration order,
+ *   sizeof(obs_head_weights), the offsets of its 7 fields in declaration order
+ * (34 values) into out[0 .. n), and returns 34.  A binding compares these with
  * its own struct layout (the reference passes its parameter structs by value
  * as #[repr(C)], src/forward.rs:22-28, src/router.rs:8-14). */
 int obs_struct_layout(int32_t* out, int n);

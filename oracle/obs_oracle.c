@@ -445,3 +445,86 @@ int orc_moe_layer(const orc_layer* L, const uint16_t* x, int T, const float* log
     if (!w_out) free(w);
     return rc;
 }
+
+/* ------------------------------------------------------------ model ends */
+void orc_embed(const uint32_t* w, const uint16_t* s, const uint16_t* b, int vocab, int H,
+               const int32_t* tokens, int T, uint16_t* out) {
+    /* forward.rs:449-460: w = nib * scale + bias per column, in f32 */
+    int groups = H / 64, words = H / 8;
+    for (int t = 0; t < T; ++t) {
+        int tok = tokens[t] >= 0 && tokens[t] < vocab ? tokens[t] : 0;
+        for (int i = 0; i < H; ++i) {
+            uint32_t q = (w[(size_t)tok * words + i / 8] >> (4 * (i % 8))) & 0xFu;
+            float sc = orc_bf16_to_f32(s[(size_t)tok * groups + i / 64]);
+            float bi = orc_bf16_to_f32(b[(size_t)tok * groups + i / 64]);
+            out[(size_t)t * H + i] = orc_f32_to_bf16(fmaf((float)q, sc, bi));
+        }
+    }
+}
+
+typedef struct {
+    const uint32_t* w;
+    const uint16_t *s, *b, *x;
+    int vocab, H, T, nthreads, id;
+    float* logits;
+} head_job;
+
+static void* head_worker(void* arg) {
+    head_job* J = (head_job*)arg;
+    int H = J->H, G = H / 64, m = G / 32;
+    float* xf = (float*)malloc(sizeof(float) * (size_t)J->T * H);
+    for (size_t i = 0; i < (size_t)J->T * H; ++i) xf[i] = orc_bf16_to_f32(J->x[i]);
+    for (int r = J->id; r < J->vocab; r += J->nthreads) {
+        const uint32_t* wr = J->w + (size_t)r * (H / 8);
+        for (int t = 0; t < J->T; ++t) {
+            float lane[32];
+            for (int l = 0; l < 32; ++l) {
+                float acc = 0.0f;
+                for (int g = l * m; g < (l + 1) * m; ++g) {
+                    float sc = orc_bf16_to_f32(J->s[(size_t)r * G + g]), bi = orc_bf16_to_f32(J->b[(size_t)r * G + g]);
+                    for (int j = 0; j < 64; ++j) {
+                        int c = g * 64 + j;
+                        uint32_t q = (wr[c / 8] >> (4 * (c % 8))) & 0xFu;
+                        acc = fmaf(fmaf((float)q, sc, bi), xf[(size_t)t * H + c], acc);
+                    }
+                }
+                lane[l] = acc;
+            }
+            for (int o = 1; o < 32; o <<= 1) {
+                float nv[32];
+                for (int l = 0; l < 32; ++l) nv[l] = lane[l] + lane[l ^ o];
+                memcpy(lane, nv, sizeof lane);
+            }
+            J->logits[(size_t)t * J->vocab + r] = lane[0];
+        }
+    }
+    free(xf);
+    return NULL;
+}
+
+int orc_lm_head_logits(const uint32_t* w, const uint16_t* s, const uint16_t* b, int vocab, int H,
+                       const uint16_t* x, int T, int nthreads, float* logits) {
+    if (H % 2048 != 0) return -1;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    head_job jobs[256];
+    pthread_t th[256];
+    for (int i = 0; i < nthreads; ++i) {
+        head_job j = {w, s, b, x, vocab, H, T, nthreads, i, logits};
+        jobs[i] = j;
+        if (i) pthread_create(&th[i], NULL, head_worker, &jobs[i]);
+    }
+    head_worker(&jobs[0]);
+    for (int i = 1; i < nthreads; ++i) pthread_join(th[i], NULL);
+    return 0;
+}
+
+void orc_argmax_rows(const float* logits, int T, int n, int32_t* ids) {
+    for (int t = 0; t < T; ++t) {
+        int best = 0;
+        float bv = -INFINITY;
+        for (int i = 0; i < n; ++i)
+            if (logits[(size_t)t * n + i] > bv) bv = logits[(size_t)t * n + i], best = i;
+        ids[t] = best;
+    }
+}

@@ -113,6 +113,20 @@ int orc_moe_layer(const orc_layer* L, const uint16_t* x, int T, const float* log
                   const uint16_t* residual, int norm_topk, int wmode, int nthreads,
                   uint16_t* out, int32_t* ids_out, float* w_out);
 
+/* ---- the model's ends (config 4; src/forward.rs:445-462, :553-566) ----
+ * Embedding: out[t][i] = bf16(fmaf(q, s, b)) of row tokens[t] (4-bit MLX layout,
+ * nibble i%8 of word i/8, low nibble first).
+ * lm_head logits fp32 [T, vocab] of the normalised rows x (bf16 [T, H]) in the
+ * canonical order: w = fmaf(q, s, b); 32 lanes, lane l chains acc = fmaf(w, x,
+ * acc) over its groups l*m .. (l+1)*m-1 (m = H/2048) in column order; the lane
+ * sums meet in the adjacent pairwise tree (offsets 1, 2, 4, 8, 16).  argmax: the
+ * first maximum (forward.rs:562-565).  Returns -1 if H is not a multiple of 2048. */
+void orc_embed(const uint32_t* w, const uint16_t* s, const uint16_t* b, int vocab, int H,
+               const int32_t* tokens, int T, uint16_t* out);
+int orc_lm_head_logits(const uint32_t* w, const uint16_t* s, const uint16_t* b, int vocab, int H,
+                       const uint16_t* x, int T, int nthreads, float* logits);
+void orc_argmax_rows(const float* logits, int T, int n, int32_t* ids);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,10 @@ def lib():
         L.orc_moe_ffn_combine.restype = C.c_int
         L.orc_moe_ffn_combine.argtypes = [C.c_void_p, _u16p, C.c_int, _i32p, _f32p, C.c_void_p,
                                           C.c_int, C.c_int, _u16p, C.c_void_p, C.c_void_p]
+        L.orc_embed.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int, _i32p, C.c_int, _u16p]
+        L.orc_lm_head_logits.restype = C.c_int
+        L.orc_lm_head_logits.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int, _u16p, C.c_int, C.c_int, _f32p]
+        L.orc_argmax_rows.argtypes = [_f32p, C.c_int, C.c_int, _i32p]
         L.orc_moe_layer.restype = C.c_int
         L.orc_moe_layer.argtypes = [C.c_void_p, _u16p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                     C.c_int, C.c_int, _u16p, _i32p, _f32p]
@@ -278,6 +282,56 @@ def moe_stack(layers, r0, bias=None, eps=1e-6, wmode=0, nthreads=None):
         x = rmsnorm_layer(r, eps)
         r, _, _ = moe_layer(L, x, bias=bias, residual=r, wmode=wmode, nthreads=nthreads)
     return r
+
+
+# ---------------------------------------------------------- the model's ends
+@dataclass
+class Head:
+    """Embedding, final norm weight and lm_head in the MLX 4-bit layout."""
+    vocab: int
+    H: int
+    embed_w: np.ndarray
+    embed_s: np.ndarray
+    embed_b: np.ndarray
+    lm_w: np.ndarray
+    lm_s: np.ndarray
+    lm_b: np.ndarray
+    norm_w: np.ndarray
+
+
+def synth_head(seed=0, vocab=151936, H=2048):
+    """Seeded head: the embedding and lm_head drawn like an expert projection
+    ((seed, layer 1000 / 1001) streams), the final norm weight ~ 1 + U(-0.1, 0.1)."""
+    ew, es, eb = synth_proj(seed, 1000, 0, 1, vocab, H)
+    lw, ls, lb = synth_proj(seed, 1001, 0, 1, vocab, H)
+    rng = np.random.default_rng(seed + 7)
+    norm_w = f32_to_bf16((1.0 + rng.uniform(-0.1, 0.1, H)).astype(np.float32))
+    return Head(vocab, H, ew[0], es[0], eb[0], lw[0], ls[0], lb[0], norm_w)
+
+
+def embed(head: Head, tokens):
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    out = np.empty((tokens.size, head.H), np.uint16)
+    lib().orc_embed(head.embed_w, head.embed_s, head.embed_b, head.vocab, head.H, tokens, tokens.size, out)
+    return out
+
+
+def lm_head(head: Head, x, nthreads=None):
+    """Final RMSNorm (model.norm) in rmsnorm.metal's order, lm_head logits in the
+    canonical order, and the first maximum: (logits fp32 [T, vocab], ids [T])."""
+    x = np.ascontiguousarray(x, np.uint16)
+    T = x.shape[0]
+    xn = np.empty_like(x)
+    for t in range(T):
+        lib().orc_rmsnorm_tg_row(x[t], head.norm_w.ctypes.data, head.H, 1e-6, xn[t])
+    logits = np.empty((T, head.vocab), np.float32)
+    rc = lib().orc_lm_head_logits(head.lm_w, head.lm_s, head.lm_b, head.vocab, head.H, xn, T,
+                                  nthreads or os.cpu_count() or 1, logits)
+    if rc:
+        raise ValueError("lm_head: hidden size must be a multiple of 2048")
+    ids = np.empty(T, np.int32)
+    lib().orc_argmax_rows(logits, T, head.vocab, ids)
+    return logits, ids
 
 
 # ------------------------------------------- reference shaders (CPU build)

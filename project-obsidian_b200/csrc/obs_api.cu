@@ -82,6 +82,15 @@ struct obs_ctx {
     int ep_world = 1, ep_rank = 0, E_local = 0, e0 = 0;
     uint8_t* ep_buf = nullptr;  // this rank's buffer, opened by its peers through CUDA IPC
     uint16_t** ep_row_ptr = nullptr;  // [R_cap] destination of each down-GEMM output row
+    // the model's ends (obs_load_head): embedding, final norm, lm_head, and their scratch
+    struct Head {
+        int vocab = 0;
+        uint8_t* mem = nullptr;
+        uint32_t *embed_w = nullptr, *lm_w = nullptr;
+        uint16_t *embed_s = nullptr, *embed_b = nullptr, *lm_s = nullptr, *lm_b = nullptr, *norm_w = nullptr;
+        uint16_t* xn = nullptr;  // [kHeadMaxT, H]
+        float* logits = nullptr; // [kHeadMaxT, vocab]
+    } head;
     size_t ep_bytes = 0;
     bool ep_connected = false;
     EpArgs ep{};
@@ -348,6 +357,7 @@ extern "C" int obs_destroy(obs_ctx* ctx) {
         for (int r = 0; r < ctx->ep_world; ++r)
             if (r != ctx->ep_rank && ctx->ep.peer[r]) cudaIpcCloseMemHandle(ctx->ep.peer[r]);
     if (ctx->ep_buf) cudaFree(ctx->ep_buf);
+    if (ctx->head.mem) cudaFree(ctx->head.mem);
     if (ctx->wmem) cudaFree(ctx->wmem);
     if (ctx->smem_pool) cudaFree(ctx->smem_pool);
     delete ctx;
@@ -425,6 +435,63 @@ extern "C" int obs_load_layer(obs_ctx* ctx, int layer, const obs_layer_weights* 
     OBS_CHECK_CTX(ctx);
     if (!w || !w->router_w || !w->router_s || !w->router_b) return fail(ctx, OBS_ERR_INVALID, "null weights");
     return load_impl(ctx, layer, w, src_on_device, 0, false);
+}
+
+extern "C" int obs_load_head(obs_ctx* ctx, int vocab, const obs_head_weights* w, int src_on_device) {
+    OBS_CHECK_CTX(ctx);
+    if (!w || !w->embed_w || !w->embed_s || !w->embed_b || !w->lm_w || !w->lm_s || !w->lm_b || !w->norm_w)
+        return fail(ctx, OBS_ERR_INVALID, "null head weight pointer");
+    if (vocab <= 0 || vocab > (1 << 24)) return fail(ctx, OBS_ERR_INVALID, "vocab out of range");
+    CU(cudaSetDevice(ctx->device), "cudaSetDevice");
+    auto& h = ctx->head;
+    if (h.mem) {
+        cudaFree(h.mem);
+        h = obs_ctx::Head{};
+    }
+    const int H = ctx->sh.H;
+    const size_t nw = (size_t)vocab * (H / 8) * 4, ng = (size_t)vocab * (H / 64) * 2;
+    const size_t sizes[] = {nw, ng, ng, nw, ng, ng, (size_t)H * 2, (size_t)kHeadMaxT * H * 2,
+                            (size_t)kHeadMaxT * vocab * 4};
+    size_t total = 0;
+    for (size_t sz : sizes) total += align_up(sz, 256);
+    CU(cudaMalloc(&h.mem, total), "head alloc");
+    uint8_t* p = h.mem;
+    void** ptrs[] = {(void**)&h.embed_w, (void**)&h.embed_s, (void**)&h.embed_b, (void**)&h.lm_w, (void**)&h.lm_s,
+                     (void**)&h.lm_b, (void**)&h.norm_w, (void**)&h.xn, (void**)&h.logits};
+    for (int i = 0; i < 9; ++i) *ptrs[i] = p, p += align_up(sizes[i], 256);
+    const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    const void* srcs[] = {w->embed_w, w->embed_s, w->embed_b, w->lm_w, w->lm_s, w->lm_b, w->norm_w};
+    for (int i = 0; i < 7; ++i) CU(cudaMemcpy(*ptrs[i], srcs[i], sizes[i], kind), "head copy");
+    h.vocab = vocab;
+    return OBS_OK;
+}
+
+extern "C" int obs_embed(obs_ctx* ctx, const int32_t* tokens, int T, uint16_t* x, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    if (!ctx->head.mem) return fail(ctx, OBS_ERR_STATE, "head not loaded (obs_load_head)");
+    if (T < 0) return fail(ctx, OBS_ERR_INVALID, "T < 0");
+    if (T == 0) return OBS_OK;
+    if (!tokens || !x) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    const auto& h = ctx->head;
+    CU(launch_embed(h.embed_w, h.embed_s, h.embed_b, tokens, T, h.vocab, ctx->sh.H, x, ctx->err_flag,
+                    as_stream(stream)),
+       "embed");
+    return OBS_OK;
+}
+
+extern "C" int obs_lm_head(obs_ctx* ctx, const uint16_t* x, int T, int32_t* ids, float* logits, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    if (!ctx->head.mem) return fail(ctx, OBS_ERR_STATE, "head not loaded (obs_load_head)");
+    if (T < 0 || T > kHeadMaxT) return fail(ctx, OBS_ERR_INVALID, "T out of range (0..16)");
+    if (T == 0) return OBS_OK;
+    if (!x || !ids) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    const auto& h = ctx->head;
+    cudaStream_t st = as_stream(stream);
+    CU(launch_rmsnorm(x, h.norm_w, T, ctx->sh.H, ctx->cfg.rms_eps, h.xn, st), "final norm");
+    CU(launch_lm_head(h.lm_w, h.lm_s, h.lm_b, h.xn, T, h.vocab, ctx->sh.H, logits ? logits : h.logits, ids,
+                      ctx->num_sms, st),
+       "lm_head");
+    return OBS_OK;
 }
 
 extern "C" int obs_synth_layer(obs_ctx* ctx, int layer, uint64_t seed) {
@@ -965,6 +1032,10 @@ extern "C" int obs_struct_layout(int32_t* out, int n) {
         OBS_OFF(obs_layer_weights, gate_w), OBS_OFF(obs_layer_weights, gate_s), OBS_OFF(obs_layer_weights, gate_b),
         OBS_OFF(obs_layer_weights, up_w), OBS_OFF(obs_layer_weights, up_s), OBS_OFF(obs_layer_weights, up_b),
         OBS_OFF(obs_layer_weights, down_w), OBS_OFF(obs_layer_weights, down_s), OBS_OFF(obs_layer_weights, down_b),
+        (int32_t)sizeof(obs_head_weights),
+        OBS_OFF(obs_head_weights, embed_w), OBS_OFF(obs_head_weights, embed_s), OBS_OFF(obs_head_weights, embed_b),
+        OBS_OFF(obs_head_weights, lm_w), OBS_OFF(obs_head_weights, lm_s), OBS_OFF(obs_head_weights, lm_b),
+        OBS_OFF(obs_head_weights, norm_w),
     };
 #undef OBS_OFF
     const int total = (int)(sizeof(v) / sizeof(v[0]));

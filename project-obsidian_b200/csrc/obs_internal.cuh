@@ -183,6 +183,14 @@ cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t
                                const uint16_t* residual, int T, const DecodeBufs& d, uint16_t* out,
                                int do_combine, cudaStream_t st);
 
+// ----------------------------------------------------------------- k_head.cu
+constexpr int kHeadMaxT = 16;  // tokens of one obs_lm_head call
+cudaError_t launch_embed(const uint32_t* w, const uint16_t* s, const uint16_t* b, const int32_t* tokens, int T,
+                         int vocab, int H, uint16_t* x, int* err, cudaStream_t st);
+// logits [T, vocab] fp32 of the normalised rows xn, then ids [T] = the first maximum of each row
+cudaError_t launch_lm_head(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* xn, int T,
+                           int vocab, int H, float* logits, int32_t* ids, int num_sms, cudaStream_t st);
+
 // ----------------------------------------------------------------- k_gemm.cu
 enum GemmEpi : int { kEpiSwiglu = 0, kEpiBf16 = 1, kEpiF32 = 2 };
 struct GemmArgs {

@@ -33,7 +33,7 @@ EXPORTS = (
     "obs_expert_gemm_f32", "obs_check_device", "obs_profile_enable", "obs_profile_read",
     "obs_trace_enable", "obs_decode_ffn_static", "obs_kernel_launches", "obs_ep_handle", "obs_ep_connect",
     "obs_rmsnorm", "obs_moe_stack_forward", "obs_set_wait_limit", "obs_probe_wait", "obs_struct_layout",
-    "obs_load_layer_safetensors", "obs_expert_file_info",
+    "obs_load_layer_safetensors", "obs_expert_file_info", "obs_load_head", "obs_embed", "obs_lm_head",
 )
 EP_HANDLE_BYTES = 64
 STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down",
@@ -52,6 +52,10 @@ class Config(C.Structure):
                 ("max_tokens", C.c_int32), ("norm_topk", C.c_int32),
                 ("decode_max_tokens", C.c_int32), ("rms_eps", C.c_float),
                 ("ep_world", C.c_int32), ("ep_rank", C.c_int32)]
+
+
+class HeadWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("embed_w", "embed_s", "embed_b", "lm_w", "lm_s", "lm_b", "norm_w")]
 
 
 class LayerWeights(C.Structure):
@@ -101,6 +105,9 @@ def lib() -> C.CDLL:
         L.obs_load_layer_safetensors.argtypes = [vp, i32, C.c_char_p, vp, vp, vp]
         L.obs_expert_file_info.argtypes = [C.c_char_p, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
                                            C.POINTER(C.c_int32)]
+        L.obs_load_head.argtypes = [vp, i32, C.POINTER(HeadWeights), i32]
+        L.obs_embed.argtypes = [vp, vp, i32, vp, vp]
+        L.obs_lm_head.argtypes = [vp, vp, i32, vp, vp, vp]
         L.obs_set_wait_limit.argtypes = [vp, i64]
         L.obs_probe_wait.argtypes = [vp, vp]
         L.obs_struct_layout.argtypes = [C.POINTER(C.c_int32), i32]
@@ -194,6 +201,18 @@ class MoeContext:
         arrays (host numpy arrays in the MLX layout)."""
         self._chk(lib().obs_load_layer_safetensors(self._h, layer, os.fsencode(path), _ptr(router_w), _ptr(router_s),
                                                    _ptr(router_b)))
+
+    def load_head(self, vocab: int, w, on_device: bool = False):
+        """The embedding, final norm and lm_head (attributes embed_w ... norm_w)."""
+        hw = HeadWeights(*[_ptr(getattr(w, n)) for n, _ in HeadWeights._fields_])
+        self._chk(lib().obs_load_head(self._h, vocab, C.byref(hw), int(on_device)))
+
+    def embed(self, tokens, T, x, stream=None):
+        self._chk(lib().obs_embed(self._h, _ptr(tokens), T, _ptr(x), _stream(stream)))
+
+    def lm_head(self, x, T, ids, logits=None, stream=None):
+        """RMSNorm(model.norm) -> lm_head -> greedy ids (first maximum); logits optional."""
+        self._chk(lib().obs_lm_head(self._h, _ptr(x), T, _ptr(ids), _ptr(logits), _stream(stream)))
 
     def synth_layer(self, layer: int, seed: int = 0):
         self._chk(lib().obs_synth_layer(self._h, layer, seed))

@@ -89,13 +89,19 @@ def header_struct_fields(name):
 
 def test_struct_layout_of_library_ctypes_and_rust_agree():
     v = obsmoe.struct_layout()
-    assert len(v) == 26
+    assert len(v) == 34
     cfg_fields = header_struct_fields("obs_config")
     lw_fields = header_struct_fields("obs_layer_weights")
-    assert len(cfg_fields) == 12 and len(lw_fields) == 12
+    hw_fields = header_struct_fields("obs_head_weights")
+    assert len(cfg_fields) == 12 and len(lw_fields) == 12 and len(hw_fields) == 7
     # the library as compiled
     lib_cfg = (v[0], list(zip(cfg_fields, v[1:13])))
     lib_lw = (v[13], list(zip(lw_fields, v[14:26])))
+    lib_hw = (v[26], list(zip(hw_fields, v[27:34])))
+    ct_hw = (C.sizeof(obsmoe.HeadWeights),
+             [(f, getattr(obsmoe.HeadWeights, f).offset) for f, _ in obsmoe.HeadWeights._fields_])
+    assert ct_hw == lib_hw
+    assert rust_struct_layout("ObsHeadWeights") == lib_hw
     # the ctypes binding
     ct_cfg = (C.sizeof(obsmoe.Config), [(f, getattr(obsmoe.Config, f).offset) for f, _ in obsmoe.Config._fields_])
     ct_lw = (C.sizeof(obsmoe.LayerWeights),

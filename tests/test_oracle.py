@@ -256,3 +256,43 @@ def test_routing_agreement_with_reference_on_config1():
             for k in range(8):
                 if oid[t, k] != rid[t, k]:
                     assert rl[t, oid[t, k]] == rl[t, rid[t, k]]
+
+
+def test_embed_is_the_reference_row_dequant():
+    """Model::embed (src/forward.rs:449-460): w = nib * scale + bias in f32 per column,
+    nibble (word >> 4*(i % 8)) & 15; the oracle rounds that f32 value to bf16 once."""
+    hd = O.synth_head(2, vocab=512)
+    toks = np.array([0, 7, 511, 300], np.int32)
+    got = O.embed(hd, toks)
+    for r, tok in enumerate(toks):
+        words = hd.embed_w[tok]
+        nib = np.array([(words[i // 8] >> (4 * (i % 8))) & 0xF for i in range(2048)], np.float32)
+        sc = np.repeat(O.bf16_to_f32(hd.embed_s[tok]), 64)
+        bi = np.repeat(O.bf16_to_f32(hd.embed_b[tok]), 64)
+        ref = (nib * sc + bi).astype(np.float32)   # q*s is exact in fp32: one rounding, as fmaf
+        assert np.array_equal(got[r], O.f32_to_bf16(ref))
+
+
+def test_lm_head_argmax_agrees_with_the_reference_kernels():
+    """The end of run_one_token (src/forward.rs:553-566) by the reference's own kernels
+    (rmsnorm.metal, fused_dequant_matvec_4bit.metal in f16, then the CPU scan where the
+    first maximum wins) against the oracle's canonical fp32 order: on 32 tokens over a
+    vocabulary of 8,192 rows the next token agrees for every token (pinned), and the
+    logits agree within 4e-3 of the largest."""
+    R = O.ref_lib()
+    if R is None:
+        pytest.skip("oracle/_ref not built")
+    hd = O.synth_head(0, vocab=8192)
+    T = 32
+    x = O.synth_x(0, 0, T, 2048)
+    lg, ids = O.lm_head(hd, x, nthreads=4)
+    f16 = lambda a: O.bf16_to_f32(a).astype(np.float16)  # noqa: E731
+    xn = np.empty((T, 2048), np.float16)
+    R.ref_rmsnorm(np.ascontiguousarray(f16(x)), np.ascontiguousarray(f16(hd.norm_w)), xn, T, 2048, 1e-6)
+    rl = np.empty((T, 8192), np.float16)
+    for t in range(T):
+        R.ref_fused_dequant_matvec_4bit(hd.lm_w, f16(hd.lm_s), f16(hd.lm_b), np.ascontiguousarray(xn[t]), rl[t],
+                                        2048, 8192, 4)
+    rid = np.array([int(np.argmax(r.astype(np.float32))) for r in rl], np.int32)
+    assert np.array_equal(rid, ids)
+    assert np.abs(rl.astype(np.float32) - lg).max() <= 4e-3 * np.abs(lg).max()
