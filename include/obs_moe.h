@@ -87,6 +87,30 @@ typedef struct obs_head_weights {
     const uint16_t* norm_w;
 } obs_head_weights;
 
+/* The attention block of a layer (Qwen3-MoE): q/k/v/o MLX 4-bit group-64,
+ * q [n_heads*head_dim, H/8], k and v [n_kv_heads*head_dim, H/8],
+ * o [H, n_heads*head_dim/8], scales/biases bf16 [rows, in/64]; in_norm bf16 [H]
+ * (input_layernorm), q_norm / k_norm bf16 [head_dim].  Host or device memory. */
+typedef struct obs_attn_weights {
+    const uint32_t* q_w; const uint16_t* q_s; const uint16_t* q_b;
+    const uint32_t* k_w; const uint16_t* k_s; const uint16_t* k_b;
+    const uint32_t* v_w; const uint16_t* v_s; const uint16_t* v_b;
+    const uint32_t* o_w; const uint16_t* o_s; const uint16_t* o_b;
+    const uint16_t* in_norm; const uint16_t* q_norm; const uint16_t* k_norm;
+} obs_attn_weights;
+
+/* Shape of the attention block and its KV caches (Qwen3MoeConfig, src/model.rs:7-35;
+ * KvCache, src/kv_cache.rs:15-24): n_seqs independent sequences, each with a
+ * bf16 cache [n_kv_heads][max_seq][head_dim] per layer for K and for V. */
+typedef struct obs_attn_config {
+    int32_t n_heads;     /* query heads (32) */
+    int32_t n_kv_heads;  /* key/value heads (4); n_heads a multiple of it */
+    int32_t head_dim;    /* <= 128, even; n_heads * head_dim a multiple of 2048 */
+    int32_t max_seq;     /* positions per cache (<= 40960) */
+    int32_t n_seqs;      /* sequences (caches) per layer */
+    float rope_theta;    /* 1e7 */
+} obs_attn_config;
+
 /* ---------------------------------------------------------------- context */
 int obs_abi_version(void);
 /* Replaces ObsidianExecutor::new (src/executor.rs:39-58) and the expert pools
@@ -147,6 +171,31 @@ int obs_embed(obs_ctx* ctx, const int32_t* tokens, int T, uint16_t* x, void* str
  * chains fma(fma(q, s, b), x, acc) over its 64-column groups, then the adjacent
  * pairwise tree), so the ids are bit-exact with the CPU oracle's. */
 int obs_lm_head(obs_ctx* ctx, const uint16_t* x, int T, int32_t* ids, float* logits, void* stream);
+
+/* ------------------------------------------------------ the attention block */
+/* Allocates the attention scratch and the RoPE table (cos/sin of
+ * pos * theta^(-2i/head_dim), computed once in double precision) for the
+ * context's n_layers layers; caches are allocated by obs_load_attn. */
+int obs_attn_init(obs_ctx* ctx, const obs_attn_config* ac);
+/* Copies one layer's attention weights into HBM (q, k and v concatenated into
+ * one projection) and allocates its KV caches (zeroed).  Synchronous. */
+int obs_load_attn(obs_ctx* ctx, int layer, const obs_attn_weights* w, int src_on_device);
+/* The attention block of Model::forward_layer (src/forward.rs:404-419) for T
+ * tokens: token t belongs to sequence seq[t] at position pos[t] (device int32
+ * arrays).  xn = RMSNorm(x, in_norm); q, k, v = 4-bit projections (canonical
+ * fp32 order, rounded to bf16); per-head RMSNorm of q and k (q_norm, k_norm);
+ * NeoX RoPE (rope.metal:10-27) at pos[t]; K and V appended to the sequence's
+ * cache at pos[t] (ops.metal:32-37); single-query GQA attention over the cache
+ * positions 0 .. pos[t] (sdpa_decode.metal:14-48); out = x + o_proj(attention).
+ * Tokens of one sequence in one call must have distinct positions, and a token
+ * sees the K/V of every position <= its own (written by this call or earlier
+ * ones): a prefill passes consecutive positions of one sequence (causal), a
+ * batched decode step one token per sequence.  x, out bf16 [T, H], no aliasing. */
+int obs_attn_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint16_t* out, int T, const int32_t* seq,
+                     const int32_t* pos, void* stream);
+/* Copies cache positions [pos0, pos0 + n) of one sequence and layer: k and v
+ * (either may be NULL) bf16 [n_kv_heads][n][head_dim], device memory. */
+int obs_kv_read(obs_ctx* ctx, int layer, int seq, int pos0, int n, uint16_t* k, uint16_t* v, void* stream);
 
 /* ------------------------------------------------------ the MoE layer path */
 /* out = [residual +] sum_k w_k * expert_k(x): router -> top-k -> dispatch ->

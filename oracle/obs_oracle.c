@@ -528,3 +528,99 @@ void orc_argmax_rows(const float* logits, int T, int n, int32_t* ids) {
         ids[t] = best;
     }
 }
+
+/* ------------------------------------------------------- attention block */
+void orc_rope_table(double theta, int hd, int max_seq, float* out) {
+    for (int p = 0; p < max_seq; ++p)
+        for (int i = 0; i < hd / 2; ++i) {
+            double ang = (double)p * pow(theta, -2.0 * i / hd);
+            out[((size_t)p * (hd / 2) + i) * 2] = (float)cos(ang);
+            out[((size_t)p * (hd / 2) + i) * 2 + 1] = (float)sin(ang);
+        }
+}
+
+int orc_attn_forward(const orc_attn* A, const uint16_t* x, int T, const int32_t* seq, const int32_t* pos,
+                     float eps, int nthreads, uint16_t* out) {
+    int H = A->H, nq = A->nq, nkv = A->nkv, hd = A->hd, half = hd / 2;
+    if (H % 2048 || (nq * hd) % 2048) return -1;
+    size_t rq = (size_t)nq * hd, rk = (size_t)nkv * hd;
+    uint16_t* xn = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)T * H);
+    float* q = (float*)malloc(sizeof(float) * (size_t)T * rq);
+    float* k = (float*)malloc(sizeof(float) * (size_t)T * rk);
+    float* v = (float*)malloc(sizeof(float) * (size_t)T * rk);
+    uint16_t* qr = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)T * rq);
+    uint16_t* att = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)T * rq);
+    float* o = (float*)malloc(sizeof(float) * (size_t)T * H);
+    float* sc = (float*)malloc(sizeof(float) * (size_t)A->max_seq);
+    for (int t = 0; t < T; ++t) orc_rmsnorm_tg_row(x + (size_t)t * H, A->in_norm, H, eps, xn + (size_t)t * H);
+    orc_lm_head_logits(A->q_w, A->q_s, A->q_b, (int)rq, H, xn, T, nthreads, q);
+    orc_lm_head_logits(A->k_w, A->k_s, A->k_b, (int)rk, H, xn, T, nthreads, k);
+    orc_lm_head_logits(A->v_w, A->v_s, A->v_b, (int)rk, H, xn, T, nthreads, v);
+    /* head norms, rope, cache append (every token before any attention) */
+    uint16_t hb[128], hn[128];
+    for (int t = 0; t < T; ++t) {
+        int s = seq[t], p = pos[t];
+        for (int h = 0; h < nq + nkv; ++h) {
+            int isq = h < nq, hh = isq ? h : h - nq;
+            const float* src = isq ? q + (size_t)t * rq + (size_t)h * hd : k + (size_t)t * rk + (size_t)hh * hd;
+            for (int d = 0; d < hd; ++d) hb[d] = orc_f32_to_bf16(src[d]);
+            orc_rmsnorm_tg_row(hb, isq ? A->q_norm : A->k_norm, hd, eps, hn);
+            uint16_t* dst = isq ? qr + ((size_t)t * nq + h) * hd
+                                : A->kc + (((size_t)s * nkv + hh) * A->max_seq + p) * hd;
+            for (int i = 0; i < half; ++i) {
+                float c = A->rope[((size_t)p * half + i) * 2], sn = A->rope[((size_t)p * half + i) * 2 + 1];
+                float x0 = orc_bf16_to_f32(hn[i]), x1 = orc_bf16_to_f32(hn[i + half]);
+                float a = x1 * sn, b = x0 * sn;
+                dst[i] = orc_f32_to_bf16(fmaf(x0, c, -a));
+                dst[i + half] = orc_f32_to_bf16(fmaf(x1, c, b));
+            }
+            if (!isq)
+                for (int d = 0; d < hd; ++d)
+                    A->vc[(((size_t)s * nkv + hh) * A->max_seq + p) * hd + d] =
+                        orc_f32_to_bf16(v[(size_t)t * rk + (size_t)hh * hd + d]);
+        }
+    }
+    /* attention */
+    float scale = 1.0f / sqrtf((float)hd);
+    for (int t = 0; t < T; ++t) {
+        int s = seq[t], p = pos[t];
+        for (int h = 0; h < nq; ++h) {
+            int kvh = h / (nq / nkv);
+            const uint16_t* qh = qr + ((size_t)t * nq + h) * hd;
+            const uint16_t* kb = A->kc + ((size_t)s * nkv + kvh) * A->max_seq * hd;
+            const uint16_t* vb = A->vc + ((size_t)s * nkv + kvh) * A->max_seq * hd;
+            float m = -INFINITY;
+            for (int j = 0; j <= p; ++j) {
+                float lane[32];
+                for (int l = 0; l < 32; ++l) {
+                    float a = 0.0f;
+                    for (int d = l; d < hd; d += 32)
+                        a = fmaf(orc_bf16_to_f32(qh[d]), orc_bf16_to_f32(kb[(size_t)j * hd + d]), a);
+                    lane[l] = a;
+                }
+                for (int off = 1; off < 32; off <<= 1) {
+                    float nv[32];
+                    for (int l = 0; l < 32; ++l) nv[l] = lane[l] + lane[l ^ off];
+                    memcpy(lane, nv, sizeof lane);
+                }
+                sc[j] = lane[0] * scale;
+                if (sc[j] > m) m = sc[j];
+            }
+            float sum = 0.0f;
+            for (int j = 0; j <= p; ++j) {
+                sc[j] = expf(sc[j] - m);
+                sum += sc[j];
+            }
+            for (int d = 0; d < hd; ++d) {
+                float acc = 0.0f;
+                for (int j = 0; j <= p; ++j) acc = fmaf(sc[j], orc_bf16_to_f32(vb[(size_t)j * hd + d]), acc);
+                att[((size_t)t * nq + h) * hd + d] = orc_f32_to_bf16(acc / sum);
+            }
+        }
+    }
+    orc_lm_head_logits(A->o_w, A->o_s, A->o_b, H, (int)rq, att, T, nthreads, o);
+    for (size_t i = 0; i < (size_t)T * H; ++i)
+        out[i] = orc_f32_to_bf16(orc_bf16_to_f32(x[i]) + orc_bf16_to_f32(orc_f32_to_bf16(o[i])));
+    free(xn); free(q); free(k); free(v); free(qr); free(att); free(o); free(sc);
+    return 0;
+}

@@ -127,6 +127,26 @@ int orc_lm_head_logits(const uint32_t* w, const uint16_t* s, const uint16_t* b, 
                        const uint16_t* x, int T, int nthreads, float* logits);
 void orc_argmax_rows(const float* logits, int T, int n, int32_t* ids);
 
+/* ---- the attention block (config 4; src/forward.rs:404-419) ----
+ * The CUDA block's arithmetic: RMSNorm in rmsnorm.metal's order; q/k/v/o in the
+ * lm_head's canonical order (orc_lm_head_logits); projections rounded to bf16;
+ * per-head RMSNorm of q and k; NeoX RoPE (rope.metal:10-27) with cos/sin from
+ * orc_rope_table (double precision) and a = x1*s, o0 = fmaf(x0, c, -a),
+ * b = x0*s, o1 = fmaf(x1, c, b); K/V appended to the caches; scores
+ * q.k * (1/sqrtf(hd)) with the dot product in the kernel's lane order (32 lanes
+ * over head_dim, then the xor tree); softmax with expf; out = x + bf16(o). */
+typedef struct {
+    int H, nq, nkv, hd, max_seq, n_seqs;
+    const uint32_t *q_w, *k_w, *v_w, *o_w;
+    const uint16_t *q_s, *q_b, *k_s, *k_b, *v_s, *v_b, *o_s, *o_b;
+    const uint16_t *in_norm, *q_norm, *k_norm;
+    const float* rope;   /* [max_seq][hd/2][2] */
+    uint16_t *kc, *vc;   /* [n_seqs][nkv][max_seq][hd] */
+} orc_attn;
+void orc_rope_table(double theta, int hd, int max_seq, float* out);
+int orc_attn_forward(const orc_attn* A, const uint16_t* x, int T, const int32_t* seq, const int32_t* pos,
+                     float eps, int nthreads, uint16_t* out);
+
 #ifdef __cplusplus
 }
 #endif

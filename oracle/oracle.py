@@ -61,6 +61,9 @@ def lib():
         L.orc_lm_head_logits.restype = C.c_int
         L.orc_lm_head_logits.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int, _u16p, C.c_int, C.c_int, _f32p]
         L.orc_argmax_rows.argtypes = [_f32p, C.c_int, C.c_int, _i32p]
+        L.orc_rope_table.argtypes = [C.c_double, C.c_int, C.c_int, _f32p]
+        L.orc_attn_forward.restype = C.c_int
+        L.orc_attn_forward.argtypes = [C.c_void_p, _u16p, C.c_int, _i32p, _i32p, C.c_float, C.c_int, _u16p]
         L.orc_moe_layer.restype = C.c_int
         L.orc_moe_layer.argtypes = [C.c_void_p, _u16p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                     C.c_int, C.c_int, _u16p, _i32p, _f32p]
@@ -334,6 +337,77 @@ def lm_head(head: Head, x, nthreads=None):
     return logits, ids
 
 
+# ------------------------------------------------------- the attention block
+@dataclass
+class Attn:
+    """One layer's attention weights (MLX 4-bit) and the shape of its block."""
+    H: int
+    nq: int
+    nkv: int
+    hd: int
+    q_w: np.ndarray
+    q_s: np.ndarray
+    q_b: np.ndarray
+    k_w: np.ndarray
+    k_s: np.ndarray
+    k_b: np.ndarray
+    v_w: np.ndarray
+    v_s: np.ndarray
+    v_b: np.ndarray
+    o_w: np.ndarray
+    o_s: np.ndarray
+    o_b: np.ndarray
+    in_norm: np.ndarray
+    q_norm: np.ndarray
+    k_norm: np.ndarray
+
+
+def synth_attn(seed=0, layer=0, H=2048, nq=32, nkv=4, hd=128):
+    """Seeded attention weights: q/k/v/o drawn like expert projections from the
+    (seed, 2000 + 4*layer + i) streams, norm weights ~ 1 + U(-0.1, 0.1)."""
+    rq, rk = nq * hd, nkv * hd
+    qw, qs, qb = (a[0] for a in synth_proj(seed, 2000 + 4 * layer, 0, 1, rq, H))
+    kw, ks, kb = (a[0] for a in synth_proj(seed, 2001 + 4 * layer, 0, 1, rk, H))
+    vw, vs, vb = (a[0] for a in synth_proj(seed, 2002 + 4 * layer, 0, 1, rk, H))
+    ow, os_, ob = (a[0] for a in synth_proj(seed, 2003 + 4 * layer, 0, 1, H, rq))
+    rng = np.random.default_rng(seed * 1000 + layer + 3)
+    nrm = lambda n: f32_to_bf16((1.0 + rng.uniform(-0.1, 0.1, n)).astype(np.float32))  # noqa: E731
+    return Attn(H, nq, nkv, hd, qw, qs, qb, kw, ks, kb, vw, vs, vb, ow, os_, ob, nrm(H), nrm(hd), nrm(hd))
+
+
+class _Attn(C.Structure):
+    _fields_ = [("H", C.c_int), ("nq", C.c_int), ("nkv", C.c_int), ("hd", C.c_int), ("max_seq", C.c_int),
+                ("n_seqs", C.c_int)] + [(n, C.c_void_p) for n in (
+                    "q_w", "k_w", "v_w", "o_w", "q_s", "q_b", "k_s", "k_b", "v_s", "v_b", "o_s", "o_b",
+                    "in_norm", "q_norm", "k_norm", "rope", "kc", "vc")]
+
+
+class AttnState:
+    """The oracle's KV caches for n_seqs sequences and its RoPE table."""
+
+    def __init__(self, A: Attn, max_seq, n_seqs, theta=1e7):
+        self.A, self.max_seq, self.n_seqs = A, max_seq, n_seqs
+        self.kc = np.zeros((n_seqs, A.nkv, max_seq, A.hd), np.uint16)
+        self.vc = np.zeros_like(self.kc)
+        self.rope = np.empty((max_seq, A.hd // 2, 2), np.float32)
+        lib().orc_rope_table(theta, A.hd, max_seq, self.rope)
+
+    def forward(self, x, seq, pos, eps=1e-6, nthreads=None):
+        A = self.A
+        x = np.ascontiguousarray(x, np.uint16)
+        T = x.shape[0]
+        out = np.empty_like(x)
+        st = _Attn(A.H, A.nq, A.nkv, A.hd, self.max_seq, self.n_seqs,
+                   *[getattr(A, n).ctypes.data for n in ("q_w", "k_w", "v_w", "o_w", "q_s", "q_b", "k_s", "k_b",
+                                                         "v_s", "v_b", "o_s", "o_b", "in_norm", "q_norm", "k_norm")],
+                   self.rope.ctypes.data, self.kc.ctypes.data, self.vc.ctypes.data)
+        rc = lib().orc_attn_forward(C.byref(st), x, T, np.ascontiguousarray(seq, np.int32),
+                                    np.ascontiguousarray(pos, np.int32), eps, nthreads or os.cpu_count() or 1, out)
+        if rc:
+            raise ValueError("attn_forward: bad shape")
+        return out
+
+
 # ------------------------------------------- reference shaders (CPU build)
 def ref_lib():
     """The reference's own kernels compiled for the CPU, or None if not built."""
@@ -352,6 +426,9 @@ def ref_lib():
         R.ref_ew_swiglu.argtypes = [_f16p, _f16p, _f16p, C.c_int]
         R.ref_ew_scaled_add.argtypes = [_f16p, _f16p, C.c_float, C.c_int]
         R.ref_rmsnorm.argtypes = [_f16p, _f16p, _f16p, C.c_int, C.c_int, C.c_float]
+        R.ref_rope.argtypes = [_f16p, C.c_int, C.c_int, C.c_int, C.c_float]
+        R.ref_attn_token.restype = C.c_int
+        R.ref_attn_token.argtypes = [C.c_void_p, _f16p, _f16p, C.c_int, _u16p, C.c_int, _f16p]
         R.ref_moe_prefill.restype = C.c_int
         R.ref_moe_prefill.argtypes = [C.c_void_p, _u16p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, _f16p,
                                       _i32p, _f32p]
@@ -409,3 +486,41 @@ def ref_moe_prefill(L: Layer, x, residual=None, nthreads=None, bias=None):
     R.ref_moe_prefill(C.byref(st), x, None if res is None else res.ctypes.data, None if b is None else b.ctypes.data,
                       T, nthreads, out, ids, w)
     return out, ids, w
+
+
+class _RefAttn(C.Structure):
+    _fields_ = [("H", C.c_int), ("nq", C.c_int), ("nkv", C.c_int), ("hd", C.c_int), ("max_len", C.c_int),
+                ("theta", C.c_float), ("eps", C.c_float)] + [(n, C.c_void_p) for n in (
+                    "q_w", "k_w", "v_w", "o_w", "q_s", "q_b", "k_s", "k_b", "v_s", "v_b", "o_s", "o_b",
+                    "in_norm", "q_norm", "k_norm")]
+
+
+class RefAttnState:
+    """The reference's attention block on the CPU (its own kernels, forward.rs:404-419),
+    one decode token per call, with its f16 KV caches [n_kv][max_len][head_dim]."""
+
+    def __init__(self, A: Attn, max_len, theta=1e7, eps=1e-6):
+        if ref_lib() is None:
+            raise RuntimeError("oracle/_ref not built")
+        self.A, self.max_len = A, max_len
+        self.kc = np.zeros((A.nkv, max_len, A.hd), np.float16)
+        self.vc = np.zeros_like(self.kc)
+        self._st = _RefAttn(A.H, A.nq, A.nkv, A.hd, max_len, theta, eps,
+                            *[getattr(A, n).ctypes.data for n in (
+                                "q_w", "k_w", "v_w", "o_w", "q_s", "q_b", "k_s", "k_b", "v_s", "v_b", "o_s", "o_b",
+                                "in_norm", "q_norm", "k_norm")])
+
+    def token(self, x_row, pos, nthreads=None):
+        out = np.empty(self.A.H, np.float16)
+        rc = ref_lib().ref_attn_token(C.byref(self._st), self.kc, self.vc, int(pos),
+                                      np.ascontiguousarray(x_row, np.uint16), nthreads or os.cpu_count() or 1, out)
+        if rc:
+            raise ValueError("ref_attn_token: position out of range")
+        return out
+
+
+def ref_rope(x16, pos, theta=1e7):
+    """rope.metal on the CPU: x16 f16 [n_heads, head_dim] rotated in place at pos."""
+    x16 = np.ascontiguousarray(x16, np.float16)
+    ref_lib().ref_rope(x16, x16.shape[0], x16.shape[1], int(pos), theta)
+    return x16

@@ -22,6 +22,9 @@ struct RtParams { unsigned n_experts, top_k, norm_topk; };                     /
 struct NParams { unsigned n; };
 struct ScaledNParams { unsigned n; float scale; };
 struct RmsParams { unsigned dim; float eps; };                               // rmsnorm.metal:7
+struct RopeParams { unsigned n_heads, head_dim, pos; float theta; };         // rope.metal:8
+struct KvParams { unsigned n_kv, head_dim, max_len, pos; };                  // ops.metal:9
+struct SdpaParams { unsigned n_heads, n_kv, head_dim, seq_len, kv_stride; float scale; };  // sdpa_decode.metal:12
 
 extern "C" {
 void dequant_matvec_8bit(const unsigned char*, const half*, const half*, const half*, half*,
@@ -34,6 +37,10 @@ void moe_routing_topk(const half*, int*, half*, const RtParams&, unsigned);
 void ew_swiglu(const half*, const half*, half*, const NParams&, unsigned);
 void ew_scaled_add(half*, const half*, const ScaledNParams&, unsigned);
 void rmsnorm(const half*, const half*, half*, const RmsParams&, unsigned, unsigned);
+void ew_add(const half*, const half*, half*, const NParams&, unsigned);
+void kv_append(const half*, half*, const KvParams&, unsigned);
+void rope_apply(half*, const RopeParams&, unsigned);
+void sdpa_decode(const half*, const half*, const half*, half*, float*, const SdpaParams&, unsigned, unsigned);
 }
 
 template <class F>
@@ -111,6 +118,25 @@ void ref_moe_routing_topk(const half* logits, int n_experts, int top_k, int norm
     RtParams p{(unsigned)n_experts, (unsigned)top_k, (unsigned)norm};
     for (unsigned t = 1; t < 256; ++t) moe_routing_topk(logits, ids, weights, p, t);
     moe_routing_topk(logits, ids, weights, p, 0);
+}
+
+// rope.metal: one "thread" per (head, pair), in place on [n_heads, head_dim]
+void ref_rope(half* x, int n_heads, int head_dim, int pos, float theta) {
+    RopeParams p{(unsigned)n_heads, (unsigned)head_dim, (unsigned)pos, theta};
+    for (unsigned t = 0; t < (unsigned)(n_heads * head_dim / 2); ++t) rope_apply(x, p, t);
+}
+
+// sdpa_decode.metal: one threadgroup of 256 per head; the scores of every
+// "thread" are in the scratch before thread 0's serial softmax, so thread 0
+// runs last.  scratch: n_heads * kv_stride floats.
+void ref_sdpa(const half* q, const half* k, const half* v, half* out, float* scratch, int n_heads, int n_kv,
+              int head_dim, int seq_len, int kv_stride, float scale) {
+    SdpaParams p{(unsigned)n_heads, (unsigned)n_kv, (unsigned)head_dim, (unsigned)seq_len, (unsigned)kv_stride,
+                 scale};
+    for (unsigned h = 0; h < (unsigned)n_heads; ++h) {
+        for (unsigned t = 1; t < 256; ++t) sdpa_decode(q, k, v, out, scratch, p, h, t);
+        sdpa_decode(q, k, v, out, scratch, p, h, 0);
+    }
 }
 
 void ref_ew_swiglu(const half* g, const half* u, half* out, int n) {
@@ -196,6 +222,53 @@ int ref_moe_prefill(const RefLayer* L, const uint16_t* x_bf16, const uint16_t* r
     });
     if (ids_out) std::memcpy(ids_out, ids.data(), sizeof(int) * ids.size());
     if (w_out) std::memcpy(w_out, wts.data(), sizeof(float) * wts.size());
+    return 0;
+}
+
+// ---- the reference's attention block for one decode token (forward.rs:404-419) ----
+// Model::forward_layer up to the residual: RMSNorm(input_layernorm) -> q/k/v
+// fused 4-bit mat-vecs -> per-head RMSNorm (q_norm, k_norm) -> RoPE at pos ->
+// kv_append of k and v -> sdpa_decode over seq_len = pos + 1 positions with
+// scale = head_dim^-0.5 (attention.rs:27-29) -> o_proj -> ew_add(x, o).
+// Weights in the repository's bf16 host format, converted to f16 as the
+// loader does; kc/vc are the layer's f16 caches [n_kv][max_len][head_dim],
+// updated in place; out f16 [H].
+struct RefAttn {
+    int H, nq, nkv, hd, max_len;
+    float theta, eps;
+    const uint32_t *q_w, *k_w, *v_w, *o_w;
+    const uint16_t *q_s, *q_b, *k_s, *k_b, *v_s, *v_b, *o_s, *o_b;
+    const uint16_t *in_norm, *q_norm, *k_norm;
+};
+
+int ref_attn_token(const RefAttn* A, half* kc, half* vc, int pos, const uint16_t* x_bf16, int nthreads, half* out) {
+    const int H = A->H, nq = A->nq, nkv = A->nkv, hd = A->hd, rq = nq * hd, rk = nkv * hd;
+    if (pos < 0 || pos >= A->max_len) return -1;
+    std::vector<half> x = to_f16(x_bf16, H), in_norm = to_f16(A->in_norm, H), qn = to_f16(A->q_norm, hd),
+                      kn = to_f16(A->k_norm, hd);
+    std::vector<half> xn(H), q(rq), k(rk), v(rk), qh(rq), kh(rk), att(rq), o(H);
+    ref_rmsnorm(x.data(), in_norm.data(), xn.data(), 1, H, A->eps);
+    struct { const uint32_t* w; const uint16_t *s, *b; half* y; int n; } proj[3] = {
+        {A->q_w, A->q_s, A->q_b, q.data(), rq}, {A->k_w, A->k_s, A->k_b, k.data(), rk},
+        {A->v_w, A->v_s, A->v_b, v.data(), rk}};
+    for (auto& pj : proj) {
+        std::vector<half> sv = to_f16(pj.s, (size_t)pj.n * (H / 64)), bv = to_f16(pj.b, (size_t)pj.n * (H / 64));
+        ref_fused_dequant_matvec_4bit(pj.w, sv.data(), bv.data(), xn.data(), pj.y, H, pj.n, nthreads);
+    }
+    ref_rmsnorm(q.data(), qn.data(), qh.data(), nq, hd, A->eps);
+    ref_rmsnorm(k.data(), kn.data(), kh.data(), nkv, hd, A->eps);
+    ref_rope(qh.data(), nq, hd, pos, A->theta);
+    ref_rope(kh.data(), nkv, hd, pos, A->theta);
+    KvParams kp{(unsigned)nkv, (unsigned)hd, (unsigned)A->max_len, (unsigned)pos};
+    for (unsigned t = 0; t < (unsigned)rk; ++t) kv_append(kh.data(), kc, kp, t);
+    for (unsigned t = 0; t < (unsigned)rk; ++t) kv_append(v.data(), vc, kp, t);
+    std::vector<float> scratch((size_t)nq * A->max_len);
+    ref_sdpa(qh.data(), kc, vc, att.data(), scratch.data(), nq, nkv, hd, pos + 1, A->max_len,
+             std::pow((float)hd, -0.5f));
+    std::vector<half> os = to_f16(A->o_s, (size_t)H * (rq / 64)), ob = to_f16(A->o_b, (size_t)H * (rq / 64));
+    ref_fused_dequant_matvec_4bit(A->o_w, os.data(), ob.data(), att.data(), o.data(), rq, H, nthreads);
+    NParams np{(unsigned)H};
+    for (unsigned t = 0; t < (unsigned)H; ++t) ew_add(x.data(), o.data(), out, np, t);
     return 0;
 }
 

@@ -19,7 +19,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libobsmoe.so")
 BUILD = os.path.join(HERE, "_build")
 SOURCES = ["obs_api.cu", "obs_static.cu", "obs_safetensors.cu", "k_synth.cu", "k_router.cu", "k_dispatch.cu",
-           "k_decode.cu", "k_gemm.cu", "k_ep.cu", "k_head.cu"]
+           "k_decode.cu", "k_gemm.cu", "k_ep.cu", "k_head.cu", "k_attn.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -179,6 +179,23 @@ static cudaError_t lm_head_t(const uint32_t* w, const uint16_t* s, const uint16_
                       logits);
 }
 
+cudaError_t launch_linear4(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x, int T,
+                           int rows, int in_f, float* y, int num_sms, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (in_f % 2048) return cudaErrorInvalidValue;
+    const int chunk = in_f <= 2048 ? kHeadMaxT : kHeadMaxT / 2;  // x of a chunk fits shared memory as fp32
+    for (int t0 = 0; t0 < T; t0 += chunk) {
+        const int n = T - t0 < chunk ? T - t0 : chunk;
+        const uint16_t* xc = x + (size_t)t0 * in_f;
+        float* yc = y + (size_t)t0 * rows;
+        cudaError_t e = n <= 1   ? lm_head_t<1>(w, s, b, xc, n, rows, in_f, yc, num_sms, st)
+                        : n <= 4 ? lm_head_t<4>(w, s, b, xc, n, rows, in_f, yc, num_sms, st)
+                                 : lm_head_t<kHeadMaxT>(w, s, b, xc, n, rows, in_f, yc, num_sms, st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaGetLastError();
+}
+
 cudaError_t launch_lm_head(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* xn, int T,
                            int vocab, int H, float* logits, int32_t* ids, int num_sms, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cmath>
 #include <cstddef>
 #include <cstdio>
 #include <cstdlib>
@@ -91,6 +92,24 @@ struct obs_ctx {
         uint16_t* xn = nullptr;  // [kHeadMaxT, H]
         float* logits = nullptr; // [kHeadMaxT, vocab]
     } head;
+    // the attention block (obs_attn_init / obs_load_attn): per layer weights and KV caches
+    struct AttnLayer {
+        uint8_t* mem = nullptr;
+        uint32_t *qkv_w = nullptr, *o_w = nullptr;  // q | k | v rows concatenated; o
+        uint16_t *qkv_s = nullptr, *qkv_b = nullptr, *o_s = nullptr, *o_b = nullptr;
+        uint16_t *in_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+        uint16_t *kc = nullptr, *vc = nullptr;      // [n_seqs][n_kv][max_seq][hd]
+        bool loaded = false;
+    };
+    obs_attn_config acfg{};
+    std::vector<AttnLayer> attn;
+    uint8_t* attn_scratch = nullptr;
+    float* rope_cs = nullptr;   // [max_seq][hd/2][2]
+    float* a_qkv = nullptr;     // [max_tokens][(nq + 2 nkv) hd]
+    uint16_t* a_xn = nullptr;   // [max_tokens][H]
+    uint16_t* a_q = nullptr;    // [max_tokens][nq hd]
+    uint16_t* a_out = nullptr;  // [max_tokens][nq hd]
+    float* a_o = nullptr;       // [max_tokens][H]
     size_t ep_bytes = 0;
     bool ep_connected = false;
     EpArgs ep{};
@@ -358,6 +377,9 @@ extern "C" int obs_destroy(obs_ctx* ctx) {
             if (r != ctx->ep_rank && ctx->ep.peer[r]) cudaIpcCloseMemHandle(ctx->ep.peer[r]);
     if (ctx->ep_buf) cudaFree(ctx->ep_buf);
     if (ctx->head.mem) cudaFree(ctx->head.mem);
+    for (auto& a : ctx->attn)
+        if (a.mem) cudaFree(a.mem);
+    if (ctx->attn_scratch) cudaFree(ctx->attn_scratch);
     if (ctx->wmem) cudaFree(ctx->wmem);
     if (ctx->smem_pool) cudaFree(ctx->smem_pool);
     delete ctx;
@@ -491,6 +513,144 @@ extern "C" int obs_lm_head(obs_ctx* ctx, const uint16_t* x, int T, int32_t* ids,
     CU(launch_lm_head(h.lm_w, h.lm_s, h.lm_b, h.xn, T, h.vocab, ctx->sh.H, logits ? logits : h.logits, ids,
                       ctx->num_sms, st),
        "lm_head");
+    return OBS_OK;
+}
+
+namespace obs {
+void rope_table(double theta, int hd, int max_seq, float* out) {
+    for (int p = 0; p < max_seq; ++p)
+        for (int i = 0; i < hd / 2; ++i) {
+            const double ang = (double)p * std::pow(theta, -2.0 * i / hd);
+            out[((size_t)p * (hd / 2) + i) * 2] = (float)std::cos(ang);
+            out[((size_t)p * (hd / 2) + i) * 2 + 1] = (float)std::sin(ang);
+        }
+}
+}  // namespace obs
+
+extern "C" int obs_attn_init(obs_ctx* ctx, const obs_attn_config* ac) {
+    OBS_CHECK_CTX(ctx);
+    if (!ac) return fail(ctx, OBS_ERR_INVALID, "null attention config");
+    if (!ctx->attn.empty()) return fail(ctx, OBS_ERR_STATE, "attention already initialised");
+    const int nq = ac->n_heads, nkv = ac->n_kv_heads, hd = ac->head_dim;
+    if (nq <= 0 || nkv <= 0 || nq % nkv || hd <= 0 || hd > 128 || hd % 2 || (nq * hd) % 2048 ||
+        ac->max_seq <= 0 || ac->max_seq > kAttnMaxSeq || ac->n_seqs <= 0 || !(ac->rope_theta > 0.0f))
+        return fail(ctx, OBS_ERR_INVALID,
+                    "bad attention config (heads divisible by kv heads, head_dim <= 128 even, heads*head_dim a "
+                    "multiple of 2048, 0 < max_seq <= 40960, n_seqs > 0, rope_theta > 0)");
+    CU(cudaSetDevice(ctx->device), "cudaSetDevice");
+    ctx->acfg = *ac;
+    const int T = ctx->cfg.max_tokens, H = ctx->sh.H, W = (nq + 2 * nkv) * hd;
+    const size_t sizes[] = {(size_t)ac->max_seq * hd * 4, (size_t)T * W * 4, (size_t)T * H * 2, (size_t)T * nq * hd * 2,
+                            (size_t)T * nq * hd * 2, (size_t)T * H * 4};
+    size_t total = 0;
+    for (size_t sz : sizes) total += align_up(sz, 256);
+    CU(cudaMalloc(&ctx->attn_scratch, total), "attention scratch");
+    uint8_t* p = ctx->attn_scratch;
+    void** ptrs[] = {(void**)&ctx->rope_cs, (void**)&ctx->a_qkv, (void**)&ctx->a_xn, (void**)&ctx->a_q,
+                     (void**)&ctx->a_out, (void**)&ctx->a_o};
+    for (int i = 0; i < 6; ++i) *ptrs[i] = p, p += align_up(sizes[i], 256);
+    std::vector<float> tab((size_t)ac->max_seq * hd);
+    rope_table(ac->rope_theta, hd, ac->max_seq, tab.data());
+    CU(cudaMemcpy(ctx->rope_cs, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice), "rope table");
+    ctx->attn.resize(ctx->cfg.n_layers);
+    return OBS_OK;
+}
+
+extern "C" int obs_load_attn(obs_ctx* ctx, int layer, const obs_attn_weights* w, int src_on_device) {
+    OBS_CHECK_CTX(ctx);
+    if (ctx->attn.empty()) return fail(ctx, OBS_ERR_STATE, "attention not initialised (obs_attn_init)");
+    if (layer < 0 || layer >= (int)ctx->attn.size()) return fail(ctx, OBS_ERR_INVALID, "layer out of range");
+    if (!w || !w->q_w || !w->q_s || !w->q_b || !w->k_w || !w->k_s || !w->k_b || !w->v_w || !w->v_s || !w->v_b ||
+        !w->o_w || !w->o_s || !w->o_b || !w->in_norm || !w->q_norm || !w->k_norm)
+        return fail(ctx, OBS_ERR_INVALID, "null attention weight pointer");
+    CU(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const auto& ac = ctx->acfg;
+    const int nq = ac.n_heads, nkv = ac.n_kv_heads, hd = ac.head_dim, H = ctx->sh.H;
+    const size_t rq = (size_t)nq * hd, rk = (size_t)nkv * hd;
+    auto& L = ctx->attn[layer];
+    if (!L.mem) {
+        const size_t cache = (size_t)ac.n_seqs * nkv * ac.max_seq * hd * 2;
+        const size_t sizes[] = {(rq + 2 * rk) * (H / 8) * 4, (rq + 2 * rk) * (H / 64) * 2, (rq + 2 * rk) * (H / 64) * 2,
+                                (size_t)H * (rq / 8) * 4,      (size_t)H * (rq / 64) * 2,    (size_t)H * (rq / 64) * 2,
+                                (size_t)H * 2,                  (size_t)hd * 2,               (size_t)hd * 2,
+                                cache,                          cache};
+        size_t total = 0;
+        for (size_t sz : sizes) total += align_up(sz, 256);
+        CU(cudaMalloc(&L.mem, total), "attention layer alloc");
+        uint8_t* p = L.mem;
+        void** ptrs[] = {(void**)&L.qkv_w, (void**)&L.qkv_s, (void**)&L.qkv_b, (void**)&L.o_w,   (void**)&L.o_s,
+                         (void**)&L.o_b,   (void**)&L.in_norm, (void**)&L.q_norm, (void**)&L.k_norm, (void**)&L.kc,
+                         (void**)&L.vc};
+        for (int i = 0; i < 11; ++i) *ptrs[i] = p, p += align_up(sizes[i], 256);
+        CU(cudaMemset(L.kc, 0, cache), "cache init");
+        CU(cudaMemset(L.vc, 0, cache), "cache init");
+    }
+    const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    const size_t wq = rq * (H / 8) * 4, wk = rk * (H / 8) * 4, gq = rq * (H / 64) * 2, gk = rk * (H / 64) * 2;
+    uint8_t* qw = reinterpret_cast<uint8_t*>(L.qkv_w);
+    uint8_t* qs = reinterpret_cast<uint8_t*>(L.qkv_s);
+    uint8_t* qb = reinterpret_cast<uint8_t*>(L.qkv_b);
+    CU(cudaMemcpy(qw, w->q_w, wq, kind), "copy");
+    CU(cudaMemcpy(qw + wq, w->k_w, wk, kind), "copy");
+    CU(cudaMemcpy(qw + wq + wk, w->v_w, wk, kind), "copy");
+    CU(cudaMemcpy(qs, w->q_s, gq, kind), "copy");
+    CU(cudaMemcpy(qs + gq, w->k_s, gk, kind), "copy");
+    CU(cudaMemcpy(qs + gq + gk, w->v_s, gk, kind), "copy");
+    CU(cudaMemcpy(qb, w->q_b, gq, kind), "copy");
+    CU(cudaMemcpy(qb + gq, w->k_b, gk, kind), "copy");
+    CU(cudaMemcpy(qb + gq + gk, w->v_b, gk, kind), "copy");
+    CU(cudaMemcpy(L.o_w, w->o_w, (size_t)H * (rq / 8) * 4, kind), "copy");
+    CU(cudaMemcpy(L.o_s, w->o_s, (size_t)H * (rq / 64) * 2, kind), "copy");
+    CU(cudaMemcpy(L.o_b, w->o_b, (size_t)H * (rq / 64) * 2, kind), "copy");
+    CU(cudaMemcpy(L.in_norm, w->in_norm, (size_t)H * 2, kind), "copy");
+    CU(cudaMemcpy(L.q_norm, w->q_norm, (size_t)hd * 2, kind), "copy");
+    CU(cudaMemcpy(L.k_norm, w->k_norm, (size_t)hd * 2, kind), "copy");
+    L.loaded = true;
+    return OBS_OK;
+}
+
+extern "C" int obs_attn_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint16_t* out, int T, const int32_t* seq,
+                                const int32_t* pos, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    if (ctx->attn.empty()) return fail(ctx, OBS_ERR_STATE, "attention not initialised (obs_attn_init)");
+    if (layer < 0 || layer >= (int)ctx->attn.size()) return fail(ctx, OBS_ERR_INVALID, "layer out of range");
+    if (!ctx->attn[layer].loaded) return fail(ctx, OBS_ERR_STATE, "attention layer not loaded");
+    if (T < 0 || T > ctx->cfg.max_tokens) return fail(ctx, OBS_ERR_INVALID, "T out of range (0..max_tokens)");
+    if (T == 0) return OBS_OK;
+    if (!x || !out || !seq || !pos) return fail(ctx, OBS_ERR_INVALID, "null pointer");
+    if (out == x) return fail(ctx, OBS_ERR_INVALID, "out may not alias x");
+    const auto& ac = ctx->acfg;
+    const auto& L = ctx->attn[layer];
+    const int nq = ac.n_heads, nkv = ac.n_kv_heads, hd = ac.head_dim, H = ctx->sh.H;
+    cudaStream_t st = as_stream(stream);
+    CU(launch_rmsnorm(x, L.in_norm, T, H, ctx->cfg.rms_eps, ctx->a_xn, st), "input norm");
+    CU(launch_linear4(L.qkv_w, L.qkv_s, L.qkv_b, ctx->a_xn, T, (nq + 2 * nkv) * hd, H, ctx->a_qkv, ctx->num_sms, st),
+       "qkv projection");
+    CU(launch_qk_norm_rope(ctx->a_qkv, T, nq, nkv, hd, L.q_norm, L.k_norm, ctx->cfg.rms_eps, ctx->rope_cs, ac.max_seq,
+                           seq, pos, ctx->a_q, L.kc, L.vc, ac.n_seqs, ctx->err_flag, st),
+       "q/k norm, rope, cache append");
+    CU(launch_sdpa(ctx->a_q, L.kc, L.vc, T, nq, nkv, hd, ac.max_seq, ac.n_seqs, seq, pos, ctx->a_out, st), "attention");
+    CU(launch_linear4(L.o_w, L.o_s, L.o_b, ctx->a_out, T, H, nq * hd, ctx->a_o, ctx->num_sms, st), "o projection");
+    CU(launch_residual_add(x, ctx->a_o, (size_t)T * H, out, st), "residual");
+    return OBS_OK;
+}
+
+extern "C" int obs_kv_read(obs_ctx* ctx, int layer, int seq, int pos0, int n, uint16_t* k, uint16_t* v,
+                           void* stream) {
+    OBS_CHECK_CTX(ctx);
+    if (ctx->attn.empty() || layer < 0 || layer >= (int)ctx->attn.size() || !ctx->attn[layer].mem)
+        return fail(ctx, OBS_ERR_STATE, "no attention layer there");
+    const auto& ac = ctx->acfg;
+    if (seq < 0 || seq >= ac.n_seqs || pos0 < 0 || n < 0 || pos0 + n > ac.max_seq)
+        return fail(ctx, OBS_ERR_INVALID, "cache range out of bounds");
+    const auto& L = ctx->attn[layer];
+    const int hd = ac.head_dim;
+    cudaStream_t st = as_stream(stream);
+    for (int h = 0; h < ac.n_kv_heads; ++h) {
+        const size_t src = (((size_t)seq * ac.n_kv_heads + h) * ac.max_seq + pos0) * hd;
+        if (k) CU(cudaMemcpyAsync(k + (size_t)h * n * hd, L.kc + src, (size_t)n * hd * 2, cudaMemcpyDeviceToDevice, st), "copy");
+        if (v) CU(cudaMemcpyAsync(v + (size_t)h * n * hd, L.vc + src, (size_t)n * hd * 2, cudaMemcpyDeviceToDevice, st), "copy");
+    }
     return OBS_OK;
 }
 
@@ -995,6 +1155,8 @@ extern "C" int obs_check_device(obs_ctx* ctx, void* stream) {
         if (flag == kDevBadTile) return fail(ctx, OBS_ERR_INVALID, "device refused a GEMM tile outside its buffers");
         if (flag == kDevBadSlot)
             return fail(ctx, OBS_ERR_INVALID, "device refused an expert-parallel row slot outside its buffers");
+        if (flag == kDevBadPos)
+            return fail(ctx, OBS_ERR_INVALID, "device refused a token's sequence or position outside the KV caches");
         return fail(ctx, OBS_ERR_INVALID, "device reported an invalid route (expert id out of range)");
     }
     return OBS_OK;
@@ -1036,6 +1198,15 @@ extern "C" int obs_struct_layout(int32_t* out, int n) {
         OBS_OFF(obs_head_weights, embed_w), OBS_OFF(obs_head_weights, embed_s), OBS_OFF(obs_head_weights, embed_b),
         OBS_OFF(obs_head_weights, lm_w), OBS_OFF(obs_head_weights, lm_s), OBS_OFF(obs_head_weights, lm_b),
         OBS_OFF(obs_head_weights, norm_w),
+        (int32_t)sizeof(obs_attn_weights),
+        OBS_OFF(obs_attn_weights, q_w), OBS_OFF(obs_attn_weights, q_s), OBS_OFF(obs_attn_weights, q_b),
+        OBS_OFF(obs_attn_weights, k_w), OBS_OFF(obs_attn_weights, k_s), OBS_OFF(obs_attn_weights, k_b),
+        OBS_OFF(obs_attn_weights, v_w), OBS_OFF(obs_attn_weights, v_s), OBS_OFF(obs_attn_weights, v_b),
+        OBS_OFF(obs_attn_weights, o_w), OBS_OFF(obs_attn_weights, o_s), OBS_OFF(obs_attn_weights, o_b),
+        OBS_OFF(obs_attn_weights, in_norm), OBS_OFF(obs_attn_weights, q_norm), OBS_OFF(obs_attn_weights, k_norm),
+        (int32_t)sizeof(obs_attn_config),
+        OBS_OFF(obs_attn_config, n_heads), OBS_OFF(obs_attn_config, n_kv_heads), OBS_OFF(obs_attn_config, head_dim),
+        OBS_OFF(obs_attn_config, max_seq), OBS_OFF(obs_attn_config, n_seqs), OBS_OFF(obs_attn_config, rope_theta),
     };
 #undef OBS_OFF
     const int total = (int)(sizeof(v) / sizeof(v[0]));

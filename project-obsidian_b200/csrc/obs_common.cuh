@@ -20,7 +20,7 @@ constexpr int kBlockBytes = kBlockWords * 4 + 2 * kRowTile * 2;  // + scales + b
 constexpr int kSegAlign = 16;     // expert segments padded to 16 rows (MMA N step)
 
 // Device-side error codes written to the context's flag word.
-enum DevErr : int { kDevOk = 0, kDevTimeout = 1, kDevBadRoute = 2, kDevBadTile = 3, kDevBadSlot = 4 };
+enum DevErr : int { kDevOk = 0, kDevTimeout = 1, kDevBadRoute = 2, kDevBadTile = 3, kDevBadSlot = 4, kDevBadPos = 5 };
 
 // ------------------------------------------------------------------- bf16
 __device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }

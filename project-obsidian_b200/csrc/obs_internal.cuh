@@ -185,11 +185,30 @@ cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t
 
 // ----------------------------------------------------------------- k_head.cu
 constexpr int kHeadMaxT = 16;  // tokens of one obs_lm_head call
+// longest KV cache (the model's max_position_embeddings): the attention kernel
+// keeps one fp32 score per cached position in shared memory (160 KB)
+constexpr int kAttnMaxSeq = 40960;
 cudaError_t launch_embed(const uint32_t* w, const uint16_t* s, const uint16_t* b, const int32_t* tokens, int T,
                          int vocab, int H, uint16_t* x, int* err, cudaStream_t st);
 // logits [T, vocab] fp32 of the normalised rows xn, then ids [T] = the first maximum of each row
 cudaError_t launch_lm_head(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* xn, int T,
                            int vocab, int H, float* logits, int32_t* ids, int num_sms, cudaStream_t st);
+
+// y [T, rows] fp32 = x [T, in_f] (bf16) . dequant(W [rows, in_f/8])^T in the canonical order (k_lm_head)
+cudaError_t launch_linear4(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x, int T,
+                           int rows, int in_f, float* y, int num_sms, cudaStream_t st);
+
+// ----------------------------------------------------------------- k_attn.cu
+cudaError_t launch_qk_norm_rope(const float* qkv, int T, int nq, int nkv, int hd, const uint16_t* qn,
+                                const uint16_t* kn, float eps, const float* rope_cs, int max_seq, const int32_t* seq,
+                                const int32_t* pos, uint16_t* qout, uint16_t* kcache, uint16_t* vcache, int n_seqs,
+                                int* err, cudaStream_t st);
+cudaError_t launch_sdpa(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int T, int nq, int nkv, int hd,
+                        int max_seq, int n_seqs, const int32_t* seq, const int32_t* pos, uint16_t* out,
+                        cudaStream_t st);
+cudaError_t launch_residual_add(const uint16_t* x, const float* o, size_t n, uint16_t* out, cudaStream_t st);
+// cos/sin of pos * theta^(-2i/hd) for pos < max_seq, i < hd/2, interleaved, computed in double, as fp32
+void rope_table(double theta, int hd, int max_seq, float* out);
 
 // ----------------------------------------------------------------- k_gemm.cu
 enum GemmEpi : int { kEpiSwiglu = 0, kEpiBf16 = 1, kEpiF32 = 2 };

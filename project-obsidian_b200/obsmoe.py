@@ -34,6 +34,7 @@ EXPORTS = (
     "obs_trace_enable", "obs_decode_ffn_static", "obs_kernel_launches", "obs_ep_handle", "obs_ep_connect",
     "obs_rmsnorm", "obs_moe_stack_forward", "obs_set_wait_limit", "obs_probe_wait", "obs_struct_layout",
     "obs_load_layer_safetensors", "obs_expert_file_info", "obs_load_head", "obs_embed", "obs_lm_head",
+    "obs_attn_init", "obs_load_attn", "obs_attn_forward", "obs_kv_read",
 )
 EP_HANDLE_BYTES = 64
 STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down",
@@ -56,6 +57,17 @@ class Config(C.Structure):
 
 class HeadWeights(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in ("embed_w", "embed_s", "embed_b", "lm_w", "lm_s", "lm_b", "norm_w")]
+
+
+class AttnWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "q_w", "q_s", "q_b", "k_w", "k_s", "k_b", "v_w", "v_s", "v_b", "o_w", "o_s", "o_b",
+        "in_norm", "q_norm", "k_norm")]
+
+
+class AttnConfig(C.Structure):
+    _fields_ = [("n_heads", C.c_int32), ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32),
+                ("max_seq", C.c_int32), ("n_seqs", C.c_int32), ("rope_theta", C.c_float)]
 
 
 class LayerWeights(C.Structure):
@@ -108,6 +120,10 @@ def lib() -> C.CDLL:
         L.obs_load_head.argtypes = [vp, i32, C.POINTER(HeadWeights), i32]
         L.obs_embed.argtypes = [vp, vp, i32, vp, vp]
         L.obs_lm_head.argtypes = [vp, vp, i32, vp, vp, vp]
+        L.obs_attn_init.argtypes = [vp, C.POINTER(AttnConfig)]
+        L.obs_load_attn.argtypes = [vp, i32, C.POINTER(AttnWeights), i32]
+        L.obs_attn_forward.argtypes = [vp, i32, vp, vp, i32, vp, vp, vp]
+        L.obs_kv_read.argtypes = [vp, i32, i32, i32, i32, vp, vp, vp]
         L.obs_set_wait_limit.argtypes = [vp, i64]
         L.obs_probe_wait.argtypes = [vp, vp]
         L.obs_struct_layout.argtypes = [C.POINTER(C.c_int32), i32]
@@ -213,6 +229,24 @@ class MoeContext:
     def lm_head(self, x, T, ids, logits=None, stream=None):
         """RMSNorm(model.norm) -> lm_head -> greedy ids (first maximum); logits optional."""
         self._chk(lib().obs_lm_head(self._h, _ptr(x), T, _ptr(ids), _ptr(logits), _stream(stream)))
+
+    # -- the attention block
+    def attn_init(self, n_heads=32, n_kv_heads=4, head_dim=128, max_seq=4096, n_seqs=1, rope_theta=1e7):
+        ac = AttnConfig(n_heads, n_kv_heads, head_dim, max_seq, n_seqs, rope_theta)
+        self._chk(lib().obs_attn_init(self._h, C.byref(ac)))
+
+    def load_attn(self, layer: int, w, on_device: bool = False):
+        """One layer's attention weights (attributes q_w ... k_norm, MLX 4-bit layout)."""
+        aw = AttnWeights(*[_ptr(getattr(w, n)) for n, _ in AttnWeights._fields_])
+        self._chk(lib().obs_load_attn(self._h, layer, C.byref(aw), int(on_device)))
+
+    def attn_forward(self, layer, x, out, T, seq, pos, stream=None):
+        """out = x + attention(x) for T tokens of sequences seq[t] at positions pos[t]; appends K/V."""
+        self._chk(lib().obs_attn_forward(self._h, layer, _ptr(x), _ptr(out), T, _ptr(seq), _ptr(pos),
+                                         _stream(stream)))
+
+    def kv_read(self, layer, seq, pos0, n, k=None, v=None, stream=None):
+        self._chk(lib().obs_kv_read(self._h, layer, seq, pos0, n, _ptr(k), _ptr(v), _stream(stream)))
 
     def synth_layer(self, layer: int, seed: int = 0):
         self._chk(lib().obs_synth_layer(self._h, layer, seed))

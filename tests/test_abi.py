@@ -89,7 +89,7 @@ def header_struct_fields(name):
 
 def test_struct_layout_of_library_ctypes_and_rust_agree():
     v = obsmoe.struct_layout()
-    assert len(v) == 34
+    assert len(v) == 57
     cfg_fields = header_struct_fields("obs_config")
     lw_fields = header_struct_fields("obs_layer_weights")
     hw_fields = header_struct_fields("obs_head_weights")
@@ -111,6 +111,15 @@ def test_struct_layout_of_library_ctypes_and_rust_agree():
     # the Rust binding a maintainer of the reference would add
     assert rust_struct_layout("ObsConfig") == lib_cfg
     assert rust_struct_layout("ObsLayerWeights") == lib_lw
+    # the attention structs
+    aw_fields = header_struct_fields("obs_attn_weights")
+    ac_fields = header_struct_fields("obs_attn_config")
+    assert len(aw_fields) == 15 and len(ac_fields) == 6
+    lib_aw = (v[34], list(zip(aw_fields, v[35:50])))
+    lib_ac = (v[50], list(zip(ac_fields, v[51:57])))
+    for ct, lib_s, rust in ((obsmoe.AttnWeights, lib_aw, "ObsAttnWeights"), (obsmoe.AttnConfig, lib_ac, "ObsAttnConfig")):
+        assert (C.sizeof(ct), [(f, getattr(ct, f).offset) for f, _ in ct._fields_]) == lib_s
+        assert rust_struct_layout(rust) == lib_s
 
 
 def test_rust_binding_declares_every_export():
