@@ -271,10 +271,12 @@ int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches);
  * for lane quarters 1-3, 4 MMA pair ready, 9 MMA fence passed, 5 MMA pair
  * committed (per pair of k-steps), 6 epilogue start, 7 epilogue done (per
  * item), 13 token tile landed (per k-step).
- * When 14 * n_steps >= 8 * (SM count), the fused decode layer (T <= 4) writes
- * instead, for every CTA b, trace[8b + k]: k = 0 start, 1 router done, 2 first
- * grid barrier passed, 3 top-k done, 4 gate/up done, 5 second barrier passed,
- * 6 down + combine done.
+ * When 14 * n_steps >= 16 * (SM count), the fused decode layer (T <= 4) writes
+ * instead, for every CTA b, trace[16b + k]: k = 0 start, 1 router done, 2 grid
+ * barrier passed, 3 weight copies issued, 4 gate/up done, 5 first h row ready,
+ * 6 down + combine done, 7 top-k done, 8/9/10 first gate/up unit of half 0
+ * landed/computed/done, 11/12 its second unit landed/done, 13/14 the first
+ * down unit landed/y written (0 where a CTA has no such unit).
  * trace = NULL switches it off.  Device memory of 14 * n_steps uint64. */
 int obs_trace_enable(obs_ctx* ctx, uint64_t* trace, int n_steps);
 /* No counterpart in the reference.  *count = the number of kernel launches the
@@ -356,7 +358,7 @@ int obs_ep_connect(obs_ctx* ctx, const void* handles);
  *   out[t] = bf16([residual[t] +] sum_k weights[t,k] * down_e(silu(gate_e x_t) * up_e x_t)),
  * e = ids[t,k], the decode path's arithmetic, from expert weights in the
  * reference (MLX) layout given as device pointers in w (router fields unused).
- * Its scratch is one fixed device array inside the library (about 7 MB,
+ * Its scratch is one fixed device array inside the library (about 8 MB,
  * held on every GPU that loads the library until the process exits).
  * Limits: T * top_k <= OBS_STATIC_MAX_PAIRS, hidden a multiple of 512 up to
  * OBS_STATIC_MAX_HIDDEN, inter a multiple of 128 up to OBS_STATIC_MAX_INTER;

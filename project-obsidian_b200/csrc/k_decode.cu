@@ -1,46 +1,159 @@
-// k_decode.cu -- decode expert FFN: fused 4-bit dequant mat-vec on CUDA cores.
+// k_decode.cu -- decode expert FFN: 4-bit dequant mat-vec on the integer units.
 //
 // Replaces the reference's per-rank loop of fused_dequant_matvec_4bit x3 +
 // ew_swiglu + ew_scaled_add (src/forward.rs:431-441; shaders/
-// fused_dequant_matvec_4bit.metal:14-53, ops.metal:18-29).  Weights are read
-// once, coalesced, 128 rows x 64 columns at a time, all of a warp's loads in
-// flight together.  The group's affine dequantisation is factored out of the
-// inner loop: over one 64-column group, sum_j (q_j s + b) x_j =
-// 16 s (sum_j f_j x_j - sum_j x_j) + b sum_j x_j with f_j = 1 + q_j/16, a float
-// built from the code with one shift and one logic op; per weight that is a
-// shift, a logic op and one fp32 FMA.  Split-K partial sums meet in a fixed
-// order in the last CTA to finish (a per-tile arrival counter that resets
-// itself), so results do not depend on CTA scheduling.
+// fused_dequant_matvec_4bit.metal:14-53, ops.metal:18-29).
+//
+// Arithmetic.  Over one 64-column group g of a weight row,
+//   sum_j (q_j s + b) x_j = s * sum_j q_j x_j + b * sum_j x_j.
+// The activations of the group are put in fixed point once per token: with
+// e the exponent of max_j |x_j| and k = 13 - e, X_j = round(x_j 2^k) (half away
+// from zero), |X_j| <= 2^14, split X_j = 256 hi_j + lo_j (hi signed 8-bit, lo
+// unsigned 8-bit).  sum_j q_j X_j is then exact in int32: dp4a multiplies four
+// 4-bit codes by four 8-bit limbs per instruction, and the codes need one
+// logic op per four of them (w & 0x0F0F0F0F, and w & 0xF0F0F0F0 which gives
+// 16 q).  Integer sums do not depend on their order, so any layout or lane
+// split gives the same integer.  Per (row, group) the fp32 value is
+//   P = fma(s, float(16 sum q X) * 2^-(k+4), b * (sum X) 2^-k),
+// and the P of the groups are added in a fixed fp32 order (below).  The
+// rounding of x to 15 significant bits (relative to the group maximum) is far
+// below the bf16 rounding of the outputs.
+//
+// Reduction orders (the same in the separate and the fused kernels, so they
+// give identical results): gate/up -- the 8 k-splits of 4 groups each: per
+// split ((P0 + P1) + P2) + P3, then the splits in order from 0; down -- the
+// groups in order from 0 (warp w sums its groups w, w + 16, ..., the warps in
+// order).  SwiGLU rounds h to bf16; the last split of each 128-feature tile
+// writes h already in fixed point for the down projection.
 //
 // The kernels read either the context's tiled 4608-byte blocks or the
-// reference's MLX row-major layout directly.
+// reference's MLX row-major layout directly (then the activations are packed
+// in the MLX nibble order).
 #include "router_dev.cuh"
 
 namespace obs {
 namespace {
 
-constexpr int kSplitGU = kDecodeSplit;  // k-splits of the gate/up mat-vec (one 64-column block per warp)
+constexpr int kSplitGU = kDecodeSplit;  // k-splits of the gate/up mat-vec
 
-// 1 + q/16 as a float, q the 4-bit code at nibble j: the code becomes mantissa bits 19-22
-__device__ __forceinline__ float nib_f16th(uint32_t w, int j) {
-    const uint32_t m = (4 * j <= 19) ? (w << (19 - 4 * j)) : (w >> (4 * j - 19));
-    return __uint_as_float((m & 0x00780000u) | 0x3F800000u);
+// ------------------------------------------------------------ fixed point
+// exact 2^n as a float (0 below the smallest subnormal)
+__device__ __forceinline__ float pow2f(int n) {
+    if (n > 127) return __uint_as_float(0x7F800000u);
+    if (n >= -126) return __uint_as_float((uint32_t)(n + 127) << 23);
+    if (n >= -149) return __uint_as_float(1u << (n + 149));
+    return 0.0f;
+}
+// k for a group whose largest magnitude has bf16 bits gm (sign cleared)
+__device__ __forceinline__ int fx_k(uint32_t gm) {
+    if (gm == 0) return 0;
+    const int ef = (int)(gm >> 7) & 0xFF;
+    return 13 - (ef == 0 ? -126 : ef - 127);
+}
+// round(x 2^k), half away from zero, for a bf16 x no larger in magnitude than
+// the group maximum (so the shift is at least 10)
+__device__ __forceinline__ int fx_round(uint32_t xb, int k) {
+    const uint32_t u = xb << 16;
+    const int ef = (int)(u >> 23) & 0xFF;
+    uint32_t mant = u & 0x7FFFFFu;
+    int e;
+    if (ef == 0) {
+        if (mant == 0) return 0;
+        e = -126;
+    } else {
+        mant |= 0x800000u;
+        e = ef - 127;
+    }
+    const int s = 23 - e - k;
+    const int mag = s >= 32 ? 0 : (int)((mant + (1u << (s - 1))) >> s);
+    return (u >> 31) ? -mag : mag;
+}
+// Byte of column j (0..63) of a packed group, limb 0 (hi) or 1 (lo).  A group
+// is two 64-byte halves (columns 0-31, 32-63) of 16 words: hi_even[4],
+// hi_odd[4], lo_even[4], lo_odd[4]; word c of "even" holds, byte by byte, the
+// columns that the even nibbles of weight word c hold (columns 8c..8c+7 of the
+// half), "odd" those of the odd nibbles.  Tiled blocks store the columns of a
+// word in the nibble order (0,2,4,6,1,3,5,7): even nibbles = (0,4,1,5), odd =
+// (2,6,3,7); the MLX layout in natural order: even = (0,2,4,6), odd = (1,3,5,7).
+template <bool kNatural>
+__device__ __forceinline__ int fx_byte(int j, int limb) {
+    const int half = j >> 5, jj = j & 31, c = jj >> 3, c8 = jj & 7;
+    const int odd = kNatural ? (c8 & 1) : ((c8 >> 1) & 1);
+    const int kb = kNatural ? (c8 >> 1) : (((c8 & 1) << 1) | (c8 >> 2));
+    return half * 64 + (limb * 8 + odd * 4 + c) * 4 + kb;
+}
+constexpr int kFxGroupBytes = 128;
+
+// One warp packs one 64-column bf16 group (x64, generic address) into
+// dst (128 bytes, generic address; may be x64 itself) and meta = (sum_j X_j
+// 2^-k, 2^-(k+4)).
+template <bool kNatural>
+__device__ __forceinline__ void fx_pack_group_warp(const uint16_t* x64, uint8_t* dst, float2* meta, int lane) {
+    const uint32_t v = reinterpret_cast<const uint32_t*>(x64)[lane];  // columns 2 lane, 2 lane + 1
+    const uint32_t m = max(v & 0x7FFFu, (v >> 16) & 0x7FFFu);
+    const int k = fx_k(__reduce_max_sync(0xffffffffu, m));
+    const int X0 = fx_round(v & 0xFFFFu, k), X1 = fx_round(v >> 16, k);
+    const int sx = __reduce_add_sync(0xffffffffu, X0 + X1);
+    __syncwarp();  // every lane has read its columns before any byte is written
+    dst[fx_byte<kNatural>(2 * lane, 0)] = (uint8_t)(X0 >> 8);
+    dst[fx_byte<kNatural>(2 * lane, 1)] = (uint8_t)(X0 & 255);
+    dst[fx_byte<kNatural>(2 * lane + 1, 0)] = (uint8_t)(X1 >> 8);
+    dst[fx_byte<kNatural>(2 * lane + 1, 1)] = (uint8_t)(X1 & 255);
+    if (lane == 0) *meta = make_float2(__fmul_rn(__int2float_rn(sx), pow2f(-k)), pow2f(-k - 4));
 }
 
-// Weight sources: 128 rows x 64 columns of one block of one expert.
-// Lane l covers rows (l>>1) + 16 i (i < 8) and the 32 columns of half (l & 1).
-// The context's gate/up array is paired: the 128 features of gate/up row tile rt
-// are blocks 2rt and 2rt+1, and feature c of block h sits in row paired_row(c)
-// (gate) and paired_row(c) + 16 (up).  Each row's dot product is the same
-// arithmetic whichever block it sits in; only the final pairing re-indexes.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {  // unsigned a bytes, signed b bytes
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// One 128 x 64 block against one packed group: lane l covers rows
+// (l >> 1) + 16 i (i < 8) and the 32 columns of half (l & 1); the lane pair's
+// integer dots are added exactly; every lane ends with P of its 8 rows.
+// xp: the lane's half of the packed group (16 words).
+__device__ __forceinline__ void block_fx(const uint4 (&q)[8], const float (&sc)[8], const float (&bi)[8],
+                                         const uint32_t* xp, float xs, float sc16, float (&P)[8]) {
+    const uint4 a = reinterpret_cast<const uint4*>(xp)[0], bq = reinterpret_cast<const uint4*>(xp)[1];
+    const uint4 c = reinterpret_cast<const uint4*>(xp)[2], d = reinterpret_cast<const uint4*>(xp)[3];
+    const uint32_t he[4] = {a.x, a.y, a.z, a.w}, ho[4] = {bq.x, bq.y, bq.z, bq.w};
+    const uint32_t le[4] = {c.x, c.y, c.z, c.w}, lo[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t w[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
+        int h0 = 0, h1 = 0;
+        uint32_t l0 = 0, l1 = 0;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            const uint32_t we = w[cc] & 0x0F0F0F0Fu, wo = w[cc] & 0xF0F0F0F0u;
+            h0 = dp4a_us(we, he[cc], h0);
+            h1 = dp4a_us(wo, ho[cc], h1);
+            l0 = __dp4a(we, le[cc], l0);
+            l1 = __dp4a(wo, lo[cc], l1);
+        }
+        int D = (h0 * 16 + h1) * 256 + (int)(l0 * 16u + l1);  // 16 sum q X over the lane's 32 columns
+        D += __shfl_xor_sync(0xffffffffu, D, 1);
+        P[i] = __fmaf_rn(sc[i], __fmul_rn(__int2float_rn(D), sc16), __fmul_rn(bi[i], xs));
+    }
+}
+
+// The tiled gate/up array is paired: the 128 features of gate/up row tile rt
+// are blocks 2rt and 2rt+1; feature c of block h sits in row paired_row(c)
+// (gate) and paired_row(c) + 16 (up).
 __device__ __forceinline__ int paired_row(int c) { return 32 * (c >> 4) + (c & 15); }
+
+// Weight sources: 128 rows x 64 columns of one block of one expert; lane l
+// loads rows (l >> 1) + 16 i and the 16 bytes of half (l & 1).
 struct TiledSrc {  // the context's blocks; nibble order c0,c2,c4,c6,c1,c3,c5,c7
     const uint8_t* base;
     int n_rt, KT, stride, off;  // block (e, rt, kt) = base + (((e*n_rt + rt)*KT + kt)*stride + off) * 4608
     static constexpr bool kNatural = false;
+    __device__ __forceinline__ const uint8_t* block(int e, int rt, int kt) const {
+        return base + ((((size_t)e * n_rt + rt) * KT + kt) * stride + off) * kBlockBytes;
+    }
     __device__ __forceinline__ void load(int e, int rt, int kt, int lane, uint4 (&q)[8], float (&sc)[8],
                                          float (&bi)[8]) const {
-        const uint8_t* blk = base + ((((size_t)e * n_rt + rt) * KT + kt) * stride + off) * kBlockBytes;
+        const uint8_t* blk = block(e, rt, kt);
         const uint4* wq = reinterpret_cast<const uint4*>(blk + (lane & 1) * 2048);
         const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
 #pragma unroll
@@ -69,47 +182,18 @@ struct MlxSrc {  // reference layout: w [E, out, in/8] (column c at nibble c), s
         }
     }
 };
-
-template <class Src>
-__device__ __forceinline__ void block_dot(const Src& src, int e, int rt, int kt, const float (&xr)[32], float xsum,
-                                          int lane, float (&acc)[8]) {
-    uint4 q[8];
-    float sc[8], bi[8];
-    src.load(e, rt, kt, lane, q, sc, bi);
+// a tiled block already in shared memory
+__device__ __forceinline__ void load_block_smem(const uint8_t* blk, int lane, uint4 (&q)[8], float (&sc)[8],
+                                                float (&bi)[8]) {
+    const uint4* wq = reinterpret_cast<const uint4*>(blk + (lane & 1) * 2048);
+    const uint16_t* sb = reinterpret_cast<const uint16_t*>(blk + kBlockWords * 4);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const uint32_t ws[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
-        float f = 0.0f;  // sum_j (1 + q_j/16) x_j over the lane's 32 columns
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                // columns in the order (0,2,4,6,1,3,5,7) of every word for both layouts, so
-                // the two give bit-identical sums: the tiled word holds that column at nibble j,
-                // the MLX word at nibble nib_col(j)
-                const int col = nib_col(j);
-                f = __fmaf_rn(nib_f16th(ws[c], Src::kNatural ? col : j), xr[c * 8 + col], f);
-            }
-        // s * sum q x + b * sum x, with sum q x = 16 (f - sum x)
-        acc[i] = __fmaf_rn(16.0f * sc[i], f - xsum, __fmaf_rn(bi[i], xsum, acc[i]));
+        const int row = (lane >> 1) + 16 * i;
+        q[i] = wq[row];
+        sc[i] = bf2f(sb[row]);
+        bi[i] = bf2f(sb[kRowTile + row]);
     }
-}
-
-__device__ __forceinline__ float load_x32(const uint16_t* __restrict__ x, float (&xr)[32]) {
-    const uint4* p = reinterpret_cast<const uint4*>(x);
-    float sum = 0.0f;
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-        uint4 q = __ldg(p + v);
-        uint32_t qs[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            xr[v * 8 + 2 * c] = __uint_as_float(qs[c] << 16);
-            xr[v * 8 + 2 * c + 1] = __uint_as_float(qs[c] & 0xFFFF0000u);
-            sum += xr[v * 8 + 2 * c] + xr[v * 8 + 2 * c + 1];
-        }
-    }
-    return sum;
 }
 
 // An out-of-range expert id is reported and replaced by 0, so every CTA still
@@ -120,15 +204,73 @@ __device__ __forceinline__ int checked_expert(int e, int E, int* err) {
     return 0;
 }
 
-// grid (I/128, kSplitGU, T*K), 256 threads.  warp w: projection w & 1,
-// k-tiles kt0 + (w >> 1) + 4 j (one block per warp for H = 2048).
+// The last split of gate/up tile (p, rt), 256 threads (t256) synchronising on
+// named barrier bid: g and u summed over the splits in split order from the
+// partials tp[split][2][128], h = bf16(silu(g) u), and h's two 64-feature
+// groups packed into hq/hmeta (pair p's row of I/64 groups) for the down
+// projection's layout.  s_gsum [2][128], s_red [8] shared.
+template <bool kNatural>
+__device__ __forceinline__ void finish_gu_tile(const float* tp, int I, int p, int rt, uint8_t* hq, float2* hmeta,
+                                               float (*s_gsum)[kRowTile], int* s_red, int t256, int bid) {
+    const int pr = t256 >> 7, row = t256 & 127, lane = t256 & 31, w = t256 >> 5;
+    float sum = 0.0f;
+#pragma unroll
+    for (int jj = 0; jj < kSplitGU; ++jj) sum += __ldcg(tp + (size_t)jj * 2 * kRowTile + pr * kRowTile + row);
+    s_gsum[pr][row] = sum;
+    named_bar_sync(bid, 256);
+    uint32_t hb = 0;
+    if (t256 < kRowTile) {
+        float g, u;
+        if (kNatural) {  // the MLX source: projection 0 = gate, 1 = up, rows in feature order
+            g = s_gsum[0][t256], u = s_gsum[1][t256];
+        } else {         // paired blocks: block 2rt + t256/64 holds feature t256
+            const int rr = paired_row(t256 & 63);
+            g = s_gsum[t256 >> 6][rr], u = s_gsum[t256 >> 6][rr + 16];
+        }
+        hb = f2bf(silu_mul(g, u));
+    }
+    if (w < 4) {
+        const uint32_t wm = __reduce_max_sync(0xffffffffu, hb & 0x7FFFu);
+        if (lane == 0) s_red[w] = (int)wm;
+    }
+    named_bar_sync(bid, 256);
+    const int gl = t256 >> 6, gi = p * (I / kGroup) + 2 * rt + gl;
+    int k = 0;
+    if (w < 4) {
+        k = fx_k((uint32_t)max(s_red[2 * gl], s_red[2 * gl + 1]));
+        const int X = fx_round(hb, k), c = t256 & 63;
+        uint8_t* dst = hq + (size_t)gi * kFxGroupBytes;
+        dst[fx_byte<kNatural>(c, 0)] = (uint8_t)(X >> 8);
+        dst[fx_byte<kNatural>(c, 1)] = (uint8_t)(X & 255);
+        const int ws = __reduce_add_sync(0xffffffffu, X);
+        if (lane == 0) s_red[4 + w] = ws;
+    }
+    named_bar_sync(bid, 256);
+    if (w < 4 && (t256 & 63) == 0)
+        hmeta[gi] = make_float2(__fmul_rn(__int2float_rn(s_red[4 + 2 * gl] + s_red[5 + 2 * gl]), pow2f(-k)),
+                                pow2f(-k - 4));
+}
+
+// Fixed-point packs of T activation rows: one warp per 64-column group.
+template <bool kNatural>
+__global__ void __launch_bounds__(256) k_fx_pack(const uint16_t* __restrict__ x, int T, int H, uint8_t* xq,
+                                                 float2* xmeta) {
+    pdl_begin();
+    const int G = H / kGroup, item = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (item >= T * G) return;
+    fx_pack_group_warp<kNatural>(x + (size_t)item * kGroup, xq + (size_t)item * kFxGroupBytes, xmeta + item,
+                                 threadIdx.x & 31);
+}
+
+// grid (I/128, kSplitGU, T*K), 256 threads.  warp w: block half / projection
+// w & 1, groups kt0 + (w >> 1) + 4 j of the split.
 template <class Src>
-__global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const uint16_t* __restrict__ x,
-                                                       const int32_t* __restrict__ ids, int H, int I, int K, int E,
-                                                       DecodeBufs d) {
+__global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const int32_t* __restrict__ ids, int H,
+                                                       int I, int K, int E, DecodeBufs d) {
     pdl_begin();
     __shared__ float s_part[8][kRowTile];
-    __shared__ float s_gu[2][kRowTile];
+    __shared__ float s_gsum[2][kRowTile];
+    __shared__ int s_red[8];
     __shared__ int s_last;
     const int rt = blockIdx.x, ks = blockIdx.y, p = blockIdx.z;
     const int n_rt = gridDim.x, KT = H / kGroup, nkt = KT / kSplitGU;
@@ -137,17 +279,21 @@ __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int j = (w >> 1); j < nkt; j += 4) {
         const int kt = ks * nkt + j;
-        float xr[32];
-        const float xs = load_x32(x + (size_t)t * H + kt * kGroup + (lane & 1) * 32, xr);
-        block_dot(proj ? usrc : gsrc, e, Src::kNatural ? rt : 2 * rt + proj, kt, xr, xs, lane, acc);
-    }
+        uint4 q[8];
+        float sc[8], bi[8], P[8];
+        (proj ? usrc : gsrc).load(e, Src::kNatural ? rt : 2 * rt + proj, kt, lane, q, sc, bi);
+        const size_t gi = (size_t)t * KT + kt;
+        const float2 m = d.xmeta[gi];
+        block_fx(q, sc, bi, reinterpret_cast<const uint32_t*>(d.xq + gi * kFxGroupBytes + (lane & 1) * 64), m.x,
+                 m.y, P);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        float v = acc[i] + __shfl_xor_sync(0xffffffffu, acc[i], 1);
-        if ((lane & 1) == 0) s_part[w][(lane >> 1) + 16 * i] = v;
+        for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], P[i]);
     }
+    if ((lane & 1) == 0)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s_part[w][(lane >> 1) + 16 * i] = acc[i];
     __syncthreads();
-    // fixed-order sum of the 4 warps of each projection (paired blocks: of each block)
+    // fixed-order sum of the 4 warps of each projection
     const int pr = tid >> 7, row = tid & 127;
     const float v = ((s_part[pr][row] + s_part[pr + 2][row]) + s_part[pr + 4][row]) + s_part[pr + 6][row];
     float* part = d.part + (((size_t)p * n_rt + rt) * kSplitGU) * 2 * kRowTile;
@@ -156,31 +302,17 @@ __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const
     __syncthreads();
     if (tid == 0) {
         uint32_t* c = d.cnt_gu + (size_t)p * n_rt + rt;
-        unsigned old = atomicAdd(c, 1u);
+        const unsigned old = atomicAdd(c, 1u);
         s_last = (old == kSplitGU - 1);
         if (s_last) *c = 0;  // ready for the next call
     }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    float sum = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kSplitGU; ++j) sum += __ldcg(part + (size_t)j * 2 * kRowTile + pr * kRowTile + row);
-    s_gu[pr][row] = sum;
-    __syncthreads();
-    if (tid < kRowTile) {
-        float g, u;
-        if constexpr (Src::kNatural) {
-            g = s_gu[0][tid], u = s_gu[1][tid];
-        } else {
-            const int rr = paired_row(tid & 63);  // block 2rt + tid/64 holds feature tid
-            g = s_gu[tid >> 6][rr], u = s_gu[tid >> 6][rr + 16];
-        }
-        d.h[(size_t)p * I + rt * kRowTile + tid] = f2bf(silu_mul(g, u));
-    }
+    finish_gu_tile<Src::kNatural>(part, I, p, rt, d.hq, d.hmeta, s_gsum, s_red, tid, 0);
 }
 
-// grid (H/128, K, T), 32 * min(I/64, 16) threads.  warp w: k-tiles w, w + nwarps, ...
+// grid (H/128, K, T), 32 * min(I/64, 16) threads.  warp w: groups w, w + nwarps, ...
 template <class Src>
 __global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __restrict__ ids,
                                                      const float* __restrict__ wts,
@@ -196,19 +328,27 @@ __global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int kt = w; kt < KT; kt += nwarps) {
-        float xr[32];
-        const float xs = load_x32(d.h + (size_t)p * I + kt * kGroup + (lane & 1) * 32, xr);
-        block_dot(dsrc, e, rt, kt, xr, xs, lane, acc);
-    }
+        uint4 q[8];
+        float sc[8], bi[8], P[8];
+        dsrc.load(e, rt, kt, lane, q, sc, bi);
+        const size_t gi = (size_t)p * KT + kt;
+        const float2 m = __ldcg(d.hmeta + gi);
+        uint32_t xp[16];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        float v = acc[i] + __shfl_xor_sync(0xffffffffu, acc[i], 1);
-        if ((lane & 1) == 0) s_part[w][(lane >> 1) + 16 * i] = v;
+        for (int v = 0; v < 4; ++v)
+            reinterpret_cast<uint4*>(xp)[v] =
+                __ldcg(reinterpret_cast<const uint4*>(d.hq + gi * kFxGroupBytes + (lane & 1) * 64) + v);
+        block_fx(q, sc, bi, xp, m.x, m.y, P);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], P[i]);
     }
+    if ((lane & 1) == 0)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s_part[w][(lane >> 1) + 16 * i] = acc[i];
     __syncthreads();
     for (int r = tid; r < kRowTile; r += blockDim.x) {  // blockDim may be below 128 (inter = 128)
         float v = 0.0f;
-        for (int j = 0; j < nwarps; ++j) v += s_part[j][r];
+        for (int j = 0; j < nwarps; ++j) v = __fadd_rn(v, s_part[j][r]);
         d.y[(size_t)p * H + rt * kRowTile + r] = f2bf(v);
     }
     if (!do_combine) return;
@@ -216,7 +356,7 @@ __global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __
     __syncthreads();
     if (tid == 0) {
         uint32_t* c = d.cnt_dn + (size_t)t * n_rt + rt;
-        unsigned old = atomicAdd(c, 1u);
+        const unsigned old = atomicAdd(c, 1u);
         s_last = (old == (unsigned)K - 1);
         if (s_last) *c = 0;
     }
@@ -238,112 +378,155 @@ __global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __
 int down_threads(int I) { return 32 * (I / kGroup < 16 ? I / kGroup : 16); }
 
 // ----------------------------------------------------------- fused decode layer
-// One cooperative launch runs the whole decode layer for T <= 4 tokens, so the
-// step pays one launch instead of four dependent ones.  One CTA of 16 warps per
-// SM; work units go round-robin over the CTAs first, so every SM works.
-//   A  router logits: one warp per (expert, 8-token chunk), canonical order;
-//      grid barrier;
-//   B  top-k: every CTA computes the routes of all T tokens itself (identical,
-//      deterministic), so no barrier follows;
-//   C  gate/up: each half-CTA (8 warps) runs one CTA of k_decode_gateup -- a
-//      (pair, row tile, split) unit, its shared-memory reduction, and, in the
-//      last split to arrive, the split sum and SwiGLU over 256 threads;
-//      grid barrier;
-//   D  down: each CTA runs one CTA of k_decode_down -- a (pair, row tile) unit,
-//      y, and in the last pair of a (token, row tile) the rank-order combine.
-// The arithmetic is that of the separate decode kernels, term for term, so the
-// two forms give identical outputs.  Barriers wait at most 2 s.
+// One cooperative launch runs the whole decode layer for T <= 4 tokens, one
+// CTA of 16 warps per SM, with no grid-wide barrier:
+//   0  each CTA takes a ticket (launch generation = ticket / grid size), loads
+//      its router row (expert b) into registers, then the layer input
+//      (RMSNormed with `normalize`) into shared memory;
+//   A  router logits of expert b, canonical order, stored with the launch's
+//      stamp in four replicas;
+//   B  warps t < T poll token t's stamped logits and run top-k (every CTA, the
+//      same result); the other warps meanwhile pack the input groups in fixed
+//      point; then lanes of warp 0 issue bulk copies of the CTA's first wave
+//      of gate/up units and its first down unit, so the layer's weights
+//      (about 21 MB at T = 1) are in flight together right after routing;
+//   C  gate/up in waves of up to kGuUnits units (pair p, row tile rt, split
+//      ks; 8 blocks each): every warp computes blocks, then the CTA reduces
+//      the wave, publishes the split partials, and the last split of a tile
+//      forms its SwiGLU row in fixed point and stamps the tile ready;
+//   D  down units (pair p, row tile) of I/64 blocks, already in shared
+//      memory, each waiting only for the stamps of its own pair's h tiles;
+//      y, and the last pair of a (token, row tile) does the rank-order combine.
+// Every wait is bounded (wait_ns); copies still in flight are drained before a
+// CTA exits after a wait gave up.
 constexpr int kFusedThreads = 512, kFusedWarps = kFusedThreads / 32;
+constexpr int kMaxDnSlots = 4;       // down-unit slots in the ring region
+constexpr int kLogitReplicas = 4;    // copies of the stamped logits (spreads the polling)
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// (logit bits | stamp << 32) as one 64-bit access: single-copy atomic, and
+// "relaxed" at gpu scope, so the polling sees other SMs' stores (a weak load
+// may keep returning a stale copy)
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
-// every CTA of the grid; false (error flag set) after a timeout.  The arrival
-// counter only grows (launch n's barriers wait for (2n+1)G and (2n+2)G arrivals,
-// n the generation read at the start), so no launch needs it cleared; the
-// comparison is wrap-safe.
-__device__ bool grid_sync(uint32_t* bar, uint32_t target, int* err, uint64_t limit_ns) {
-    __shared__ int s_ok;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(bar, 1u);
-        int ok = 1;
-        const uint64_t t0 = global_ns();
-        while ((int)(ld_acquire_gpu(bar) - target) < 0) {
-            if (global_ns() - t0 > limit_ns) {
-                ok = 0;
-                atomicExch(err, kDevTimeout);
-                break;
+// Router row of expert e (H = 2048: one 64-column group per lane), loaded into
+// registers before anything else so its latency overlaps the input's.
+struct RouterRow {
+    uint4 q[4];
+    float sc, bi;
+};
+__device__ __forceinline__ void router_row_load(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
+                                                const uint16_t* __restrict__ b, int H, int e, int lane,
+                                                RouterRow& r) {
+    const int G = H / kGroup;
+    const uint4* wr = reinterpret_cast<const uint4*>(w + (size_t)e * (H / 4) + (size_t)lane * 16);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) r.q[v] = __ldg(wr + v);
+    r.sc = bf2f(__ldg(s + (size_t)e * G + lane));
+    r.bi = bf2f(__ldg(b + (size_t)e * G + lane));
+}
+// router_warp_item's arithmetic for one group per lane, x in shared memory;
+// lanes r < 4 store (logit, stamp) of every token into replica r
+__device__ __forceinline__ void router_row_logits(const RouterRow& r, const uint16_t* x, int T, int H, int E, int e,
+                                                  int lane, uint32_t stamp, uint64_t* lst) {
+    float wf[64];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        const uint32_t qs[4] = {r.q[v].x, r.q[v].y, r.q[v].z, r.q[v].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) wf[v * 16 + c * 4 + j] = __fmaf_rn((float)((qs[c] >> (8 * j)) & 0xFFu), r.sc, r.bi);
+    }
+    for (int t = 0; t < T; ++t) {
+        const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)t * H + (size_t)lane * 64);
+        float a = 0.0f;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            const uint4 q = xr[v];
+            const uint32_t qs[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                a = __fmaf_rn(wf[v * 8 + c * 2], __uint_as_float(qs[c] << 16), a);
+                a = __fmaf_rn(wf[v * 8 + c * 2 + 1], __uint_as_float(qs[c] & 0xFFFF0000u), a);
             }
         }
-        s_ok = ok;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if (lane < kLogitReplicas)
+            st_relaxed_u64(lst + ((size_t)lane * kFusedMaxT + t) * E + e,
+                           (uint64_t)__float_as_uint(a) | ((uint64_t)stamp << 32));
     }
-    __syncthreads();
-    return s_ok != 0;
 }
 
-// load_x32 from shared memory (or any generic address)
-__device__ __forceinline__ float load_x32_gen(const uint16_t* x, float (&xr)[32]) {
-    const uint4* p = reinterpret_cast<const uint4*>(x);
-    float sum = 0.0f;
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-        uint4 q = p[v];
-        uint32_t qs[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            xr[v * 8 + 2 * c] = __uint_as_float(qs[c] << 16);
-            xr[v * 8 + 2 * c + 1] = __uint_as_float(qs[c] & 0xFFFF0000u);
-            sum += xr[v * 8 + 2 * c] + xr[v * 8 + 2 * c + 1];
-        }
-    }
-    return sum;
-}
-
-// load_x32 for data written earlier in this kernel (read through L2)
-__device__ __forceinline__ float load_x32_cg(const uint16_t* __restrict__ x, float (&xr)[32]) {
-    const uint4* p = reinterpret_cast<const uint4*>(x);
-    float sum = 0.0f;
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-        uint4 q = __ldcg(p + v);
-        uint32_t qs[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            xr[v * 8 + 2 * c] = __uint_as_float(qs[c] << 16);
-            xr[v * 8 + 2 * c + 1] = __uint_as_float(qs[c] & 0xFFFF0000u);
-            sum += xr[v * 8 + 2 * c] + xr[v * 8 + 2 * c + 1];
-        }
-    }
-    return sum;
+// bounded wait on an mbarrier phase that ignores the abort flag (draining
+// copies in flight before the CTA exits)
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (global_ns() - t0 > limit_ns) return;
 }
 
 __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
     const uint32_t* __restrict__ rw, const uint16_t* __restrict__ rs, const uint16_t* __restrict__ rb,
     TiledSrc gsrc, TiledSrc dsrc, const uint16_t* __restrict__ x_in, const uint16_t* __restrict__ residual,
     const float* __restrict__ bias, int T, int H, int I, int E, int K, int norm, int normalize, float eps,
-    FusedDecodeBufs f, uint16_t* __restrict__ out) {
-    extern __shared__ __align__(16) uint16_t s_x[];  // [T][H] the layer input, this CTA's copy
+    FusedDecodeBufs f, FusedPlan pl, uint16_t* __restrict__ out) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    // [T][H] bf16 layer input; after phase A, in place, its fixed-point packs [T][H/64][128 B]
+    uint16_t* s_x = reinterpret_cast<uint16_t*>(smem + pl.off_x);
+    uint8_t* s_xq = smem + pl.off_x;
+    uint8_t* s_hq = smem + pl.off_h;  // [units][I/64][128 B] packed h rows of a down batch
+    __shared__ float2 s_xm[kFusedMaxT * 32];
+    __shared__ float2 s_hm[48];
     __shared__ float s_sq[2][256];
     __shared__ int s_ids[kFusedMaxT * kMaxK];
     __shared__ float s_wts[kFusedMaxT * kMaxK];
-    __shared__ float s_part[kFusedWarps][kRowTile];  // C: [half][8 warps]; D: [16 warps]
-    __shared__ int s_last[1];
+    __shared__ float s_blk[48][kRowTile];  // per-block row values: C a tile's 32, D a batch's units
+    __shared__ float s_gsum[1][1][kRowTile];
+    __shared__ int s_red[2][8];
+    __shared__ __align__(8) uint64_t s_bar[8 + kMaxDnSlots];  // ring slots, down slots
+    __shared__ int s_issued[8 + kMaxDnSlots];                 // copies issued per slot
+    __shared__ int s_lastd[kMaxDnSlots];
+    __shared__ uint32_t s_gen;
+    __shared__ volatile int s_abort;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, b = blockIdx.x;
-    // phase timeline (diagnostics): start, A done, barrier 1, B done, C done, barrier 2, D done
+    // phase timeline (diagnostics, thread 0 of each CTA, 24 entries per CTA): 0 start, 1 A done,
+    // 2 logits seen, 3 copies issued, 4 C done, 5 first h ready, 6 D done, 7 top-k + packs done;
+    // 8 first wave landed, 9 computed, 10 done; 13 first down unit landed, 14 y written;
+    // 16-18 inside top-k (logits in, softmax sum, selection)
     auto mark = [&](int k) {
-        if (f.trace && tid == 0) f.trace[8 * b + k] = global_ns();
+        if (f.trace && tid == 0) f.trace[24 * b + k] = global_ns();
     };
     mark(0);
-    // barrier generation of this launch (advanced by CTA 0 after the last barrier)
-    const uint32_t gen = *reinterpret_cast<volatile uint32_t*>(f.bar + 1);
+    if (tid == 0) {
+        s_gen = atomicAdd(f.bar, 1u) / (uint32_t)G;  // every CTA of launch n draws a ticket in [nG, (n+1)G)
+        for (int i = 0; i < 8 + kMaxDnSlots; ++i) mbar_init(smem_u32(&s_bar[i]), 1), s_issued[i] = 0;
+        s_abort = 0;
+        fence_mbar_init();
+        fence_proxy_async_smem();
+    }
+    // 0a: this CTA's router rows (experts b, b + G, ...: one per warp) into registers
+    RouterRow rrow;
+    const int e_r = b + G * warp;
+    if (e_r < E) router_row_load(rw, rs, rb, H, e_r, lane, rrow);
 
-    // 0: the layer input into shared memory; with `normalize`, the MoE input
+    // 0b: the layer input into shared memory; with `normalize`, the MoE input
     // RMSNorm of rmsnorm.metal:9-37 in k_rmsnorm's order (256 threads per row,
     // strided rounded squares, halving tree, IEEE divide and square root)
     for (int t0 = 0; t0 < T; t0 += 2) {
@@ -373,157 +556,293 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
         }
     }
     __syncthreads();
-    const uint16_t* x = s_x;
+    const uint32_t stamp = s_gen + 1;
 
-    // A: router logits; item i on warp i / G of CTA i % G
-    const int n_tc = (T + kWarpTok - 1) / kWarpTok;
-    for (int item = warp * G + b; item < E * n_tc; item += kFusedWarps * G)
-        router_warp_item<true>(rw, rs, rb, x, T, H, E, item % E, (item / E) * kWarpTok, lane, f.logits);
+    // A: router logits, stamped
+    if (e_r < E) router_row_logits(rrow, s_x, T, H, E, e_r, lane, stamp, f.lst);
     mark(1);
-    if (!grid_sync(f.bar, (2 * gen + 1) * G, f.err, f.wait_ns)) return;
-    mark(2);
+    __syncthreads();  // the router has read s_x: it may be packed in place
 
-    // B: top-k of every token, in every CTA
+    const int KT = H / kGroup, nkt = KT / kSplitGU, P = T * K;
+    // gate/up work: tiles (p, r2) -- pair p's 64-feature block row r2 (both its gate
+    // and up rows), all 8 splits = 32 blocks -- on CTAs b, b + G, ...; each tile
+    // streams through an 8-slot ring as 8 units (one split = 4 contiguous blocks)
+    const int n_r2 = I / kGroup, n_tiles = P * n_r2;
+    const int Nt = b < n_tiles ? (n_tiles - 1 - b) / G + 1 : 0;
+    const int n_rd = H / kRowTile, KTd = I / kGroup, nwd = KTd < 16 ? KTd : 16, D = P * n_rd;
+    // down units (pair p, row tile) round-robin over the CTAs, those with fewer
+    // tiles first (CTAs b >= n_tiles mod G): d = pos(b) + m G
+    const int dfirst = (b - n_tiles % G + G) % G, dstep = G;
+    const int Nd = dfirst < D ? (D - 1 - dfirst) / dstep + 1 : 0;
+    const int nslot = pl.nslot;  // down slots in the region
+    uint8_t* region = smem + pl.off_ring;
+    // unit v of this CTA's tiles: tile v / 8, split v % 8, ring slot v % 8
+    auto issue_unit = [&](int v) {
+        const int tau = b + (v >> 3) * G, ks = v & 7;
+        const int p = tau / n_r2, r2 = tau % n_r2;
+        const int e = checked_expert(s_ids[p], E, f.err);
+        const uint32_t bar = smem_u32(&s_bar[v & 7]);
+        mbar_arrive_expect_tx(bar, (uint32_t)pl.unit_bytes);
+        bulk_g2s(smem_u32(region + (size_t)(v & 7) * pl.unit_bytes), gsrc.block(e, r2, ks * nkt),
+                 (uint32_t)pl.unit_bytes, bar);
+        ++s_issued[v & 7];
+    };
+    // this CTA's m-th down unit, slot m % nslot
+    auto issue_dn = [&](int m) {
+        const int d = dfirst + m * dstep;
+        const int p = d / n_rd, rt = d % n_rd, si = m % nslot;
+        const int e = checked_expert(s_ids[p], E, f.err);
+        const uint32_t bar = smem_u32(&s_bar[8 + si]);
+        mbar_arrive_expect_tx(bar, (uint32_t)pl.dn_bytes);
+        bulk_g2s(smem_u32(region + (size_t)si * pl.dn_bytes), dsrc.block(e, rt, 0), (uint32_t)pl.dn_bytes, bar);
+        ++s_issued[8 + si];
+    };
+    // warp 0 issues everything there is room for: the first tile's 8 units, or
+    // (a CTA without tiles) its first down units -- one copy per lane
+    auto issue_first = [&]() {
+        if (Nt > 0) {
+            if (lane < 8) issue_unit(lane);
+        } else if (lane < nslot && lane < Nd) {
+            issue_dn(lane);
+        }
+    };
     if (warp < T) {
+        // B: token `warp`'s logits from replica b % 4, once all carry this launch's stamp
         const int t = warp;
-        auto logit = [&](int e) { return __ldcg(f.logits + (size_t)t * E + e); };
+        const uint64_t* src = f.lst + ((size_t)(b % kLogitReplicas) * kFusedMaxT + t) * E;
+        float lv[kMaxE / 32];
+        const uint64_t t0 = global_ns();
+        for (;;) {
+            bool ok = true;
+#pragma unroll
+            for (int i = 0; i < kMaxE / 32; ++i) {
+                const int e = lane + 32 * i;
+                lv[i] = 0.0f;
+                if (e < E) {
+                    const uint64_t v = ld_relaxed_u64(src + e);
+                    lv[i] = __uint_as_float((uint32_t)v);
+                    ok = ok && (uint32_t)(v >> 32) == stamp;
+                }
+            }
+            if (__all_sync(0xffffffffu, ok)) break;
+            if (global_ns() - t0 > f.wait_ns) {
+                if (lane == 0) atomicExch(f.err, kDevTimeout);
+                s_abort = 1;
+                break;
+            }
+        }
+        if (t == 0) mark(2);
         int ik;
         float wk;
-        topk_token(logit, bias, E, K, norm, lane, &ik, &wk);
+        topk_token([&](int i, int) { return lv[i]; }, bias, E, K, norm, lane, &ik, &wk,
+                   [&](int k) { mark(16 + k); });
         if (lane < K) {
             s_ids[t * K + lane] = ik;
             s_wts[t * K + lane] = wk;
             if (b == 0) f.ids[t * K + lane] = ik, f.wts[t * K + lane] = wk;
         }
+        if (T == 1 && !s_abort) {
+            // one token: this warp holds every route, so the weight copies go out now
+            __syncwarp();
+            issue_first();
+            mark(3);
+        }
+    } else {
+        // the input groups in fixed point, in place (tiled order)
+        for (int it = warp - T; it < T * KT; it += kFusedWarps - T)
+            fx_pack_group_warp<false>(s_x + (size_t)it * kGroup, s_xq + (size_t)it * kFxGroupBytes, &s_xm[it],
+                                      lane);
     }
     __syncthreads();
-    mark(3);
+    mark(7);
+    if (T > 1 && warp == 0 && !s_abort) issue_first();
 
-    // C: gate/up -- half-CTA h takes units (pair p, row tile rt, split ks) like one
-    // CTA of k_decode_gateup: warp w8 = block half (w8 & 1) of paired blocks
-    // 2rt, 2rt+1, k-tiles ks*nkt + (w8 >> 1) + 4j
-    {
-        const int h = warp >> 3, w8 = warp & 7, t256 = tid & 255, half = w8 & 1;
-        const int n_rt = I / kRowTile, KT = H / kGroup, nkt = KT / kSplitGU, n_pairs = T * K;
-        const int units = n_pairs * n_rt * kSplitGU;
-        float* part = f.part_gu;  // [p][rt][ks][2][128]
-        for (int u = h * G + b; u < units; u += 2 * G) {
-            const int ks = u % kSplitGU, rt = (u / kSplitGU) % n_rt, p = u / (kSplitGU * n_rt);
-            const int t = p / K, e = checked_expert(s_ids[p], E, f.err);
-            float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int j = (w8 >> 1); j < nkt; j += 4) {
-                const int kt = ks * nkt + j;
-                float xr[32];
-                const float xs = load_x32_gen(x + (size_t)t * H + kt * kGroup + (lane & 1) * 32, xr);
-                block_dot(gsrc, e, 2 * rt + half, kt, xr, xs, lane, acc);
-            }
+    // C: gate/up tiles.  32 blocks per tile, warp w takes blocks w and w + 16
+    // (split bi / 4, group ks * 4 + bi % 4); each row's value is summed over the
+    // splits in order, each split's 4 groups as ((P0 + P1) + P2) + P3 (the
+    // separate kernel's order); then SwiGLU over the 64 features, h in fixed
+    // point, and the tile's stamp.
+    for (int i = 0; i < Nt; ++i) {
+        const int tau = b + i * G, p = tau / n_r2, r2 = tau % n_r2, t = p / K;
+        for (int bi = warp; bi < 32; bi += kFusedWarps) {
+            const int ks = bi >> 2, j = bi & 3, v = 8 * i + ks, kt = ks * nkt + j;
+            if (!s_abort && mbar_wait(smem_u32(&s_bar[v & 7]), (uint32_t)(v >> 3) & 1u, &s_abort, 1, f.wait_ns)) {
+                if (i == 0 && bi == 0) mark(8);
+                uint4 q[8];
+                float sc[8], bv[8], Pv[8];
+                load_block_smem(region + (size_t)(v & 7) * pl.unit_bytes + (size_t)j * kBlockBytes, lane, q, sc, bv);
+                const int gi = t * KT + kt;
+                block_fx(q, sc, bv, reinterpret_cast<const uint32_t*>(s_xq + (size_t)gi * kFxGroupBytes + (lane & 1) * 64),
+                         s_xm[gi].x, s_xm[gi].y, Pv);
+                if ((lane & 1) == 0)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float v = acc[i] + __shfl_xor_sync(0xffffffffu, acc[i], 1);
-                if ((lane & 1) == 0) s_part[h * 8 + w8][(lane >> 1) + 16 * i] = v;
+                    for (int r = 0; r < 8; ++r) s_blk[bi][(lane >> 1) + 16 * r] = Pv[r];
             }
-            named_bar_sync(1 + h, 256);
-            // fixed-order sum of the 4 warps of each block; the split partials meet in
-            // phase D, after the grid barrier has published them
-            const int pr = t256 >> 7, row = t256 & 127;
-            const float* sp = &s_part[h * 8][0];
-            const float v = ((sp[pr * kRowTile + row] + sp[(pr + 2) * kRowTile + row]) + sp[(pr + 4) * kRowTile + row]) +
-                            sp[(pr + 6) * kRowTile + row];
-            float* tp = part + (((size_t)p * n_rt + rt) * kSplitGU) * 2 * kRowTile;
-            tp[(size_t)ks * 2 * kRowTile + pr * kRowTile + row] = v;
-            named_bar_sync(1 + h, 256);  // s_part free for the next unit
         }
+        __syncthreads();
+        if (i == 0) mark(9);
+        // the ring is free: the next tile's units, or after the last tile the
+        // first down units, go out now
+        if (warp == 0 && !s_abort) {
+            if (i + 1 < Nt) {
+                if (lane < 8) {
+                    fence_proxy_async_smem();
+                    issue_unit(8 * (i + 1) + lane);
+                }
+            } else if (lane < nslot && lane < Nd) {
+                fence_proxy_async_smem();
+                issue_dn(lane);
+            }
+        }
+        if (tid < kRowTile) {
+            float sum = 0.0f;
+#pragma unroll
+            for (int ks = 0; ks < kSplitGU; ++ks)
+                sum += ((s_blk[4 * ks][tid] + s_blk[4 * ks + 1][tid]) + s_blk[4 * ks + 2][tid]) + s_blk[4 * ks + 3][tid];
+            s_gsum[0][0][tid] = sum;
+        }
+        __syncthreads();
+        // SwiGLU of the 64 features (rows paired_row(c) and + 16), fixed point, stamp
+        if (warp < 2) {
+            const int rr = paired_row(tid);
+            const uint32_t hb = f2bf(silu_mul(s_gsum[0][0][rr], s_gsum[0][0][rr + 16]));
+            const uint32_t wm = __reduce_max_sync(0xffffffffu, hb & 0x7FFFu);
+            if (lane == 0) s_red[0][warp] = (int)wm;
+            named_bar_sync(1, 64);
+            const int k = fx_k((uint32_t)max(s_red[0][0], s_red[0][1]));
+            const int X = fx_round(hb, k);
+            const size_t gi = (size_t)p * n_r2 + r2;
+            uint8_t* dst = f.hq + gi * kFxGroupBytes;
+            dst[fx_byte<false>(tid, 0)] = (uint8_t)(X >> 8);
+            dst[fx_byte<false>(tid, 1)] = (uint8_t)(X & 255);
+            const int ws = __reduce_add_sync(0xffffffffu, X);
+            if (lane == 0) s_red[1][warp] = ws;
+            named_bar_sync(1, 64);
+            if (tid == 0)
+                f.hmeta[gi] = make_float2(__fmul_rn(__int2float_rn(s_red[1][0] + s_red[1][1]), pow2f(-k)), pow2f(-k - 4));
+            __threadfence();
+            named_bar_sync(1, 64);
+            if (tid == 0) st_release_gpu(f.hstamp + gi, stamp);
+        }
+        __syncthreads();  // s_blk, s_gsum free for the next tile
+        if (i == 0) mark(10);
     }
     mark(4);
-    if (!grid_sync(f.bar, (2 * gen + 2) * G, f.err, f.wait_ns)) return;
-    mark(5);
-    // every CTA read `gen` before the first barrier: the next launch may use the next one
-    if (b == 0 && tid == 0) *reinterpret_cast<volatile uint32_t*>(f.bar + 1) = gen + 1;
 
-    // D: down -- CTA units (pair p, row tile rt) like one CTA of k_decode_down
-    {
-        const int n_rd = H / kRowTile, KTd = I / kGroup, nwd = KTd < 16 ? KTd : 16, n_pairs = T * K;
-        const int n_rt = I / kRowTile;
-        uint16_t* s_h = s_x + (size_t)T * H;  // [I] this unit's SwiGLU input row, bf16
-        int p_h = -1;                          // the pair s_h holds
-        for (int u = b; u < n_pairs * n_rd; u += G) {
-            const int rt = u % n_rd, p = u / n_rd, t = p / K;
-            const int e = checked_expert(s_ids[p], E, f.err);
-            if (p != p_h) {
-                // h of pair p: gate and up summed over the k-splits in split order, then
-                // SwiGLU (the last-split step of k_decode_gateup, term for term)
-                for (int i = tid; i < I; i += kFusedThreads) {
-                    const int rg = i / kRowTile, tt = i % kRowTile, pr = tt >> 6, rr = paired_row(tt & 63);
-                    const float* tp = f.part_gu + (((size_t)p * n_rt + rg) * kSplitGU) * 2 * kRowTile + pr * kRowTile;
-                    float g = 0.0f, uu = 0.0f;
-#pragma unroll
-                    for (int jj = 0; jj < kSplitGU; ++jj) {
-                        g += __ldcg(tp + (size_t)jj * 2 * kRowTile + rr);
-                        uu += __ldcg(tp + (size_t)jj * 2 * kRowTile + rr + 16);
-                    }
-                    s_h[i] = f2bf(silu_mul(g, uu));
+    // D: down units d = dfirst + m dstep (the first batch already issued, by
+    // warp 0 at top-k or after the CTA's last tile), in batches of up to nslot resident
+    // units: the stamps of every unit's pair, the h rows, all blocks of the
+    // batch (warp w: blocks w, w + 16, ...), then y = sum_kt P_kt in order per
+    // unit, one fence for the batch's counters, and the rank-order combine by
+    // the last pair of each (token, row tile)
+    for (int m0 = 0; m0 < Nd; m0 += nslot) {
+        const int nb = Nd - m0 < nslot ? Nd - m0 : nslot;
+        if (tid < nb * n_r2 && !s_abort) {
+            const int u = tid / n_r2, g = tid % n_r2, p = (dfirst + (m0 + u) * dstep) / n_rd;
+            const uint32_t* sp = f.hstamp + (size_t)p * n_r2 + g;
+            const uint64_t t0 = global_ns();
+            while (ld_acquire_gpu(sp) != stamp)
+                if (global_ns() - t0 > f.wait_ns) {
+                    atomicExch(f.err, kDevTimeout);
+                    s_abort = 2;
+                    break;
                 }
-                __syncthreads();
-                p_h = p;
-            }
-            if (warp < nwd) {
-                float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                for (int kt = warp; kt < KTd; kt += nwd) {
-                    float xr[32];
-                    const float xs = load_x32_gen(s_h + kt * kGroup + (lane & 1) * 32, xr);
-                    block_dot(dsrc, e, rt, kt, xr, xs, lane, acc);
-                }
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float v = acc[i] + __shfl_xor_sync(0xffffffffu, acc[i], 1);
-                    if ((lane & 1) == 0) s_part[warp][(lane >> 1) + 16 * i] = v;
-                }
-            }
-            __syncthreads();
-            if (tid < kRowTile) {
-                float v = 0.0f;
-                for (int j = 0; j < nwd; ++j) v += s_part[j][tid];
-                f.y[(size_t)p * H + rt * kRowTile + tid] = f2bf(v);
-            }
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) {
-                uint32_t* c = f.cnt_dn + (size_t)t * n_rd + rt;
-                const unsigned old = atomicAdd(c, 1u);
-                s_last[0] = (old == (unsigned)K - 1);
-                if (s_last[0]) *c = 0;
-            }
-            __syncthreads();
-            if (s_last[0]) {
-                __threadfence();
-                if (tid < kRowTile) {
-                    // rank-order combine, same operation order as k_combine (forward.rs:225-232)
-                    const int fo = rt * kRowTile + tid;
-                    float a = residual ? bf2f(residual[(size_t)t * H + fo]) : 0.0f;
-                    for (int jk = 0; jk < K; ++jk) {
-                        const uint16_t yv = __ldcg(f.y + ((size_t)t * K + jk) * H + fo);
-                        a = __fmaf_rn(s_wts[t * K + jk], bf2f(yv), a);
-                    }
-                    out[(size_t)t * H + fo] = f2bf(a);
-                }
-            }
-            __syncthreads();  // s_part / s_last free for the next unit
         }
+        __syncthreads();
+        if (m0 == 0) mark(5);
+        if (s_abort) break;
+        for (int i = tid; i < nb * KTd * (kFxGroupBytes / 16); i += kFusedThreads) {
+            const int u = i / (KTd * (kFxGroupBytes / 16)), r = i % (KTd * (kFxGroupBytes / 16));
+            const int p = (dfirst + (m0 + u) * dstep) / n_rd;
+            reinterpret_cast<uint4*>(s_hq)[i] =
+                __ldcg(reinterpret_cast<const uint4*>(f.hq + (size_t)p * KTd * kFxGroupBytes) + r);
+        }
+        if (tid < nb * KTd) {
+            const int u = tid / KTd, p = (dfirst + (m0 + u) * dstep) / n_rd;
+            s_hm[tid] = __ldcg(f.hmeta + (size_t)p * KTd + tid % KTd);
+        }
+        __syncthreads();
+        for (int bi = warp; bi < nb * KTd; bi += kFusedWarps) {
+            const int u = bi / KTd, kt = bi % KTd, m = m0 + u, si = m % nslot;
+            if (!s_abort && mbar_wait(smem_u32(&s_bar[8 + si]), (uint32_t)(m / nslot) & 1u, &s_abort, 3, f.wait_ns)) {
+                if (m0 == 0 && bi == 0) mark(13);
+                uint4 q[8];
+                float sc[8], bv[8], Pv[8];
+                load_block_smem(region + (size_t)si * pl.dn_bytes + (size_t)kt * kBlockBytes, lane, q, sc, bv);
+                block_fx(q, sc, bv, reinterpret_cast<const uint32_t*>(s_hq + (size_t)bi * kFxGroupBytes + (lane & 1) * 64),
+                         s_hm[bi].x, s_hm[bi].y, Pv);
+                if ((lane & 1) == 0)
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) s_blk[bi][(lane >> 1) + 16 * r] = Pv[r];
+            }
+        }
+        __syncthreads();
+        if (s_abort) break;
+        // the slots are free: the next batch's units go out now
+        if (warp == 0 && lane < nslot && m0 + nslot + lane < Nd) {
+            fence_proxy_async_smem();
+            issue_dn(m0 + nslot + lane);
+        }
+        for (int it = tid; it < nb * kRowTile; it += kFusedThreads) {
+            const int u = it >> 7, row = it & 127, d = dfirst + (m0 + u) * dstep;
+            float v = 0.0f;
+            for (int kt = 0; kt < KTd; ++kt) v = __fadd_rn(v, s_blk[u * KTd + kt][row]);
+            f.y[(size_t)(d / n_rd) * H + (d % n_rd) * kRowTile + row] = f2bf(v);
+        }
+        if (m0 == 0) mark(14);
+        __threadfence();
+        __syncthreads();
+        if (tid < nb) {
+            const int d = dfirst + (m0 + tid) * dstep, t = (d / n_rd) / K;
+            uint32_t* c = f.cnt_dn + (size_t)t * n_rd + d % n_rd;
+            const unsigned old = atomicAdd(c, 1u);
+            s_lastd[tid] = (old == (unsigned)K - 1);
+            if (s_lastd[tid]) *c = 0;
+        }
+        __syncthreads();
+        __threadfence();
+        for (int it = tid; it < nb * kRowTile; it += kFusedThreads) {
+            const int u = it >> 7, row = it & 127;
+            if (!s_lastd[u]) continue;
+            // rank-order combine, same operation order as k_combine (forward.rs:225-232)
+            const int d = dfirst + (m0 + u) * dstep, t = (d / n_rd) / K, fo = (d % n_rd) * kRowTile + row;
+            float a = residual ? bf2f(residual[(size_t)t * H + fo]) : 0.0f;
+            for (int jk = 0; jk < K; ++jk) {
+                const uint16_t yv = __ldcg(f.y + ((size_t)t * K + jk) * H + fo);
+                a = __fmaf_rn(s_wts[t * K + jk], bf2f(yv), a);
+            }
+            out[(size_t)t * H + fo] = f2bf(a);
+        }
+        __syncthreads();  // s_blk / s_lastd free for the next batch
     }
     mark(6);
+    // copies still in flight (only after a wait gave up) land before the CTA exits
+    __syncthreads();
+    if (tid == 0 && s_abort) {
+        for (int si = 0; si < 8 + kMaxDnSlots; ++si)
+            if (s_issued[si]) mbar_drain(smem_u32(&s_bar[si]), (uint32_t)(s_issued[si] - 1) & 1u, f.wait_ns);
+    }
 }
 
 }  // namespace
 
+template <bool kNatural>
+static cudaError_t launch_fx_pack(const uint16_t* x, int T, int H, uint8_t* xq, float2* xmeta, cudaStream_t st) {
+    const int items = T * (H / kGroup);
+    const cudaError_t e = launch_pdl(k_fx_pack<kNatural>, dim3((items + 7) / 8), dim3(256), 0, st, x, T, H, xq, xmeta);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
 cudaError_t launch_decode_gateup(const LayerDev& L, const Shape& sh, const uint16_t* x, const int32_t* ids, int T,
                                  const DecodeBufs& d, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
+    cudaError_t e = launch_fx_pack<false>(x, T, sh.H, d.xq, d.xmeta, st);
+    if (e != cudaSuccess) return e;
     const TiledSrc g{L.gateup, sh.I / 64, sh.H / kGroup, 1, 0}, u = g;  // paired blocks
     dim3 grid(sh.I / kRowTile, kSplitGU, T * sh.K);
-    {
-        const cudaError_t le_ = launch_pdl(k_decode_gateup<TiledSrc>, dim3(grid), dim3(256), 0, st, g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
-        if (le_ != cudaSuccess) return le_;
-    }
+    e = launch_pdl(k_decode_gateup<TiledSrc>, grid, dim3(256), 0, st, g, u, ids, sh.H, sh.I, sh.K, sh.E, d);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
@@ -533,28 +852,69 @@ cudaError_t launch_decode_down(const LayerDev& L, const Shape& sh, const int32_t
     if (T <= 0) return cudaSuccess;
     const TiledSrc dn{L.down, sh.H / kRowTile, sh.I / kGroup, 1, 0};
     dim3 grid(sh.H / kRowTile, sh.K, T);
-    {
-        const cudaError_t le_ = launch_pdl(k_decode_down<TiledSrc>, dim3(grid), dim3(down_threads(sh.I)), 0, st, dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out,
-                                                                 do_combine);
-        if (le_ != cudaSuccess) return le_;
-    }
+    const cudaError_t e = launch_pdl(k_decode_down<TiledSrc>, grid, dim3(down_threads(sh.I)), 0, st, dn, ids, w,
+                                     residual, sh.H, sh.I, sh.K, sh.E, d, out, do_combine);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
+}
+
+FusedPlan fused_plan(int T, int H, int I) {
+    FusedPlan pl{};
+    const int nkt = (H / kGroup) / kSplitGU;
+    pl.off_x = 0;
+    pl.off_h = (T * H * 2 + 127) / 128 * 128;
+    pl.off_ring = pl.off_h + (kMaxDnSlots * I * 2 + 127) / 128 * 128;
+    pl.unit_bytes = nkt * kBlockBytes;       // one split of one block row
+    pl.dn_bytes = (I / kGroup) * kBlockBytes;  // one down unit
+    // the region holds a whole tile (8 units) or up to kMaxDnSlots down units
+    // (at most 3 of them beyond the ring's size, within 168 KB)
+    const int ring = 8 * pl.unit_bytes;
+    int nslot = 3;
+    while (nslot > 1 && nslot * pl.dn_bytes > (ring > 172032 ? ring : 172032)) --nslot;
+    pl.region_bytes = ring > nslot * pl.dn_bytes ? ring : nslot * pl.dn_bytes;
+    while (nslot < kMaxDnSlots && (nslot + 1) * pl.dn_bytes <= pl.region_bytes) ++nslot;
+    pl.nslot = nslot;
+    pl.smem_bytes = pl.off_ring + pl.region_bytes;
+    return pl;
+}
+
+// dynamic shared memory the fused layer may use on this device (opt-in limit
+// minus the kernel's static shared memory)
+static int fused_smem_limit() {
+    static int limit = -1;
+    if (limit < 0) {
+        int dev = 0, optin = 0;
+        cudaFuncAttributes fa{};
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+            cudaFuncGetAttributes(&fa, k_decode_fused) != cudaSuccess)
+            return 0;
+        limit = optin - (int)fa.sharedSizeBytes;
+    }
+    return limit;
+}
+
+bool decode_fused_supported(const Shape& sh, int T) {
+    if (T <= 0 || T > kFusedMaxT || sh.K > kMaxK || sh.E > kMaxE || sh.H != 2048 || sh.I % 256 || sh.I > 1024)
+        return false;
+    return fused_plan(T, sh.H, sh.I).smem_bytes <= fused_smem_limit();
 }
 
 cudaError_t launch_decode_fused(const LayerDev& L, const Shape& sh, const uint16_t* x, const uint16_t* residual,
                                 const float* bias, int T, int norm, int normalize, float eps,
                                 const FusedDecodeBufs& f, uint16_t* out, int num_sms, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    if (T > kFusedMaxT || sh.K > kMaxK || sh.E > kMaxE || sh.H % 2048) return cudaErrorInvalidValue;
+    if (!decode_fused_supported(sh, T)) return cudaErrorInvalidValue;
+    if ((sh.E + num_sms - 1) / num_sms > kFusedWarps) return cudaErrorInvalidValue;  // router rows: one per warp
     const TiledSrc g{L.gateup, sh.I / 64, sh.H / kGroup, 1, 0};  // paired blocks
     const TiledSrc dn{L.down, sh.H / kRowTile, sh.I / kGroup, 1, 0};
-    const size_t smem = (size_t)T * sh.H * 2 + (size_t)sh.I * 2;  // the layer input rows, one SwiGLU row
-    cudaError_t e = cudaFuncSetAttribute(k_decode_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const FusedPlan pl = fused_plan(T, sh.H, sh.I);
+    cudaError_t e = cudaFuncSetAttribute(k_decode_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem_bytes);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);  // one CTA per SM: every CTA is resident (cooperative)
     cfg.blockDim = dim3(kFusedThreads);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = pl.smem_bytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
@@ -563,7 +923,7 @@ cudaError_t launch_decode_fused(const LayerDev& L, const Shape& sh, const uint16
     cfg.numAttrs = 1;
     note_launch();
     return cudaLaunchKernelEx(&cfg, k_decode_fused, L.router_w, L.router_s, L.router_b, g, dn, x, residual, bias, T,
-                              sh.H, sh.I, sh.E, sh.K, norm, normalize, eps, f, out);
+                              sh.H, sh.I, sh.E, sh.K, norm, normalize, eps, f, pl, out);
 }
 
 cudaError_t launch_decode_ffn_mlx(const uint32_t* gw, const uint16_t* gs, const uint16_t* gb, const uint32_t* uw,
@@ -572,19 +932,18 @@ cudaError_t launch_decode_ffn_mlx(const uint32_t* gw, const uint16_t* gs, const 
                                   const float* w, const uint16_t* residual, int T, const DecodeBufs& d, uint16_t* out,
                                   cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
+    cudaError_t e = launch_fx_pack<true>(x, T, sh.H, d.xq, d.xmeta, st);
+    if (e != cudaSuccess) return e;
     const MlxSrc g{gw, gs, gb, sh.I, sh.H}, u{uw, us, ub, sh.I, sh.H}, dn{dw, ds, db, sh.H, sh.I};
     dim3 g1(sh.I / kRowTile, kSplitGU, T * sh.K);
-    {
-        const cudaError_t le_ = launch_pdl(k_decode_gateup<MlxSrc>, dim3(g1), dim3(256), 0, st, g, u, x, ids, sh.H, sh.I, sh.K, sh.E, d);
-        if (le_ != cudaSuccess) return le_;
-    }
-    cudaError_t e = cudaGetLastError();
+    e = launch_pdl(k_decode_gateup<MlxSrc>, g1, dim3(256), 0, st, g, u, ids, sh.H, sh.I, sh.K, sh.E, d);
+    if (e != cudaSuccess) return e;
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     dim3 g2(sh.H / kRowTile, sh.K, T);
-    {
-        const cudaError_t le_ = launch_pdl(k_decode_down<MlxSrc>, dim3(g2), dim3(down_threads(sh.I)), 0, st, dn, ids, w, residual, sh.H, sh.I, sh.K, sh.E, d, out, 1);
-        if (le_ != cudaSuccess) return le_;
-    }
+    e = launch_pdl(k_decode_down<MlxSrc>, g2, dim3(down_threads(sh.I)), 0, st, dn, ids, w, residual, sh.H, sh.I, sh.K,
+                   sh.E, d, out, 1);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, 
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = t0 + warp;
     if (warp >= kTopkTok || t >= T) return;
-    auto logit = [&](int e) { return s_l[warp][e]; };
+    auto logit = [&](int, int e) { return s_l[warp][e]; };
     int ik;
     float wk;
     topk_token(logit, bias, E, K, norm, lane, &ik, &wk);

@@ -266,7 +266,10 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->ybuf, (size_t)ctx->R_cap * s.H * 2},
         {(void**)&ctx->dec.part, (size_t)DT * K * (s.I / kRowTile) * kDecodeSplit * 2 * kRowTile * 4},
         {(void**)&ctx->dec.cnt_gu, (size_t)DT * K * (s.I / kRowTile) * 4},
-        {(void**)&ctx->dec.h, (size_t)DT * K * s.I * 2},
+        {(void**)&ctx->dec.hq, (size_t)DT * K * s.I * 2},
+        {(void**)&ctx->dec.hmeta, (size_t)DT * K * (s.I / kGroup) * 8},
+        {(void**)&ctx->dec.xq, (size_t)DT * s.H * 2},
+        {(void**)&ctx->dec.xmeta, (size_t)DT * (s.H / kGroup) * 8},
         {(void**)&ctx->dec.y, (size_t)DT * K * s.H * 2},
         {(void**)&ctx->dec.cnt_dn, (size_t)DT * (s.H / kRowTile) * 4},
         {(void**)&ctx->err_flag, 16},
@@ -288,6 +291,8 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->fused.cnt_gu, (size_t)kFusedMaxT * K * (s.I / kRowTile) * 4},
         {(void**)&ctx->fused.cnt_dn, (size_t)kFusedMaxT * (s.H / kRowTile) * 4},
         {(void**)&ctx->fused.bar, 16},
+        {(void**)&ctx->fused.hstamp, (size_t)kFusedMaxT * K * (s.I / kGroup) * 4},
+        {(void**)&ctx->fused.lst, (size_t)4 * kFusedMaxT * E * 8},
         {(void**)&ctx->probe_stamp, 16},
         {(void**)&ctx->ep.send_cnt, (size_t)kMaxWorld * 4},
         {(void**)&ctx->ep.done, 16},
@@ -314,10 +319,10 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         off += align_up(it.bytes ? it.bytes : 16, 1024);
     }
     ctx->dec.err = ctx->err_flag;
-    ctx->fused.logits = ctx->logits;
     ctx->fused.ids = ctx->ids;
     ctx->fused.wts = ctx->wts;
-    ctx->fused.h = ctx->dec.h;
+    ctx->fused.hq = ctx->dec.hq;
+    ctx->fused.hmeta = ctx->dec.hmeta;
     ctx->fused.y = ctx->dec.y;
     ctx->fused.err = ctx->err_flag;
     ctx->fused.wait_ns = ctx->wait_ns;
@@ -962,7 +967,7 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
     const Shape& s = ctx->sh;
     const LayerDev& L = ctx->layers[layer];
     cudaStream_t st = as_stream(stream);
-    if (path == OBS_PATH_DECODE && T <= kFusedMaxT) {
+    if (path == OBS_PATH_DECODE && decode_fused_supported(s, T)) {
         // router, top-k, experts and combine in one cooperative launch
         prof_begin(ctx, OBS_STAGE_DECODE_FUSED, st);
         CU(launch_decode_fused(L, s, x, residual, logit_bias, T, ctx->cfg.norm_topk, 0, 0.0f, ctx->fused, out,
@@ -1035,7 +1040,7 @@ extern "C" int obs_moe_stack_forward(obs_ctx* ctx, int layer0, int n_layers, uin
     uint16_t* r = resid;
     uint16_t* other = ctx->rtmp_dev;
     const int eff = path == OBS_PATH_AUTO ? (T <= ctx->decode_max ? OBS_PATH_DECODE : OBS_PATH_PREFILL) : path;
-    const bool fused = ctx->ep_world <= 1 && eff == OBS_PATH_DECODE && T > 0 && T <= kFusedMaxT;
+    const bool fused = ctx->ep_world <= 1 && eff == OBS_PATH_DECODE && decode_fused_supported(ctx->sh, T);
     for (int l = layer0; l < layer0 + n_layers; ++l) {
         if (fused) {
             // RMSNorm, router, top-k, experts and the residual combine of the layer in one launch
@@ -1147,6 +1152,10 @@ extern "C" int obs_check_device(obs_ctx* ctx, void* stream) {
         CU(cudaMemset(ctx->err_flag, 0, 8), "clear flag");
         // a wait that gave up leaves the fused decode layer's barrier counts behind: start over
         CU(cudaMemset(ctx->fused.bar, 0, 8), "reset barrier");
+        CU(cudaMemset(ctx->fused.cnt_gu, 0, (size_t)kFusedMaxT * ctx->sh.K * (ctx->sh.I / kRowTile) * 4), "reset");
+        CU(cudaMemset(ctx->fused.cnt_dn, 0, (size_t)kFusedMaxT * (ctx->sh.H / kRowTile) * 4), "reset");
+        CU(cudaMemset(ctx->fused.hstamp, 0, (size_t)kFusedMaxT * ctx->sh.K * (ctx->sh.I / kGroup) * 4), "reset");
+        CU(cudaMemset(ctx->fused.lst, 0, (size_t)4 * kFusedMaxT * ctx->sh.E * 8), "reset");
         if (flag == kDevTimeout) {
             char msg[96];
             snprintf(msg, sizeof msg, "a device-side wait gave up (timeout; GEMM wait code %d)", words[1]);
@@ -1260,6 +1269,6 @@ extern "C" int obs_trace_enable(obs_ctx* ctx, uint64_t* trace, int n_steps) {
     ctx->trace = trace;
     ctx->trace_n = trace ? n_steps : 0;
     // the fused decode layer records the phase timeline of every CTA when the buffer holds it
-    ctx->fused.trace = trace && (size_t)n_steps * kTrRoles >= (size_t)8 * ctx->num_sms ? trace : nullptr;
+    ctx->fused.trace = trace && (size_t)n_steps * kTrRoles >= (size_t)24 * ctx->num_sms ? trace : nullptr;
     return OBS_OK;
 }

@@ -150,7 +150,10 @@ constexpr int kDecodeSplit = 8;  // k-splits of the decode gate/up mat-vec
 struct DecodeBufs {
     float* part;        // [T*K][n_rt_gu][kDecodeSplit][2][128] gate/up partials
     uint32_t* cnt_gu;   // [T*K][n_rt_gu]
-    uint16_t* h;        // [T*K][I] bf16
+    uint8_t* hq;        // [T*K][I/64][128 B] SwiGLU rows h in fixed point (k_decode.cu)
+    float2* hmeta;      // [T*K][I/64] (sum X 2^-k, 2^-(k+4)) per h group
+    uint8_t* xq;        // [T][H/64][128 B] the layer input in fixed point
+    float2* xmeta;      // [T][H/64]
     uint16_t* y;        // [T*K][H] bf16
     uint32_t* cnt_dn;   // [T][n_rt_dn]
     int* err;           // device error flag (expert id out of range)
@@ -159,19 +162,32 @@ struct DecodeBufs {
 // combine in one cooperative launch) for T <= kFusedMaxT tokens.
 constexpr int kFusedMaxT = 4;
 struct FusedDecodeBufs {
-    float* logits;      // [T][E]
+    uint64_t* lst;      // [4][kFusedMaxT][E] logit bits | launch stamp << 32: router logits, four replicas
     int32_t* ids;       // [T][K]
     float* wts;         // [T][K]
     float* part_gu;     // [T*K][n_rt_gu][kDecodeSplit][2][128] gate/up split partials
     uint32_t* cnt_gu;   // [T*K][n_rt_gu]  self-resetting arrival counters
     uint32_t* cnt_dn;   // [T][n_rt_dn]
-    uint32_t* bar;      // [0] grid barrier arrivals (only grows), [1] launch generation
-    uint16_t* h;        // [T*K][I]
+    uint32_t* bar;      // [0] launch tickets (only grows; generation = ticket / grid size)
+    uint32_t* hstamp;   // [T*K][I/64] launch generation + 1 once that h group is written
+    uint8_t* hq;        // as DecodeBufs
+    float2* hmeta;
     uint16_t* y;        // [T*K][H]
     int* err;
-    uint64_t* trace;    // optional: thread 0 of CTA b writes %globaltimer at 7 points to trace[8b .. 8b+6]
-    uint64_t wait_ns;   // limit of the grid-barrier waits
+    uint64_t* trace;    // optional diagnostics: 24 %globaltimer marks per CTA (obs_trace_enable)
+    uint64_t wait_ns;   // limit of every device-side wait
 };
+// Dynamic shared-memory plan of the fused layer (byte offsets): the input
+// rows (then their fixed-point packs), one packed SwiGLU row, and a region that
+// holds an 8-unit ring of gate/up weight blocks or a few down units.
+struct FusedPlan {
+    int off_x, off_h, off_ring;
+    int unit_bytes, dn_bytes, region_bytes, nslot, smem_bytes;
+};
+FusedPlan fused_plan(int T, int H, int I);
+// Whether the fused layer handles this shape and T (H = 2048, I a multiple of
+// 256 up to 1024, T <= kFusedMaxT, and its shared-memory plan fits the device).
+bool decode_fused_supported(const Shape& sh, int T);
 // normalize = 1: x is the residual stream and the kernel applies the MoE input
 // RMSNorm (eps) itself, bit-identical to launch_rmsnorm.
 cudaError_t launch_decode_fused(const LayerDev& L, const Shape& sh, const uint16_t* x, const uint16_t* residual,

@@ -9,7 +9,8 @@
 // and no allocation: its scratch (split-K partial sums, the SwiGLU outputs h,
 // the per-expert outputs y, the arrival counters and an error word) lives in
 // one file-scope device array of fixed size, present on every GPU that loads
-// the library until the process exits.
+// the library until the process exits.  (The scratch also holds the fixed-point
+// forms of x and h that the decode kernels compute with.)
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -32,7 +33,10 @@ constexpr size_t kPartBytes = (size_t)OBS_STATIC_MAX_PAIRS * (OBS_STATIC_MAX_INT
 constexpr size_t kCntGuBytes = (size_t)OBS_STATIC_MAX_PAIRS * (OBS_STATIC_MAX_INTER / 128) * 4;
 constexpr size_t kCntDnBytes = (size_t)OBS_STATIC_MAX_PAIRS * (OBS_STATIC_MAX_HIDDEN / 128) * 4;
 constexpr size_t kErrBytes = 256;
-constexpr size_t kHBytes = (size_t)OBS_STATIC_MAX_PAIRS * OBS_STATIC_MAX_INTER * 2;
+constexpr size_t kHBytes = (size_t)OBS_STATIC_MAX_PAIRS * OBS_STATIC_MAX_INTER * 2;  // h in fixed point
+constexpr size_t kHMetaBytes = (size_t)OBS_STATIC_MAX_PAIRS * (OBS_STATIC_MAX_INTER / 64) * 8;
+constexpr size_t kXBytes = (size_t)OBS_STATIC_MAX_PAIRS * OBS_STATIC_MAX_HIDDEN * 2;  // x in fixed point (T <= pairs)
+constexpr size_t kXMetaBytes = (size_t)OBS_STATIC_MAX_PAIRS * (OBS_STATIC_MAX_HIDDEN / 64) * 8;
 constexpr size_t kYBytes = (size_t)OBS_STATIC_MAX_PAIRS * OBS_STATIC_MAX_HIDDEN * 2;
 // counters and the error word first: one memset clears everything that must start at zero
 constexpr size_t kOffCntGu = 0;
@@ -41,8 +45,11 @@ constexpr size_t kOffErr = kOffCntDn + kCntDnBytes;
 constexpr size_t kZeroBytes = kOffErr + kErrBytes;
 constexpr size_t kOffPart = (kZeroBytes + 255) / 256 * 256;
 constexpr size_t kOffH = kOffPart + kPartBytes;
-constexpr size_t kOffY = kOffH + kHBytes;
-constexpr size_t kScratchBytes = kOffY + kYBytes;  // about 7 MB
+constexpr size_t kOffHMeta = kOffH + kHBytes;
+constexpr size_t kOffX = kOffHMeta + kHMetaBytes;
+constexpr size_t kOffXMeta = kOffX + kXBytes;
+constexpr size_t kOffY = kOffXMeta + kXMetaBytes;
+constexpr size_t kScratchBytes = kOffY + kYBytes;  // about 8 MB
 constexpr int kMaxDevices = 64;
 
 std::mutex g_mu;
@@ -103,7 +110,10 @@ extern "C" int obs_decode_ffn_static(const obs_layer_weights* w, int n_experts, 
     d.cnt_dn = reinterpret_cast<uint32_t*>(base + kOffCntDn);
     d.err = reinterpret_cast<int*>(base + kOffErr);
     d.part = reinterpret_cast<float*>(base + kOffPart);
-    d.h = reinterpret_cast<uint16_t*>(base + kOffH);
+    d.hq = base + kOffH;
+    d.hmeta = reinterpret_cast<float2*>(base + kOffHMeta);
+    d.xq = base + kOffX;
+    d.xmeta = reinterpret_cast<float2*>(base + kOffXMeta);
     d.y = reinterpret_cast<uint16_t*>(base + kOffY);
     const obs::Shape sh{hidden, inter, n_experts, top_k};
     e = obs::launch_decode_ffn_mlx(w->gate_w, w->gate_s, w->gate_b, w->up_w, w->up_s, w->up_b, w->down_w, w->down_s,

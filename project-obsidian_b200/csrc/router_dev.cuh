@@ -79,34 +79,29 @@ __device__ __forceinline__ float key_value(uint32_t k) {
 }
 
 // One warp, one token (moe_routing_topk.metal:31-56): softmax in fp32, K
-// rounds of argmax (lowest index on ties), renormalise.  logit(e) returns the
-// token's logit of expert e; lane k < K ends with (*id, *wt) of rank k.  The
-// rounds only select; lane k then forms its own probability
-// exp(l_k - max) / sum, and the renormalising sum adds them in rank order.
-template <class LogitFn>
+// rounds of argmax (lowest index on ties), renormalise.  logit(i, e) returns
+// the token's logit of expert e = lane + 32 i; lane k < K ends with (*id,
+// *wt) of rank k.  The rounds only select; the maximum is the first winner's
+// logit, and lane k forms e_k = exp(l_k - max).  With renormalisation the
+// weights are e_k / sum_{j<K} e_j (the softmax denominator cancels; the sum
+// adds in rank order), otherwise e_k / sum_e exp(l_e - max) (lane-strided
+// partial sums, then the xor tree).
+struct NoMark {
+    __device__ __forceinline__ void operator()(int) const {}
+};
+template <class LogitFn, class Mark = NoMark>
 __device__ __forceinline__ void topk_token(LogitFn logit, const float* __restrict__ bias, int E, int K, int norm,
-                                           int lane, int* id, float* wt) {
+                                           int lane, int* id, float* wt, Mark mark = Mark()) {
     uint32_t key[kMaxE / 32];
-    float mx = -INFINITY;
 #pragma unroll
     for (int i = 0; i < kMaxE / 32; ++i) {
         const int e = lane + 32 * i;
         key[i] = 0;  // below every real key: never selected
-        if (e < E) {
-            const float l = __fadd_rn(logit(e), bias ? bias[e] : 0.0f);
-            key[i] = order_key(l);
-            mx = fmaxf(mx, l);
-        }
+        if (e < E) key[i] = order_key(__fadd_rn(logit(i, e), bias ? bias[e] : 0.0f));
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float se = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kMaxE / 32; ++i)
-        if (lane + 32 * i < E) se += expf(key_value(key[i]) - mx);
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
-    uint32_t kk = 0;
+    mark(0);
+    const int ne = (E + 31) >> 5;
+    uint32_t kk = 0, top = 0;
     int ik = 0;
 #pragma unroll
     for (int k = 0; k < kMaxK; ++k) {
@@ -115,7 +110,7 @@ __device__ __forceinline__ void topk_token(LogitFn logit, const float* __restric
         int ib = 0x7fffffff;
 #pragma unroll
         for (int i = 0; i < kMaxE / 32; ++i)
-            if (key[i] > kb) kb = key[i], ib = lane + 32 * i;
+            if (i < ne && key[i] > kb) kb = key[i], ib = lane + 32 * i;
         const uint32_t best = __reduce_max_sync(0xffffffffu, kb);
         const int bi = (int)__reduce_min_sync(0xffffffffu, kb == best ? (uint32_t)ib : 0x7fffffffu);
         // clear the winner's key (compile-time indices: key[] stays in registers)
@@ -123,12 +118,28 @@ __device__ __forceinline__ void topk_token(LogitFn logit, const float* __restric
         for (int i = 0; i < kMaxE / 32; ++i)
             if (bi == lane + 32 * i) key[i] = 0;
         if (lane == k) kk = best, ik = bi;
+        if (k == 0) top = best;
     }
-    const float p = lane < K ? expf(key_value(kk) - mx) / se : 0.0f;
-    float wsum = 0.0f;
-    for (int k = 0; k < K; ++k) wsum += __shfl_sync(0xffffffffu, p, k);
+    mark(1);
+    const float mx = key_value(top);
+    const float ek = lane < K ? expf(key_value(kk) - mx) : 0.0f;
+    float den = 0.0f;
+    if (norm) {
+#pragma unroll
+        for (int k = 0; k < kMaxK; ++k)
+            if (k < K) den += __shfl_sync(0xffffffffu, ek, k);
+    } else {
+#pragma unroll
+        for (int i = 0; i < kMaxE / 32; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E) den += expf(__fadd_rn(logit(i, e), bias ? bias[e] : 0.0f) - mx);
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    }
+    mark(2);
     *id = ik;
-    *wt = (norm && wsum > 0.0f) ? p / wsum : p;
+    *wt = den > 0.0f ? ek / den : ek;
 }
 
 }  // namespace obs
