@@ -380,27 +380,27 @@ int down_threads(int I) { return 32 * (I / kGroup < 16 ? I / kGroup : 16); }
 // ----------------------------------------------------------- fused decode layer
 // One cooperative launch runs the whole decode layer for T <= 4 tokens, one
 // CTA of 16 warps per SM, with no grid-wide barrier:
-//   0  each CTA takes a ticket (launch generation = ticket / grid size), loads
-//      its router row (expert b) into registers, then the layer input
-//      (RMSNormed with `normalize`) into shared memory;
-//   A  router logits of expert b, canonical order, stored with the launch's
-//      stamp in four replicas;
+//   0  warp 0 takes the CTA's ticket (launch generation = ticket / grid size)
+//      and, for an input given as is, computes its router row (expert b)
+//      straight from global memory; the other warps stage the input
+//      (RMSNormed with `normalize`, then the router reads it from shared
+//      memory);
+//   A  router logits are stored with the launch's stamp in four replicas;
 //   B  warps t < T poll token t's stamped logits and run top-k (every CTA, the
 //      same result); the other warps meanwhile pack the input groups in fixed
-//      point; then lanes of warp 0 issue bulk copies of the CTA's first wave
-//      of gate/up units and its first down unit, so the layer's weights
-//      (about 21 MB at T = 1) are in flight together right after routing;
-//   C  gate/up in waves of up to kGuUnits units (pair p, row tile rt, split
-//      ks; 8 blocks each): every warp computes blocks, then the CTA reduces
-//      the wave, publishes the split partials, and the last split of a tile
-//      forms its SwiGLU row in fixed point and stamps the tile ready;
-//   D  down units (pair p, row tile) of I/64 blocks, already in shared
-//      memory, each waiting only for the stamps of its own pair's h tiles;
-//      y, and the last pair of a (token, row tile) does the rank-order combine.
+//      point; warp 0 then issues the bulk copies of the CTA's first tile;
+//   C  tiles (pair p, 64-feature group r2): the 32 gate/up blocks of block row
+//      r2 (8 splits, streamed through an 8-slot ring) reduced in the CTA,
+//      SwiGLU and h in fixed point in shared memory, then the 16 blocks of the
+//      down projection's column group r2 (loaded into the ring once the
+//      gate/up blocks are consumed); the 2048 down partials go to global
+//      memory, each stored together with the launch's stamp;
+//   D  combine jobs (token, 32 rows), on the CTAs with fewer tiles: once the
+//      K * I/64 stamped partials of each row are in, y of every pair (the
+//      groups summed in order, rounded to bf16) and the rank-order combine.
 // Every wait is bounded (wait_ns); copies still in flight are drained before a
 // CTA exits after a wait gave up.
 constexpr int kFusedThreads = 512, kFusedWarps = kFusedThreads / 32;
-constexpr int kMaxDnSlots = 4;       // down-unit slots in the ring region
 constexpr int kLogitReplicas = 4;    // copies of the stamped logits (spreads the polling)
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
@@ -439,8 +439,10 @@ __device__ __forceinline__ void router_row_load(const uint32_t* __restrict__ w, 
     r.sc = bf2f(__ldg(s + (size_t)e * G + lane));
     r.bi = bf2f(__ldg(b + (size_t)e * G + lane));
 }
-// router_warp_item's arithmetic for one group per lane, x in shared memory;
-// lanes r < 4 store (logit, stamp) of every token into replica r
+// router_warp_item's arithmetic for one group per lane, x in global
+// (kGlobalX) or shared memory; lanes r < 4 store (logit, stamp) of every token
+// into replica r
+template <bool kGlobalX>
 __device__ __forceinline__ void router_row_logits(const RouterRow& r, const uint16_t* x, int T, int H, int E, int e,
                                                   int lane, uint32_t stamp, uint64_t* lst) {
     float wf[64];
@@ -457,7 +459,7 @@ __device__ __forceinline__ void router_row_logits(const RouterRow& r, const uint
         float a = 0.0f;
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
-            const uint4 q = xr[v];
+            const uint4 q = kGlobalX ? __ldg(xr + v) : xr[v];
             const uint32_t qs[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -490,18 +492,17 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
     // [T][H] bf16 layer input; after phase A, in place, its fixed-point packs [T][H/64][128 B]
     uint16_t* s_x = reinterpret_cast<uint16_t*>(smem + pl.off_x);
     uint8_t* s_xq = smem + pl.off_x;
-    uint8_t* s_hq = smem + pl.off_h;  // [units][I/64][128 B] packed h rows of a down batch
+    uint8_t* s_hq = smem + pl.off_h;  // [128 B] the tile's h group in fixed point
     __shared__ float2 s_xm[kFusedMaxT * 32];
-    __shared__ float2 s_hm[48];
+    __shared__ float2 s_hm[1];
     __shared__ float s_sq[2][256];
     __shared__ int s_ids[kFusedMaxT * kMaxK];
     __shared__ float s_wts[kFusedMaxT * kMaxK];
-    __shared__ float s_blk[48][kRowTile];  // per-block row values: C a tile's 32, D a batch's units
+    __shared__ float s_blk[32][kRowTile];  // C: a tile's per-block row values; D: the pairs' y of a job
     __shared__ float s_gsum[1][1][kRowTile];
     __shared__ int s_red[2][8];
-    __shared__ __align__(8) uint64_t s_bar[8 + kMaxDnSlots];  // ring slots, down slots
-    __shared__ int s_issued[8 + kMaxDnSlots];                 // copies issued per slot
-    __shared__ int s_lastd[kMaxDnSlots];
+    __shared__ __align__(8) uint64_t s_bar[9];  // ring slots 0-7, the down column group
+    __shared__ int s_issued[9];                 // copies issued per barrier
     __shared__ uint32_t s_gen;
     __shared__ volatile int s_abort;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -514,17 +515,29 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
         if (f.trace && tid == 0) f.trace[24 * b + k] = global_ns();
     };
     mark(0);
-    if (tid == 0) {
-        s_gen = atomicAdd(f.bar, 1u) / (uint32_t)G;  // every CTA of launch n draws a ticket in [nG, (n+1)G)
-        for (int i = 0; i < 8 + kMaxDnSlots; ++i) mbar_init(smem_u32(&s_bar[i]), 1), s_issued[i] = 0;
-        s_abort = 0;
-        fence_mbar_init();
-        fence_proxy_async_smem();
-    }
     // 0a: this CTA's router rows (experts b, b + G, ...: one per warp) into registers
     RouterRow rrow;
     const int e_r = b + G * warp;
     if (e_r < E) router_row_load(rw, rs, rb, H, e_r, lane, rrow);
+    if (warp == 0) {
+        // every CTA of launch n draws a ticket in [nG, (n+1)G): generation n
+        uint32_t tk = 0;
+        if (lane == 0) {
+            tk = atomicAdd(f.bar, 1u);
+            for (int i = 0; i < 9; ++i) mbar_init(smem_u32(&s_bar[i]), 1), s_issued[i] = 0;
+            s_abort = 0;
+            fence_mbar_init();
+            fence_proxy_async_smem();
+        }
+        const uint32_t gen = __shfl_sync(0xffffffffu, tk, 0) / (uint32_t)G;
+        if (lane == 0) s_gen = gen;
+        // A (input as given): warp 0's router row straight from global memory,
+        // while the other warps stage the input
+        if (!normalize && e_r < E) {
+            router_row_logits<true>(rrow, x_in, T, H, E, e_r, lane, gen + 1, f.lst);
+            mark(1);
+        }
+    }
 
     // 0b: the layer input into shared memory; with `normalize`, the MoE input
     // RMSNorm of rmsnorm.metal:9-37 in k_rmsnorm's order (256 threads per row,
@@ -558,23 +571,24 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
     __syncthreads();
     const uint32_t stamp = s_gen + 1;
 
-    // A: router logits, stamped
-    if (e_r < E) router_row_logits(rrow, s_x, T, H, E, e_r, lane, stamp, f.lst);
-    mark(1);
+    // A (normalised input, and any further router rows): from shared memory
+    if (e_r < E && (normalize || warp > 0)) {
+        router_row_logits<false>(rrow, s_x, T, H, E, e_r, lane, stamp, f.lst);
+        if (warp == 0) mark(1);
+    }
     __syncthreads();  // the router has read s_x: it may be packed in place
 
     const int KT = H / kGroup, nkt = KT / kSplitGU, P = T * K;
-    // gate/up work: tiles (p, r2) -- pair p's 64-feature block row r2 (both its gate
-    // and up rows), all 8 splits = 32 blocks -- on CTAs b, b + G, ...; each tile
-    // streams through an 8-slot ring as 8 units (one split = 4 contiguous blocks)
+    // Work: tiles (p, r2) -- pair p's 64-feature group r2: the gate/up block
+    // row r2 (its gate and up rows, all 8 splits = 32 blocks, streamed through
+    // an 8-slot ring as 8 units of 4 contiguous blocks) and the down
+    // projection's column group r2 (16 blocks, one per 128-row tile) -- on CTAs
+    // b, b + G, ...; then combine jobs (token t, row tile rt) on the CTAs with
+    // fewer tiles first.
     const int n_r2 = I / kGroup, n_tiles = P * n_r2;
     const int Nt = b < n_tiles ? (n_tiles - 1 - b) / G + 1 : 0;
-    const int n_rd = H / kRowTile, KTd = I / kGroup, nwd = KTd < 16 ? KTd : 16, D = P * n_rd;
-    // down units (pair p, row tile) round-robin over the CTAs, those with fewer
-    // tiles first (CTAs b >= n_tiles mod G): d = pos(b) + m G
-    const int dfirst = (b - n_tiles % G + G) % G, dstep = G;
-    const int Nd = dfirst < D ? (D - 1 - dfirst) / dstep + 1 : 0;
-    const int nslot = pl.nslot;  // down slots in the region
+    const int n_rd = H / kRowTile, KTd = I / kGroup;
+    const int n_jobs = T * H / 32, jfirst = (b - n_tiles % G + G) % G;
     uint8_t* region = smem + pl.off_ring;
     // unit v of this CTA's tiles: tile v / 8, split v % 8, ring slot v % 8
     auto issue_unit = [&](int v) {
@@ -587,24 +601,25 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
                  (uint32_t)pl.unit_bytes, bar);
         ++s_issued[v & 7];
     };
-    // this CTA's m-th down unit, slot m % nslot
-    auto issue_dn = [&](int m) {
-        const int d = dfirst + m * dstep;
-        const int p = d / n_rd, rt = d % n_rd, si = m % nslot;
-        const int e = checked_expert(s_ids[p], E, f.err);
-        const uint32_t bar = smem_u32(&s_bar[8 + si]);
-        mbar_arrive_expect_tx(bar, (uint32_t)pl.dn_bytes);
-        bulk_g2s(smem_u32(region + (size_t)si * pl.dn_bytes), dsrc.block(e, rt, 0), (uint32_t)pl.dn_bytes, bar);
-        ++s_issued[8 + si];
-    };
-    // warp 0 issues everything there is room for: the first tile's 8 units, or
-    // (a CTA without tiles) its first down units -- one copy per lane
-    auto issue_first = [&]() {
-        if (Nt > 0) {
-            if (lane < 8) issue_unit(lane);
-        } else if (lane < nslot && lane < Nd) {
-            issue_dn(lane);
+    // the down column group of this CTA's tile i: lane rt < 16 copies block (e, rt, r2)
+    // into the ring's first 16 x 4608 bytes (slots 0-3); warp 0, all lanes
+    auto issue_down_group = [&](int i) {
+        const int tau = b + i * G, p = tau / n_r2, r2 = tau % n_r2;
+        const uint32_t bar = smem_u32(&s_bar[8]);
+        if (lane == 0) {
+            mbar_arrive_expect_tx(bar, (uint32_t)(n_rd * kBlockBytes));
+            ++s_issued[8];
         }
+        __syncwarp();
+        if (lane < n_rd) {
+            const int e = checked_expert(s_ids[p], E, f.err);
+            bulk_g2s(smem_u32(region + (size_t)lane * kBlockBytes), dsrc.block(e, lane, r2), (uint32_t)kBlockBytes,
+                     bar);
+        }
+    };
+    // warp 0: the first tile's 8 units, one copy per lane
+    auto issue_first = [&]() {
+        if (Nt > 0 && lane < 8) issue_unit(lane);
     };
     if (warp < T) {
         // B: token `warp`'s logits from replica b % 4, once all carry this launch's stamp
@@ -657,15 +672,26 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
     mark(7);
     if (T > 1 && warp == 0 && !s_abort) issue_first();
 
-    // C: gate/up tiles.  32 blocks per tile, warp w takes blocks w and w + 16
-    // (split bi / 4, group ks * 4 + bi % 4); each row's value is summed over the
-    // splits in order, each split's 4 groups as ((P0 + P1) + P2) + P3 (the
-    // separate kernel's order); then SwiGLU over the 64 features, h in fixed
-    // point, and the tile's stamp.
+    // C: tiles.  Gate/up: 32 blocks, warp w takes blocks w and w + 16 (split
+    // bi / 4, group ks * 4 + bi % 4); each row is summed over the splits in
+    // order, each split's 4 groups as ((P0 + P1) + P2) + P3 (the separate
+    // kernel's order); SwiGLU over the 64 features and h in fixed point, kept in
+    // shared memory.  Down: warp w computes row tile w of the column group; the
+    // 2048 values go to ypart[p][r2], and each row tile's counter of (token,
+    // row tile) gets one acq_rel arrival.
     for (int i = 0; i < Nt; ++i) {
         const int tau = b + i * G, p = tau / n_r2, r2 = tau % n_r2, t = p / K;
+        // two rounds: splits 0-3 (slots 0-3), then -- with the down column
+        // group already on its way into slots 0-3 -- splits 4-7
         for (int bi = warp; bi < 32; bi += kFusedWarps) {
             const int ks = bi >> 2, j = bi & 3, v = 8 * i + ks, kt = ks * nkt + j;
+            if (bi == kFusedWarps + warp) {
+                __syncthreads();  // slots 0-3 consumed
+                if (warp == 0 && !s_abort) {
+                    fence_proxy_async_smem();
+                    issue_down_group(i);
+                }
+            }
             if (!s_abort && mbar_wait(smem_u32(&s_bar[v & 7]), (uint32_t)(v >> 3) & 1u, &s_abort, 1, f.wait_ns)) {
                 if (i == 0 && bi == 0) mark(8);
                 uint4 q[8];
@@ -681,18 +707,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
         }
         __syncthreads();
         if (i == 0) mark(9);
-        // the ring is free: the next tile's units, or after the last tile the
-        // first down units, go out now
-        if (warp == 0 && !s_abort) {
-            if (i + 1 < Nt) {
-                if (lane < 8) {
-                    fence_proxy_async_smem();
-                    issue_unit(8 * (i + 1) + lane);
-                }
-            } else if (lane < nslot && lane < Nd) {
-                fence_proxy_async_smem();
-                issue_dn(lane);
-            }
+        // slots 4-7 are free: the next tile's units 4-7 go out now
+        if (warp == 0 && !s_abort && i + 1 < Nt && lane >= 4 && lane < 8) {
+            fence_proxy_async_smem();
+            issue_unit(8 * (i + 1) + lane);
         }
         if (tid < kRowTile) {
             float sum = 0.0f;
@@ -702,7 +720,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
             s_gsum[0][0][tid] = sum;
         }
         __syncthreads();
-        // SwiGLU of the 64 features (rows paired_row(c) and + 16), fixed point, stamp
+        // SwiGLU of the 64 features (rows paired_row(c) and + 16), h in fixed point
         if (warp < 2) {
             const int rr = paired_row(tid);
             const uint32_t hb = f2bf(silu_mul(s_gsum[0][0][rr], s_gsum[0][0][rr + 16]));
@@ -711,115 +729,93 @@ __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
             named_bar_sync(1, 64);
             const int k = fx_k((uint32_t)max(s_red[0][0], s_red[0][1]));
             const int X = fx_round(hb, k);
-            const size_t gi = (size_t)p * n_r2 + r2;
-            uint8_t* dst = f.hq + gi * kFxGroupBytes;
-            dst[fx_byte<false>(tid, 0)] = (uint8_t)(X >> 8);
-            dst[fx_byte<false>(tid, 1)] = (uint8_t)(X & 255);
+            s_hq[fx_byte<false>(tid, 0)] = (uint8_t)(X >> 8);
+            s_hq[fx_byte<false>(tid, 1)] = (uint8_t)(X & 255);
             const int ws = __reduce_add_sync(0xffffffffu, X);
             if (lane == 0) s_red[1][warp] = ws;
             named_bar_sync(1, 64);
             if (tid == 0)
-                f.hmeta[gi] = make_float2(__fmul_rn(__int2float_rn(s_red[1][0] + s_red[1][1]), pow2f(-k)), pow2f(-k - 4));
-            __threadfence();
-            named_bar_sync(1, 64);
-            if (tid == 0) st_release_gpu(f.hstamp + gi, stamp);
+                s_hm[0] = make_float2(__fmul_rn(__int2float_rn(s_red[1][0] + s_red[1][1]), pow2f(-k)), pow2f(-k - 4));
         }
-        __syncthreads();  // s_blk, s_gsum free for the next tile
+        __syncthreads();
+        // down: row tile `warp` of column group r2
+        if (warp < n_rd && !s_abort &&
+            mbar_wait(smem_u32(&s_bar[8]), (uint32_t)i & 1u, &s_abort, 3, f.wait_ns)) {
+            if (i == 0 && warp == 0) mark(13);
+            uint4 q[8];
+            float sc[8], bv[8], Pv[8];
+            load_block_smem(region + (size_t)warp * kBlockBytes, lane, q, sc, bv);
+            block_fx(q, sc, bv, reinterpret_cast<const uint32_t*>(s_hq + (lane & 1) * 64), s_hm[0].x, s_hm[0].y, Pv);
+            // each partial carries the launch's stamp (one 64-bit store: the
+            // reader sees the value together with its stamp, no fence needed)
+            uint64_t* yp = f.ypart + ((size_t)p * n_r2 + r2) * H + warp * kRowTile;
+            if ((lane & 1) == 0)
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    st_relaxed_u64(yp + (lane >> 1) + 16 * r, (uint64_t)__float_as_uint(Pv[r]) | ((uint64_t)stamp << 32));
+        }
+        __syncthreads();  // the ring is free again
+        if (i == 0) mark(14);
+        if (s_abort) break;
+        if (warp == 0 && i + 1 < Nt && lane < 4) {
+            fence_proxy_async_smem();
+            issue_unit(8 * (i + 1) + lane);
+        }
         if (i == 0) mark(10);
     }
     mark(4);
 
-    // D: down units d = dfirst + m dstep (the first batch already issued, by
-    // warp 0 at top-k or after the CTA's last tile), in batches of up to nslot resident
-    // units: the stamps of every unit's pair, the h rows, all blocks of the
-    // batch (warp w: blocks w, w + 16, ...), then y = sum_kt P_kt in order per
-    // unit, one fence for the batch's counters, and the rank-order combine by
-    // the last pair of each (token, row tile)
-    for (int m0 = 0; m0 < Nd; m0 += nslot) {
-        const int nb = Nd - m0 < nslot ? Nd - m0 : nslot;
-        if (tid < nb * n_r2 && !s_abort) {
-            const int u = tid / n_r2, g = tid % n_r2, p = (dfirst + (m0 + u) * dstep) / n_rd;
-            const uint32_t* sp = f.hstamp + (size_t)p * n_r2 + g;
+    // D: combine jobs (token t, 32 rows): thread (row, pair k) polls the I/64
+    // stamped partials of its row until all carry this launch's stamp, sums them
+    // in group order and rounds y to bf16; then the rank-order combine
+    // (forward.rs:225-232) into out
+    for (int jb = jfirst; jb < n_jobs && !s_abort; jb += G) {
+        const int t = jb / (4 * n_rd), r0 = (jb % (4 * n_rd)) * 32;
+        const int row = tid & 31, k = tid >> 5;
+        if (k < K) {
+            const uint64_t* yp = f.ypart + (size_t)(t * K + k) * n_r2 * H + r0 + row;
+            float pv[16];
             const uint64_t t0 = global_ns();
-            while (ld_acquire_gpu(sp) != stamp)
+            for (;;) {
+                bool ok = true;
+#pragma unroll
+                for (int g = 0; g < 16; ++g) {
+                    pv[g] = 0.0f;
+                    if (g < n_r2) {
+                        const uint64_t v = ld_relaxed_u64(yp + (size_t)g * H);
+                        pv[g] = __uint_as_float((uint32_t)v);
+                        ok = ok && (uint32_t)(v >> 32) == stamp;
+                    }
+                }
+                if (ok) break;
                 if (global_ns() - t0 > f.wait_ns) {
                     atomicExch(f.err, kDevTimeout);
                     s_abort = 2;
                     break;
                 }
-        }
-        __syncthreads();
-        if (m0 == 0) mark(5);
-        if (s_abort) break;
-        for (int i = tid; i < nb * KTd * (kFxGroupBytes / 16); i += kFusedThreads) {
-            const int u = i / (KTd * (kFxGroupBytes / 16)), r = i % (KTd * (kFxGroupBytes / 16));
-            const int p = (dfirst + (m0 + u) * dstep) / n_rd;
-            reinterpret_cast<uint4*>(s_hq)[i] =
-                __ldcg(reinterpret_cast<const uint4*>(f.hq + (size_t)p * KTd * kFxGroupBytes) + r);
-        }
-        if (tid < nb * KTd) {
-            const int u = tid / KTd, p = (dfirst + (m0 + u) * dstep) / n_rd;
-            s_hm[tid] = __ldcg(f.hmeta + (size_t)p * KTd + tid % KTd);
-        }
-        __syncthreads();
-        for (int bi = warp; bi < nb * KTd; bi += kFusedWarps) {
-            const int u = bi / KTd, kt = bi % KTd, m = m0 + u, si = m % nslot;
-            if (!s_abort && mbar_wait(smem_u32(&s_bar[8 + si]), (uint32_t)(m / nslot) & 1u, &s_abort, 3, f.wait_ns)) {
-                if (m0 == 0 && bi == 0) mark(13);
-                uint4 q[8];
-                float sc[8], bv[8], Pv[8];
-                load_block_smem(region + (size_t)si * pl.dn_bytes + (size_t)kt * kBlockBytes, lane, q, sc, bv);
-                block_fx(q, sc, bv, reinterpret_cast<const uint32_t*>(s_hq + (size_t)bi * kFxGroupBytes + (lane & 1) * 64),
-                         s_hm[bi].x, s_hm[bi].y, Pv);
-                if ((lane & 1) == 0)
-#pragma unroll
-                    for (int r = 0; r < 8; ++r) s_blk[bi][(lane >> 1) + 16 * r] = Pv[r];
             }
-        }
-        __syncthreads();
-        if (s_abort) break;
-        // the slots are free: the next batch's units go out now
-        if (warp == 0 && lane < nslot && m0 + nslot + lane < Nd) {
-            fence_proxy_async_smem();
-            issue_dn(m0 + nslot + lane);
-        }
-        for (int it = tid; it < nb * kRowTile; it += kFusedThreads) {
-            const int u = it >> 7, row = it & 127, d = dfirst + (m0 + u) * dstep;
             float v = 0.0f;
-            for (int kt = 0; kt < KTd; ++kt) v = __fadd_rn(v, s_blk[u * KTd + kt][row]);
-            f.y[(size_t)(d / n_rd) * H + (d % n_rd) * kRowTile + row] = f2bf(v);
-        }
-        if (m0 == 0) mark(14);
-        __threadfence();
-        __syncthreads();
-        if (tid < nb) {
-            const int d = dfirst + (m0 + tid) * dstep, t = (d / n_rd) / K;
-            uint32_t* c = f.cnt_dn + (size_t)t * n_rd + d % n_rd;
-            const unsigned old = atomicAdd(c, 1u);
-            s_lastd[tid] = (old == (unsigned)K - 1);
-            if (s_lastd[tid]) *c = 0;
+#pragma unroll
+            for (int g = 0; g < 16; ++g)
+                if (g < n_r2) v = __fadd_rn(v, pv[g]);
+            s_blk[k][row] = bf2f(f2bf(v));  // y, rounded to bf16
         }
         __syncthreads();
-        __threadfence();
-        for (int it = tid; it < nb * kRowTile; it += kFusedThreads) {
-            const int u = it >> 7, row = it & 127;
-            if (!s_lastd[u]) continue;
-            // rank-order combine, same operation order as k_combine (forward.rs:225-232)
-            const int d = dfirst + (m0 + u) * dstep, t = (d / n_rd) / K, fo = (d % n_rd) * kRowTile + row;
+        if (jb == jfirst) mark(5);
+        if (s_abort) break;
+        if (tid < 32) {
+            const int fo = r0 + tid;
             float a = residual ? bf2f(residual[(size_t)t * H + fo]) : 0.0f;
-            for (int jk = 0; jk < K; ++jk) {
-                const uint16_t yv = __ldcg(f.y + ((size_t)t * K + jk) * H + fo);
-                a = __fmaf_rn(s_wts[t * K + jk], bf2f(yv), a);
-            }
+            for (int kk = 0; kk < K; ++kk) a = __fmaf_rn(s_wts[t * K + kk], s_blk[kk][tid], a);
             out[(size_t)t * H + fo] = f2bf(a);
         }
-        __syncthreads();  // s_blk / s_lastd free for the next batch
+        __syncthreads();
     }
     mark(6);
     // copies still in flight (only after a wait gave up) land before the CTA exits
     __syncthreads();
     if (tid == 0 && s_abort) {
-        for (int si = 0; si < 8 + kMaxDnSlots; ++si)
+        for (int si = 0; si < 9; ++si)
             if (s_issued[si]) mbar_drain(smem_u32(&s_bar[si]), (uint32_t)(s_issued[si] - 1) & 1u, f.wait_ns);
     }
 }
@@ -863,17 +859,11 @@ FusedPlan fused_plan(int T, int H, int I) {
     const int nkt = (H / kGroup) / kSplitGU;
     pl.off_x = 0;
     pl.off_h = (T * H * 2 + 127) / 128 * 128;
-    pl.off_ring = pl.off_h + (kMaxDnSlots * I * 2 + 127) / 128 * 128;
-    pl.unit_bytes = nkt * kBlockBytes;       // one split of one block row
-    pl.dn_bytes = (I / kGroup) * kBlockBytes;  // one down unit
-    // the region holds a whole tile (8 units) or up to kMaxDnSlots down units
-    // (at most 3 of them beyond the ring's size, within 168 KB)
-    const int ring = 8 * pl.unit_bytes;
-    int nslot = 3;
-    while (nslot > 1 && nslot * pl.dn_bytes > (ring > 172032 ? ring : 172032)) --nslot;
-    pl.region_bytes = ring > nslot * pl.dn_bytes ? ring : nslot * pl.dn_bytes;
-    while (nslot < kMaxDnSlots && (nslot + 1) * pl.dn_bytes <= pl.region_bytes) ++nslot;
-    pl.nslot = nslot;
+    pl.off_ring = pl.off_h + kFxGroupBytes;
+    pl.unit_bytes = nkt * kBlockBytes;  // one split of one block row
+    pl.dn_bytes = (H / kRowTile) * kBlockBytes;  // a down column group (in slots 0-3)
+    pl.region_bytes = 8 * pl.unit_bytes;
+    pl.nslot = 8;
     pl.smem_bytes = pl.off_ring + pl.region_bytes;
     return pl;
 }
@@ -895,7 +885,8 @@ static int fused_smem_limit() {
 }
 
 bool decode_fused_supported(const Shape& sh, int T) {
-    if (T <= 0 || T > kFusedMaxT || sh.K > kMaxK || sh.E > kMaxE || sh.H != 2048 || sh.I % 256 || sh.I > 1024)
+    if (T <= 0 || T > kFusedMaxT || sh.K > kMaxK || sh.E > kMaxE || sh.H != 2048 || sh.I % 256 || sh.I > 1024 ||
+        sh.K > 32)
         return false;
     return fused_plan(T, sh.H, sh.I).smem_bytes <= fused_smem_limit();
 }

@@ -287,11 +287,8 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->hs[1].bias, (size_t)E * 4},
         {(void**)&ctx->xnorm_dev, (size_t)T * s.H * 2},
         {(void**)&ctx->rtmp_dev, (size_t)T * s.H * 2},
-        {(void**)&ctx->fused.part_gu, (size_t)kFusedMaxT * K * (s.I / kRowTile) * kDecodeSplit * 2 * kRowTile * 4},
-        {(void**)&ctx->fused.cnt_gu, (size_t)kFusedMaxT * K * (s.I / kRowTile) * 4},
-        {(void**)&ctx->fused.cnt_dn, (size_t)kFusedMaxT * (s.H / kRowTile) * 4},
+        {(void**)&ctx->fused.ypart, (size_t)kFusedMaxT * K * (s.I / kGroup) * s.H * 8},
         {(void**)&ctx->fused.bar, 16},
-        {(void**)&ctx->fused.hstamp, (size_t)kFusedMaxT * K * (s.I / kGroup) * 4},
         {(void**)&ctx->fused.lst, (size_t)4 * kFusedMaxT * E * 8},
         {(void**)&ctx->probe_stamp, 16},
         {(void**)&ctx->ep.send_cnt, (size_t)kMaxWorld * 4},
@@ -321,9 +318,6 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     ctx->dec.err = ctx->err_flag;
     ctx->fused.ids = ctx->ids;
     ctx->fused.wts = ctx->wts;
-    ctx->fused.hq = ctx->dec.hq;
-    ctx->fused.hmeta = ctx->dec.hmeta;
-    ctx->fused.y = ctx->dec.y;
     ctx->fused.err = ctx->err_flag;
     ctx->fused.wait_ns = ctx->wait_ns;
     ctx->ep.wait_ns = ctx->wait_ns;
@@ -1151,10 +1145,8 @@ extern "C" int obs_check_device(obs_ctx* ctx, void* stream) {
     if (flag) {
         CU(cudaMemset(ctx->err_flag, 0, 8), "clear flag");
         // a wait that gave up leaves the fused decode layer's barrier counts behind: start over
-        CU(cudaMemset(ctx->fused.bar, 0, 8), "reset barrier");
-        CU(cudaMemset(ctx->fused.cnt_gu, 0, (size_t)kFusedMaxT * ctx->sh.K * (ctx->sh.I / kRowTile) * 4), "reset");
-        CU(cudaMemset(ctx->fused.cnt_dn, 0, (size_t)kFusedMaxT * (ctx->sh.H / kRowTile) * 4), "reset");
-        CU(cudaMemset(ctx->fused.hstamp, 0, (size_t)kFusedMaxT * ctx->sh.K * (ctx->sh.I / kGroup) * 4), "reset");
+        CU(cudaMemset(ctx->fused.bar, 0, 8), "reset tickets");
+        CU(cudaMemset(ctx->fused.ypart, 0, (size_t)kFusedMaxT * ctx->sh.K * (ctx->sh.I / kGroup) * ctx->sh.H * 8), "reset");
         CU(cudaMemset(ctx->fused.lst, 0, (size_t)4 * kFusedMaxT * ctx->sh.E * 8), "reset");
         if (flag == kDevTimeout) {
             char msg[96];

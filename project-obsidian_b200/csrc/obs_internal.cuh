@@ -165,21 +165,15 @@ struct FusedDecodeBufs {
     uint64_t* lst;      // [4][kFusedMaxT][E] logit bits | launch stamp << 32: router logits, four replicas
     int32_t* ids;       // [T][K]
     float* wts;         // [T][K]
-    float* part_gu;     // [T*K][n_rt_gu][kDecodeSplit][2][128] gate/up split partials
-    uint32_t* cnt_gu;   // [T*K][n_rt_gu]  self-resetting arrival counters
-    uint32_t* cnt_dn;   // [T][n_rt_dn]
     uint32_t* bar;      // [0] launch tickets (only grows; generation = ticket / grid size)
-    uint32_t* hstamp;   // [T*K][I/64] launch generation + 1 once that h group is written
-    uint8_t* hq;        // as DecodeBufs
-    float2* hmeta;
-    uint16_t* y;        // [T*K][H]
+    uint64_t* ypart;    // [T*K][I/64][H] down partials per h group: value bits | launch stamp << 32
     int* err;
     uint64_t* trace;    // optional diagnostics: 24 %globaltimer marks per CTA (obs_trace_enable)
     uint64_t wait_ns;   // limit of every device-side wait
 };
 // Dynamic shared-memory plan of the fused layer (byte offsets): the input
-// rows (then their fixed-point packs), one packed SwiGLU row, and a region that
-// holds an 8-unit ring of gate/up weight blocks or a few down units.
+// rows (then their fixed-point packs), one packed h group, and an 8-unit ring
+// of gate/up weight blocks (slots 0-3 also take a down column group).
 struct FusedPlan {
     int off_x, off_h, off_ring;
     int unit_bytes, dn_bytes, region_bytes, nslot, smem_bytes;

@@ -20,6 +20,18 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (runs the CUDA path through the C ABI)")
 
 
+def pytest_collection_modifyitems(config, items):
+    # a bound on every test: the device-side waits are bounded (2 s by default),
+    # so a test that keeps hitting them fails here instead of running for long
+    try:
+        import pytest_timeout  # noqa: F401
+    except ImportError:
+        return
+    for item in items:
+        if item.get_closest_marker("timeout") is None:
+            item.add_marker(pytest.mark.timeout(600))
+
+
 @pytest.fixture(scope="session")
 def cuda():
     import torch
