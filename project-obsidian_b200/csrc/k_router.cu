@@ -9,8 +9,9 @@
 // Top-k follows moe_routing_topk.metal:31-56 (softmax in fp32, repeated
 // argmax with the lowest index winning ties, renormalise), selecting on the
 // fp32 logits so the choice depends only on bit-exact values.  For T > 16 the
-// logits are produced as the 32 leaf sums [32][T][E] (more CTAs) and combined in
-// the fixed tree by the top-k kernel.
+// logits are produced as 8 partial sums [8][T][E] (each the first two tree
+// levels over four leaves) and combined in the rest of the fixed tree by the
+// top-k kernel.
 #include "router_dev.cuh"
 
 namespace obs {
@@ -40,126 +41,138 @@ __global__ void __launch_bounds__(256) k_router_warp(const uint32_t* __restrict_
 }
 
 // ---------------------------------------------------------------- prefill form
-// One CTA per (64 tokens, 128 experts, leaf): a leaf is lane l's share of the
-// canonical order, groups [l*m, (l+1)*m).  The CTA stages each group's
-// dequantised weights and activations (fp32) in shared memory; each of its 256
-// threads keeps a 4 x 8 register tile of (token, expert) accumulators (tokens
-// tt + 16i, experts te + 16j; a warp's activation reads cover 16 rows and its
-// weight reads two, served by broadcast) and chains the group's 64 columns in
-// order with fused multiply-adds.  The leaf sums land in parts[leaf][T][E];
-// top-k (or k_router_finish) adds them in the adjacent pairwise tree, which is
-// the decode form's xor-butterfly (offsets 1, 2, 4, 8, 16).
+// One CTA per (64 tokens, 128 experts, node): node q covers the canonical
+// order's leaves 4q .. 4q+3 (lane l's share: groups [l*m, (l+1)*m)) and adds
+// them as the first two levels of the adjacent pairwise tree,
+// (leaf 4q + leaf 4q+1) + (leaf 4q+2 + leaf 4q+3).  For each group the CTA
+// stages the dequantised weights and activations (fp32) in shared memory; each
+// of its 256 threads keeps a 4 x 8 register tile of (token, expert)
+// accumulators (tokens tt + 16i, experts te + 16j; a warp's activation reads
+// cover 16 rows and its weight reads two, served by broadcast) and chains the
+// group's 64 columns in order with fused multiply-adds.  The node sums land in
+// parts[node][T][E]; top-k (or k_router_finish) adds the 8 nodes in the rest of
+// the tree, which together is the decode form's xor-butterfly (offsets 1, 2,
+// 4, 8, 16).
 constexpr int kRT = 64, kRE = 128, kRPad = 68, kLeafThreads = 256;
+constexpr int kNodes = kLeaves / 4;  // partial planes of the prefill form
 constexpr size_t kLeafSmem = (size_t)(kRT + kRE) * kRPad * 4;  // 52,224 bytes
 
-__global__ void __launch_bounds__(kLeafThreads) k_router_leaf(const uint32_t* __restrict__ w,
-                                                              const uint16_t* __restrict__ s,
-                                                              const uint16_t* __restrict__ b,
-                                                              const uint16_t* __restrict__ x, int T, int H, int E,
-                                                              float* __restrict__ parts,
-                                                              int32_t* __restrict__ zero_counts) {
+__global__ void __launch_bounds__(kLeafThreads, 1) k_router_leaf(const uint32_t* __restrict__ w,
+                                                                 const uint16_t* __restrict__ s,
+                                                                 const uint16_t* __restrict__ b,
+                                                                 const uint16_t* __restrict__ x, int T, int H, int E,
+                                                                 float* __restrict__ parts,
+                                                                 int32_t* __restrict__ zero_counts) {
     pdl_begin();
     zero_on_first_cta(zero_counts, E);
     extern __shared__ __align__(16) float rsm[];
     float(*xs)[kRPad] = reinterpret_cast<float(*)[kRPad]>(rsm);
     float(*ws)[kRPad] = reinterpret_cast<float(*)[kRPad]>(rsm + kRT * kRPad);
     const int tid = threadIdx.x, tt = tid & 15, te = tid >> 4;
-    const int t0 = blockIdx.x * kRT, e0 = blockIdx.y * kRE, leaf = blockIdx.z;
+    const int t0 = blockIdx.x * kRT, e0 = blockIdx.y * kRE, node = blockIdx.z;
     const int G = H / kGroup, m = G / 32;
-    float acc[4][8];
+    float acc[4][8], pair[4][8], first[4][8];
+    for (int lf = 0; lf < 4; ++lf) {
+        const int leaf = node * 4 + lf;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-    for (int g = leaf * m; g < (leaf + 1) * m; ++g) {
-        __syncthreads();  // the previous group's tiles are consumed
-        // activations: 32 tokens x 64 columns bf16 -> fp32 (8 columns per uint4)
+            for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+        for (int g = leaf * m; g < (leaf + 1) * m; ++g) {
+            __syncthreads();  // the previous group's tiles are consumed
+            // activations: 64 tokens x 64 columns bf16 -> fp32 (8 columns per uint4)
 #pragma unroll
-        for (int u = 0; u < kRT * 8 / kLeafThreads; ++u) {
-            const int i = tid + kLeafThreads * u, r = i >> 3, c8 = i & 7, t = t0 + r;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (t < T) v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + (size_t)g * 64) + c8);
-            const uint32_t q[4] = {v.x, v.y, v.z, v.w};
-            float* d = &xs[r][c8 * 8];
+            for (int u = 0; u < kRT * 8 / kLeafThreads; ++u) {
+                const int i = tid + kLeafThreads * u, r = i >> 3, c8 = i & 7, t = t0 + r;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (t < T) v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + (size_t)g * 64) + c8);
+                const uint32_t q[4] = {v.x, v.y, v.z, v.w};
+                float* d = &xs[r][c8 * 8];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) d[2 * c] = __uint_as_float(q[c] << 16), d[2 * c + 1] = __uint_as_float(q[c] & 0xFFFF0000u);
-        }
-        // weights: 128 experts x 64 codes (16 per uint4), w = q * s + b (dequant_matvec_8bit.metal:26)
-#pragma unroll
-        for (int u = 0; u < kRE * 4 / kLeafThreads; ++u) {
-            const int i = tid + kLeafThreads * u, r = i >> 2, c16 = i & 3, e = e0 + r;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            float sc = 0.0f, bi = 0.0f;
-            if (e < E) {
-                v = __ldg(reinterpret_cast<const uint4*>(w + (size_t)e * (H / 4) + (size_t)g * 16) + c16);
-                sc = bf2f(s[(size_t)e * G + g]);
-                bi = bf2f(b[(size_t)e * G + g]);
+                for (int c = 0; c < 4; ++c) d[2 * c] = __uint_as_float(q[c] << 16), d[2 * c + 1] = __uint_as_float(q[c] & 0xFFFF0000u);
             }
-            const uint32_t q[4] = {v.x, v.y, v.z, v.w};
-            float* d = &ws[r][c16 * 16];
+            // weights: 128 experts x 64 codes (16 per uint4), w = q * s + b (dequant_matvec_8bit.metal:26)
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
+            for (int u = 0; u < kRE * 4 / kLeafThreads; ++u) {
+                const int i = tid + kLeafThreads * u, r = i >> 2, c16 = i & 3, e = e0 + r;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                float sc = 0.0f, bi = 0.0f;
+                if (e < E) {
+                    v = __ldg(reinterpret_cast<const uint4*>(w + (size_t)e * (H / 4) + (size_t)g * 16) + c16);
+                    sc = bf2f(s[(size_t)e * G + g]);
+                    bi = bf2f(b[(size_t)e * G + g]);
+                }
+                const uint32_t q[4] = {v.x, v.y, v.z, v.w};
+                float* d = &ws[r][c16 * 16];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) d[4 * c + j] = __fmaf_rn((float)((q[c] >> (8 * j)) & 0xFFu), sc, bi);
-        }
-        __syncthreads();
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) d[4 * c + j] = __fmaf_rn((float)((q[c] >> (8 * j)) & 0xFFu), sc, bi);
+            }
+            __syncthreads();
 #pragma unroll 2
-        for (int j = 0; j < 64; j += 4) {
-            float4 xv[4], wv[8];
+            for (int j = 0; j < 64; j += 4) {
+                float4 xv[4], wv[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[tt + 16 * i][j]);
+                for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[tt + 16 * i][j]);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) wv[i] = *reinterpret_cast<const float4*>(&ws[te + 16 * i][j]);
-            // column by column: 32 independent FMAs per column, each chain in column order
+                for (int i = 0; i < 8; ++i) wv[i] = *reinterpret_cast<const float4*>(&ws[te + 16 * i][j]);
+                // column by column: 32 independent FMAs per column, each chain in column order
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+                for (int a = 0; a < 4; ++a)
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].x, xv[a].x, acc[a][c]);
+                    for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].x, xv[a].x, acc[a][c]);
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+                for (int a = 0; a < 4; ++a)
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].y, xv[a].y, acc[a][c]);
+                    for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].y, xv[a].y, acc[a][c]);
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+                for (int a = 0; a < 4; ++a)
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].z, xv[a].z, acc[a][c]);
+                    for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].z, xv[a].z, acc[a][c]);
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+                for (int a = 0; a < 4; ++a)
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].w, xv[a].w, acc[a][c]);
+                    for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c].w, xv[a].w, acc[a][c]);
+            }
         }
+        // the first two tree levels: (l0 + l1) + (l2 + l3)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (lf == 0) first[i][j] = acc[i][j];
+                else if (lf == 1) pair[i][j] = __fadd_rn(first[i][j], acc[i][j]);
+                else if (lf == 2) first[i][j] = acc[i][j];
+                else pair[i][j] = __fadd_rn(pair[i][j], __fadd_rn(first[i][j], acc[i][j]));
+            }
     }
-    // leaf sums out through shared memory ([token][expert]) for coalesced stores
+    // node sums out through shared memory ([token][expert]) for coalesced stores
     __syncthreads();
     float(*os)[kRE + 4] = reinterpret_cast<float(*)[kRE + 4]>(rsm);
 #pragma unroll
     for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int c = 0; c < 8; ++c) os[tt + 16 * a][te + 16 * c] = acc[a][c];
+        for (int c = 0; c < 8; ++c) os[tt + 16 * a][te + 16 * c] = pair[a][c];
     __syncthreads();
-    float* pl = parts + (size_t)leaf * T * E;
+    float* pl = parts + (size_t)node * T * E;
     for (int i = tid; i < kRT * kRE; i += kLeafThreads) {
         const int r = i / kRE, c = i % kRE, t = t0 + r, e = e0 + c;
         if (t < T && e < E) pl[(size_t)t * E + e] = os[r][c];
     }
 }
 
-// logit = the adjacent pairwise tree over the 32 leaf sums
-__device__ __forceinline__ float tree32(const float* __restrict__ p, size_t plane, size_t i) {
-    float v[16];
-#pragma unroll
-    for (int l = 0; l < 16; ++l) v[l] = __fadd_rn(p[(2 * l) * plane + i], p[(2 * l + 1) * plane + i]);
-#pragma unroll
-    for (int n = 8; n > 0; n >>= 1)
-#pragma unroll
-        for (int l = 0; l < n; ++l) v[l] = __fadd_rn(v[2 * l], v[2 * l + 1]);
-    return v[0];
+// logit = the rest of the adjacent pairwise tree over the 8 node sums
+__device__ __forceinline__ float tree8(const float* __restrict__ p, size_t plane, size_t i) {
+    const float n0 = p[i], n1 = p[plane + i], n2 = p[2 * plane + i], n3 = p[3 * plane + i];
+    const float n4 = p[4 * plane + i], n5 = p[5 * plane + i], n6 = p[6 * plane + i], n7 = p[7 * plane + i];
+    return __fadd_rn(__fadd_rn(__fadd_rn(n0, n1), __fadd_rn(n2, n3)), __fadd_rn(__fadd_rn(n4, n5), __fadd_rn(n6, n7)));
 }
 
 __global__ void k_router_finish(const float* __restrict__ parts, size_t n, float* __restrict__ logits) {
     pdl_begin();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        logits[i] = tree32(parts, n, i);
+        logits[i] = tree8(parts, n, i);
 }
 
 // ---------------------------------------------------------------------- top-k
@@ -181,7 +194,7 @@ __global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, 
         const int tt = i / E, e = i - tt * E, t = t0 + tt;
         if (t < T) {
             const size_t idx = (size_t)t * E + e;
-            const float l = nparts == kLeaves ? tree32(logits, plane, idx) : logits[idx];
+            const float l = nparts == kNodes ? tree8(logits, plane, idx) : logits[idx];
             s_l[tt][e] = l;
             if (logits_out) logits_out[idx] = l;
         }
@@ -202,7 +215,7 @@ __global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, 
 
 }  // namespace
 
-int router_parts(int T) { return T <= 2 * kWarpTok ? 1 : kLeaves; }
+int router_parts(int T) { return T <= 2 * kWarpTok ? 1 : kNodes; }
 
 cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint16_t* x, int T, float* parts,
                                  cudaStream_t st, int32_t* zero_counts) {
@@ -217,7 +230,7 @@ cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint1
         cudaError_t e = cudaFuncSetAttribute(k_router_leaf, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kLeafSmem);  // 52 KB of dynamic shared memory
         if (e != cudaSuccess) return e;
-        dim3 grid((T + kRT - 1) / kRT, (sh.E + kRE - 1) / kRE, kLeaves);
+        dim3 grid((T + kRT - 1) / kRT, (sh.E + kRE - 1) / kRE, kNodes);
         {
             const cudaError_t le_ = launch_pdl(k_router_leaf, dim3(grid), dim3(kLeafThreads), kLeafSmem, st, L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E,
                                                               parts, zero_counts);

@@ -252,7 +252,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     const int DT = ctx->decode_max > 0 ? kDecodeMaxT : 0;
     struct Item { void** p; size_t bytes; };
     std::vector<Item> items = {
-        {(void**)&ctx->logits, (size_t)32 * T * E * 4},  // router leaf planes (router_parts)
+        {(void**)&ctx->logits, (size_t)8 * T * E * 4},  // router partial planes (router_parts)
         {(void**)&ctx->ids, (size_t)T * K * 4},
         {(void**)&ctx->wts, (size_t)T * K * 4},
         {(void**)&ctx->disp.counts, (size_t)E * 4},
