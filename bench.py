@@ -244,7 +244,7 @@ def run_stack(args, rank, world, local, ranks):
     shape = obsmoe.MoeShape(H, I, E, K, n_layers=nl, max_tokens=max(T, 16), decode_max_tokens=args.decode_max,
                             ep_world=world if ep else 1, ep_rank=rank if ep else 0)
     ctx = obsmoe.MoeContext(shape, local)
-    decode_max = args.decode_max if args.decode_max > 0 else 2
+    decode_max = args.decode_max if args.decode_max > 0 else 4  # the library's default
     if ep:
         ctx.ep_connect(ranks.gather(ctx.ep_handle()))
     for l in range(nl):

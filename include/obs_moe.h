@@ -64,7 +64,7 @@ typedef struct obs_config {
     int32_t n_layers;          /* layers whose weights the context holds */
     int32_t max_tokens;        /* largest T of one call (sizes the scratch) */
     int32_t norm_topk;         /* renormalise the top-k weights (norm_topk_prob) */
-    int32_t decode_max_tokens; /* OBS_PATH_AUTO threshold; <= 0 picks 2 */
+    int32_t decode_max_tokens; /* OBS_PATH_AUTO threshold; <= 0 picks 4 */
     float rms_eps;             /* RMSNorm epsilon of the fused input norm */
     int32_t ep_world;          /* expert parallelism: ranks sharing the experts (<= 1: off, max 8) */
     int32_t ep_rank;           /* this context's rank: it holds experts [rank*E/world, (rank+1)*E/world) */
@@ -259,7 +259,7 @@ int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert, const uin
 enum obs_stage {
     OBS_STAGE_ROUTER = 0, OBS_STAGE_TOPK = 1, OBS_STAGE_DISPATCH = 2, OBS_STAGE_GEMM_GATEUP = 3,
     OBS_STAGE_GEMM_DOWN = 4, OBS_STAGE_COMBINE = 5, OBS_STAGE_DECODE_GATEUP = 6, OBS_STAGE_DECODE_DOWN = 7,
-    OBS_STAGE_DECODE_FUSED = 8  /* the whole decode layer in one launch (T <= 4) */
+    OBS_STAGE_DECODE_FUSED = 8  /* the whole decode layer in one launch (T <= 8) */
 };
 int obs_profile_enable(obs_ctx* ctx, int enable);
 int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches);
@@ -271,12 +271,13 @@ int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches);
  * for lane quarters 1-3, 4 MMA pair ready, 9 MMA fence passed, 5 MMA pair
  * committed (per pair of k-steps), 6 epilogue start, 7 epilogue done (per
  * item), 13 token tile landed (per k-step).
- * When 14 * n_steps >= 16 * (SM count), the fused decode layer (T <= 4) writes
- * instead, for every CTA b, trace[16b + k]: k = 0 start, 1 router done, 2 grid
- * barrier passed, 3 weight copies issued, 4 gate/up done, 5 first h row ready,
- * 6 down + combine done, 7 top-k done, 8/9/10 first gate/up unit of half 0
- * landed/computed/done, 11/12 its second unit landed/done, 13/14 the first
- * down unit landed/y written (0 where a CTA has no such unit).
+ * When 14 * n_steps >= 24 * (SM count), the fused decode layer (T <= 8) writes
+ * instead, for every CTA b, trace[24b + k]: k = 0 start, 1 router row done,
+ * 2 stamped logits seen, 3 weight copies issued, 4 tiles done, 5 first combine
+ * job's partials seen, 6 end, 7 top-k and input packs done, 8/9/10 first
+ * tile's data landed / gate-up computed / tile done, 13/14 its down column
+ * group landed / partials stored, 16-18 inside top-k (0 where a CTA has no
+ * such phase).
  * trace = NULL switches it off.  Device memory of 14 * n_steps uint64. */
 int obs_trace_enable(obs_ctx* ctx, uint64_t* trace, int n_steps);
 /* No counterpart in the reference.  *count = the number of kernel launches the
@@ -286,6 +287,13 @@ int obs_kernel_launches(uint64_t* count);
 /* Waits for the stream and reports any device-side error flag (bounded waits
  * that gave up) raised since the last check; clears the flags. */
 int obs_check_device(obs_ctx* ctx, void* stream);
+/* Test hook, no counterpart in the reference: runs the gate/up grouped GEMM of
+ * `layer` over a caller-given token-tile list (host int32 [n_tiles][4]:
+ * expert, first row, rows, 0) on the context's activation scratch.  The GEMM
+ * validates every tile (expert id, row range, the count against the tile
+ * buffer) before any work; a bad list makes every CTA skip its work and
+ * obs_check_device report OBS_ERR_INVALID.  Synchronises on the stream. */
+int obs_debug_gemm_tiles(obs_ctx* ctx, int layer, const int32_t* tiles, int n_tiles, void* stream);
 /* No counterpart in the reference (its waits are host-side and unbounded,
  * src/router.rs:47-48).  Every device-side wait of the context's kernels (GEMM
  * pipeline barriers, the fused decode layer's grid barriers, expert-parallel

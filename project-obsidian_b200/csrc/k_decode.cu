@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __
 int down_threads(int I) { return 32 * (I / kGroup < 16 ? I / kGroup : 16); }
 
 // ----------------------------------------------------------- fused decode layer
-// One cooperative launch runs the whole decode layer for T <= 4 tokens, one
+// One cooperative launch runs the whole decode layer for T <= 8 tokens, one
 // CTA of 16 warps per SM, with no grid-wide barrier:
 //   0  warp 0 takes the CTA's ticket (launch generation = ticket / grid size)
 //      and, for an input given as is, computes its router row (expert b)

@@ -204,12 +204,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
     const uint32_t tmem = *tmem_slot;
     const int n_tiles = *a.n_tiles;
     // (each tile holds >= 16 rows, so a count above atoms / 2 is corrupt)
-    const int n_items = n_tiles >= 0 && n_tiles <= a.atoms / 2 ? n_tiles * a.n_rt : 0;
+    const bool count_ok = n_tiles >= 0 && n_tiles <= a.atoms / 2 && n_tiles <= a.max_tiles;
+    const int n_items = count_ok ? n_tiles * a.n_rt : 0;
     const int KS = a.n_kt / kKS;  // MMA steps per item (even: n_kt is a multiple of 4)
     // Every role walks the same items, so a tile outside the buffers (a corrupt
     // tile list) is refused up front by the whole CTA: error recorded, no work.
     {
-        bool bad = n_tiles < 0 || n_tiles > a.atoms / 2;
+        bool bad = !count_ok;
         for (int item = blockIdx.x + tid * gridDim.x; item < n_items; item += blockDim.x * gridDim.x) {
             const int4 tl = a.tiles[item / a.n_rt];
             bad |= tl.x < 0 || tl.x >= a.n_experts || tl.y < 0 || (tl.y & 15) || tl.z < kSegAlign || tl.z > a.bn ||

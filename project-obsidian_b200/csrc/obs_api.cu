@@ -74,7 +74,7 @@ struct obs_ctx {
     bool hs_ready = false;
     uint16_t* xnorm_dev = nullptr;  // the layer stack's normalised input
     uint16_t* rtmp_dev = nullptr;   // the layer stack's other residual buffer
-    int R_cap = 0, max_tiles = 0, decode_max = 2;
+    int R_cap = 0, max_tiles = 0, decode_max = kDecodeAutoT;
     uint64_t wait_ns = kDefaultWaitNs;  // limit of every bounded device wait (obs_set_wait_limit)
     uint32_t* probe_stamp = nullptr;    // a stamp nothing writes (obs_probe_wait)
     uint64_t* trace = nullptr;  // obs_trace_enable
@@ -207,7 +207,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
     ctx->E_local = s.E / ctx->ep_world;
     ctx->e0 = ctx->ep_rank * ctx->E_local;
     // measured on B200: the mat-vec (fused) layer wins up to 2 tokens, the grouped GEMM from 3
-    ctx->decode_max = cfg->decode_max_tokens > 0 ? cfg->decode_max_tokens : 2;
+    ctx->decode_max = cfg->decode_max_tokens > 0 ? cfg->decode_max_tokens : kDecodeAutoT;
     if (ctx->decode_max > kDecodeMaxT) ctx->decode_max = kDecodeMaxT;
     ctx->device = device;
     cudaError_t e = cudaSetDevice(device);
@@ -741,6 +741,7 @@ static GemmArgs gemm_gateup(obs_ctx* ctx, const LayerDev& L, const uint16_t* x) 
     g.atoms = ctx->disp.atoms;
     g.tiles = ctx->disp.tiles;
     g.n_tiles = ctx->disp.n_tiles;
+    g.max_tiles = ctx->max_tiles;
     g.n_rt = s.I / 64;
     g.n_kt = s.H / kGroup;
     g.bn = ctx->disp.bn;
@@ -764,6 +765,7 @@ static GemmArgs gemm_down(obs_ctx* ctx, const LayerDev& L) {
     g.atoms = ctx->disp.atoms;
     g.tiles = ctx->disp.tiles;
     g.n_tiles = ctx->disp.n_tiles;
+    g.max_tiles = ctx->max_tiles;
     g.n_rt = s.H / kRowTile;
     g.n_kt = s.I / kGroup;
     g.bn = ctx->disp.bn;
@@ -780,6 +782,22 @@ static GemmArgs gemm_down(obs_ctx* ctx, const LayerDev& L) {
 static int prefill_ffn(obs_ctx* ctx, const LayerDev& L, const uint16_t* x, cudaStream_t st) {
     CU(launch_gemm(gemm_gateup(ctx, L, x), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");
     CU(launch_gemm(gemm_down(ctx, L), kEpiBf16, ctx->num_sms, st), "gemm down");
+    return OBS_OK;
+}
+
+extern "C" int obs_debug_gemm_tiles(obs_ctx* ctx, int layer, const int32_t* tiles, int n_tiles, void* stream) {
+    OBS_CHECK_CTX(ctx);
+    if (ctx->ep_world > 1) return fail(ctx, OBS_ERR_UNSUPPORTED, "single-GPU only (ep_world > 1)");
+    int rc = check_layer(ctx, layer, true);
+    if (rc) return rc;
+    if (!tiles || n_tiles < 0) return fail(ctx, OBS_ERR_INVALID, "bad tile list");
+    cudaStream_t st = as_stream(stream);
+    const int n_copy = n_tiles < ctx->max_tiles ? n_tiles : ctx->max_tiles;  // the count itself is not clipped
+    if (n_copy)
+        CU(cudaMemcpyAsync(ctx->disp.tiles, tiles, (size_t)n_copy * 16, cudaMemcpyHostToDevice, st), "copy");
+    CU(cudaMemcpyAsync(ctx->disp.n_tiles, &n_tiles, 4, cudaMemcpyHostToDevice, st), "copy");
+    CU(cudaStreamSynchronize(st), "sync");  // the host arrays may go away after the call
+    CU(launch_gemm(gemm_gateup(ctx, ctx->layers[layer], nullptr), kEpiSwiglu, ctx->num_sms, st), "gemm gate/up");
     return OBS_OK;
 }
 
@@ -840,6 +858,7 @@ extern "C" int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert
     g.atoms = ctx->disp.atoms;
     g.tiles = ctx->disp.tiles;
     g.n_tiles = ctx->disp.n_tiles;
+    g.max_tiles = ctx->max_tiles;
     g.n_rt = proj == 2 ? out_f / kRowTile : out_f / 64;
     g.n_kt = in_f / kGroup;
     g.bn = kBNTile;

@@ -160,7 +160,12 @@ struct DecodeBufs {
 };
 // The fused decode layer (router -> top-k -> gate/up -> SwiGLU -> down ->
 // combine in one cooperative launch) for T <= kFusedMaxT tokens.
-constexpr int kFusedMaxT = 4;
+constexpr int kFusedMaxT = 8;
+// OBS_PATH_AUTO's default decode threshold: measured on B200 at the model's
+// shape, the fused layer beats the grouped GEMM to T = 4 (37 vs 59 us per
+// layer) and loses at T = 8 (68 vs 63 us: it reads each (token, expert) pair's
+// weights, the GEMM each routed expert's once)
+constexpr int kDecodeAutoT = 4;
 struct FusedDecodeBufs {
     uint64_t* lst;      // [4][kFusedMaxT][E] logit bits | launch stamp << 32: router logits, four replicas
     int32_t* ids;       // [T][K]
@@ -230,6 +235,7 @@ struct GemmArgs {
     int atoms;                // row atoms of the activation layout
     const int4* tiles;        // token tiles {expert, row0, nrows, 0}
     const int32_t* n_tiles;   // device count of token tiles
+    int max_tiles;            // entries of the tiles buffer (a larger count is refused)
     int n_rt;                 // weight row tiles per expert (I/64 for the paired array, H/128 for down)
     int n_kt;                 // k-tiles (in / 64), a multiple of 4
     int bn;                   // max token rows per tile (<= 128)

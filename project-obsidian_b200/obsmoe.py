@@ -34,7 +34,7 @@ EXPORTS = (
     "obs_trace_enable", "obs_decode_ffn_static", "obs_kernel_launches", "obs_ep_handle", "obs_ep_connect",
     "obs_rmsnorm", "obs_moe_stack_forward", "obs_set_wait_limit", "obs_probe_wait", "obs_struct_layout",
     "obs_load_layer_safetensors", "obs_expert_file_info", "obs_load_head", "obs_embed", "obs_lm_head",
-    "obs_attn_init", "obs_load_attn", "obs_attn_forward", "obs_kv_read",
+    "obs_attn_init", "obs_load_attn", "obs_attn_forward", "obs_kv_read", "obs_debug_gemm_tiles",
 )
 EP_HANDLE_BYTES = 64
 STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down",
@@ -120,6 +120,7 @@ def lib() -> C.CDLL:
         L.obs_load_head.argtypes = [vp, i32, C.POINTER(HeadWeights), i32]
         L.obs_embed.argtypes = [vp, vp, i32, vp, vp]
         L.obs_lm_head.argtypes = [vp, vp, i32, vp, vp, vp]
+        L.obs_debug_gemm_tiles.argtypes = [vp, i32, vp, i32, vp]
         L.obs_attn_init.argtypes = [vp, C.POINTER(AttnConfig)]
         L.obs_load_attn.argtypes = [vp, i32, C.POINTER(AttnWeights), i32]
         L.obs_attn_forward.argtypes = [vp, i32, vp, vp, i32, vp, vp, vp]
@@ -329,6 +330,13 @@ class MoeContext:
     def trace(self, buf, n_steps: int):
         """Record the gate/up GEMM pipeline timeline of CTA 0 into buf (uint64 [8, n_steps])."""
         self._chk(lib().obs_trace_enable(self._h, _ptr(buf), n_steps if buf is not None else 0))
+
+    def debug_gemm_tiles(self, layer, tiles, stream=None):
+        """Test hook: the gate/up GEMM over a given tile list (numpy int32 [n][4])."""
+        import numpy as np
+
+        t = np.ascontiguousarray(tiles, dtype=np.int32).reshape(-1, 4)
+        self._chk(lib().obs_debug_gemm_tiles(self._h, layer, t.ctypes.data, len(t), _stream(stream)))
 
     def check_device(self, stream=None):
         self._chk(lib().obs_check_device(self._h, _stream(stream)))

@@ -51,3 +51,36 @@ def test_bounded_wait_runs_out_and_context_survives(cuda):
     with pytest.raises(obsmoe.ObsError, match="wait limit"):
         ctx.set_wait_limit(1000)  # below 1 ms
     ctx.close()
+
+
+@pytest.mark.parametrize("case", ["expert", "rows_past_buffer", "rows_unaligned", "rows_above_tile", "count"])
+def test_corrupt_gemm_tiles_are_refused(cuda, case):
+    """A token-tile list the dispatch could never produce (made on the host and handed
+    to the gate/up GEMM through obs_debug_gemm_tiles) is refused by the GEMM's own
+    check before any work: kDevBadTile, reported as OBS_ERR_INVALID; the context keeps
+    working afterwards."""
+    torch = cuda
+    E, H, I, K, T = 16, 2048, 256, 4, 64
+    ctx = obsmoe.MoeContext(obsmoe.MoeShape(H, I, E, K, n_layers=1, max_tokens=T), 0)
+    ctx.load_layer(0, O.synth_layer(4, 0, E=E, H=H, I=I, K=K))
+    good = [[0, 0, 16, 0], [3, 16, 32, 0]]
+    ctx.debug_gemm_tiles(0, good)
+    ctx.check_device()  # a valid list runs
+    bad = {"expert": [[E, 0, 16, 0]],
+           "rows_past_buffer": [[1, 100000, 16, 0]],
+           "rows_unaligned": [[1, 0, 24, 0]],
+           "rows_above_tile": [[1, 0, 128, 0]],
+           # more tiles than the tile buffer holds (each entry valid on its own)
+           "count": [[0, 0, 16, 0]] * 1000}[case]
+    ctx.debug_gemm_tiles(0, bad)
+    with pytest.raises(obsmoe.ObsError, match="GEMM tile") as ei:
+        ctx.check_device()
+    assert ei.value.status == 1  # OBS_ERR_INVALID
+    x = dev(torch, O.synth_x(4, 0, 8, H))
+    a = torch.empty((8, H), dtype=torch.int16, device="cuda")
+    b = torch.empty((8, H), dtype=torch.int16, device="cuda")
+    ctx.moe_forward(0, x, a, 8, path=obsmoe.PATH_PREFILL)
+    ctx.moe_forward(0, x, b, 8, path=obsmoe.PATH_PREFILL)
+    ctx.check_device()
+    assert torch.equal(a, b)
+    ctx.close()

@@ -1,6 +1,6 @@
-"""The fused decode layer (one cooperative launch for T <= 4) against the
+"""The fused decode layer (one cooperative launch for T <= 8) against the
 separate decode kernels (router, top-k, gate/up mat-vec, down mat-vec, combine
-as four launches, taken for T = 5).  Every output row depends on its own input
+as separate launches, taken for T = 9).  Every output row depends on its own input
 row only, so rows [r, r+T) of a fused call on x[r:r+T] must equal the same rows
 of the separate kernels' call on all of x, bit for bit: same router order, same
 split-K chains, same combine order.  Also checked against the oracle."""
@@ -31,7 +31,7 @@ def forward(torch, ctx, x, res, bias, T):
 @pytest.mark.parametrize("E,I,K,seed", [(16, 256, 4, 17), (128, 768, 8, 0)])
 def test_fused_decode_equals_separate_kernels(cuda, E, I, K, seed):
     torch = cuda
-    H, N = 2048, 5
+    H, N = 2048, 9
     L = O.synth_layer(seed, 0, E=E, H=H, I=I, K=K)
     ctx = obsmoe.MoeContext(obsmoe.MoeShape(H, I, E, K, n_layers=1, max_tokens=16), 0)
     ctx.load_layer(0, L)
@@ -41,8 +41,8 @@ def test_fused_decode_equals_separate_kernels(cuda, E, I, K, seed):
     bias[3] = 0.75
     x, r, b = dev(torch, xn), dev(torch, rn), dev(torch, bias)
     for with_res in (False, True):
-        ref = forward(torch, ctx, x, r if with_res else None, b, N)  # T = 5: separate kernels
-        for T in (1, 2, 3, 4):
+        ref = forward(torch, ctx, x, r if with_res else None, b, N)  # T = 9: separate kernels
+        for T in (1, 2, 3, 4, 8):
             for r0 in sorted({0, N - T}):
                 got = forward(torch, ctx, x[r0:r0 + T], r[r0:r0 + T] if with_res else None, b, T)
                 assert np.array_equal(got, ref[r0:r0 + T]), (T, r0, with_res)
