@@ -89,6 +89,9 @@ def parse():
     ap.add_argument("--decode-max", type=int, default=0,
                     help="largest T the decode (mat-vec) path takes under OBS_PATH_AUTO (0: the library's default)")
     ap.add_argument("--ref-tokens", type=int, default=256, help="reference arm: tokens per step (a slice of T)")
+    ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="expert parallelism: experts placed on the GPUs by the routed loads of a separate "
+                         "calibration batch (balanced), or GPU g holding experts [g*E/G, (g+1)*E/G)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: N data-parallel replicas (every GPU holds all experts) instead of expert parallelism")
     return ap.parse_args()
@@ -227,6 +230,30 @@ def calibrate_beta(ctx, r0, T):
     return best
 
 
+def layer_loads(ctx, r_in, nl, T, bias, path, stream):
+    """Routed rows per expert of this rank's T tokens at every layer of the stack (the residual
+    stream advanced through each layer), [nl][E], and the ids of each layer."""
+    import numpy as np
+    import torch
+
+    logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    xn = torch.empty_like(r_in)
+    rr = r_in.clone()
+    counts, all_ids = [], []
+    for l in range(nl):
+        ctx.rmsnorm(rr, xn, T)
+        ctx.gate_gpu(l, xn, logits, T)
+        ctx.route(logits, T, ids, wts, bias=bias)
+        mine = ids.cpu().numpy().ravel()
+        all_ids.append(mine)
+        counts.append(np.bincount(mine, minlength=E))
+        ctx.moe_stack_forward(l, 1, rr, T, bias=bias, path=path, stream=stream)
+    torch.cuda.synchronize()
+    return counts, all_ids
+
+
 def run_stack(args, rank, world, local, ranks):
     """Configs 2 and 3: a stack of MoE layers on a residual stream; a step is one
     pass of the batch through every layer, captured in one CUDA graph."""
@@ -257,6 +284,19 @@ def run_stack(args, rank, world, local, ranks):
         beta, imbalance0 = calibrate_beta(ctx, r0, T)
         beta = ranks.gather(beta)[0]  # every rank uses rank 0's bias
         bias = zipf_bias_device(beta)
+    placement = None
+    if ep and args.placement == "balanced":
+        # per-layer expert loads of a separate calibration batch (other seeded tokens), summed over
+        # the ranks; the same plan on every rank; the layers are generated again for the new placement
+        rcal = torch.empty_like(r0)
+        obsmoe.synth_activations(rank, 0, T, T, H, rcal)
+        cal, _ = layer_loads(ctx, rcal, nl, T, bias, path, stream)
+        tot = np.sum(ranks.gather(np.stack(cal)), axis=0)
+        placement = [obsmoe.plan_placement(tot[l], world) for l in range(nl)]
+        for l in range(nl):
+            ctx.ep_set_placement(l, placement[l])
+            ctx.synth_layer(l, 0)
+        ranks.barrier()
     r = torch.empty_like(r0)
 
     def step(s=stream):
@@ -321,29 +361,24 @@ def run_stack(args, rank, world, local, ranks):
     stage_us = {k: round(v[0] / max(v[1], 1) * 1e3, 2) for k, v in prof.items() if v[1]}
 
     # ---------------------------------- per-layer routing of this step (the same inputs), eagerly
-    logits = torch.empty((T, E), dtype=torch.float32, device="cuda")
-    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
-    wts = torch.empty((T, K), dtype=torch.float32, device="cuda")
-    xn = torch.empty_like(r0)
-    rr = r0.clone()
+    _, step_ids = layer_loads(ctx, r0, nl, T, bias, path, stream)
     U, loads, local_rows, sent_rows = [], [], [], []
     EL = E // world if ep else E
     for l in range(nl):
-        ctx.rmsnorm(rr, xn, T)
-        ctx.gate_gpu(l, xn, logits, T)
-        ctx.route(logits, T, ids, wts, bias=bias)
-        mine = ids.cpu().numpy().ravel()
+        mine = step_ids[l]
+        # gpu_of[e]: the GPU holding expert e at this layer
+        gpu_of = np.arange(E) // EL
+        if placement is not None:
+            gpu_of[np.asarray(placement[l])] = np.arange(E) // EL
         if ep:  # rows this rank sends to other ranks: once per (token, rank); outputs back per (token, expert)
-            dest = (mine // EL).reshape(T, K)
+            dest = gpu_of[mine].reshape(T, K)
             sent_rows.append((sum(int(np.sum(np.any(dest == d, axis=1))) for d in range(world) if d != rank),
                               int(np.sum(dest != rank))))
         every = np.concatenate(ranks.gather(mine)) if ep else mine
         U.append(len(np.unique(every)))
         cnt = np.bincount(every, minlength=E)
         loads.append(cnt)
-        local_rows.append(int(cnt[rank * EL:(rank + 1) * EL].sum()) if ep else int(cnt.sum()))
-        ctx.moe_stack_forward(l, 1, rr, T, bias=bias, path=path, stream=stream)
-    torch.cuda.synchronize()
+        local_rows.append(int(cnt[gpu_of == rank].sum()) if ep else int(cnt.sum()))
     load = np.sum(loads, axis=0)
     hbm, bf16, bf16_sus, peak_kind = peaks()
     if decode:
@@ -394,6 +429,9 @@ def run_stack(args, rank, world, local, ranks):
         rows_per_gpu = ranks.gather(float(np.mean(local_rows)))
         sent = ranks.gather([float(np.mean([r[0] for r in sent_rows])), float(np.mean([r[1] for r in sent_rows]))])
         line["ep"] = {"experts_per_gpu": EL,
+                      "placement": ("balanced: per-layer greedy plan (obs_ep_plan_placement) from the routed "
+                                    "loads of a separate seeded calibration batch" if placement is not None else
+                                    "contiguous: GPU g holds experts [g*E/G, (g+1)*E/G)"),
                       "rows_per_gpu_per_layer": rows_per_gpu,
                       "gpu_rows_max_over_mean": float(max(rows_per_gpu) / np.mean(rows_per_gpu)),
                       "a2a_bytes_per_gpu_per_layer": {"dispatch": [s[0] * H * 2 for s in sent],

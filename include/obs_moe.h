@@ -255,11 +255,16 @@ int obs_expert_gemm_f32(obs_ctx* ctx, int layer, int proj, int expert, const uin
  * every kernel launch of the layer is bracketed by CUDA events on the
  * caller's stream.  obs_profile_read fills ms_total[OBS_N_STAGES] and
  * launches[OBS_N_STAGES] with the sums since the last read, then resets. */
-#define OBS_N_STAGES 9
+#define OBS_N_STAGES 12
 enum obs_stage {
     OBS_STAGE_ROUTER = 0, OBS_STAGE_TOPK = 1, OBS_STAGE_DISPATCH = 2, OBS_STAGE_GEMM_GATEUP = 3,
     OBS_STAGE_GEMM_DOWN = 4, OBS_STAGE_COMBINE = 5, OBS_STAGE_DECODE_GATEUP = 6, OBS_STAGE_DECODE_DOWN = 7,
-    OBS_STAGE_DECODE_FUSED = 8  /* the whole decode layer in one launch (T <= 8) */
+    OBS_STAGE_DECODE_FUSED = 8, /* the whole decode layer in one launch (T <= 8) */
+    /* expert parallelism (ep_world > 1): the rows' sends to the owning GPUs; the wait for
+     * every source and the received rows' routing table; the wait for every GPU's returned
+     * outputs.  DISPATCH then covers the local dispatch of the received rows and COMBINE
+     * the combine alone. */
+    OBS_STAGE_EP_SEND = 9, OBS_STAGE_EP_RECV = 10, OBS_STAGE_EP_RETURN = 11
 };
 int obs_profile_enable(obs_ctx* ctx, int enable);
 int obs_profile_read(obs_ctx* ctx, float* ms_total, int32_t* launches);
@@ -356,6 +361,21 @@ int obs_moe_stack_forward(obs_ctx* ctx, int layer0, int n_layers, uint16_t* resi
 #define OBS_EP_HANDLE_BYTES 64
 int obs_ep_handle(obs_ctx* ctx, void* handle);
 int obs_ep_connect(obs_ctx* ctx, const void* handles);
+/* Expert placement (ep_world > 1).  experts[E] lists the global experts by slot:
+ * GPU g holds experts[g*E/G .. (g+1)*E/G) as its local experts 0 .. E/G-1; every
+ * expert appears once.  layer = -1 sets every layer.  Every rank must set the
+ * same table.  A layer whose table changes is marked not loaded: load (or
+ * synthesise) its weights again; obs_load_layer then keeps the listed experts.
+ * The default is the identity (GPU g holds experts [g*E/G, (g+1)*E/G)).  The
+ * result of a forward does not depend on the placement (bit for bit). */
+int obs_ep_set_placement(obs_ctx* ctx, int layer, const int32_t* experts);
+int obs_ep_get_placement(obs_ctx* ctx, int layer, int32_t* experts);
+/* A balanced placement from per-expert loads (routed rows, e.g. a calibration
+ * batch's histogram summed over the ranks); host only, no context.  Experts in
+ * decreasing load (ties: lower id first) each go to the GPU with the smallest
+ * total load among those with fewer than E/G experts (ties: lower GPU); each
+ * GPU's experts are then listed in increasing id.  Writes experts[E]. */
+int obs_ep_plan_placement(const int64_t* load, int n_experts, int world, int32_t* experts);
 
 /* ------------------------------------------- allocation-free decode FFN */
 /* No counterpart in the reference.  For callers that cannot allocate device

@@ -41,12 +41,12 @@ __device__ __forceinline__ void rope_pair(float x0, float x1, float c, float s, 
 // [T][nq*hd + 2*nkv*hd] (q | k | v).  The head's rms in rmsnorm.metal's order
 // (256 "threads" strided over hd, halving tree) -- here 128 threads carry the
 // first 128 partials and the upper 128 are zero, which is the same sum.
-__global__ void __launch_bounds__(kAttnThreads) k_qk_norm_rope(const float* __restrict__ qkv, int T, int nq, int nkv,
+__global__ void __launch_bounds__(kAttnThreads) k_qk_norm_rope(const float* qkv, int T, int nq, int nkv,
                                                                int hd, const uint16_t* __restrict__ qn,
                                                                const uint16_t* __restrict__ kn, float eps,
                                                                const float* __restrict__ rope_cs, int max_seq,
-                                                               const int32_t* __restrict__ seq,
-                                                               const int32_t* __restrict__ pos,
+                                                               const int32_t* seq,
+                                                               const int32_t* pos,
                                                                uint16_t* __restrict__ qout, uint16_t* kcache,
                                                                uint16_t* vcache, int n_seqs, int* err) {
     pdl_begin();
@@ -99,11 +99,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_qk_norm_rope(const float* __re
 // (one warp per key, lanes over head_dim, fixed tree), m = max s, p_j =
 // exp(s_j - m), out = (sum_j p_j v_j) / (sum_j p_j).  grid (T, nq), 128 threads;
 // scores in shared memory (max_seq floats).
-__global__ void __launch_bounds__(kAttnThreads) k_sdpa(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
-                                                       const uint16_t* __restrict__ vc, int nq, int nkv, int hd,
+__global__ void __launch_bounds__(kAttnThreads) k_sdpa(const uint16_t* q, const uint16_t* kc,
+                                                       const uint16_t* vc, int nq, int nkv, int hd,
                                                        int max_seq, int n_seqs, float scale,
-                                                       const int32_t* __restrict__ seq,
-                                                       const int32_t* __restrict__ pos, uint16_t* __restrict__ out) {
+                                                       const int32_t* seq,
+                                                       const int32_t* pos, uint16_t* __restrict__ out) {
     pdl_begin();
     extern __shared__ float s_sc[];  // [max_seq]
     __shared__ float s_q[128];
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_sdpa(const uint16_t* __restric
 }
 
 // x1 = x + bf16(o): the o projection rounded to bf16, the residual add in fp32, one rounding
-__global__ void k_residual_add(const uint16_t* __restrict__ x, const float* __restrict__ o, size_t n,
+__global__ void k_residual_add(const uint16_t* x, const float* o, size_t n,
                                uint16_t* __restrict__ out) {
     pdl_begin();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)

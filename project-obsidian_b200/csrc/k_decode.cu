@@ -253,7 +253,7 @@ __device__ __forceinline__ void finish_gu_tile(const float* tp, int I, int p, in
 
 // Fixed-point packs of T activation rows: one warp per 64-column group.
 template <bool kNatural>
-__global__ void __launch_bounds__(256) k_fx_pack(const uint16_t* __restrict__ x, int T, int H, uint8_t* xq,
+__global__ void __launch_bounds__(256) k_fx_pack(const uint16_t* x, int T, int H, uint8_t* xq,
                                                  float2* xmeta) {
     pdl_begin();
     const int G = H / kGroup, item = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(256) k_fx_pack(const uint16_t* __restrict__ x,
 // grid (I/128, kSplitGU, T*K), 256 threads.  warp w: block half / projection
 // w & 1, groups kt0 + (w >> 1) + 4 j of the split.
 template <class Src>
-__global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const int32_t* __restrict__ ids, int H,
+__global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const int32_t* ids, int H,
                                                        int I, int K, int E, DecodeBufs d) {
     pdl_begin();
     __shared__ float s_part[8][kRowTile];
@@ -314,9 +314,9 @@ __global__ void __launch_bounds__(256) k_decode_gateup(Src gsrc, Src usrc, const
 
 // grid (H/128, K, T), 32 * min(I/64, 16) threads.  warp w: groups w, w + nwarps, ...
 template <class Src>
-__global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* __restrict__ ids,
-                                                     const float* __restrict__ wts,
-                                                     const uint16_t* __restrict__ residual, int H, int I, int K,
+__global__ void __launch_bounds__(512) k_decode_down(Src dsrc, const int32_t* ids,
+                                                     const float* wts,
+                                                     const uint16_t* residual, int H, int I, int K,
                                                      int E, DecodeBufs d, uint16_t* __restrict__ out,
                                                      int do_combine) {
     pdl_begin();
@@ -441,7 +441,9 @@ __device__ __forceinline__ void router_row_load(const uint32_t* __restrict__ w, 
 }
 // router_warp_item's arithmetic for one group per lane, x in global
 // (kGlobalX) or shared memory; lanes r < 4 store (logit, stamp) of every token
-// into replica r
+// into replica r.  The read-only path for x is safe here: the fused layer is a
+// cooperative launch, never a programmatic dependent, so everything earlier in
+// the stream has completed when it starts.
 template <bool kGlobalX>
 __device__ __forceinline__ void router_row_logits(const RouterRow& r, const uint16_t* x, int T, int H, int E, int e,
                                                   int lane, uint32_t stamp, uint64_t* lst) {
@@ -485,8 +487,8 @@ __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, uint64
 
 __global__ void __launch_bounds__(kFusedThreads, 1) k_decode_fused(
     const uint32_t* __restrict__ rw, const uint16_t* __restrict__ rs, const uint16_t* __restrict__ rb,
-    TiledSrc gsrc, TiledSrc dsrc, const uint16_t* __restrict__ x_in, const uint16_t* __restrict__ residual,
-    const float* __restrict__ bias, int T, int H, int I, int E, int K, int norm, int normalize, float eps,
+    TiledSrc gsrc, TiledSrc dsrc, const uint16_t* x_in, const uint16_t* residual,
+    const float* bias, int T, int H, int I, int E, int K, int norm, int normalize, float eps,
     FusedDecodeBufs f, FusedPlan pl, uint16_t* __restrict__ out) {
     extern __shared__ __align__(128) uint8_t smem[];
     // [T][H] bf16 layer input; after phase A, in place, its fixed-point packs [T][H/64][128 B]

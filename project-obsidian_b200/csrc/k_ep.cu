@@ -1,15 +1,20 @@
 // k_ep.cu -- expert parallelism over NVLink peer memory.
 //
 // The reference runs every expert on one device (src/forward.rs:164-247); on a
-// multi-GPU box the experts are split across G ranks (rank g holds experts
-// [g*E/G, (g+1)*E/G)) and the routed token rows travel to the ranks that hold
-// their experts and the expert outputs travel back.  A token row is sent to a
+// multi-GPU box the experts are split across G ranks (E/G each) and the routed
+// token rows travel to the ranks that hold their experts and the expert
+// outputs travel back.  A token row is sent to a
 // rank once, however many of its K experts live there, with the list of those
 // experts (local id and rank-order position k) as metadata; the outputs come
 // back once per (token, expert) pair, since each pair's output is distinct --
 // written by the down GEMM's epilogue straight into the source rank's memory,
 // so the return all-to-all overlaps the GEMM tile by tile.  Rows and outputs
 // that stay on their rank are not copied at all.
+//
+// Which rank holds which expert is a per-layer table (obs_ep_set_placement; by
+// default rank g holds experts [g*E/G, (g+1)*E/G)): a balanced placement keeps
+// the busiest rank's GEMMs, which every rank's combine waits for, short under a
+// skewed expert load.
 //
 // Each rank owns one device buffer (opened by its peers through CUDA IPC) laid
 // out identically on every rank:
@@ -73,7 +78,7 @@ __device__ __forceinline__ T* at(uint8_t* base, size_t off) {
 // the (k, local expert) list and the token index -- for this rank itself only
 // the list and the index: the permute reads the row from x.  The last CTA to
 // finish publishes the per-destination counts and stamps.
-__global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids, const uint16_t* __restrict__ x,
+__global__ void __launch_bounds__(256) k_ep_send(const int32_t* ids, const uint16_t* x,
                                                  int T, int E, EpArgs a) {
     pdl_begin();
     __shared__ int s_last;
@@ -82,12 +87,13 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids
     const int t = blockIdx.x * 8 + warp;
     if (t < T) {
         int id = lane < a.K ? ids[(size_t)t * a.K + lane] : 0;
-        if (lane < a.K && (id < 0 || id >= E)) {
+        int slot_e = lane < a.K && id >= 0 && id < E ? a.place[id] : 0;
+        if (lane < a.K && (id < 0 || id >= E || slot_e < 0 || slot_e >= E)) {
             atomicExch(a.err, kDevBadRoute);
-            id = 0;
+            slot_e = 0;
         }
-        const int dest = lane < a.K ? id / a.E_local : -1;
-        const int le = lane < a.K ? id - dest * a.E_local : 0;
+        const int dest = lane < a.K ? slot_e / a.E_local : -1;
+        const int le = lane < a.K ? slot_e - dest * a.E_local : 0;
         const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * a.H);
         for (int d = 0; d < a.world; ++d) {
             if (!__any_sync(0xffffffffu, dest == d)) continue;
@@ -99,13 +105,13 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids
                 const size_t row = (size_t)a.rank * a.cap_rows + slot;
                 if (d != a.rank) {
                     uint4* dst = at<uint4>(pb, a.off_rx + row * a.H * 2);
-                    for (int c = lane; c < a.H / 8; c += 32) dst[c] = __ldg(src + c);
+                    for (int c = lane; c < a.H / 8; c += 32) dst[c] = src[c];
                 }
                 if (lane < 16)
                     at<int16_t>(pb, a.off_meta + row * 32)[lane] = (int16_t)(dest == d ? (lane << 8) | le : -1);
                 if (lane == 0) at<int32_t>(pb, a.off_mtok + row * 4)[0] = t;
             } else if (lane == 0) {
-                atomicExch(a.err, kDevBadSlot);  // more rows than the source's region holds: refused
+                refuse_slot(a.err, kSiteSendFull, slot);  // more rows than the source's region holds: refused
             }
         }
     }
@@ -131,10 +137,9 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* __restrict__ ids
 // Wait for every source's stamp, then turn the received rows into a local
 // routing problem of W*cap_rows "tokens" with K slots each:
 // ids_local[row*K + k] = local expert of slot k of the row (-1: none, or beyond
-// the source's count), src_item = the source's item t*K + k, and a histogram per
-// local expert.  The rows this rank sent itself are read from x: row_src[row] is
+// the source's count) and src_item = the source's item t*K + k.  The rows this rank sent itself are read from x: row_src[row] is
 // the row to permute, x[t] for its own region, recv_x[row] otherwise.
-__global__ void __launch_bounds__(256) k_ep_recv(const uint16_t* __restrict__ x, EpArgs a) {
+__global__ void __launch_bounds__(256) k_ep_recv(const uint16_t* x, EpArgs a) {
     pdl_begin();
     const uint32_t e = *a.epoch + 1;
     uint8_t* mine = a.peer[a.rank];
@@ -157,7 +162,6 @@ __global__ void __launch_bounds__(256) k_ep_recv(const uint16_t* __restrict__ x,
                     atomicExch(a.err, kDevBadRoute);
                 } else {
                     le = l, item = t * a.K + k;
-                    atomicAdd(a.counts + le, 1);
                 }
             }
         }
@@ -172,8 +176,8 @@ __global__ void __launch_bounds__(256) k_ep_recv(const uint16_t* __restrict__ x,
 // received (row, k) pair each, whose output goes to its source rank's ret_y row
 // (item t*K + k) over NVLink -- or, for this rank's own items, stays in y and is
 // noted in local_slot for the combine.
-__global__ void __launch_bounds__(256) k_ep_rowptr(const int32_t* __restrict__ slot_of,
-                                                   const int32_t* __restrict__ src, const int32_t* __restrict__ seg_end,
+__global__ void __launch_bounds__(256) k_ep_rowptr(const int32_t* slot_of,
+                                                   const int32_t* src, const int32_t* seg_end,
                                                    uint16_t* y, uint16_t** __restrict__ row_ptr, EpArgs a) {
     pdl_begin();
     const int total = min(*seg_end, a.rows_cap), n = a.world * a.cap_rows * a.K;
@@ -185,8 +189,12 @@ __global__ void __launch_bounds__(256) k_ep_rowptr(const int32_t* __restrict__ s
         const int j = i - total;
         if (a.ids_local[j] < 0) continue;
         const int s = j / (a.K * a.cap_rows), item = a.src_item[j], slot = slot_of[j];
-        if (slot < 0 || slot >= total || item < 0 || item >= a.cap_items) {  // refused, recorded
-            atomicExch(a.err, kDevBadSlot);
+        if (slot < 0 || slot >= total) {  // refused, recorded
+            refuse_slot(a.err, kSiteRowSlot, slot * 65536 + total);
+            continue;
+        }
+        if (item < 0 || item >= a.cap_items) {
+            refuse_slot(a.err, kSiteRowItem, item);
             continue;
         }
         if (s == a.rank) {

@@ -517,14 +517,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(GemmArgs a) {
                 named_bar_sync(1, kEpThreads);
                 uint8_t* yb = reinterpret_cast<uint8_t*>(a.out) + ((size_t)tl.y * a.out_ld + rt * kRowTile) * 2;
                 const int nstore = min(tl.z, a.row_limit - tl.y);
-                for (int i = et; i < nstore * 16; i += kEpThreads) {
-                    const int jr = i >> 4, c = i & 15;
-                    // with row_ptr (expert parallelism) the row goes straight to its destination, for a
-                    // row computed for another rank that rank's return buffer over NVLink
-                    uint8_t* yrow = a.row_ptr ? reinterpret_cast<uint8_t*>(a.row_ptr[tl.y + jr]) + rt * kRowTile * 2
-                                              : yb + (size_t)jr * a.out_ld * 2;
-                    *reinterpret_cast<uint4*>(yrow + c * 16) =
-                        *reinterpret_cast<const uint4*>(stg + jr * 256 + ((c ^ ((jr & 1) << 2)) << 4));
+                if (a.row_ptr) {
+                    // expert parallelism: each row goes straight to its destination, for a row
+                    // computed for another rank that rank's return buffer over NVLink; a row
+                    // without a destination is refused and recorded
+                    for (int i = et; i < nstore * 16; i += kEpThreads) {
+                        const int jr = i >> 4, c = i & 15;
+                        uint8_t* dst = reinterpret_cast<uint8_t*>(a.row_ptr[tl.y + jr]);
+                        if (!dst) {
+                            if (c == 0) refuse_slot(a.err, kSiteGemmRow, tl.y + jr);
+                            continue;
+                        }
+                        *reinterpret_cast<uint4*>(dst + rt * kRowTile * 2 + c * 16) =
+                            *reinterpret_cast<const uint4*>(stg + jr * 256 + ((c ^ ((jr & 1) << 2)) << 4));
+                    }
+                } else {
+                    for (int i = et; i < nstore * 16; i += kEpThreads) {
+                        const int jr = i >> 4, c = i & 15;
+                        *reinterpret_cast<uint4*>(yb + (size_t)jr * a.out_ld * 2 + c * 16) =
+                            *reinterpret_cast<const uint4*>(stg + jr * 256 + ((c ^ ((jr & 1) << 2)) << 4));
+                    }
                 }
                 if (et == 0) trace_at<TRACE>(a, kTrEpDone, it);
             }

@@ -26,7 +26,7 @@ constexpr int kHeadRowsPerWarp = 2;           // rows a warp has in flight toget
 
 // embedding rows: one CTA per token, one thread per packed word (8 columns)
 __global__ void __launch_bounds__(256) k_embed(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
-                                               const uint16_t* __restrict__ b, const int32_t* __restrict__ tokens,
+                                               const uint16_t* __restrict__ b, const int32_t* tokens,
                                                int vocab, int H, uint16_t* __restrict__ x, int* __restrict__ err) {
     pdl_begin();
     const int t = blockIdx.x;
@@ -58,7 +58,7 @@ template <int MAXT>
 __global__ void __launch_bounds__(32 * kHeadWarps) k_lm_head(const uint32_t* __restrict__ w,
                                                             const uint16_t* __restrict__ s,
                                                             const uint16_t* __restrict__ b,
-                                                            const uint16_t* __restrict__ xin, int T, int vocab, int H,
+                                                            const uint16_t* xin, int T, int vocab, int H,
                                                             float* __restrict__ logits) {
     pdl_begin();
     extern __shared__ __align__(16) float s_x[];  // [T][H]
@@ -135,7 +135,7 @@ __device__ __forceinline__ bool better(uint32_t ka, int ia, uint32_t kb, int ib)
 }
 
 // greedy next token: the first maximum of each token's logits (forward.rs:562-565)
-__global__ void __launch_bounds__(1024) k_head_argmax(const float* __restrict__ logits, int vocab,
+__global__ void __launch_bounds__(1024) k_head_argmax(const float* logits, int vocab,
                                                       int32_t* __restrict__ ids) {
     pdl_begin();
     const int t = blockIdx.x;

@@ -22,19 +22,10 @@ namespace {
 // dequantised weights per group stay in registers across the chunk's tokens.
 constexpr int kLeaves = 32;  // lanes of the canonical order = leaf sums of the prefill form
 
-// the expert histogram of this forward starts at zero (written by the first CTA,
-// after the previous kernel of the stream has completed)
-__device__ __forceinline__ void zero_on_first_cta(int32_t* counts, int E) {
-    if (counts && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
-        for (int i = threadIdx.x; i < E; i += blockDim.x) counts[i] = 0;
-}
-
 __global__ void __launch_bounds__(256) k_router_warp(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
-                                                     const uint16_t* __restrict__ b, const uint16_t* __restrict__ x,
-                                                     int T, int H, int E, float* __restrict__ logits,
-                                                     int32_t* __restrict__ zero_counts) {
+                                                     const uint16_t* __restrict__ b, const uint16_t* x,
+                                                     int T, int H, int E, float* __restrict__ logits) {
     pdl_begin();
-    zero_on_first_cta(zero_counts, E);
     const int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (e >= E) return;
     router_warp_item(w, s, b, x, T, H, E, e, blockIdx.y * kWarpTok, threadIdx.x & 31, logits);
@@ -60,11 +51,9 @@ constexpr size_t kLeafSmem = (size_t)(kRT + kRE) * kRPad * 4;  // 52,224 bytes
 __global__ void __launch_bounds__(kLeafThreads, 1) k_router_leaf(const uint32_t* __restrict__ w,
                                                                  const uint16_t* __restrict__ s,
                                                                  const uint16_t* __restrict__ b,
-                                                                 const uint16_t* __restrict__ x, int T, int H, int E,
-                                                                 float* __restrict__ parts,
-                                                                 int32_t* __restrict__ zero_counts) {
+                                                                 const uint16_t* x, int T, int H, int E,
+                                                                 float* __restrict__ parts) {
     pdl_begin();
-    zero_on_first_cta(zero_counts, E);
     extern __shared__ __align__(16) float rsm[];
     float(*xs)[kRPad] = reinterpret_cast<float(*)[kRPad]>(rsm);
     float(*ws)[kRPad] = reinterpret_cast<float(*)[kRPad]>(rsm + kRT * kRPad);
@@ -85,7 +74,7 @@ __global__ void __launch_bounds__(kLeafThreads, 1) k_router_leaf(const uint32_t*
             for (int u = 0; u < kRT * 8 / kLeafThreads; ++u) {
                 const int i = tid + kLeafThreads * u, r = i >> 3, c8 = i & 7, t = t0 + r;
                 uint4 v = make_uint4(0, 0, 0, 0);
-                if (t < T) v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + (size_t)g * 64) + c8);
+                if (t < T) v = reinterpret_cast<const uint4*>(x + (size_t)t * H + (size_t)g * 64)[c8];
                 const uint32_t q[4] = {v.x, v.y, v.z, v.w};
                 float* d = &xs[r][c8 * 8];
 #pragma unroll
@@ -169,7 +158,7 @@ __device__ __forceinline__ float tree8(const float* __restrict__ p, size_t plane
     return __fadd_rn(__fadd_rn(__fadd_rn(n0, n1), __fadd_rn(n2, n3)), __fadd_rn(__fadd_rn(n4, n5), __fadd_rn(n6, n7)));
 }
 
-__global__ void k_router_finish(const float* __restrict__ parts, size_t n, float* __restrict__ logits) {
+__global__ void k_router_finish(const float* parts, size_t n, float* __restrict__ logits) {
     pdl_begin();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         logits[i] = tree8(parts, n, i);
@@ -182,10 +171,10 @@ __global__ void k_router_finish(const float* __restrict__ parts, size_t n, float
 // router_dev.cuh).  Enough CTAs to fill the GPU at prefill sizes.
 constexpr int kTopkTok = 2;
 
-__global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, int nparts,
-                                              const float* __restrict__ bias, int T, int E, int K, int norm,
+__global__ void __launch_bounds__(256) k_topk(const float* logits, int nparts,
+                                              const float* bias, int T, int E, int K, int norm,
                                               int32_t* __restrict__ ids, float* __restrict__ wout,
-                                              int32_t* __restrict__ counts, float* __restrict__ logits_out) {
+                                              float* __restrict__ logits_out) {
     pdl_begin();
     __shared__ float s_l[kTopkTok][kMaxE];
     const int t0 = blockIdx.x * kTopkTok;
@@ -209,7 +198,6 @@ __global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, 
     if (lane < K) {
         ids[(size_t)t * K + lane] = ik;
         wout[(size_t)t * K + lane] = wk;
-        if (counts) atomicAdd(counts + ik, 1);
     }
 }
 
@@ -218,12 +206,12 @@ __global__ void __launch_bounds__(256) k_topk(const float* __restrict__ logits, 
 int router_parts(int T) { return T <= 2 * kWarpTok ? 1 : kNodes; }
 
 cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint16_t* x, int T, float* parts,
-                                 cudaStream_t st, int32_t* zero_counts) {
+                                 cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (router_parts(T) == 1) {
         dim3 grid((sh.E + 7) / 8, (T + kWarpTok - 1) / kWarpTok);
         {
-            const cudaError_t le_ = launch_pdl(k_router_warp, dim3(grid), dim3(256), 0, st, L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E, parts, zero_counts);
+            const cudaError_t le_ = launch_pdl(k_router_warp, dim3(grid), dim3(256), 0, st, L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E, parts);
             if (le_ != cudaSuccess) return le_;
         }
     } else {
@@ -233,7 +221,7 @@ cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint1
         dim3 grid((T + kRT - 1) / kRT, (sh.E + kRE - 1) / kRE, kNodes);
         {
             const cudaError_t le_ = launch_pdl(k_router_leaf, dim3(grid), dim3(kLeafThreads), kLeafSmem, st, L.router_w, L.router_s, L.router_b, x, T, sh.H, sh.E,
-                                                              parts, zero_counts);
+                                                              parts);
             if (le_ != cudaSuccess) return le_;
         }
     }
@@ -251,12 +239,12 @@ cudaError_t launch_router_finish(const float* parts, int T, int E, float* logits
 }
 
 cudaError_t launch_topk(const float* logits, int nparts, const float* bias, int T, int E, int K, int norm,
-                        int32_t* ids, float* w, int32_t* counts, float* logits_out, cudaStream_t st) {
+                        int32_t* ids, float* w, float* logits_out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (E > kMaxE || K > kMaxK || K > 32) return cudaErrorInvalidValue;
     {
         const cudaError_t le_ = launch_pdl(k_topk, dim3((T + kTopkTok - 1) / kTopkTok), dim3(256), 0, st, logits, nparts,
-                                           bias, T, E, K, norm, ids, w, counts, logits_out);
+                                           bias, T, E, K, norm, ids, w, logits_out);
         if (le_ != cudaSuccess) return le_;
     }
     return cudaGetLastError();

@@ -9,6 +9,7 @@
 // sequence of kernel launches with no host synchronisation.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstddef>
@@ -79,8 +80,11 @@ struct obs_ctx {
     uint32_t* probe_stamp = nullptr;    // a stamp nothing writes (obs_probe_wait)
     uint64_t* trace = nullptr;  // obs_trace_enable
     int trace_n = 0;
-    // expert parallelism (ep_world > 1): this rank holds experts [e0, e0 + E_local)
+    // expert parallelism (ep_world > 1): this rank holds E_local experts of each layer,
+    // placement[layer][ep_rank * E_local + l] for local expert l (default: [e0, e0 + E_local))
     int ep_world = 1, ep_rank = 0, E_local = 0, e0 = 0;
+    std::vector<std::vector<int32_t>> placement;  // [n_layers][E] global expert of each slot
+    int32_t* place_dev = nullptr;                 // [n_layers][E] slot of each global expert
     uint8_t* ep_buf = nullptr;  // this rank's buffer, opened by its peers through CUDA IPC
     uint16_t** ep_row_ptr = nullptr;  // [R_cap] destination of each down-GEMM output row
     // the model's ends (obs_load_head): embedding, final norm, lm_head, and their scratch
@@ -256,6 +260,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->ids, (size_t)T * K * 4},
         {(void**)&ctx->wts, (size_t)T * K * 4},
         {(void**)&ctx->disp.counts, (size_t)E * 4},
+        {(void**)&ctx->disp.hist, (size_t)((W * T + kDispChunk - 1) / kDispChunk) * E * 4},
         {(void**)&ctx->disp.seg, (size_t)(E + 1) * 4},
         {(void**)&ctx->disp.slot_of, (size_t)W * T * K * 4},
         {(void**)&ctx->disp.src, (size_t)ctx->R_cap * 4},
@@ -291,6 +296,7 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         {(void**)&ctx->fused.bar, 16},
         {(void**)&ctx->fused.lst, (size_t)4 * kFusedMaxT * E * 8},
         {(void**)&ctx->probe_stamp, 16},
+        {(void**)&ctx->place_dev, (size_t)cfg->n_layers * E * 4},
         {(void**)&ctx->ep.send_cnt, (size_t)kMaxWorld * 4},
         {(void**)&ctx->ep.done, 16},
         {(void**)&ctx->ep.epoch, 16},
@@ -326,7 +332,6 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         EpArgs& a = ctx->ep;
         a.world = W, a.rank = ctx->ep_rank, a.H = s.H, a.K = K, a.E_local = EL;
         a.cap_rows = T, a.cap_items = T * K;
-        a.counts = ctx->disp.counts;
         a.rows_cap = ctx->R_cap;
         a.err = ctx->err_flag;
         size_t o = 0;
@@ -348,9 +353,19 @@ extern "C" int obs_create(const obs_config* cfg, int device, obs_ctx** out) {
         }
     }
     ctx->disp.atoms = ctx->R_cap / 8;
+    ctx->disp.rows_cap = ctx->R_cap;
+    ctx->disp.max_tiles = ctx->max_tiles;
+    ctx->disp.max_chunks = (W * T + kDispChunk - 1) / kDispChunk;
+    ctx->disp.err = ctx->err_flag;
     ctx->disp.bn = kBNTile;
     // counters must start at zero; the tiled buffers are zeroed so padding rows are finite
     e = cudaMemset(ctx->smem_pool, 0, total);
+    // the identity placement of every layer
+    ctx->placement.assign(cfg->n_layers, std::vector<int32_t>(E));
+    for (auto& pl : ctx->placement)
+        for (int i = 0; i < E; ++i) pl[i] = i;
+    for (int l = 0; l < cfg->n_layers && e == cudaSuccess; ++l)
+        e = cudaMemcpy(ctx->place_dev + (size_t)l * E, ctx->placement[l].data(), (size_t)E * 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         g_create_err = std::string("scratch init: ") + cudaGetErrorString(e);
@@ -407,7 +422,11 @@ static int load_impl(obs_ctx* ctx, int layer, const obs_layer_weights* w, int on
     CU(cudaSetDevice(ctx->device), "cudaSetDevice");
     const Shape& s = ctx->sh;
     LayerDev& L = ctx->layers[layer];
-    const int EL = ctx->E_local, e0 = ctx->e0;  // this context's experts (all of them without EP)
+    // this context's experts (all of them without EP): placement[layer][e0 + l] for local expert l
+    const int EL = ctx->E_local;
+    const int32_t* mine = ctx->placement[layer].data() + ctx->e0;
+    bool contiguous = true;
+    for (int l = 1; l < EL; ++l) contiguous = contiguous && mine[l] == mine[0] + l;
     const size_t maxw = (size_t)EL * s.I * s.H / 8 * 4;  // one projection's words (all same size)
     const size_t maxg = (size_t)EL * s.I * s.H / 64 * 2;
     uint8_t* stage = nullptr;
@@ -427,9 +446,14 @@ static int load_impl(obs_ctx* ctx, int layer, const obs_layer_weights* w, int on
     }
     for (int proj = 0; proj < 3 && e == cudaSuccess; ++proj) {
         const int out_f = proj == 2 ? s.H : s.I, in_f = proj == 2 ? s.I : s.H;
-        const size_t nw = (size_t)EL * out_f * in_f / 8 * 4, ng = (size_t)EL * out_f * (in_f / 64) * 2;
+        const size_t wpe = (size_t)out_f * (in_f / 8), gpe = (size_t)out_f * (in_f / 64);  // per expert
         if (synth) {
-            step(launch_synth_proj(seed, (uint32_t)layer, proj, e0, EL, out_f, in_f, sw, ss, sb, 0));
+            if (contiguous)
+                step(launch_synth_proj(seed, (uint32_t)layer, proj, mine[0], EL, out_f, in_f, sw, ss, sb, 0));
+            else
+                for (int l = 0; l < EL; ++l)
+                    step(launch_synth_proj(seed, (uint32_t)layer, proj, mine[l], 1, out_f, in_f, sw + l * wpe,
+                                           ss + l * gpe, sb + l * gpe, 0));
         } else {
             const uint32_t* pw = proj == 0 ? w->gate_w : proj == 1 ? w->up_w : w->down_w;
             const uint16_t* ps = proj == 0 ? w->gate_s : proj == 1 ? w->up_s : w->down_s;
@@ -438,9 +462,13 @@ static int load_impl(obs_ctx* ctx, int layer, const obs_layer_weights* w, int on
                 cudaFree(stage);
                 return fail(ctx, OBS_ERR_INVALID, "null weight pointer");
             }
-            step(cudaMemcpy(sw, pw + (size_t)e0 * out_f * (in_f / 8), nw, kind));
-            step(cudaMemcpy(ss, ps + (size_t)e0 * out_f * (in_f / 64), ng, kind));
-            step(cudaMemcpy(sb, pb + (size_t)e0 * out_f * (in_f / 64), ng, kind));
+            const int runs = contiguous ? 1 : EL, per = contiguous ? EL : 1;  // copies of `per` experts each
+            for (int r = 0; r < runs; ++r) {
+                const size_t ge = (size_t)mine[r];
+                step(cudaMemcpy(sw + r * wpe, pw + ge * wpe, per * wpe * 4, kind));
+                step(cudaMemcpy(ss + r * gpe, ps + ge * gpe, per * gpe * 2, kind));
+                step(cudaMemcpy(sb + r * gpe, pb + ge * gpe, per * gpe * 2, kind));
+            }
         }
         if (proj < 2) step(launch_retile(sw, ss, sb, EL, out_f, in_f, L.gateup, 1, proj, 0));
         else step(launch_retile(sw, ss, sb, EL, out_f, in_f, L.down, 0, 0, 0));
@@ -694,7 +722,7 @@ extern "C" int obs_route(obs_ctx* ctx, const float* logits, const float* bias, i
     if (rc) return rc;
     if (T == 0) return OBS_OK;
     if (!logits || !ids || !w) return fail(ctx, OBS_ERR_INVALID, "null pointer");
-    CU(launch_topk(logits, 1, bias, T, ctx->sh.E, ctx->sh.K, ctx->cfg.norm_topk, ids, w, nullptr, nullptr,
+    CU(launch_topk(logits, 1, bias, T, ctx->sh.E, ctx->sh.K, ctx->cfg.norm_topk, ids, w, nullptr,
                    as_stream(stream)),
        "topk");
     return OBS_OK;
@@ -725,9 +753,7 @@ extern "C" int obs_dispatch(obs_ctx* ctx, const int32_t* ids, int T, int32_t* co
 static int dispatch_from_ids(obs_ctx* ctx, const int32_t* ids, const uint16_t* x, int T, int permute,
                              cudaStream_t st) {
     const Shape& s = ctx->sh;
-    CU(cudaMemsetAsync(ctx->disp.counts, 0, s.E * 4, st), "memset");
     if (T) CU(cudaMemsetAsync(ctx->disp.slot_of, 0, (size_t)T * s.K * 4, st), "memset");
-    CU(launch_histogram(ids, T * s.K, s.E, ctx->disp.counts, ctx->err_flag, st), "histogram");
     CU(launch_dispatch(ids, x, T, s, ctx->disp, permute, st), "dispatch");
     return OBS_OK;
 }
@@ -911,29 +937,89 @@ extern "C" int obs_ep_connect(obs_ctx* ctx, const void* handles) {
     return OBS_OK;
 }
 
+extern "C" int obs_ep_set_placement(obs_ctx* ctx, int layer, const int32_t* experts) {
+    OBS_CHECK_CTX(ctx);
+    if (ctx->ep_world <= 1) return fail(ctx, OBS_ERR_UNSUPPORTED, "placement needs expert parallelism (ep_world > 1)");
+    if (!experts) return fail(ctx, OBS_ERR_INVALID, "null placement");
+    const int E = ctx->sh.E, n = (int)ctx->layers.size();
+    if (layer < -1 || layer >= n) return fail(ctx, OBS_ERR_INVALID, "layer out of range");
+    std::vector<int32_t> slot(E, -1);
+    for (int i = 0; i < E; ++i) {
+        if (experts[i] < 0 || experts[i] >= E || slot[experts[i]] >= 0)
+            return fail(ctx, OBS_ERR_INVALID, "placement is not a permutation of the experts");
+        slot[experts[i]] = i;
+    }
+    CU(cudaSetDevice(ctx->device), "cudaSetDevice");
+    for (int l = layer < 0 ? 0 : layer; l < (layer < 0 ? n : layer + 1); ++l) {
+        if (std::equal(ctx->placement[l].begin(), ctx->placement[l].end(), experts)) continue;
+        CU(cudaMemcpy(ctx->place_dev + (size_t)l * E, slot.data(), (size_t)E * 4, cudaMemcpyHostToDevice),
+           "placement copy");
+        ctx->placement[l].assign(experts, experts + E);
+        ctx->layers[l].loaded = false;  // this rank's experts changed: load them again
+    }
+    return OBS_OK;
+}
+
+extern "C" int obs_ep_get_placement(obs_ctx* ctx, int layer, int32_t* experts) {
+    OBS_CHECK_CTX(ctx);
+    if (!experts) return fail(ctx, OBS_ERR_INVALID, "null placement");
+    if (layer < 0 || layer >= (int)ctx->layers.size()) return fail(ctx, OBS_ERR_INVALID, "layer out of range");
+    std::copy(ctx->placement[layer].begin(), ctx->placement[layer].end(), experts);
+    return OBS_OK;
+}
+
+extern "C" int obs_ep_plan_placement(const int64_t* load, int n_experts, int world, int32_t* experts) {
+    if (!load || !experts || n_experts <= 0 || world <= 0 || n_experts % world) return OBS_ERR_INVALID;
+    for (int i = 0; i < n_experts; ++i)
+        if (load[i] < 0) return OBS_ERR_INVALID;
+    const int per = n_experts / world;
+    std::vector<int> order(n_experts);
+    for (int i = 0; i < n_experts; ++i) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return load[a] > load[b]; });
+    std::vector<int64_t> total(world, 0);
+    std::vector<std::vector<int32_t>> held(world);
+    for (int e : order) {
+        int best = -1;
+        for (int g = 0; g < world; ++g)
+            if ((int)held[g].size() < per && (best < 0 || total[g] < total[best])) best = g;
+        held[best].push_back(e);
+        total[best] += load[e];
+    }
+    for (int g = 0; g < world; ++g) {
+        std::sort(held[g].begin(), held[g].end());
+        std::copy(held[g].begin(), held[g].end(), experts + (size_t)g * per);
+    }
+    return OBS_OK;
+}
+
 // One layer with the experts spread over the ranks (layout and protocol in k_ep.cu).
-static int forward_ep(obs_ctx* ctx, const LayerDev& L, const uint16_t* x, uint16_t* out, const uint16_t* residual,
+static int forward_ep(obs_ctx* ctx, int layer, const uint16_t* x, uint16_t* out, const uint16_t* residual,
                       int T, const float* logit_bias, cudaStream_t st) {
     if (!ctx->ep_connected) return fail(ctx, OBS_ERR_STATE, "expert parallelism not connected (obs_ep_connect)");
     const Shape& s = ctx->sh;
-    const EpArgs& a = ctx->ep;
+    const LayerDev& L = ctx->layers[layer];
+    EpArgs a = ctx->ep;
+    a.place = ctx->place_dev + (size_t)layer * s.E;
     prof_begin(ctx, OBS_STAGE_ROUTER, st);
     if (T > 0) CU(launch_router_logits(L, s, x, T, ctx->logits, st), "router");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_TOPK, st);
     if (T > 0)
         CU(launch_topk(ctx->logits, router_parts(T), logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids, ctx->wts,
-                       nullptr, nullptr, st),
+                       nullptr, st),
            "topk");
     prof_end(ctx, st);
-    prof_begin(ctx, OBS_STAGE_DISPATCH, st);
+    prof_begin(ctx, OBS_STAGE_EP_SEND, st);
     CU(launch_ep_send(ctx->ids, x, T, s.E, a, st), "ep send");
-    CU(cudaMemsetAsync(ctx->disp.counts, 0, ctx->E_local * 4, st), "memset");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_EP_RECV, st);
     CU(launch_ep_recv(x, a, st), "ep receive");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_DISPATCH, st);
     // the received rows as a local routing problem: row j of source s (j < its count) with up to K
     // local experts; the other entries are -1
     const Shape sl{s.H, s.I, ctx->E_local, s.K};
-    CU(launch_dispatch(a.ids_local, nullptr, a.world * a.cap_rows, sl, ctx->disp, 1, st, a.row_src), "dispatch");
+    CU(launch_dispatch(a.ids_local, nullptr, a.world * a.cap_rows, sl, ctx->disp, 1, st, a.row_src, 1), "dispatch");
     CU(launch_ep_rowptr(ctx->disp.slot_of, ctx->disp.src, ctx->disp.seg + ctx->E_local, ctx->ybuf, ctx->ep_row_ptr, a,
                         st),
        "ep row destinations");
@@ -948,9 +1034,11 @@ static int forward_ep(obs_ctx* ctx, const LayerDev& L, const uint16_t* x, uint16
     gd.row_ptr = ctx->ep_row_ptr;
     CU(launch_gemm(gd, kEpiBf16, ctx->num_sms, st), "gemm down");
     prof_end(ctx, st);
-    prof_begin(ctx, OBS_STAGE_COMBINE, st);
+    prof_begin(ctx, OBS_STAGE_EP_RETURN, st);
     CU(launch_ep_returned(a, st), "ep returned");
     CU(launch_ep_finish(a, st), "ep finish");
+    prof_end(ctx, st);
+    prof_begin(ctx, OBS_STAGE_COMBINE, st);
     if (T > 0)
         CU(launch_combine(reinterpret_cast<const uint16_t*>(ctx->ep_buf + a.off_ret), s.H, nullptr, ctx->wts, residual,
                           T, s.H, s.K, out, st, ctx->ybuf, a.local_slot),
@@ -970,7 +1058,7 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
         if (T > 0 && (!x || !out)) return fail(ctx, OBS_ERR_INVALID, "null pointer");
         if (path != OBS_PATH_AUTO && path != OBS_PATH_DECODE && path != OBS_PATH_PREFILL)
             return fail(ctx, OBS_ERR_INVALID, "bad path");
-        return forward_ep(ctx, ctx->layers[layer], x, out, residual, T, logit_bias, as_stream(stream));
+        return forward_ep(ctx, layer, x, out, residual, T, logit_bias, as_stream(stream));
     }
     if (T == 0) return OBS_OK;
     if (!x || !out) return fail(ctx, OBS_ERR_INVALID, "null pointer");
@@ -990,14 +1078,12 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
         return OBS_OK;
     }
     prof_begin(ctx, OBS_STAGE_ROUTER, st);
-    // the grouped-GEMM path's expert histogram is zeroed by the router kernel
-    CU(launch_router_logits(L, s, x, T, ctx->logits, st, path == OBS_PATH_DECODE ? nullptr : ctx->disp.counts),
-       "router");
+    CU(launch_router_logits(L, s, x, T, ctx->logits, st), "router");
     prof_end(ctx, st);
     if (path == OBS_PATH_DECODE) {
         prof_begin(ctx, OBS_STAGE_TOPK, st);
         CU(launch_topk(ctx->logits, router_parts(T), logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids,
-                       ctx->wts, nullptr, nullptr, st),
+                       ctx->wts, nullptr, st),
            "topk");
         prof_end(ctx, st);
         prof_begin(ctx, OBS_STAGE_DECODE_GATEUP, st);
@@ -1010,7 +1096,7 @@ extern "C" int obs_moe_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint1
     }
     prof_begin(ctx, OBS_STAGE_TOPK, st);
     CU(launch_topk(ctx->logits, router_parts(T), logit_bias, T, s.E, s.K, ctx->cfg.norm_topk, ctx->ids,
-                   ctx->wts, ctx->disp.counts, nullptr, st),
+                   ctx->wts, nullptr, st),
        "topk");
     prof_end(ctx, st);
     prof_begin(ctx, OBS_STAGE_DISPATCH, st);
@@ -1158,11 +1244,11 @@ extern "C" int obs_check_device(obs_ctx* ctx, void* stream) {
     OBS_CHECK_CTX(ctx);
     CU(cudaStreamSynchronize(as_stream(stream)), "stream sync");
     CU(cudaGetLastError(), "pending error");
-    int words[2] = {0, 0};
-    CU(cudaMemcpy(words, ctx->err_flag, 8, cudaMemcpyDeviceToHost), "read flag");
+    int words[4] = {0, 0, 0, 0};
+    CU(cudaMemcpy(words, ctx->err_flag, 16, cudaMemcpyDeviceToHost), "read flag");
     const int flag = words[0];
     if (flag) {
-        CU(cudaMemset(ctx->err_flag, 0, 8), "clear flag");
+        CU(cudaMemset(ctx->err_flag, 0, 16), "clear flag");
         // a wait that gave up leaves the fused decode layer's barrier counts behind: start over
         CU(cudaMemset(ctx->fused.bar, 0, 8), "reset tickets");
         CU(cudaMemset(ctx->fused.ypart, 0, (size_t)kFusedMaxT * ctx->sh.K * (ctx->sh.I / kGroup) * ctx->sh.H * 8), "reset");
@@ -1173,8 +1259,15 @@ extern "C" int obs_check_device(obs_ctx* ctx, void* stream) {
             return fail(ctx, OBS_ERR_TIMEOUT, msg);
         }
         if (flag == kDevBadTile) return fail(ctx, OBS_ERR_INVALID, "device refused a GEMM tile outside its buffers");
-        if (flag == kDevBadSlot)
-            return fail(ctx, OBS_ERR_INVALID, "device refused an expert-parallel row slot outside its buffers");
+        if (flag == kDevBadSlot) {
+            static const char* const site[] = {"?", "source region full", "received pair without a slot",
+                                               "received pair with a bad item", "dispatch beyond the row buffers",
+                                               "permute row without data", "down-GEMM row without a destination"};
+            char msg[192];
+            snprintf(msg, sizeof msg, "device refused an expert-parallel row slot outside its buffers (first: %s; %d)",
+                     site[words[2] >= 0 && words[2] <= 6 ? words[2] : 0], words[3]);
+            return fail(ctx, OBS_ERR_INVALID, msg);
+        }
         if (flag == kDevBadPos)
             return fail(ctx, OBS_ERR_INVALID, "device refused a token's sequence or position outside the KV caches");
         return fail(ctx, OBS_ERR_INVALID, "device reported an invalid route (expert id out of range)");

@@ -21,6 +21,20 @@ constexpr int kSegAlign = 16;     // expert segments padded to 16 rows (MMA N st
 
 // Device-side error codes written to the context's flag word.
 enum DevErr : int { kDevOk = 0, kDevTimeout = 1, kDevBadRoute = 2, kDevBadTile = 3, kDevBadSlot = 4, kDevBadPos = 5 };
+// Which check refused a row slot first (word 2 of the flag, next to kDevBadSlot in
+// word 0) and a value it saw (word 3: the slot, row or token it refused).
+enum SlotSite : int {
+    kSiteSendFull = 1,  // a source sent more rows to a rank than its region holds
+    kSiteRowSlot = 2,   // a received (row, k) pair without a slot below the dispatch's end
+    kSiteRowItem = 3,   // a received (row, k) pair naming an item outside the source's batch
+    kSiteDispatch = 4,  // more routed rows than the row buffers hold
+    kSitePermute = 5,   // a slot naming a token outside the batch, or a row without data
+    kSiteGemmRow = 6    // a down-GEMM output row without a destination
+};
+__device__ __forceinline__ void refuse_slot(int* err, int site, int value = 0) {
+    if (atomicCAS(err + 2, 0, site) == 0) atomicExch(err + 3, value);
+    atomicExch(err, kDevBadSlot);
+}
 
 // ------------------------------------------------------------------- bf16
 __device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
@@ -55,6 +69,13 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(
 // memory to be visible) before touching anything that kernel wrote.  The next
 // kernel's launch latency overlaps this kernel's tail.  Both are no-ops for a
 // kernel launched without the programmatic-serialization attribute.
+// Memory that an earlier kernel of the stream wrote is read with ordinary loads
+// after pdl_begin(), never through the read-only path (__ldg, or a pointer
+// parameter declared const __restrict__): those loads may be issued ahead of
+// the wait or served from the non-coherent cache, and returned the previous
+// forward's values when a kernel of the chain waited long (an expert-parallel
+// receive waiting for a peer) and its dependents started early.  Weights and
+// other memory written before the forward keep the read-only path.
 __device__ __forceinline__ void pdl_begin() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");

@@ -71,22 +71,23 @@ cudaError_t launch_retile(const uint32_t* w, const uint16_t* s, const uint16_t* 
 
 // --------------------------------------------------------------- k_router.cu
 // Router logits for T tokens: router_parts(T) partial planes [parts][T][E]
-// (1: final logits; 32: leaf sums that launch_topk / launch_router_finish
-// combine in the fixed tree).  `parts` must hold 32*T*E floats.
+// (1: final logits; 8: node sums that launch_topk / launch_router_finish
+// combine in the fixed tree).  `parts` must hold 8*T*E floats.
 int router_parts(int T);
-// zero_counts (optional, E ints): zeroed by the router kernel once the previous
-// kernel of the stream has completed, so the expert histogram needs no memset
-// node between router and top-k (a memset breaks the dependent-launch chain).
 cudaError_t launch_router_logits(const LayerDev& L, const Shape& sh, const uint16_t* x, int T, float* parts,
-                                 cudaStream_t st, int32_t* zero_counts = nullptr);
+                                 cudaStream_t st);
 cudaError_t launch_router_finish(const float* parts, int T, int E, float* logits, cudaStream_t st);
 // logits_out (optional) receives the combined logits.
 cudaError_t launch_topk(const float* logits, int nparts, const float* bias, int T, int E, int K, int norm,
-                        int32_t* ids, float* w, int32_t* counts, float* logits_out, cudaStream_t st);
+                        int32_t* ids, float* w, float* logits_out, cudaStream_t st);
 
 // ------------------------------------------------------------- k_dispatch.cu
+constexpr int kDispChunk = 512;  // tokens per dispatch chunk (one CTA of the histogram / placement)
 struct DispatchBufs {
-    int32_t* counts;    // [E]
+    int32_t* counts;    // [E] routes per expert (written by the dispatch)
+    int32_t* hist;      // [max_chunks][E] routes per (token chunk, expert)
+    int max_chunks;     // chunks of kDispChunk tokens the hist buffer holds
+    int* err;           // the context's device error word (kDevBadRoute)
     int32_t* seg;       // [E+1] padded segment starts
     int32_t* slot_of;   // [T*K]
     int32_t* src;       // [R_cap] source token of each slot (-1 for pad rows)
@@ -94,11 +95,15 @@ struct DispatchBufs {
     int32_t* n_tiles;   // [1]
     uint16_t* xp;       // tiled activations [R_cap x H]
     int atoms;          // R_cap / 8
+    int rows_cap;       // R_cap: rows of src / xp
+    int max_tiles;      // entries of tiles
     int bn;             // token rows per GEMM tile
 };
-// row_src (optional): the row of token t is row_src[t] instead of x + t*H
+// row_src (optional): the row of token t is row_src[t] instead of x + t*H.
+// allow_none: an id of -1 means "no expert" (received rows without a local expert).
 cudaError_t launch_dispatch(const int32_t* ids, const uint16_t* x, int T, const Shape& sh, const DispatchBufs& d,
-                            int permute, cudaStream_t st, const uint16_t* const* row_src = nullptr);
+                            int permute, cudaStream_t st, const uint16_t* const* row_src = nullptr,
+                            int allow_none = 0);
 // y_local / local (expert parallelism): items computed on this rank, read from y_local (see k_combine)
 cudaError_t launch_combine(const uint16_t* y, int y_ld, const int32_t* slot_of, const float* w,
                            const uint16_t* residual, int T, int H, int K, uint16_t* out, cudaStream_t st,
@@ -107,7 +112,6 @@ cudaError_t launch_gather_rows(const uint16_t* y, const int32_t* slot_of, int ro
                                cudaStream_t st);
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps, uint16_t* out,
                            cudaStream_t st);
-cudaError_t launch_histogram(const int32_t* ids, int n, int E, int32_t* counts, int* err, cudaStream_t st);
 cudaError_t launch_tile_rows(const uint16_t* x, int n, int cols, int atoms, uint16_t* dst, cudaStream_t st);
 
 // ------------------------------------------------------------------- k_ep.cu
@@ -115,6 +119,7 @@ constexpr int kMaxWorld = 8;
 struct EpArgs {
     uint8_t* peer[kMaxWorld];  // every rank's EP buffer (this rank's included), same layout
     int world, rank, H, K, E_local;
+    const int32_t* place; // [E] slot of each global expert (slot = rank * E_local + local expert), this layer
     int cap_rows;        // rows of one source region: a token goes to a rank at most once (max_tokens)
     int cap_items;       // (token, rank) items of one source (max_tokens * K)
     size_t off_rx, off_meta, off_mtok, off_cnt, off_rflag, off_ret, off_retflag;
@@ -123,7 +128,6 @@ struct EpArgs {
     uint32_t* epoch;     // [1] completed forwards
     int32_t* ids_local;  // [world * cap_rows * K] local expert of each received (row, k), -1 = none
     int32_t* src_item;   // [world * cap_rows * K] source item t*K+k of each received (row, k)
-    int32_t* counts;     // [E_local] received (row, k) pairs per local expert (zeroed before k_ep_recv)
     int32_t* local_slot; // [cap_items] 1 + this rank's output slot of each of its own items computed here,
                          // 0 otherwise (set by k_ep_rowptr, cleared by the combine)
     const uint16_t** row_src;  // [world * cap_rows] where each received row's data is (k_ep_recv)

@@ -12,11 +12,11 @@ constexpr int kMaxE = 256, kMaxK = 16;
 // One warp: logits of expert e for tokens t0 .. t0+7 in the canonical order
 // (dequant_matvec_8bit.metal:8-31): lane l chains fma(w, x, acc) over its
 // groups l*m .. (l+1)*m-1 in column order, the lanes meet in the adjacent
-// pairwise tree (xor-butterfly offsets 1, 2, 4, 8, 16).  kGenericX: x may live
-// in shared memory (plain loads instead of the read-only path).
-template <bool kGenericX = false>
+// pairwise tree (xor-butterfly offsets 1, 2, 4, 8, 16).  The weights come
+// through the read-only path; x, written by an earlier kernel of the stream,
+// with ordinary loads after the dependent-launch wait.
 __device__ __forceinline__ void router_warp_item(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
-                                                 const uint16_t* __restrict__ b, const uint16_t* __restrict__ x,
+                                                 const uint16_t* __restrict__ b, const uint16_t* x,
                                                  int T, int H, int E, int e, int t0, int lane,
                                                  float* __restrict__ logits) {
     const int G = H / kGroup, m = G / 32;
@@ -45,7 +45,7 @@ __device__ __forceinline__ void router_warp_item(const uint32_t* __restrict__ w,
                 float a = acc[i];
 #pragma unroll
                 for (int v = 0; v < 8; ++v) {
-                    uint4 q = kGenericX ? xr[v] : __ldg(xr + v);
+                    uint4 q = xr[v];
                     uint32_t qs[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
@@ -90,7 +90,7 @@ struct NoMark {
     __device__ __forceinline__ void operator()(int) const {}
 };
 template <class LogitFn, class Mark = NoMark>
-__device__ __forceinline__ void topk_token(LogitFn logit, const float* __restrict__ bias, int E, int K, int norm,
+__device__ __forceinline__ void topk_token(LogitFn logit, const float* bias, int E, int K, int norm,
                                            int lane, int* id, float* wt, Mark mark = Mark()) {
     uint32_t key[kMaxE / 32];
 #pragma unroll

@@ -35,10 +35,11 @@ EXPORTS = (
     "obs_rmsnorm", "obs_moe_stack_forward", "obs_set_wait_limit", "obs_probe_wait", "obs_struct_layout",
     "obs_load_layer_safetensors", "obs_expert_file_info", "obs_load_head", "obs_embed", "obs_lm_head",
     "obs_attn_init", "obs_load_attn", "obs_attn_forward", "obs_kv_read", "obs_debug_gemm_tiles",
+    "obs_ep_set_placement", "obs_ep_get_placement", "obs_ep_plan_placement",
 )
 EP_HANDLE_BYTES = 64
 STAGES = ("router", "topk", "dispatch", "gemm_gateup", "gemm_down", "combine", "decode_gateup", "decode_down",
-          "decode_fused")
+          "decode_fused", "ep_send", "ep_recv", "ep_return")
 
 
 class ObsError(RuntimeError):
@@ -112,6 +113,9 @@ def lib() -> C.CDLL:
         L.obs_kernel_launches.argtypes = [C.POINTER(C.c_uint64)]
         L.obs_ep_handle.argtypes = [vp, vp]
         L.obs_ep_connect.argtypes = [vp, vp]
+        L.obs_ep_set_placement.argtypes = [vp, i32, C.POINTER(C.c_int32)]
+        L.obs_ep_get_placement.argtypes = [vp, i32, C.POINTER(C.c_int32)]
+        L.obs_ep_plan_placement.argtypes = [C.POINTER(C.c_int64), i32, i32, C.POINTER(C.c_int32)]
         L.obs_rmsnorm.argtypes = [vp, vp, vp, i32, vp, vp]
         L.obs_moe_stack_forward.argtypes = [vp, i32, i32, vp, i32, vp, i32, vp]
         L.obs_load_layer_safetensors.argtypes = [vp, i32, C.c_char_p, vp, vp, vp]
@@ -287,6 +291,17 @@ class MoeContext:
         buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
         self._chk(lib().obs_ep_connect(self._h, buf))
 
+    def ep_set_placement(self, layer, experts):
+        """Which GPU holds which expert (obs_ep_set_placement): experts[g*E/G + l] is GPU g's local
+        expert l; layer = -1 for every layer.  Changed layers must be loaded again."""
+        arr = (C.c_int32 * self.shape.n_experts)(*[int(e) for e in experts])
+        self._chk(lib().obs_ep_set_placement(self._h, layer, arr))
+
+    def ep_get_placement(self, layer) -> list:
+        arr = (C.c_int32 * self.shape.n_experts)()
+        self._chk(lib().obs_ep_get_placement(self._h, layer, arr))
+        return list(arr)
+
     def moe_forward(self, layer, x, out, T, residual=None, bias=None, path=PATH_AUTO, stream=None):
         self._chk(lib().obs_moe_forward(self._h, layer, _ptr(x), _ptr(out), _ptr(residual), T,
                                         _ptr(bias), path, _stream(stream)))
@@ -368,6 +383,17 @@ def expert_file_info(path: str) -> tuple[int, int, int]:
     if rc != OBS_OK:
         raise ObsError(rc, lib().obs_last_error(None).decode())
     return e.value, h.value, i.value
+
+
+def plan_placement(load, world: int) -> list:
+    """A balanced expert placement from per-expert loads (obs_ep_plan_placement; host only)."""
+    E = len(load)
+    lo = (C.c_int64 * E)(*[int(v) for v in load])
+    out = (C.c_int32 * E)()
+    rc = lib().obs_ep_plan_placement(lo, E, world, out)
+    if rc != 0:
+        raise ObsError(rc, "obs_ep_plan_placement: bad arguments")
+    return list(out)
 
 
 def struct_layout() -> list[int]:

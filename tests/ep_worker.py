@@ -2,7 +2,8 @@
 torch.distributed.run).  Each rank holds E/world experts of an oracle-generated
 layer, runs the EP forward on its own tokens (eagerly and from a CUDA graph),
 and rank 0 checks every rank's output bit for bit against a single-GPU context
-holding all experts.  Exit status 0 = pass."""
+holding all experts, also after the experts are placed on the ranks by a
+permutation.  Exit status 0 = pass."""
 import datetime
 import os
 import sys
@@ -64,6 +65,30 @@ def main():
         dist.barrier()
     del g
     ctx.check_device()
+    # another expert placement (the same seeded permutation on every rank): every rank refuses
+    # the forward until the layer is loaded again, then the output is the same bits
+    perm = [int(e) for e in np.random.default_rng(5).permutation(E)]
+    ctx.ep_set_placement(0, perm)
+    ok_local = ctx.ep_get_placement(0) == perm
+    try:
+        ctx.moe_forward(0, xd, out, T)
+        ok_local = False
+    except obsmoe.ObsError:
+        pass
+    ctx.load_layer(0, L)
+    dist.barrier()
+    for rep in range(2):
+        out = torch.full((max(T, 1), H), -1, dtype=torch.int16, device="cuda")
+        ctx.moe_forward(0, xd, out, T)
+        torch.cuda.synchronize()
+        outs.append(out[:T].cpu().numpy().view(np.uint16).copy())
+        try:  # every rank checks and goes on, so the ranks stay in step
+            ctx.check_device()
+        except obsmoe.ObsError as err:
+            print(f"rank {rank}: forward {rep} after the placement: {err}", flush=True)
+            ok_local = False
+        dist.barrier()
+    print(f"rank {rank}: placement set, refused before reload, read back, device clean: {ok_local}", flush=True)
 
     gathered = [None] * world
     dist.gather_object((x, outs), gathered if rank == 0 else None, dst=0)
@@ -88,7 +113,9 @@ def main():
                 ok &= same
         ref_ctx.check_device()
         ref_ctx.close()
-    flag = [ok]
+    oks = [None] * world
+    dist.all_gather_object(oks, ok_local)
+    flag = [ok and all(oks)]
     dist.broadcast_object_list(flag, src=0)
     ctx.close()
     dist.destroy_process_group()
