@@ -73,6 +73,8 @@ __device__ __forceinline__ T* at(uint8_t* base, size_t off) {
     return reinterpret_cast<T*>(base + off);
 }
 
+constexpr int kSendPiece = 2048, kSendChunks = kSendPiece / 8 / 32;  // 16-byte chunks per lane and piece
+
 // One warp per token: for every rank that holds one or more of the token's K
 // experts, one copy of row x[t] into that rank's region for this source, with
 // the (k, local expert) list and the token index -- for this rank itself only
@@ -94,24 +96,45 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* ids, const uint1
         }
         const int dest = lane < a.K ? slot_e / a.E_local : -1;
         const int le = lane < a.K ? slot_e - dest * a.E_local : 0;
-        const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * a.H);
-        for (int d = 0; d < a.world; ++d) {
-            if (!__any_sync(0xffffffffu, dest == d)) continue;
+        // one slot per destination rank first (with the row's metadata), then the row in pieces
+        // of 2048 columns: each piece in registers once, then independent 16-byte stores to every
+        // remote destination, so all of a warp's peer stores of a piece are in flight together
+        int slot_of_d[kMaxWorld];
+#pragma unroll
+        for (int d = 0; d < kMaxWorld; ++d) {
+            slot_of_d[d] = -1;
+            if (d >= a.world || !__any_sync(0xffffffffu, dest == d)) continue;
             int slot = 0;
             if (lane == 0) slot = atomicAdd(a.send_cnt + d, 1);
             slot = __shfl_sync(0xffffffffu, slot, 0);
             if (slot < a.cap_rows) {
                 uint8_t* pb = a.peer[d];
                 const size_t row = (size_t)a.rank * a.cap_rows + slot;
-                if (d != a.rank) {
-                    uint4* dst = at<uint4>(pb, a.off_rx + row * a.H * 2);
-                    for (int c = lane; c < a.H / 8; c += 32) dst[c] = src[c];
-                }
                 if (lane < 16)
                     at<int16_t>(pb, a.off_meta + row * 32)[lane] = (int16_t)(dest == d ? (lane << 8) | le : -1);
                 if (lane == 0) at<int32_t>(pb, a.off_mtok + row * 4)[0] = t;
+                if (d != a.rank) slot_of_d[d] = slot;
             } else if (lane == 0) {
                 refuse_slot(a.err, kSiteSendFull, slot);  // more rows than the source's region holds: refused
+            }
+        }
+        bool remote = false;
+#pragma unroll
+        for (int d = 0; d < kMaxWorld; ++d) remote |= slot_of_d[d] >= 0;
+        if (remote) {
+            const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * a.H);
+            for (int c0 = 0; c0 < a.H / 8; c0 += 32 * kSendChunks) {
+                uint4 v[kSendChunks];
+#pragma unroll
+                for (int u = 0; u < kSendChunks; ++u) v[u] = src[c0 + lane + 32 * u];
+#pragma unroll
+                for (int d = 0; d < kMaxWorld; ++d) {
+                    if (slot_of_d[d] < 0) continue;
+                    const size_t row = (size_t)a.rank * a.cap_rows + slot_of_d[d];
+                    uint4* dst = at<uint4>(a.peer[d], a.off_rx + row * a.H * 2) + c0 + lane;
+#pragma unroll
+                    for (int u = 0; u < kSendChunks; ++u) dst[32 * u] = v[u];
+                }
             }
         }
     }
@@ -233,7 +256,7 @@ __global__ void k_ep_finish(EpArgs a) {
 }  // namespace
 
 cudaError_t launch_ep_send(const int32_t* ids, const uint16_t* x, int T, int E, const EpArgs& a, cudaStream_t st) {
-    if (a.K > 16) return cudaErrorInvalidValue;  // 16 metadata slots per row
+    if (a.K > 16 || a.H % kSendPiece) return cudaErrorInvalidValue;  // 16 metadata slots per row; whole pieces
     const int grid = T > 0 ? (T + 7) / 8 : 1;   // one warp per token; one CTA at least: it publishes the counts
     {
         const cudaError_t le_ = launch_pdl(k_ep_send, dim3(grid), dim3(256), 0, st, ids, x, T, E, a);
