@@ -84,6 +84,7 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* ids, const uint1
                                                  int T, int E, EpArgs a) {
     pdl_begin();
     __shared__ int s_last;
+    __shared__ int s_slot[8][kMaxWorld];  // per warp: the row's slot at each rank, -1 = not sent there
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t e = *a.epoch + 1;
     const int t = blockIdx.x * 8 + warp;
@@ -96,41 +97,42 @@ __global__ void __launch_bounds__(256) k_ep_send(const int32_t* ids, const uint1
         }
         const int dest = lane < a.K ? slot_e / a.E_local : -1;
         const int le = lane < a.K ? slot_e - dest * a.E_local : 0;
-        // one slot per destination rank first (with the row's metadata), then the row in pieces
-        // of 2048 columns: each piece in registers once, then independent 16-byte stores to every
-        // remote destination, so all of a warp's peer stores of a piece are in flight together
-        int slot_of_d[kMaxWorld];
-#pragma unroll
-        for (int d = 0; d < kMaxWorld; ++d) {
-            slot_of_d[d] = -1;
-            if (d >= a.world || !__any_sync(0xffffffffu, dest == d)) continue;
-            int slot = 0;
-            if (lane == 0) slot = atomicAdd(a.send_cnt + d, 1);
-            slot = __shfl_sync(0xffffffffu, slot, 0);
-            if (slot < a.cap_rows) {
-                uint8_t* pb = a.peer[d];
-                const size_t row = (size_t)a.rank * a.cap_rows + slot;
-                if (lane < 16)
-                    at<int16_t>(pb, a.off_meta + row * 32)[lane] = (int16_t)(dest == d ? (lane << 8) | le : -1);
-                if (lane == 0) at<int32_t>(pb, a.off_mtok + row * 4)[0] = t;
-                if (d != a.rank) slot_of_d[d] = slot;
-            } else if (lane == 0) {
+        // the destinations of the row (a bit per rank); lane d takes the slot at rank d, all in parallel
+        const unsigned need = __reduce_or_sync(0xffffffffu, dest >= 0 ? 1u << dest : 0u);
+        int slot = -1;
+        if (lane < a.world && (need >> lane & 1u)) {
+            slot = atomicAdd(a.send_cnt + lane, 1);
+            if (slot >= a.cap_rows) {
                 refuse_slot(a.err, kSiteSendFull, slot);  // more rows than the source's region holds: refused
+                slot = -1;
             }
         }
-        bool remote = false;
-#pragma unroll
-        for (int d = 0; d < kMaxWorld; ++d) remote |= slot_of_d[d] >= 0;
-        if (remote) {
+        if (lane < kMaxWorld) s_slot[warp][lane] = slot;
+        __syncwarp();
+        // the (k, local expert) list and the token index at every destination
+        for (int d = 0; d < a.world; ++d) {
+            const int sd = s_slot[warp][d];
+            if (sd < 0) continue;
+            uint8_t* pb = a.peer[d];
+            const size_t row = (size_t)a.rank * a.cap_rows + sd;
+            if (lane < 16) at<int16_t>(pb, a.off_meta + row * 32)[lane] = (int16_t)(dest == d ? (lane << 8) | le : -1);
+            if (lane == 0) at<int32_t>(pb, a.off_mtok + row * 4)[0] = t;
+        }
+        // the row to every remote destination, in pieces of 2048 columns: each piece in registers
+        // once, then independent 16-byte stores.  Each token starts at a different peer (offset
+        // 1 + t mod (world - 1) from this rank), so the warps of all ranks spread their stores over
+        // the peers instead of all writing to the same GPU at once.
+        if (need & ~(1u << a.rank)) {
             const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * a.H);
             for (int c0 = 0; c0 < a.H / 8; c0 += 32 * kSendChunks) {
                 uint4 v[kSendChunks];
 #pragma unroll
                 for (int u = 0; u < kSendChunks; ++u) v[u] = src[c0 + lane + 32 * u];
-#pragma unroll
-                for (int d = 0; d < kMaxWorld; ++d) {
-                    if (slot_of_d[d] < 0) continue;
-                    const size_t row = (size_t)a.rank * a.cap_rows + slot_of_d[d];
+                for (int i = 0; i < a.world - 1; ++i) {
+                    const int d = (a.rank + 1 + (i + t) % (a.world - 1)) % a.world;  // every peer once
+                    const int sd = s_slot[warp][d];
+                    if (sd < 0) continue;
+                    const size_t row = (size_t)a.rank * a.cap_rows + sd;
                     uint4* dst = at<uint4>(a.peer[d], a.off_rx + row * a.H * 2) + c0 + lane;
 #pragma unroll
                     for (int u = 0; u < kSendChunks; ++u) dst[32 * u] = v[u];
