@@ -69,7 +69,15 @@ CONFIGS = {
     2: dict(T=None, name="config2: 48-layer MoE stack, decode of B independent tokens per step", stack=True),
     3: dict(T=4096, name="config3: 48-layer MoE stack, prefill of T=4096 tokens, Zipf(1.1) expert bias",
             stack=True),
+    4: dict(T=None, name="config4: full Qwen3-30B-A3B forward (random init), prefill of 2048 tokens per sequence "
+                         "then greedy decode of 128 tokens at batch B, 4096-token bf16 KV caches", full=True),
 }
+# config 4: the model around the MoE path (Qwen3MoeConfig)
+VOCAB, NQ, NKV, HD, KV_SEQ, PREFILL, DECODE = 151936, 32, 4, 128, 4096, 2048, 128
+ATTN_BYTES = (NQ + 2 * NKV) * HD * (H // 8) * 4 + (NQ + 2 * NKV) * HD * (H // 64) * 4 \
+    + H * (NQ * HD // 8) * 4 + H * (NQ * HD // 64) * 4  # q/k/v/o codes + scales + biases, one layer
+HEAD_BYTES = VOCAB * (H // 8) * 4 + VOCAB * (H // 64) * 4  # lm_head codes + scales + biases
+REF_PUBLISHED_DECODE = 3.71  # tokens/s, full-model decode at batch 1 (Apple M4, experts paged from SSD)
 EXTRA_SECONDS = 0.5   # timed region of the extra config 0 / config 1 measurements
 
 
@@ -82,7 +90,9 @@ def parse():
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="config 3 on one GPU: skip the config 0/1 keys")
-    ap.add_argument("--batch", type=int, default=32, help="config 2: tokens per decode step (1, 8, 32, 128)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="config 2: tokens per decode step (1, 8, 32, 128; default 32); config 4: sequences "
+                         "decoded together (1 or 16; default 1)")
     ap.add_argument("--layers", type=int, default=48, help="configs 2 and 3: layers in the stack")
     ap.add_argument("--tokens", type=int, default=0,
                     help="configs 0 and 1: override T (a sweep point, not a BASELINE config)")
@@ -657,6 +667,190 @@ def run_layer(args, cfg_id, rank, world, local, ranks, steps, warmup, tokens=0, 
     return line
 
 
+class RandLinear4:
+    """Random weights of one MLX 4-bit group-64 linear layer on the device: uniform codes, bf16
+    scales U(lo, hi) and biases -8*scale + N(0, 1e-3) (the expert weights' distribution)."""
+
+    def __init__(self, torch, gen, rows, in_f, lo=0.002, hi=0.02):
+        self.w = torch.randint(-2 ** 31, 2 ** 31 - 1, (rows, in_f // 8), dtype=torch.int32, device="cuda",
+                               generator=gen)
+        sc = torch.empty((rows, in_f // 64), device="cuda").uniform_(lo, hi, generator=gen)
+        self.s = sc.to(torch.bfloat16)
+        self.b = (-8.0 * sc + 1e-3 * torch.randn(sc.shape, device="cuda", generator=gen)).to(torch.bfloat16)
+
+
+def run_full(args, rank, world, local, ranks):
+    """Config 4: the whole model through the library's entry points -- embed, 48 x (attention
+    block, then RMSNorm + MoE + residual), final norm + lm_head + greedy token -- with random
+    weights generated on the device.  Each of B sequences is prefilled with 2048 random tokens
+    (256-token chunks, eager, timed as the prefill rate), then 128 greedy decode steps of all B
+    sequences at once are timed, each step one CUDA graph replay.  N > 1: N replicas."""
+    import types
+
+    import numpy as np
+    import torch
+
+    import obsmoe
+
+    cfg = CONFIGS[args.config]
+    B, nl, C = args.batch, args.layers, 256
+    stream = torch.cuda.current_stream()
+    shape = obsmoe.MoeShape(H, I, E, K, n_layers=nl, max_tokens=C, decode_max_tokens=args.decode_max)
+    ctx = obsmoe.MoeContext(shape, local)
+    ctx.attn_init(NQ, NKV, HD, KV_SEQ, B, 1e7)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(4 + 1000 * rank)
+    ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device="cuda")  # noqa: E731
+    for l in range(nl):
+        ctx.synth_layer(l, 0)
+        q, k, v = (RandLinear4(torch, gen, n * HD, H) for n in (NQ, NKV, NKV))
+        o = RandLinear4(torch, gen, H, NQ * HD)
+        w = types.SimpleNamespace(q_w=q.w, q_s=q.s, q_b=q.b, k_w=k.w, k_s=k.s, k_b=k.b, v_w=v.w, v_s=v.s, v_b=v.b,
+                                  o_w=o.w, o_s=o.s, o_b=o.b, in_norm=ones(H), q_norm=ones(HD), k_norm=ones(HD))
+        ctx.load_attn(l, w, on_device=True)
+    emb, lm = RandLinear4(torch, gen, VOCAB, H, 0.001, 0.01), RandLinear4(torch, gen, VOCAB, H, 0.001, 0.01)
+    ctx.load_head(VOCAB, types.SimpleNamespace(embed_w=emb.w, embed_s=emb.s, embed_b=emb.b, lm_w=lm.w, lm_s=lm.s,
+                                               lm_b=lm.b, norm_w=ones(H)), on_device=True)
+    del emb, lm
+    torch.cuda.synchronize()
+    xa = torch.empty((C, H), dtype=torch.int16, device="cuda")
+    xb = torch.empty_like(xa)
+
+    def layers(n, seqs, pos, st):
+        """The residual rows xa[:n] through every layer (ping-pong through xb); ends in xa."""
+        x, y = xa, xb
+        for l in range(nl):
+            ctx.attn_forward(l, x, y, n, seqs, pos, stream=st)
+            ctx.moe_stack_forward(l, 1, y, n, path=obsmoe.PATH_AUTO, stream=st)
+            x, y = y, x
+        return x
+
+    # ---- prefill: every sequence's 2048 random tokens, 256 at a time; its last row gives its first token
+    prompts = torch.randint(0, VOCAB, (B, PREFILL), dtype=torch.int32, device="cuda", generator=gen)
+    ids = torch.empty(B, dtype=torch.int32, device="cuda")
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ranks.barrier()
+    p0.record(stream)
+    for sq in range(B):
+        seq_c = torch.full((C,), sq, dtype=torch.int32, device="cuda")
+        for c0 in range(0, PREFILL, C):
+            pos_c = torch.arange(c0, c0 + C, dtype=torch.int32, device="cuda")
+            ctx.embed(prompts[sq, c0:c0 + C], C, xa, stream=stream)
+            last = layers(C, seq_c, pos_c, stream)
+        ctx.lm_head(last[C - 1:C], 1, ids[sq:sq + 1], stream=stream)
+    p1.record(stream)
+    ranks.barrier()
+    prefill_s = ranks.max(p0.elapsed_time(p1)) / 1e3
+    ctx.check_device()
+
+    # ---- decode: one token of every sequence per step, positions 2048, 2049, ...
+    seqs = torch.arange(B, dtype=torch.int32, device="cuda")
+    pos = torch.full((B,), PREFILL, dtype=torch.int32, device="cuda")
+
+    def dstep(st):
+        ctx.embed(ids, B, xa, stream=st)
+        ctx.lm_head(layers(B, seqs, pos, st)[:B], B, ids, stream=st)
+        pos.add_(1)
+
+    # one eager step that also records the distinct experts each layer routes to (the HBM bytes)
+    logits = torch.empty((B, E), dtype=torch.float32, device="cuda")
+    rids = torch.empty((B, K), dtype=torch.int32, device="cuda")
+    rw = torch.empty((B, K), dtype=torch.float32, device="cuda")
+    xn = torch.empty((B, H), dtype=torch.int16, device="cuda")
+    U = []
+    ctx.embed(ids, B, xa, stream=stream)
+    x, y = xa, xb
+    for l in range(nl):
+        ctx.attn_forward(l, x, y, B, seqs, pos, stream=stream)
+        ctx.rmsnorm(y[:B], xn, B, stream=stream)
+        ctx.gate_gpu(l, xn, logits, B, stream=stream)
+        ctx.route(logits, B, rids, rw, stream=stream)
+        U.append(len(np.unique(rids.cpu().numpy())))
+        ctx.moe_stack_forward(l, 1, y, B, path=obsmoe.PATH_AUTO, stream=stream)
+        x, y = y, x
+    ctx.lm_head(x[:B], B, ids, stream=stream)
+    pos.add_(1)
+    n0 = obsmoe.kernel_launches()
+    dstep(stream)
+    torch.cuda.synchronize()
+    launches_per_step = obsmoe.kernel_launches() - n0
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(g, stream=cap):
+            dstep(cap)
+    stream.wait_stream(cap)
+    for _ in range(max(args.warmup, 3) - 2):
+        g.replay()
+    ranks.barrier()
+    ctx.check_device()
+    clocks = Clocks(local)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ranks.barrier()
+    ev0.record(stream)
+    for _ in range(DECODE):
+        g.replay()
+    ev1.record(stream)
+    ranks.barrier()
+    clk = clocks.stop()
+    ms = ranks.max(ev0.elapsed_time(ev1))
+    ctx.check_device()
+    step_s = ms / DECODE / 1e3
+    last_pos = int(pos[0].item())
+    # e2e: the same steps with each step's tokens read back to pinned host memory (a serving loop)
+    ids_host = torch.empty(B, dtype=torch.int32).pin_memory()
+    pos.fill_(last_pos - DECODE)  # rewrite the last 128 positions of the caches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ranks.barrier()
+    e0.record(stream)
+    for _ in range(DECODE):
+        g.replay()
+        ids_host.copy_(ids, non_blocking=True)
+    e1.record(stream)
+    ranks.barrier()
+    e2e_s = ranks.max(e0.elapsed_time(e1)) / 1e3 / DECODE
+    finite = bool(torch.isfinite(xa[:B].view(torch.bfloat16).float()).all().item())
+    del g
+    ctx.check_device()
+
+    # HBM roofline of a decode step: every layer's attention weights, its router and routed
+    # experts, the KV cache rows read (mean position of the timed steps), the lm_head
+    hbm, _, _, peak_kind = peaks()
+    mean_pos = last_pos - DECODE / 2
+    kv_bytes = nl * B * 2 * NKV * (mean_pos + 1) * HD * 2
+    step_bytes = nl * (ATTN_BYTES + ROUTER_BYTES) + sum(U) * EXPERT_BYTES + kv_bytes + HEAD_BYTES
+    achieved = step_bytes / step_s / 1e9
+    value = world * B / step_s
+    line = {
+        "metric": "full-model decode tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": DECODE, "warmup": max(args.warmup, 3), "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "dtype": "bf16",
+        "vs_baseline": value / REF_PUBLISHED_DECODE if B == 1 and world == 1 else None,
+        "vs_baseline_note": "the reference's published full-model decode, 3.71 tokens/s at batch 1 on an Apple M4 "
+                            "with experts paged from SSD (other hardware)",
+        "data": "synthetic (random weights generated on the device: MoE layers seeded as configs 2/3, attention and "
+                "head uniform 4-bit codes; random prompt tokens)",
+        "config": {"workload": cfg["name"], "batch": B, "layers": nl, "prefill_tokens": PREFILL,
+                   "decode_tokens": DECODE, "kv_cache": KV_SEQ, "vocab": VOCAB,
+                   "parallelism": f"data parallel x{world} (replicas)" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2: {nl} resident layers per step",
+                   "moe_path": "decode (fused layer)" if B <= 4 else "grouped GEMM"},
+        "prefill": {"tokens_per_s": world * B * PREFILL / prefill_s, "seconds": prefill_s,
+                    "note": "eager, 256-token chunks, attention by 16-row mat-vec projections"},
+        "roofline": {"bound": "hbm", "kernel": "whole decode step (attention, MoE, lm_head)", "achieved": achieved,
+                     "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+                     "algorithmic_bytes_per_launch": step_bytes, "distinct_experts_per_layer": float(np.mean(U)),
+                     "traffic": None},
+        "e2e": {"value": world * B / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": B * 4},
+        "gpu_launches": launches_per_step * DECODE, "clocks": clk, "finite": finite,
+    }
+    ranks.barrier()
+    return line
+
+
 def extra_summary(line):
     """The keys of a config 0 / config 1 line that the default line carries."""
     keep = ("value", "unit", "ms_per_step", "steps", "roofline", "stage_us", "e2e", "gpu_launches", "clocks",
@@ -676,6 +870,11 @@ def run_reference(args, rank, world):
     import synthetic
 
     cfg = CONFIGS[args.config]
+    if cfg.get("full"):
+        print(json.dumps({"impl": "reference", "unavailable": "config 4 (the full forward after a 2048-token "
+                          "prefill) has no bounded CPU sample: the reference's host kernels cover the MoE path "
+                          "only, and a CPU prefill of 2048 tokens through 48 layers takes hours"}))
+        return
     T = cfg["T"] if cfg["T"] is not None else args.batch
     if O.ref_lib() is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libobs_refshaders.so was not built"}))
@@ -724,6 +923,8 @@ def run_reference(args, rank, world):
 
 def main():
     args = parse()
+    if args.batch <= 0:
+        args.batch = 1 if args.config == 4 else 32
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -733,7 +934,9 @@ def main():
 
     torch.cuda.set_device(local)
     ranks = Ranks(world)
-    if CONFIGS[args.config].get("stack"):
+    if CONFIGS[args.config].get("full"):
+        line = run_full(args, rank, world, local, ranks)
+    elif CONFIGS[args.config].get("stack"):
         line = run_stack(args, rank, world, local, ranks)
         if args.config == 3 and world == 1 and not args.no_extras:
             # the decode target (config 0) and config 1, each timed for ~EXTRA_SECONDS

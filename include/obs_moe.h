@@ -104,8 +104,8 @@ typedef struct obs_attn_weights {
  * bf16 cache [n_kv_heads][max_seq][head_dim] per layer for K and for V. */
 typedef struct obs_attn_config {
     int32_t n_heads;     /* query heads (32) */
-    int32_t n_kv_heads;  /* key/value heads (4); n_heads a multiple of it */
-    int32_t head_dim;    /* <= 128, even; n_heads * head_dim a multiple of 2048 */
+    int32_t n_kv_heads;  /* key/value heads (4); n_heads a multiple of it, at most 8 times it */
+    int32_t head_dim;    /* <= 128, a multiple of 8; n_heads * head_dim a multiple of 2048 */
     int32_t max_seq;     /* positions per cache (<= 40960) */
     int32_t n_seqs;      /* sequences (caches) per layer */
     float rope_theta;    /* 1e7 */

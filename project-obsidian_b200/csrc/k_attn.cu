@@ -94,63 +94,138 @@ __global__ void __launch_bounds__(kAttnThreads) k_qk_norm_rope(const float* qkv,
     }
 }
 
-// Single-query GQA attention (sdpa_decode.metal:14-48) of token t, head h over
-// its sequence's cache positions 0 .. pos[t]: scores s_j = (q . k_j) / sqrt(hd)
-// (one warp per key, lanes over head_dim, fixed tree), m = max s, p_j =
-// exp(s_j - m), out = (sum_j p_j v_j) / (sum_j p_j).  grid (T, nq), 128 threads;
-// scores in shared memory (max_seq floats).
-__global__ void __launch_bounds__(kAttnThreads) k_sdpa(const uint16_t* q, const uint16_t* kc,
-                                                       const uint16_t* vc, int nq, int nkv, int hd,
-                                                       int max_seq, int n_seqs, float scale,
-                                                       const int32_t* seq,
-                                                       const int32_t* pos, uint16_t* __restrict__ out) {
+// Single-query GQA attention (sdpa_decode.metal:14-48) of token t over its
+// sequence's cache positions 0 .. pos[t], split over the positions so a decode
+// step fills the GPU: scores s_j = (q . k_j) / sqrt(hd), out = sum_j e^(s_j - m)
+// v_j / sum_j e^(s_j - m).  k_sdpa_part: one CTA per (token, KV head, split)
+// takes the split's positions for all query heads of the KV head (each K and V
+// row is read once for the group), 128 positions at a time (one per thread: its
+// K row against every head's q, fp32, dimensions in order), with a running
+// maximum and sum per head (the online softmax) and each thread accumulating one
+// dimension of every head's sum p_j v_j; it leaves (m, l, acc) per (token, head,
+// split).  k_sdpa_merge: one CTA per (token, head) rescales the splits to the
+// common maximum and divides.  Against the reference's single pass this changes
+// only the order of the fp32 sums and the rescalings.
+constexpr int kSdpaTile = 128;      // cache positions per pass of a CTA, one per thread
+constexpr int kSdpaMaxGroup = 8;    // query heads per KV head (one CTA takes them all)
+constexpr int kSdpaMaxSplits = 32;  // position splits per (token, KV head)
+
+__global__ void __launch_bounds__(kSdpaTile) k_sdpa_part(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
+                                                         int nq, int nkv, int hd, int max_seq, int n_seqs,
+                                                         float scale, const int32_t* seq, const int32_t* pos,
+                                                         float* __restrict__ part_acc, float* __restrict__ part_ml) {
     pdl_begin();
-    extern __shared__ float s_sc[];  // [max_seq]
-    __shared__ float s_q[128];
-    __shared__ float s_red[kAttnThreads / 32];
-    const int t = blockIdx.x, h = blockIdx.y, l = threadIdx.x, lane = l & 31, warp = l >> 5;
-    const int s_id = seq[t], p = pos[t], kvh = h / (nq / nkv);
-    if (s_id < 0 || s_id >= n_seqs || p < 0 || p >= max_seq) return;  // flagged by k_qk_norm_rope
-    if (l < hd) s_q[l] = bf2f(q[((size_t)t * nq + h) * hd + l]);
-    __syncthreads();
+    __shared__ float s_q[kSdpaMaxGroup][128];
+    __shared__ float s_p[kSdpaMaxGroup][kSdpaTile];
+    __shared__ float s_m[kSdpaMaxGroup], s_l[kSdpaMaxGroup], s_corr[kSdpaMaxGroup];
+    const int t = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z, S = gridDim.z;
+    const int G = nq / nkv, l = threadIdx.x, lane = l & 31, warp = l >> 5;
+    const int s_id = seq[t], p = pos[t];
+    if (s_id < 0 || s_id >= n_seqs || p < 0 || p >= max_seq) return;  // refused and recorded by k_qk_norm_rope
+    const int n = p + 1, chunk = (n + S - 1) / S, js = sp * chunk, je = min(n, js + chunk);
+    if (js >= je) return;  // no positions in this split: the merge reads only the splits that have some
+    for (int i = l; i < G * hd; i += kSdpaTile) s_q[i / hd][i % hd] = bf2f(q[((size_t)t * nq + kvh * G) * hd + i]);
+    if (l < kSdpaMaxGroup) s_m[l] = -INFINITY, s_l[l] = 0.0f;
     const uint16_t* kbase = kc + ((size_t)s_id * nkv + kvh) * max_seq * hd;
     const uint16_t* vbase = vc + ((size_t)s_id * nkv + kvh) * max_seq * hd;
-    const int n = p + 1;
-    for (int j = warp; j < n; j += kAttnThreads / 32) {
-        const uint16_t* kr = kbase + (size_t)j * hd;
-        float a = 0.0f;
-        for (int d = lane; d < hd; d += 32) a = __fmaf_rn(s_q[d], bf2f(kr[d]), a);
+    float acc[kSdpaMaxGroup];
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-        if (lane == 0) s_sc[j] = __fmul_rn(a, scale);
+    for (int h = 0; h < kSdpaMaxGroup; ++h) acc[h] = 0.0f;
+    __syncthreads();
+    for (int j0 = js; j0 < je; j0 += kSdpaTile) {
+        const int j = j0 + l, len = min(kSdpaTile, je - j0);
+        // scores of position j against every head of the group
+        float sc[kSdpaMaxGroup];
+#pragma unroll
+        for (int h = 0; h < kSdpaMaxGroup; ++h) sc[h] = 0.0f;
+        if (l < len) {
+            const uint4* kr = reinterpret_cast<const uint4*>(kbase + (size_t)j * hd);
+            for (int c = 0; c < hd / 8; ++c) {
+                const uint4 v = kr[c];
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float k0 = __uint_as_float(w4[e] << 16), k1 = __uint_as_float(w4[e] & 0xFFFF0000u);
+#pragma unroll
+                    for (int h = 0; h < kSdpaMaxGroup; ++h)
+                        if (h < G) sc[h] = __fmaf_rn(s_q[h][8 * c + 2 * e + 1], k1, __fmaf_rn(s_q[h][8 * c + 2 * e], k0, sc[h]));
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < kSdpaMaxGroup; ++h)
+            if (h < G) s_p[h][l] = l < len ? __fmul_rn(sc[h], scale) : -INFINITY;
+        __syncthreads();
+        // per head (warp w takes heads w, w + 4): the tile's maximum, the new running maximum,
+        // the probabilities, the rescaling of what came before and the running sum
+        for (int h = warp; h < G; h += kSdpaTile / 32) {
+            float mt = -INFINITY;
+            for (int x = lane; x < len; x += 32) mt = fmaxf(mt, s_p[h][x]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+            const float m_old = s_m[h], m_new = fmaxf(m_old, mt);
+            float sum = 0.0f;
+            for (int x = lane; x < len; x += 32) {
+                const float e = expf(s_p[h][x] - m_new);
+                s_p[h][x] = e;
+                sum += e;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            __syncwarp();
+            if (lane == 0) {
+                const float corr = expf(m_old - m_new);  // 0 for the first tile (m_old = -inf)
+                s_corr[h] = corr;
+                s_m[h] = m_new;
+                s_l[h] = __fmaf_rn(s_l[h], corr, sum);
+            }
+        }
+        __syncthreads();
+        // dimension l of every head: rescale, then add the tile's p_j v_j
+        if (l < hd) {
+#pragma unroll
+            for (int h = 0; h < kSdpaMaxGroup; ++h)
+                if (h < G) acc[h] = __fmul_rn(acc[h], s_corr[h]);
+            for (int x = 0; x < len; ++x) {
+                const float v = bf2f(vbase[(size_t)(j0 + x) * hd + l]);
+#pragma unroll
+                for (int h = 0; h < kSdpaMaxGroup; ++h)
+                    if (h < G) acc[h] = __fmaf_rn(s_p[h][x], v, acc[h]);
+            }
+        }
+        __syncthreads();  // s_p is rewritten by the next tile
     }
-    __syncthreads();
-    float m = -INFINITY;
-    for (int j = l; j < n; j += kAttnThreads) m = fmaxf(m, s_sc[j]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) s_red[warp] = m;
-    __syncthreads();
-    m = s_red[0];
-    for (int w = 1; w < kAttnThreads / 32; ++w) m = fmaxf(m, s_red[w]);
-    __syncthreads();
-    float sum = 0.0f;
-    for (int j = l; j < n; j += kAttnThreads) {
-        const float e = expf(s_sc[j] - m);
-        s_sc[j] = e;
-        sum += e;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) s_red[warp] = sum;
-    __syncthreads();
-    sum = 0.0f;
-    for (int w = 0; w < kAttnThreads / 32; ++w) sum += s_red[w];
+    const size_t row0 = ((size_t)t * nq + kvh * G) * S + sp;  // (token, first head of the group, split)
     if (l < hd) {
-        float acc = 0.0f;
-        for (int j = 0; j < n; ++j) acc = __fmaf_rn(s_sc[j], bf2f(vbase[(size_t)j * hd + l]), acc);
-        out[((size_t)t * nq + h) * hd + l] = f2bf(__fdiv_rn(acc, sum));
+#pragma unroll
+        for (int h = 0; h < kSdpaMaxGroup; ++h)
+            if (h < G) part_acc[(row0 + (size_t)h * S) * hd + l] = acc[h];
     }
+    if (l < G) {
+        part_ml[(row0 + (size_t)l * S) * 2] = s_m[l];
+        part_ml[(row0 + (size_t)l * S) * 2 + 1] = s_l[l];
+    }
+}
+
+__global__ void __launch_bounds__(kAttnThreads) k_sdpa_merge(const float* part_acc, const float* part_ml, int S,
+                                                             int nq, int hd, int max_seq, int n_seqs,
+                                                             const int32_t* seq, const int32_t* pos,
+                                                             uint16_t* __restrict__ out) {
+    pdl_begin();
+    const int t = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    const int s_id = seq[t], p = pos[t];
+    if (s_id < 0 || s_id >= n_seqs || p < 0 || p >= max_seq) return;
+    const int n = p + 1, chunk = (n + S - 1) / S, used = (n + chunk - 1) / chunk;
+    const size_t row0 = ((size_t)t * nq + h) * S;
+    float M = -INFINITY;
+    for (int s = 0; s < used; ++s) M = fmaxf(M, part_ml[(row0 + s) * 2]);
+    float L = 0.0f, a = 0.0f;
+    for (int s = 0; s < used; ++s) {
+        const float w = expf(part_ml[(row0 + s) * 2] - M);
+        L = __fmaf_rn(w, part_ml[(row0 + s) * 2 + 1], L);
+        if (d < hd) a = __fmaf_rn(w, part_acc[(row0 + s) * hd + d], a);
+    }
+    if (d < hd) out[((size_t)t * nq + h) * hd + d] = f2bf(__fdiv_rn(a, L));
 }
 
 // x1 = x + bf16(o): the o projection rounded to bf16, the residual add in fp32, one rounding
@@ -175,16 +250,34 @@ cudaError_t launch_qk_norm_rope(const float* qkv, int T, int nq, int nkv, int hd
     return cudaGetLastError();
 }
 
+int sdpa_splits(int T, int nkv, int num_sms) {
+    const int want = (4 * num_sms + T * nkv - 1) / (T * nkv);
+    return want < 1 ? 1 : want > kSdpaMaxSplits ? kSdpaMaxSplits : want;
+}
+
+size_t sdpa_part_floats(int max_tokens, int nq, int nkv, int hd, int num_sms) {
+    size_t rows = 0;  // the largest T * splits of any launch
+    for (int T = 1; T <= max_tokens; ++T) {
+        const size_t r = (size_t)T * sdpa_splits(T, nkv, num_sms);
+        if (r > rows) rows = r;
+    }
+    return rows * nq * (hd + 2);
+}
+
 cudaError_t launch_sdpa(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int T, int nq, int nkv, int hd,
-                        int max_seq, int n_seqs, const int32_t* seq, const int32_t* pos, uint16_t* out,
-                        cudaStream_t st) {
+                        int max_seq, int n_seqs, const int32_t* seq, const int32_t* pos, uint16_t* out, float* part,
+                        int num_sms, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    const size_t smem = (size_t)max_seq * 4;
-    cudaError_t e = cudaFuncSetAttribute(k_sdpa, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+    if (hd > 128 || hd % 8 || nq % nkv || nq / nkv > kSdpaMaxGroup) return cudaErrorInvalidValue;
+    const int S = sdpa_splits(T, nkv, num_sms);
+    float* part_acc = part;
+    float* part_ml = part + (size_t)T * nq * S * hd;
     const float scale = 1.0f / sqrtf((float)hd);
-    e = launch_pdl(k_sdpa, dim3(T, nq), dim3(kAttnThreads), smem, st, q, kc, vc, nq, nkv, hd, max_seq, n_seqs, scale, seq,
-                   pos, out);
+    cudaError_t e = launch_pdl(k_sdpa_part, dim3(T, nkv, S), dim3(kSdpaTile), 0, st, q, kc, vc, nq, nkv, hd, max_seq,
+                               n_seqs, scale, seq, pos, part_acc, part_ml);
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(k_sdpa_merge, dim3(T, nq), dim3(kAttnThreads), 0, st, (const float*)part_acc,
+                   (const float*)part_ml, S, nq, hd, max_seq, n_seqs, seq, pos, out);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

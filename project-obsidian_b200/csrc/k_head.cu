@@ -63,7 +63,16 @@ __global__ void __launch_bounds__(32 * kHeadWarps) k_lm_head(const uint32_t* __r
     pdl_begin();
     extern __shared__ __align__(16) float s_x[];  // [T][H]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int i = threadIdx.x; i < T * H; i += blockDim.x) s_x[i] = bf2f(xin[i]);
+    // 8 bf16 per 16-byte load, several loads in flight per thread (H is a multiple of 2048)
+#pragma unroll 4
+    for (int i = threadIdx.x; i < T * H / 8; i += blockDim.x) {
+        const uint4 v = reinterpret_cast<const uint4*>(xin)[i];
+        float4* d = reinterpret_cast<float4*>(s_x + 8 * (size_t)i);
+        d[0] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                           __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+        d[1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
+                           __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
+    }
     __syncthreads();
     const int G = H / kGroup, m = G / 32;
     const int nwarps = gridDim.x * kHeadWarps, gw = blockIdx.x * kHeadWarps + warp;
@@ -175,7 +184,14 @@ static cudaError_t lm_head_t(const uint32_t* w, const uint16_t* s, const uint16_
     const size_t smem = (size_t)T * H * 4;
     cudaError_t e = cudaFuncSetAttribute(k_lm_head<MAXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_lm_head<MAXT>, dim3(4 * num_sms), dim3(32 * kHeadWarps), smem, st, w, s, b, xn, T, vocab, H,
+    // one wave: as many CTAs as fit on the SMs at once (shared memory, 8 x 256 threads), and no
+    // more than the rows need, so no CTA stages x without rows to use it on
+    int per_sm = (int)((size_t)220 * 1024 / smem);
+    per_sm = per_sm < 1 ? 1 : per_sm > 8 ? 8 : per_sm;
+    const int rows_per_cta = kHeadWarps * kHeadRowsPerWarp;
+    int grid = (vocab + rows_per_cta - 1) / rows_per_cta;
+    if (grid > num_sms * per_sm) grid = num_sms * per_sm;
+    return launch_pdl(k_lm_head<MAXT>, dim3(grid), dim3(32 * kHeadWarps), smem, st, w, s, b, xn, T, vocab, H,
                       logits);
 }
 

@@ -114,6 +114,7 @@ struct obs_ctx {
     uint16_t* a_q = nullptr;    // [max_tokens][nq hd]
     uint16_t* a_out = nullptr;  // [max_tokens][nq hd]
     float* a_o = nullptr;       // [max_tokens][H]
+    float* a_part = nullptr;    // the attention splits' partial sums (sdpa_part_floats)
     size_t ep_bytes = 0;
     bool ep_connected = false;
     EpArgs ep{};
@@ -559,23 +560,25 @@ extern "C" int obs_attn_init(obs_ctx* ctx, const obs_attn_config* ac) {
     if (!ac) return fail(ctx, OBS_ERR_INVALID, "null attention config");
     if (!ctx->attn.empty()) return fail(ctx, OBS_ERR_STATE, "attention already initialised");
     const int nq = ac->n_heads, nkv = ac->n_kv_heads, hd = ac->head_dim;
-    if (nq <= 0 || nkv <= 0 || nq % nkv || hd <= 0 || hd > 128 || hd % 2 || (nq * hd) % 2048 ||
+    if (nq <= 0 || nkv <= 0 || nq % nkv || nq / nkv > 8 || hd <= 0 || hd > 128 || hd % 8 || (nq * hd) % 2048 ||
         ac->max_seq <= 0 || ac->max_seq > kAttnMaxSeq || ac->n_seqs <= 0 || !(ac->rope_theta > 0.0f))
         return fail(ctx, OBS_ERR_INVALID,
-                    "bad attention config (heads divisible by kv heads, head_dim <= 128 even, heads*head_dim a "
-                    "multiple of 2048, 0 < max_seq <= 40960, n_seqs > 0, rope_theta > 0)");
+                    "bad attention config (heads a multiple of kv heads, at most 8 per kv head, head_dim <= 128 "
+                    "a multiple of 8, heads*head_dim a multiple of 2048, 0 < max_seq <= 40960, n_seqs > 0, "
+                    "rope_theta > 0)");
     CU(cudaSetDevice(ctx->device), "cudaSetDevice");
     ctx->acfg = *ac;
     const int T = ctx->cfg.max_tokens, H = ctx->sh.H, W = (nq + 2 * nkv) * hd;
     const size_t sizes[] = {(size_t)ac->max_seq * hd * 4, (size_t)T * W * 4, (size_t)T * H * 2, (size_t)T * nq * hd * 2,
-                            (size_t)T * nq * hd * 2, (size_t)T * H * 4};
+                            (size_t)T * nq * hd * 2, (size_t)T * H * 4,
+                            sdpa_part_floats(T, nq, nkv, hd, ctx->num_sms) * 4};
     size_t total = 0;
     for (size_t sz : sizes) total += align_up(sz, 256);
     CU(cudaMalloc(&ctx->attn_scratch, total), "attention scratch");
     uint8_t* p = ctx->attn_scratch;
     void** ptrs[] = {(void**)&ctx->rope_cs, (void**)&ctx->a_qkv, (void**)&ctx->a_xn, (void**)&ctx->a_q,
-                     (void**)&ctx->a_out, (void**)&ctx->a_o};
-    for (int i = 0; i < 6; ++i) *ptrs[i] = p, p += align_up(sizes[i], 256);
+                     (void**)&ctx->a_out, (void**)&ctx->a_o, (void**)&ctx->a_part};
+    for (int i = 0; i < 7; ++i) *ptrs[i] = p, p += align_up(sizes[i], 256);
     std::vector<float> tab((size_t)ac->max_seq * hd);
     rope_table(ac->rope_theta, hd, ac->max_seq, tab.data());
     CU(cudaMemcpy(ctx->rope_cs, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice), "rope table");
@@ -656,7 +659,9 @@ extern "C" int obs_attn_forward(obs_ctx* ctx, int layer, const uint16_t* x, uint
     CU(launch_qk_norm_rope(ctx->a_qkv, T, nq, nkv, hd, L.q_norm, L.k_norm, ctx->cfg.rms_eps, ctx->rope_cs, ac.max_seq,
                            seq, pos, ctx->a_q, L.kc, L.vc, ac.n_seqs, ctx->err_flag, st),
        "q/k norm, rope, cache append");
-    CU(launch_sdpa(ctx->a_q, L.kc, L.vc, T, nq, nkv, hd, ac.max_seq, ac.n_seqs, seq, pos, ctx->a_out, st), "attention");
+    CU(launch_sdpa(ctx->a_q, L.kc, L.vc, T, nq, nkv, hd, ac.max_seq, ac.n_seqs, seq, pos, ctx->a_out, ctx->a_part,
+                   ctx->num_sms, st),
+       "attention");
     CU(launch_linear4(L.o_w, L.o_s, L.o_b, ctx->a_out, T, H, nq * hd, ctx->a_o, ctx->num_sms, st), "o projection");
     CU(launch_residual_add(x, ctx->a_o, (size_t)T * H, out, st), "residual");
     return OBS_OK;

@@ -222,9 +222,12 @@ cudaError_t launch_qk_norm_rope(const float* qkv, int T, int nq, int nkv, int hd
                                 const uint16_t* kn, float eps, const float* rope_cs, int max_seq, const int32_t* seq,
                                 const int32_t* pos, uint16_t* qout, uint16_t* kcache, uint16_t* vcache, int n_seqs,
                                 int* err, cudaStream_t st);
+// part: sdpa_part_floats(max_tokens, ...) floats of scratch (the splits' partial sums)
 cudaError_t launch_sdpa(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int T, int nq, int nkv, int hd,
-                        int max_seq, int n_seqs, const int32_t* seq, const int32_t* pos, uint16_t* out,
-                        cudaStream_t st);
+                        int max_seq, int n_seqs, const int32_t* seq, const int32_t* pos, uint16_t* out, float* part,
+                        int num_sms, cudaStream_t st);
+int sdpa_splits(int T, int nkv, int num_sms);
+size_t sdpa_part_floats(int max_tokens, int nq, int nkv, int hd, int num_sms);
 cudaError_t launch_residual_add(const uint16_t* x, const float* o, size_t n, uint16_t* out, cudaStream_t st);
 // cos/sin of pos * theta^(-2i/hd) for pos < max_seq, i < hd/2, interleaved, computed in double, as fp32
 void rope_table(double theta, int hd, int max_seq, float* out);
