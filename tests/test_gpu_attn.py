@@ -104,5 +104,7 @@ def test_attention_host_errors(attn):
     with pytest.raises(obsmoe.ObsError, match="bad attention config"):
         c2.attn_init(NQ, 5, HD, MAX_SEQ, 1, THETA)
     with pytest.raises(obsmoe.ObsError, match="bad attention config"):
+        c2.attn_init(NQ, 2, HD, MAX_SEQ, 1, THETA)  # 16 query heads per KV head: more than one CTA takes
+    with pytest.raises(obsmoe.ObsError, match="bad attention config"):
         c2.attn_init(NQ, NKV, HD, 40961, 1, THETA)
     c2.close()
